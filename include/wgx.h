@@ -1,0 +1,218 @@
+/*
+ * wgx.h - C ABI of the B200-native dense-contraction engine behind the
+ * wgpu-executorch operator / program API.
+ *
+ * Every entry point returns an int status (WGX_OK == 0). On failure the
+ * calling thread's message is available from wgx_last_error(); the message
+ * wording follows the reference's thrown Error strings so that a host shim
+ * (Node-API, ctypes) can rethrow them unchanged.
+ *
+ * Reference interfaces replaced (paths inside barhanc/wgpu-executorch):
+ *   src/context.ts  WgpuExecutionContext      -> wgx_context_* / wgx_submit ...
+ *   src/tensor.ts   Tensor                    -> wgx_tensor_*
+ *   src/program.ts  Program + resolveArgs     -> wgx_record_program
+ *   src/shader.ts   Shader.recordIn           -> wgx_record_op
+ *   src/command.ts  createComputeBundle       -> (internal: launch records)
+ *   src/shaders/mm, convolution, conv-with-clamp (WGSL kernels)
+ *                                             -> wgx_mm / wgx_conv2d
+ *
+ * No torch types appear here: plain pointers, sizes and opaque handles.
+ */
+#ifndef WGX_H
+#define WGX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define WGX_API __attribute__((visibility("default")))
+#else
+#define WGX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ */
+/* status codes                                                        */
+/* ------------------------------------------------------------------ */
+#define WGX_OK 0
+#define WGX_ERR_INVALID 1   /* validation error (the reference throws Error) */
+#define WGX_ERR_CUDA 2      /* a CUDA runtime call failed                     */
+#define WGX_ERR_DESTROYED 3 /* context used after destroy()                   */
+#define WGX_ERR_NOMEM 4     /* device or pinned allocation failed             */
+#define WGX_ERR_DEVICE 5    /* a kernel reported an error (bounded wait ran out) */
+#define WGX_ERR_UNSUPPORTED 6
+
+/* dtypes, in the order of src/tensor.ts:4-5 (DType) */
+#define WGX_FLOAT32 0
+#define WGX_FLOAT16 1
+#define WGX_INT32 2
+#define WGX_INT8 3
+#define WGX_UINT8 4
+#define WGX_BOOL 5
+#define WGX_FLOAT64 6
+#define WGX_INT64 7
+
+/* buffer usage bits: the GPUBufferUsage values the reference checks
+ * (src/context.ts:10-11, 175-180; src/tensor.ts:67-69, 118-120) */
+#define WGX_USAGE_MAP_READ 0x0001u
+#define WGX_USAGE_COPY_SRC 0x0004u
+#define WGX_USAGE_COPY_DST 0x0008u
+#define WGX_USAGE_UNIFORM 0x0040u
+#define WGX_USAGE_STORAGE 0x0080u
+
+#define WGX_MAX_NDIM 8 /* src/tensor.ts:23 MAX_NDIM */
+
+typedef struct wgx_context wgx_context;
+typedef struct wgx_buffer wgx_buffer;
+typedef struct wgx_tensor wgx_tensor;
+
+/* Positional operator argument: the resolved form of one Program value
+ * (src/program.ts:188-224 resolveArgs: Tensor | scalar | number[] |
+ * Tensor[] | undefined). */
+#define WGX_ARG_NULL 0
+#define WGX_ARG_TENSOR 1
+#define WGX_ARG_NUMBER 2 /* JS number: f64 */
+#define WGX_ARG_BOOL 3
+#define WGX_ARG_INT_LIST 4
+#define WGX_ARG_TENSOR_LIST 5
+#define WGX_ARG_STRING 6
+
+typedef struct wgx_arg {
+  int32_t kind;
+  int32_t count; /* list length */
+  union {
+    wgx_tensor *tensor;
+    double number;
+    int32_t boolean;
+    const int64_t *ints;
+    wgx_tensor *const *tensors;
+    const char *string;
+  } v;
+} wgx_arg;
+
+/* ------------------------------------------------------------------ */
+/* errors / library                                                    */
+/* ------------------------------------------------------------------ */
+WGX_API const char *wgx_last_error(void);
+WGX_API int wgx_version(void);
+WGX_API int wgx_device_count(int *count);
+
+/* ------------------------------------------------------------------ */
+/* context: src/context.ts:17 WgpuExecutionContext                     */
+/* ------------------------------------------------------------------ */
+/* new WgpuExecutionContext(device)  (src/context.ts:28-30) */
+WGX_API int wgx_context_create(int device, wgx_context **out);
+/* destroy(): frees owned buffers, idempotent; afterwards every call fails
+ * with "WgpuExecutionContext is destroyed" (src/context.ts:52-72). */
+WGX_API int wgx_context_destroy(wgx_context *ctx);
+/* frees the handle itself (after destroy); the JS object's finaliser */
+WGX_API int wgx_context_release(wgx_context *ctx);
+/* storageBuffer(size): STORAGE|COPY_SRC|COPY_DST, size rounded up to 4,
+ * minimum 4, owned by the context (src/context.ts:86-92). */
+WGX_API int wgx_storage_buffer(wgx_context *ctx, uint64_t size, wgx_buffer **out);
+/* device.createBuffer({size, usage}) on CUDA device `device`: a buffer no
+ * context owns (tests/api/context.test.ts:31-67 build such buffers). */
+WGX_API int wgx_buffer_create(int device, uint64_t size, uint32_t usage, wgx_buffer **out);
+WGX_API int wgx_buffer_destroy(wgx_buffer *buf);
+WGX_API int wgx_buffer_info(const wgx_buffer *buf, uint64_t *size, uint32_t *usage, void **device_ptr);
+/* tensor(dtype, shape, buffer?) (src/context.ts:135-147): buffer NULL ->
+ * a new storage buffer owned by ctx; else a non-owning view, and ctx may be
+ * NULL (new Tensor(dtype, shape, device, buffer), src/tensor.ts:50-71). */
+WGX_API int wgx_tensor_create(wgx_context *ctx, int dtype, const int64_t *shape, int ndim,
+                      wgx_buffer *buffer_or_null, wgx_tensor **out);
+WGX_API int wgx_tensor_release(wgx_tensor *t);
+WGX_API int wgx_tensor_info(const wgx_tensor *t, int *dtype, int *ndim, int64_t *shape,
+                    uint64_t *byte_length, void **device_ptr);
+/* Tensor.setData (src/tensor.ts:115-135): prefix write, padded with zeros
+ * to 4 bytes, error if larger than the tensor. */
+WGX_API int wgx_tensor_set_data(wgx_tensor *t, const void *src, uint64_t nbytes);
+/* Tensor.getData (src/tensor.ts:142-158): waits for submitted work and
+ * copies byteLength bytes to dst. */
+WGX_API int wgx_tensor_get_data(wgx_tensor *t, void *dst, uint64_t nbytes);
+/* copy(src, dst) (src/context.ts:172-192): recorded buffer copy. */
+WGX_API int wgx_copy(wgx_context *ctx, wgx_tensor *src, wgx_tensor *dst);
+/* recordShader(shader, args) (src/context.ts:201-205) with the shader
+ * looked up by ExecuTorch name (src/shaders/index.ts:58-60). */
+WGX_API int wgx_record_op(wgx_context *ctx, const char *op_name, const wgx_arg *args, int nargs);
+/* recordProgram(program, weights, args) (src/context.ts:219-317); the
+ * Program is its JSON text (src/program.ts:150-165). args are the I/O
+ * values [in..., out...]. */
+WGX_API int wgx_record_program(wgx_context *ctx, const char *json, uint64_t json_len,
+                       const void *weights, uint64_t weights_len, const wgx_arg *args,
+                       int nargs);
+/* submit() (src/context.ts:323-370): first call after recording captures
+ * the command list into a CUDA graph, every call launches the graph. */
+WGX_API int wgx_submit(wgx_context *ctx);
+/* sync() (src/context.ts:377-380) */
+WGX_API int wgx_sync(wgx_context *ctx);
+/* reset() (src/context.ts:386-389) */
+WGX_API int wgx_reset(wgx_context *ctx);
+/* number of recorded commands and of kernel launches one submit replays */
+WGX_API int wgx_context_stats(const wgx_context *ctx, int64_t *n_commands, int64_t *n_kernel_launches);
+/* the context's CUDA stream (cudaStream_t) for callers that interleave work */
+WGX_API int wgx_context_stream(const wgx_context *ctx, void **stream);
+
+/* ------------------------------------------------------------------ */
+/* stateless hot-path kernels                                          */
+/* ------------------------------------------------------------------ */
+/* out[M,N] = a[M,K] @ b[K,N], row-major, dtype WGX_FLOAT32 or
+ * WGX_FLOAT16 (src/shaders/mm/index.ts:32-93; mm-64x64.wgsl.ts:8-115).
+ * fp16 accumulates in fp32. scratch: wgx_mm_scratch_bytes(). */
+WGX_API int wgx_mm_scratch_bytes(int64_t M, int64_t N, int64_t K, int dtype, uint64_t *bytes);
+WGX_API int wgx_mm(const void *a, const void *b, void *out, int64_t M, int64_t N, int64_t K, int dtype,
+           void *scratch, uint64_t scratch_bytes, void *stream);
+
+/* epilogue activations */
+#define WGX_ACT_NONE 0
+#define WGX_ACT_CLAMP 1 /* et_vk.conv_with_clamp: clamp(v, min, max) */
+#define WGX_ACT_SILU 2  /* v * sigmoid(v): conv -> sigmoid -> mul      */
+
+/* aten.convolution / et_vk.conv_with_clamp geometry: the 80-byte
+ * ConvParams of src/shaders/convolution/index.ts:149-162 plus the clamp
+ * words of src/shaders/conv-with-clamp/index.ts:146-164. */
+typedef struct wgx_conv2d_params {
+  int32_t B, IC, IH, IW;
+  int32_t OC, OH, OW;
+  int32_t KH, KW;
+  int32_t sH, sW, pH, pW, dH, dW;
+  int32_t groups;
+  int32_t has_bias;
+  int32_t dtype;      /* WGX_FLOAT32 / WGX_FLOAT16 */
+  int32_t act;        /* WGX_ACT_* */
+  float out_min;      /* clamp bounds (-inf/+inf when absent) */
+  float out_max;
+} wgx_conv2d_params;
+
+/* kernel variant chosen for a convolution (host-only, no GPU needed) */
+#define WGX_CONV_UMMA 1       /* tcgen05/TMEM implicit GEMM (fp16) */
+#define WGX_CONV_SIMT_GEMM 2  /* FFMA implicit GEMM (fp32, odd shapes) */
+#define WGX_CONV_DEPTHWISE 3  /* memory-bound depthwise */
+#define WGX_CONV_DIRECT 4     /* grouped direct conv */
+#define WGX_CONV_POINTWISE1 5 /* single output channel 1x1 */
+
+typedef struct wgx_conv2d_plan {
+  int32_t variant;
+  int32_t n_launches;
+  uint64_t scratch_bytes;
+  uint64_t grid_ctas; /* CTAs of the main kernel */
+} wgx_conv2d_plan;
+
+WGX_API int wgx_conv2d_plan_for(const wgx_conv2d_params *p, wgx_conv2d_plan *out);
+/* in: NCHW [B,IC,IH,IW]; w: OIHW [OC,IC/groups,KH,KW]; bias: [OC] or NULL;
+ * out: NCHW [B,OC,OH,OW]. The packed-weight cache lives in scratch. */
+WGX_API int wgx_conv2d(const wgx_conv2d_params *p, const void *in, const void *w, const void *bias,
+               void *out, void *scratch, uint64_t scratch_bytes, void *stream);
+
+/* ------------------------------------------------------------------ */
+/* device error word: kernels with bounded waits set it instead of      */
+/* hanging; wgx_sync reports it.                                        */
+/* ------------------------------------------------------------------ */
+WGX_API int wgx_device_error(int device, uint32_t *code, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WGX_H */

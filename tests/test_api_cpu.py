@@ -1,0 +1,101 @@
+"""CPU-only checks of the C-ABI library: it loads, exports every symbol the
+header declares, plans kernel variants without a GPU, and fails cleanly
+when no device is present."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import wgx
+from wgx import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    src = open(os.path.join(ROOT, "include", "wgx.h")).read()
+    return sorted(set(re.findall(r"WGX_API\s+(?:const\s+)?\w+\s*\*?\s*(wgx_\w+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    syms = header_symbols()
+    assert "wgx_record_program" in syms and "wgx_conv2d" in syms and "wgx_mm" in syms
+    assert len(syms) >= 28
+
+
+def test_library_exports_every_header_symbol():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    missing = [s for s in header_symbols() if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_header():
+    assert set(header_symbols()) <= set(_lib.SIGNATURES)
+
+
+def test_version_and_device_count():
+    assert _lib.lib.wgx_version() == 1
+    assert wgx.device_count() >= 0
+
+
+@pytest.mark.skipif(wgx.device_count() > 0, reason="a GPU is present")
+def test_context_without_gpu_raises_cleanly():
+    with pytest.raises(wgx.WgxError, match="no CUDA device"):
+        wgx.WgpuExecutionContext(0)
+
+
+def test_tensor_shape_validation_messages():
+    dev = wgx.Device(0)
+    with pytest.raises(wgx.WgxError, match="exceeds maximum rank"):
+        wgx.Tensor("float32", [1] * (wgx.MAX_NDIM + 1), dev, None)
+    with pytest.raises(wgx.WgxError, match="positive integers"):
+        wgx.Tensor("float32", [0, 3], dev, None)
+    with pytest.raises(wgx.WgxError, match="positive integers"):
+        wgx.Tensor("float32", [-1, 3], dev, None)
+    with pytest.raises(wgx.WgxError, match="positive integers"):
+        wgx.Tensor("float32", [1.5, 3], dev, None)
+
+
+def plan(**kw):
+    p = _lib.ConvParams()
+    d = dict(B=1, IC=1, IH=1, IW=1, OC=1, OH=1, OW=1, KH=1, KW=1, sH=1, sW=1, pH=0, pW=0, dH=1,
+             dW=1, groups=1, has_bias=1, dtype=1, act=0, out_min=-np.inf, out_max=np.inf)
+    d.update(kw)
+    for k, v in d.items():
+        setattr(p, k, v)
+    out = _lib.ConvPlan()
+    _lib.check(_lib.lib.wgx_conv2d_plan_for(ctypes.byref(p), ctypes.byref(out)))
+    return out
+
+
+def test_plan_selects_tensor_core_path_for_dense_fp16():
+    # [8,64,160,160] x [128,64,3,3], s1 p1
+    p = plan(B=8, IC=64, IH=160, IW=160, OC=128, OH=160, OW=160, KH=3, KW=3, pH=1, pW=1)
+    assert p.variant == _lib.CONV_UMMA
+    # 128 output channels x 512 positions per CTA: 51 tiles per image
+    assert p.grid_ctas == 8 * 51
+    assert p.scratch_bytes > 8 * 64 * 162 * 162 * 2
+
+
+def test_plan_depthwise_and_pointwise_of_config3():
+    dw = plan(B=16, IC=256, IH=80, IW=80, OC=256, OH=80, OW=80, KH=5, KW=5, pH=2, pW=2,
+              groups=256)
+    assert dw.variant == _lib.CONV_DEPTHWISE
+    pw = plan(B=16, IC=256, IH=80, IW=80, OC=256, OH=80, OW=80)
+    assert pw.variant == _lib.CONV_UMMA
+
+
+def test_plan_fallbacks():
+    assert plan(dtype=0, B=1, IC=64, IH=8, IW=8, OC=64, OH=8, OW=8).variant == _lib.CONV_SIMT_GEMM
+    assert plan(IC=3, OC=1, IH=4, IW=4, OH=4, OW=4).variant == _lib.CONV_POINTWISE1
+    assert plan(IC=4, OC=4, groups=2, IH=2, IW=2, OH=2, OW=2).variant == _lib.CONV_DIRECT
+    # YOLO stem: IC=3, stride 2 -> CUDA-core implicit GEMM
+    assert plan(IC=3, IH=640, IW=640, OC=16, OH=320, OW=320, KH=3, KW=3, sH=2, sW=2, pH=1,
+                pW=1).variant == _lib.CONV_SIMT_GEMM
+
+
+def test_plan_rejects_bad_geometry():
+    with pytest.raises(wgx.WgxError):
+        plan(IC=3, OC=4, groups=2)

@@ -1,0 +1,305 @@
+"""Parity of the B200 kernels with the CPU oracle on seeded inputs.
+
+Tolerances (metric: max|y - ref| / max|ref|, ``oracle.rel_err``):
+  * fp32 paths (FFMA, fp32 accumulation): <= 1e-4 against both the exact
+    oracle and the reference's own fp32 arithmetic (north-star bound 1e-4).
+  * fp16 paths (tcgen05 fp32 accumulation, one rounding to fp16):
+    <= 2e-3 against the exact oracle (one fp16 rounding is 2^-11 of a value)
+    and <= 2e-2 against the reference's f16-accumulating arithmetic
+    (north-star bound 2e-2).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+import wgx
+from wgx import _lib
+
+pytestmark = pytest.mark.gpu
+
+F16_EXACT, F16_WGSL, F32_TOL = 2e-3, 2e-2, 1e-4
+
+
+def dtname(a):
+    return "float16" if a.dtype == np.float16 else "float32"
+
+
+def engine_conv(ctx, x, w, b, stride, pad, dil, groups, clamp=None):
+    dt = dtname(x)
+    tx = ctx.tensor(dt, x.shape).setData(x)
+    tw = ctx.tensor(dt, w.shape).setData(w)
+    tb = ctx.tensor(dt, b.shape).setData(b) if b is not None else None
+    B, IC, H, W = x.shape
+    OC, _, KH, KW = w.shape
+    OH, OW = oracle.conv_out_hw(H, W, KH, KW, (stride,) * 2 if np.isscalar(stride) else stride,
+                                (pad,) * 2 if np.isscalar(pad) else pad,
+                                (dil,) * 2 if np.isscalar(dil) else dil)
+    out = ctx.tensor(dt, [B, OC, OH, OW])
+    hw = lambda v: [v, v] if np.isscalar(v) else list(v)
+    if clamp is None:
+        ctx.recordShader(wgx.shaders.convolution,
+                         [tx, tw, tb, hw(stride), hw(pad), hw(dil), False, [0, 0], groups, out])
+    else:
+        ctx.recordShader(wgx.shaders.convWithClamp,
+                         [tx, tw, tb, hw(stride), hw(pad), hw(dil), False, [0, 0], groups,
+                          clamp[0], clamp[1], out])
+    ctx.submit()
+    ctx.sync()
+    res = out.numpy()
+    ctx.reset()
+    return res
+
+
+def check_f16(y, x, w, b, stride, pad, dil, groups, act=oracle.ACT_NONE, lo=-np.inf, hi=np.inf,
+              clamp_op=False):
+    ex = oracle.conv2d(x, w, b, stride, pad, dil, groups, act=act, out_min=lo, out_max=hi,
+                       mode="exact", clamp_op=clamp_op)
+    e1 = oracle.rel_err(y, ex)
+    assert np.all(np.isfinite(y.astype(np.float32)))
+    assert e1 <= F16_EXACT, f"vs exact oracle: {e1}"
+    if act != oracle.ACT_SILU:
+        wg = oracle.conv2d(x, w, b, stride, pad, dil, groups, act=act, out_min=lo, out_max=hi,
+                           mode="wgsl", clamp_op=clamp_op)
+        e2 = oracle.rel_err(y, wg)
+        assert e2 <= F16_WGSL, f"vs reference f16 arithmetic: {e2}"
+    return e1
+
+
+def kaiming(shape, seed, dtype=np.float16):
+    fan_in = int(np.prod(shape[1:]))
+    (w,) = oracle.make_inputs([shape], seed=seed, dtype=np.float32)
+    return (w * np.sqrt(2.0 / fan_in)).astype(dtype)
+
+
+# (B, IC, H, W, OC, KH, KW, pad, dil): stride-1 dense fp16 -> tensor-core path
+DENSE_F16 = [
+    (1, 64, 160, 160, 128, 3, 3, 1, 1),   # BASELINE config 2 geometry, one image
+    (2, 8, 7, 9, 5, 3, 3, 1, 1),
+    (1, 40, 13, 11, 130, 3, 3, 1, 1),     # two output-channel tiles, IC % 32 != 0
+    (3, 32, 20, 20, 16, 1, 1, 0, 1),      # 1x1
+    (1, 16, 9, 33, 64, 5, 5, 2, 1),
+    (1, 24, 17, 17, 33, 7, 7, 3, 1),
+    (2, 64, 10, 10, 32, 3, 3, 2, 2),      # dilation 2
+    (1, 256, 20, 20, 256, 3, 3, 1, 1),
+    (1, 8, 1, 600, 8, 1, 3, 0, 1),        # 1-row image, KH != KW
+    (1, 96, 40, 40, 96, 3, 3, 1, 1),
+]
+
+
+@pytest.mark.parametrize("geom", DENSE_F16, ids=[str(g) for g in DENSE_F16])
+def test_dense_f16_tensor_core(ctx, geom):
+    B, IC, H, W, OC, KH, KW, pad, dil = geom
+    (x,) = oracle.make_inputs([(B, IC, H, W)], seed=10)
+    w = kaiming((OC, IC, KH, KW), 11)
+    (b,) = oracle.make_inputs([(OC,)], seed=12, scale=0.01)
+    pads = (pad if KH > 1 else 0, pad)
+    y = engine_conv(ctx, x, w, b, 1, pads, dil, 1)
+    check_f16(y, x, w, b, 1, pads, dil, 1)
+
+
+def test_dense_f16_no_bias_and_clamp(ctx):
+    (x,) = oracle.make_inputs([(2, 48, 15, 17)], seed=20)
+    w = kaiming((40, 48, 3, 3), 21)
+    y = engine_conv(ctx, x, w, None, 1, 1, 1, 1)
+    check_f16(y, x, w, None, 1, 1, 1, 1)
+    y = engine_conv(ctx, x, w, None, 1, 1, 1, 1, clamp=(0.0, float(np.finfo(np.float64).max)))
+    check_f16(y, x, w, None, 1, 1, 1, 1, act=oracle.ACT_CLAMP, lo=0.0, hi=np.inf, clamp_op=True)
+
+
+@pytest.mark.parametrize("geom", [
+    (1, 3, 64, 64, 16, 3, 2, 1),     # YOLO stem shape (stride 2, IC = 3)
+    (2, 32, 21, 19, 64, 3, 2, 1),    # stride-2 downsampling conv
+    (1, 5, 7, 7, 3, 3, 1, 1),        # IC < 8
+])
+def test_dense_f16_cuda_core_fallback(ctx, geom):
+    B, IC, H, W, OC, K, s, p = geom
+    (x,) = oracle.make_inputs([(B, IC, H, W)], seed=30)
+    w = kaiming((OC, IC, K, K), 31)
+    (b,) = oracle.make_inputs([(OC,)], seed=32, scale=0.01)
+    y = engine_conv(ctx, x, w, b, s, p, 1, 1)
+    check_f16(y, x, w, b, s, p, 1, 1)
+
+
+@pytest.mark.parametrize("geom", [
+    (1, 256, 80, 80, 5, 1, 2, 1),    # BASELINE config 3 depthwise, one image
+    (2, 8, 9, 13, 3, 2, 1, 1),
+    (1, 16, 33, 31, 7, 1, 3, 1),
+    (1, 12, 24, 24, 3, 1, 2, 2),
+    (3, 32, 40, 40, 3, 1, 1, 1),
+    (1, 4, 224, 224, 3, 2, 1, 1),
+])
+@pytest.mark.parametrize("dtype", [np.float16, np.float32])
+def test_depthwise(ctx, geom, dtype):
+    B, C, H, W, K, s, p, d = geom
+    (x,) = oracle.make_inputs([(B, C, H, W)], seed=40, dtype=dtype)
+    (w, b) = oracle.make_inputs([(C, 1, K, K), (C,)], seed=41, scale=[0.1, 0.01], dtype=dtype)
+    y = engine_conv(ctx, x, w, b, s, p, d, C)
+    if dtype == np.float16:
+        check_f16(y, x, w, b, s, p, d, C)
+    else:
+        ex = oracle.conv2d(x, w, b, s, p, d, C, mode="exact")
+        assert oracle.rel_err(y, ex) <= F32_TOL
+        assert oracle.rel_err(y, oracle.conv2d(x, w, b, s, p, d, C, mode="wgsl")) <= F32_TOL
+
+
+def test_depthwise_relu6_clamp(ctx):
+    (x,) = oracle.make_inputs([(2, 24, 28, 28)], seed=42)
+    (w, b) = oracle.make_inputs([(24, 1, 3, 3), (24,)], seed=43, scale=[0.5, 0.1])
+    y = engine_conv(ctx, x, w, b, 1, 1, 1, 24, clamp=(0.0, 6.0))
+    check_f16(y, x, w, b, 1, 1, 1, 24, act=oracle.ACT_CLAMP, lo=0.0, hi=6.0, clamp_op=True)
+
+
+@pytest.mark.parametrize("dtype", [np.float16, np.float32])
+def test_grouped_direct(ctx, dtype):
+    (x, w, b) = oracle.make_inputs([(2, 8, 11, 9), (6, 4, 3, 3), (6,)], seed=50, dtype=dtype)
+    y = engine_conv(ctx, x, w, b, 1, 1, 1, 2)
+    ex = oracle.conv2d(x, w, b, 1, 1, 1, 2, mode="exact")
+    tol = F16_EXACT if dtype == np.float16 else F32_TOL
+    assert oracle.rel_err(y, ex) <= tol
+
+
+@pytest.mark.parametrize("geom", [(2, 16, 8, 8, 3), (1, 64, 12, 12, 5), (2, 3, 9, 9, 4)])
+@pytest.mark.parametrize("dtype", [np.float32])
+def test_fp32_dense(ctx, geom, dtype):
+    B, IC, H, W, OC = geom
+    (x, w, b) = oracle.make_inputs([(B, IC, H, W), (OC, IC, 3, 3), (OC,)], seed=60, dtype=dtype)
+    y = engine_conv(ctx, x, w, b, 1, 1, 1, 1)
+    assert oracle.rel_err(y, oracle.conv2d(x, w, b, 1, 1, 1, 1, mode="exact")) <= F32_TOL
+    assert oracle.rel_err(y, oracle.conv2d(x, w, b, 1, 1, 1, 1, mode="wgsl")) <= F32_TOL
+
+
+def test_single_channel_pointwise_f16(ctx):
+    (x, w, b) = oracle.make_inputs([(3, 24, 20, 28), (1, 24, 1, 1), (1,)], seed=70)
+    y = engine_conv(ctx, x, w, b, 1, 0, 1, 1, clamp=(-1.0, 1.0))
+    check_f16(y, x, w, b, 1, 0, 1, 1, act=oracle.ACT_CLAMP, lo=-1.0, hi=1.0, clamp_op=True)
+
+
+# ------------------------------------------------------------------ mm
+def engine_mm(ctx, a, b):
+    dt = dtname(a)
+    ta = ctx.tensor(dt, a.shape).setData(a)
+    tb = ctx.tensor(dt, b.shape).setData(b)
+    out = ctx.tensor(dt, [a.shape[0], b.shape[1]])
+    ctx.recordShader(wgx.shaders.mm, [ta, tb, out])
+    ctx.submit()
+    ctx.sync()
+    r = out.numpy()
+    ctx.reset()
+    return r
+
+
+def test_mm_fp32_config1(ctx):
+    # A[512,512] @ B[512,512], U(-1,1), seed 0
+    a, b = oracle.make_inputs([(512, 512), (512, 512)], seed=0, dist="uniform", dtype=np.float32)
+    y = engine_mm(ctx, a, b)
+    assert oracle.rel_err(y, oracle.mm(a, b, "exact")) <= F32_TOL
+    assert oracle.rel_err(y, oracle.mm(a, b, "wgsl")) <= F32_TOL
+
+
+@pytest.mark.parametrize("mkn", [(512, 512, 512), (100, 72, 300), (64, 8, 1000), (300, 200, 7),
+                                 (257, 1024, 129), (5, 7, 3)])
+def test_mm_fp16(ctx, mkn):
+    M, K, N = mkn
+    a, b = oracle.make_inputs([(M, K), (K, N)], seed=80, dist="uniform")
+    y = engine_mm(ctx, a, b)
+    assert oracle.rel_err(y, oracle.mm(a, b, "exact")) <= F16_EXACT
+    assert oracle.rel_err(y, oracle.mm(a, b, "wgsl")) <= F16_WGSL
+
+
+# ----------------------------------------------- stateless C-ABI entry
+def c_conv(ctx, x, w, b, pad, act, lo=-np.inf, hi=np.inf):
+    """wgx_conv2d with device pointers, a caller-provided scratch and the
+    context's stream."""
+    B, IC, H, W = x.shape
+    OC, _, KH, KW = w.shape
+    p = _lib.ConvParams(B, IC, H, W, OC, H + 2 * pad - KH + 1, W + 2 * pad - KW + 1, KH, KW, 1, 1,
+                        pad, pad, 1, 1, 1, int(b is not None), 1, act, lo, hi)
+    plan = _lib.ConvPlan()
+    _lib.check(_lib.lib.wgx_conv2d_plan_for(ctypes.byref(p), ctypes.byref(plan)))
+    tx = ctx.tensor("float16", x.shape).setData(x)
+    tw = ctx.tensor("float16", w.shape).setData(w)
+    tb = ctx.tensor("float16", b.shape).setData(b) if b is not None else None
+    out = ctx.tensor("float16", [B, OC, p.OH, p.OW])
+    scratch = ctx.storageBuffer(max(16, plan.scratch_bytes))
+    _lib.check(_lib.lib.wgx_conv2d(ctypes.byref(p), tx.data_ptr, tw.data_ptr,
+                                   tb.data_ptr if tb else None, out.data_ptr, scratch.device_ptr,
+                                   scratch.size, ctx.stream))
+    ctx.sync()
+    return out.numpy(), plan
+
+
+def test_stateless_conv_silu_config2_geometry(ctx):
+    (x,) = oracle.make_inputs([(1, 64, 160, 160)], seed=90)
+    w = kaiming((128, 64, 3, 3), 91)
+    (b,) = oracle.make_inputs([(128,)], seed=92, scale=0.01)
+    y, plan = c_conv(ctx, x, w, b, 1, _lib.ACT_SILU)
+    assert plan.variant == _lib.CONV_UMMA
+    check_f16(y, x, w, b, 1, 1, 1, 1, act=oracle.ACT_SILU)
+
+
+def test_config2_full_batch_properties(ctx):
+    """BASELINE config 2 at full size ([8,64,160,160], fused SiLU): image 0
+    against the oracle, and every image equal (bit for bit) to the same
+    image convolved alone."""
+    x = oracle.make_inputs([(8, 64, 160, 160)], seed=0)[0]
+    w = kaiming((128, 64, 3, 3), 1)
+    (b,) = oracle.make_inputs([(128,)], seed=2, scale=0.01)
+    y, _ = c_conv(ctx, x, w, b, 1, _lib.ACT_SILU)
+    check_f16(y[:1], x[:1], w, b, 1, 1, 1, 1, act=oracle.ACT_SILU)
+    for i in (3, 7):
+        yi, _ = c_conv(ctx, x[i:i + 1], w, b, 1, _lib.ACT_SILU)
+        np.testing.assert_array_equal(yi[0], y[i])
+
+
+# --------------------------------------------------- program fusion
+@pytest.mark.parametrize("out_pool,commands", [(3, 3), (0, 5)])
+def test_program_conv_sigmoid_mul_fusion(ctx, out_pool, commands):
+    """conv -> sigmoid -> mul becomes one conv with a SiLU epilogue (input
+    copy + conv + output copy = 3 commands); when the mul's output shares the
+    conv input's pool the ops stay separate (5 commands)."""
+    (x,) = oracle.make_inputs([(2, 32, 24, 24)], seed=100)
+    w = kaiming((48, 32, 3, 3), 101)
+    (b,) = oracle.make_inputs([(48,)], seed=102, scale=0.01)
+    wbytes = w.tobytes() + b.tobytes()
+    prog = {
+        "version": "1",
+        "chain": [
+            {"name": "aten.convolution.default", "args": [0, 1, 2, 3, 4, 5, 6, 7, 8, 9]},
+            {"name": "aten.sigmoid.default", "args": [9, 10]},
+            {"name": "aten.mul.Tensor", "args": [9, 10, 11]},
+        ],
+        "values": [
+            {"type": "tensor", "shape": [2, 32, 24, 24], "dtype": "float16", "memObjId": 0},
+            {"type": "tensor", "shape": [48, 32, 3, 3], "dtype": "float16", "weightsOffset": 0,
+             "weightsLength": w.nbytes},
+            {"type": "tensor", "shape": [48], "dtype": "float16", "weightsOffset": w.nbytes,
+             "weightsLength": b.nbytes},
+            {"type": "list", "items": [1, 1]},
+            {"type": "list", "items": [1, 1]},
+            {"type": "list", "items": [1, 1]},
+            {"type": "scalar", "value": False},
+            {"type": "list", "items": [0, 0]},
+            {"type": "scalar", "value": 1},
+            {"type": "tensor", "shape": [2, 48, 24, 24], "dtype": "float16", "memObjId": 1},
+            {"type": "tensor", "shape": [2, 48, 24, 24], "dtype": "float16", "memObjId": 2},
+            {"type": "tensor", "shape": [2, 48, 24, 24], "dtype": "float16",
+             "memObjId": out_pool},
+        ],
+        "inputIds": [0],
+        "outputIds": [11],
+        "memoryPlan": {"pools": [{"id": 0, "size": 2 * 48 * 24 * 24 * 2},
+                                 {"id": 1, "size": 2 * 48 * 24 * 24 * 2},
+                                 {"id": 2, "size": 2 * 48 * 24 * 24 * 2},
+                                 {"id": 3, "size": 2 * 48 * 24 * 24 * 2}]},
+    }
+    tin = ctx.tensor("float16", x.shape).setData(x)
+    tout = ctx.tensor("float16", [2, 48, 24, 24])
+    ctx.recordProgram(prog, wbytes, [tin, tout])
+    ctx.submit()
+    ctx.sync()
+    y = tout.numpy()
+    assert ctx.stats()["commands"] == commands
+    ex = oracle.conv2d(x, w, b, 1, 1, 1, 1, act=oracle.ACT_SILU, mode="exact")
+    assert oracle.rel_err(y, ex) <= 5e-3

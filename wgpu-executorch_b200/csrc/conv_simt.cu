@@ -1,0 +1,538 @@
+// CUDA-core convolution kernels and the convolution dispatcher.
+//
+// The reference computes every aten.convolution / et_vk.conv_with_clamp
+// variant with WGSL kernels (src/shaders/convolution/*.wgsl.ts,
+// src/shaders/conv-with-clamp/*.wgsl.ts) selected in
+// src/shaders/convolution/index.ts:171-238 and
+// src/shaders/conv-with-clamp/index.ts:173-243. Here the dense fp16 case
+// runs on tcgen05 tensor cores (umma_conv.cu); this file holds the
+// remaining variants:
+//   * simt_gemm_conv: fp32 (and odd-shaped fp16) implicit-im2col GEMM,
+//     the FFMA path for fp32 models (fp32 accumulation);
+//   * depthwise: groups == IC == OC, memory bound, smem row tile, f32 acc;
+//   * direct: any other grouping (grouped direct conv of conv2d.wgsl.ts);
+//   * conv_transpose: transposed conv gather (conv-transpose2d.wgsl.ts);
+//   * pointwise_single: 1x1 conv with one output channel, f32 accumulation
+//     (conv-with-clamp-1x1-single-channel*.wgsl.ts).
+// All of them apply bias, then the activation (clamp or SiLU) in fp32 and
+// round once to the storage type.
+#include "internal.h"
+#include "umma_conv.h"
+
+namespace wgx {
+
+template <class T>
+__device__ __forceinline__ float ld_f(const T *p) {
+  return float(*p);
+}
+template <>
+__device__ __forceinline__ float ld_f<__half>(const __half *p) {
+  return __half2float(*p);
+}
+template <class T>
+__device__ __forceinline__ T to_t(float v);
+template <>
+__device__ __forceinline__ float to_t<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ __half to_t<__half>(float v) {
+  return __float2half_rn(v);
+}
+
+__device__ __forceinline__ float apply_act(float v, int act, float lo, float hi) {
+  if (act == WGX_ACT_CLAMP) return fminf(fmaxf(v, lo), hi);
+  if (act == WGX_ACT_SILU) return v / (1.0f + __expf(-v));
+  return v;
+}
+
+struct ConvGeom {
+  int B, IC, IH, IW, OC, OH, OW, KH, KW, sH, sW, pH, pW, dH, dW, groups, has_bias, act;
+  float lo, hi;
+};
+
+static ConvGeom geom_of(const wgx_conv2d_params &p) {
+  return ConvGeom{p.B,  p.IC, p.IH, p.IW, p.OC, p.OH, p.OW,     p.KH,       p.KW,  p.sH, p.sW,
+                  p.pH, p.pW, p.dH, p.dW, p.groups, p.has_bias, p.act, p.out_min, p.out_max};
+}
+
+// ---------------------------------------------------------------------------
+// simt_gemm_conv: implicit-im2col GEMM on CUDA cores, groups == 1.
+// GEMM view (as in conv2d-tile64.wgsl.ts:35-41): M = OC, N = B*OH*OW,
+// K = IC*KH*KW, weights OIHW = [M, K] row-major, input gathered per
+// element with zero fill outside the image. 64x64 tile, 256 threads, 4x4
+// outputs per thread, K step 16, fp32 accumulation.
+// ---------------------------------------------------------------------------
+template <class T>
+__global__ void __launch_bounds__(256) simt_gemm_conv(ConvGeom g, const T *__restrict__ x,
+                                                      const T *__restrict__ w,
+                                                      const T *__restrict__ bias,
+                                                      T *__restrict__ out) {
+  constexpr int BM = 64, BN = 64, BK = 16;
+  __shared__ float As[BK][BM + 4];
+  __shared__ float Bs[BK][BN + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid % 16, ty = tid / 16;
+  const long long M = g.OC;
+  const long long ohw = (long long)g.OH * g.OW;
+  const long long N = (long long)g.B * ohw;
+  const long long K = (long long)g.IC * g.KH * g.KW;
+  const int khw = g.KH * g.KW;
+  const long long m0 = (long long)blockIdx.y * BM;
+  const long long n0 = (long long)blockIdx.x * BN;
+
+  // Each thread loads 4 weights (row a_r, k cols a_c..) and 4 inputs.
+  const int a_r = tid / 4, a_c = (tid % 4) * 4;  // 64 rows x 16 k
+  const int b_k = tid / 16, b_n = (tid % 16) * 4;  // 16 k x 64 n
+  long long nb[4];
+  int ihb[4], iwb[4];
+  bool nv[4];
+  for (int j = 0; j < 4; ++j) {
+    long long n = n0 + b_n + j;
+    nv[j] = n < N;
+    long long nn = nv[j] ? n : 0;
+    long long b = nn / ohw, sp = nn % ohw;
+    int oh = int(sp / g.OW), ow = int(sp % g.OW);
+    nb[j] = b;
+    ihb[j] = oh * g.sH - g.pH;
+    iwb[j] = ow * g.sW - g.pW;
+  }
+  float acc[4][4] = {};
+  for (long long k0 = 0; k0 < K; k0 += BK) {
+    for (int j = 0; j < 4; ++j) {
+      long long m = m0 + a_r, k = k0 + a_c + j;
+      As[a_c + j][a_r] = (m < M && k < K) ? ld_f(&w[m * K + k]) : 0.f;
+    }
+    {
+      long long k = k0 + b_k;
+      int ic = 0, kh = 0, kw = 0;
+      bool kv = k < K;
+      if (kv) {
+        ic = int(k / khw);
+        int r = int(k % khw);
+        kh = r / g.KW;
+        kw = r % g.KW;
+      }
+      for (int j = 0; j < 4; ++j) {
+        float v = 0.f;
+        if (kv && nv[j]) {
+          int ih = ihb[j] + kh * g.dH, iw = iwb[j] + kw * g.dW;
+          if (ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW)
+            v = ld_f(&x[((nb[j] * g.IC + ic) * g.IH + ih) * (long long)g.IW + iw]);
+        }
+        Bs[b_k][b_n + j] = v;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float a[4], b[4];
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+      for (int i = 0; i < 4; ++i)
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  for (int i = 0; i < 4; ++i) {
+    long long m = m0 + ty * 4 + i;
+    if (m >= M) continue;
+    float bv = g.has_bias ? ld_f(&bias[m]) : 0.f;
+    for (int j = 0; j < 4; ++j) {
+      long long n = n0 + tx * 4 + j;
+      if (n >= N) continue;
+      long long b = n / ohw, sp = n % ohw;
+      float v = apply_act(acc[i][j] + bv, g.act, g.lo, g.hi);
+      out[(b * g.OC + m) * ohw + sp] = to_t<T>(v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// direct grouped conv: one thread per output element (conv2d.wgsl.ts).
+// ---------------------------------------------------------------------------
+template <class T>
+__global__ void direct_conv(ConvGeom g, const T *__restrict__ x, const T *__restrict__ w,
+                            const T *__restrict__ bias, T *__restrict__ out, long long total) {
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  int ow = int(i % g.OW);
+  long long t = i / g.OW;
+  int oh = int(t % g.OH);
+  t /= g.OH;
+  int oc = int(t % g.OC);
+  long long b = t / g.OC;
+  int icpg = g.IC / g.groups, ocpg = g.OC / g.groups;
+  int grp = oc / ocpg;
+  float acc = g.has_bias ? ld_f(&bias[oc]) : 0.f;
+  for (int c = 0; c < icpg; ++c) {
+    int ic = grp * icpg + c;
+    for (int kh = 0; kh < g.KH; ++kh) {
+      int ih = oh * g.sH - g.pH + kh * g.dH;
+      if (ih < 0 || ih >= g.IH) continue;
+      for (int kw = 0; kw < g.KW; ++kw) {
+        int iw = ow * g.sW - g.pW + kw * g.dW;
+        if (iw < 0 || iw >= g.IW) continue;
+        acc = fmaf(ld_f(&x[((b * g.IC + ic) * g.IH + ih) * (long long)g.IW + iw]),
+                   ld_f(&w[((long long)(oc * icpg + c) * g.KH + kh) * g.KW + kw]), acc);
+      }
+    }
+  }
+  out[i] = to_t<T>(apply_act(acc, g.act, g.lo, g.hi));
+}
+
+// ---------------------------------------------------------------------------
+// transposed conv gather (conv-transpose2d.wgsl.ts): weight [IC, OC/g, KH, KW]
+// ---------------------------------------------------------------------------
+template <class T>
+__global__ void conv_transpose_gather(ConvGeom g, const T *__restrict__ x, const T *__restrict__ w,
+                                      const T *__restrict__ bias, T *__restrict__ out,
+                                      long long total) {
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  int ow = int(i % g.OW);
+  long long t = i / g.OW;
+  int oh = int(t % g.OH);
+  t /= g.OH;
+  int oc = int(t % g.OC);
+  long long b = t / g.OC;
+  int icpg = g.IC / g.groups, ocpg = g.OC / g.groups;
+  int grp = oc / ocpg, ocl = oc % ocpg;
+  float acc = g.has_bias ? ld_f(&bias[oc]) : 0.f;
+  for (int c = 0; c < icpg; ++c) {
+    int ic = grp * icpg + c;
+    for (int kh = 0; kh < g.KH; ++kh) {
+      int th = oh + g.pH - kh * g.dH;
+      if (th < 0 || th % g.sH) continue;
+      int ih = th / g.sH;
+      if (ih >= g.IH) continue;
+      for (int kw = 0; kw < g.KW; ++kw) {
+        int tw = ow + g.pW - kw * g.dW;
+        if (tw < 0 || tw % g.sW) continue;
+        int iw = tw / g.sW;
+        if (iw >= g.IW) continue;
+        acc = fmaf(ld_f(&x[((b * g.IC + ic) * g.IH + ih) * (long long)g.IW + iw]),
+                   ld_f(&w[((long long)(ic * ocpg + ocl) * g.KH + kh) * g.KW + kw]), acc);
+      }
+    }
+  }
+  out[i] = to_t<T>(apply_act(acc, g.act, g.lo, g.hi));
+}
+
+// ---------------------------------------------------------------------------
+// depthwise: groups == IC == OC, one input channel per output channel.
+// The reference's conv2d-depthwise-f16.wgsl.ts reads every tap straight
+// from global memory with 2-element strides; here one CTA owns a band of
+// TH output rows of one (b, c) plane, stages the input rows it needs (with
+// zero padding) in shared memory using 16-byte loads when the rows are
+// 16-byte aligned, and each thread produces 8 consecutive outputs of a row
+// so the stores are 16-byte vectors. Accumulation is fp32 starting from
+// the bias like the reference (acc = bias; acc += x*w), the activation is
+// applied in fp32, one rounding at the store.
+// Shared tile: (TH*sH + (KH-1)*dH) rows x TWs columns (input width + pads).
+// ---------------------------------------------------------------------------
+constexpr int DW_THREADS = 256;
+constexpr int DW_MAX_TAPS = 64;
+
+template <class T>
+__global__ void __launch_bounds__(DW_THREADS)
+    depthwise_conv(ConvGeom g, int TH, int TWs, const T *__restrict__ x, const T *__restrict__ w,
+                   const T *__restrict__ bias, T *__restrict__ out, int vec_in, int vec_out) {
+  extern __shared__ __align__(16) unsigned char dw_smem[];
+  float *wsm = reinterpret_cast<float *>(dw_smem);  // KH*KW weights
+  T *tile = reinterpret_cast<T *>(dw_smem + DW_MAX_TAPS * sizeof(float));
+  const int plane = blockIdx.y;  // b*C + c
+  const int c = plane % g.OC;
+  const int oh0 = blockIdx.x * TH;
+  const int taps = g.KH * g.KW;
+  for (int i = threadIdx.x; i < taps; i += blockDim.x) wsm[i] = ld_f(&w[(long long)c * taps + i]);
+  const int rows = (TH - 1) * g.sH + (g.KH - 1) * g.dH + 1;
+  const int ih0 = oh0 * g.sH - g.pH;
+  const T *xp = x + (long long)plane * g.IH * g.IW;
+  // stage rows [ih0, ih0+rows) x cols [-pW, -pW+TWs) into the tile; column j
+  // of the tile is input column j - pW.
+  if (vec_in) {
+    // interior: 16-byte vectors of 8 (f16) / 4 (f32) elements
+    constexpr int V = 16 / sizeof(T);
+    const int nvec = g.IW / V;
+    for (int idx = threadIdx.x; idx < rows * nvec; idx += blockDim.x) {
+      int r = idx / nvec, v = idx % nvec;
+      int ih = ih0 + r;
+      T *dst = tile + (long long)r * TWs + g.pW + v * V;
+      if (ih >= 0 && ih < g.IH) {
+        uint4 val = *reinterpret_cast<const uint4 *>(xp + (long long)ih * g.IW + v * V);
+        const T *vv = reinterpret_cast<const T *>(&val);
+#pragma unroll
+        for (int e = 0; e < V; ++e) dst[e] = vv[e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < V; ++e) dst[e] = to_t<T>(0.f);
+      }
+    }
+    // left/right padding columns
+    const int padc = TWs - g.IW;
+    for (int idx = threadIdx.x; idx < rows * padc; idx += blockDim.x) {
+      int r = idx / padc, j = idx % padc;
+      int col = j < g.pW ? j : g.IW + j;
+      tile[(long long)r * TWs + col] = to_t<T>(0.f);
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < rows * TWs; idx += blockDim.x) {
+      int r = idx / TWs, j = idx % TWs;
+      int ih = ih0 + r, iw = j - g.pW;
+      T v = to_t<T>(0.f);
+      if (ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW) v = xp[(long long)ih * g.IW + iw];
+      tile[(long long)r * TWs + j] = v;
+    }
+  }
+  __syncthreads();
+  const float bv = g.has_bias ? ld_f(&bias[c]) : 0.f;
+  const int ohn = min(TH, g.OH - oh0);
+  const int ngrp = (g.OW + 7) / 8;
+  T *op = out + (long long)plane * g.OH * g.OW;
+  for (int idx = threadIdx.x; idx < ohn * ngrp; idx += blockDim.x) {
+    int r = idx / ngrp, q = idx % ngrp;
+    int ow0 = q * 8;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = bv;
+    for (int kh = 0; kh < g.KH; ++kh) {
+      const T *trow = tile + (long long)(r * g.sH + kh * g.dH) * TWs;
+      for (int kw = 0; kw < g.KW; ++kw) {
+        float wv = wsm[kh * g.KW + kw];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          int col = (ow0 + e) * g.sW + kw * g.dW;  // tile column (input col + pW)
+          if (col < TWs) acc[e] = fmaf(ld_f(&trow[col]), wv, acc[e]);
+        }
+      }
+    }
+    T *orow = op + (long long)(oh0 + r) * g.OW;
+    if (vec_out && ow0 + 8 <= g.OW) {
+      alignas(16) T res[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) res[e] = to_t<T>(apply_act(acc[e], g.act, g.lo, g.hi));
+      if (sizeof(T) == 2) {
+        *reinterpret_cast<uint4 *>(orow + ow0) = *reinterpret_cast<const uint4 *>(res);
+      } else {
+        reinterpret_cast<uint4 *>(orow + ow0)[0] = reinterpret_cast<const uint4 *>(res)[0];
+        reinterpret_cast<uint4 *>(orow + ow0)[1] = reinterpret_cast<const uint4 *>(res)[1];
+      }
+    } else {
+      for (int e = 0; e < 8 && ow0 + e < g.OW; ++e)
+        orow[ow0 + e] = to_t<T>(apply_act(acc[e], g.act, g.lo, g.hi));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 1x1 conv with a single output channel: out[b,0,p] = sum_c x[b,c,p]*w[c]
+// with fp32 accumulation (conv-with-clamp-1x1-single-channel-f16.wgsl.ts:44-58).
+// ---------------------------------------------------------------------------
+template <class T>
+__global__ void pointwise_single(ConvGeom g, const T *__restrict__ x, const T *__restrict__ w,
+                                 const T *__restrict__ bias, T *__restrict__ out) {
+  long long hw = (long long)g.OH * g.OW;
+  long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  int b = blockIdx.y;
+  if (p >= hw) return;
+  const T *xb = x + (long long)b * g.IC * hw + p;
+  float acc = 0.f;
+  for (int c = 0; c < g.IC; ++c) acc = fmaf(ld_f(&xb[c * hw]), ld_f(&w[c]), acc);
+  if (g.has_bias) acc += ld_f(&bias[0]);
+  out[(long long)b * hw + p] = to_t<T>(apply_act(acc, g.act, g.lo, g.hi));
+}
+
+// ---------------------------------------------------------------- dispatch
+static bool is_depthwise(const wgx_conv2d_params &p) {
+  return p.groups == p.OC && p.IC == p.OC && p.groups > 1;
+}
+
+wgx_conv2d_plan plan_conv2d(const wgx_conv2d_params &p) {
+  wgx_conv2d_plan plan{};
+  if (p.dtype != WGX_FLOAT32 && p.dtype != WGX_FLOAT16) fail("conv2d: dtype must be fp32 or fp16");
+  if (p.groups < 1 || p.IC % p.groups || p.OC % p.groups) fail("conv2d: bad groups");
+  if (p.B <= 0 || p.IC <= 0 || p.OC <= 0 || p.OH <= 0 || p.OW <= 0 || p.KH <= 0 || p.KW <= 0)
+    fail("conv2d: non-positive dimension");
+  bool unit1x1 = p.KH == 1 && p.KW == 1 && p.sH == 1 && p.sW == 1 && p.pH == 0 && p.pW == 0;
+  if (p.groups == 1 && p.dtype == WGX_FLOAT16 && umma_conv_supported(p)) {
+    plan.variant = WGX_CONV_UMMA;
+    plan.scratch_bytes = conv2d_scratch_bytes(p, true);
+    plan.grid_ctas = umma_conv_grid(p);
+    plan.n_launches = 3;
+  } else if (p.groups == 1 && p.OC == 1 && unit1x1) {
+    plan.variant = WGX_CONV_POINTWISE1;
+    plan.n_launches = 1;
+    plan.grid_ctas = uint64_t((int64_t(p.OH) * p.OW + 255) / 256) * p.B;
+  } else if (p.groups == 1) {
+    plan.variant = WGX_CONV_SIMT_GEMM;
+    plan.n_launches = 1;
+    plan.grid_ctas = uint64_t((int64_t(p.B) * p.OH * p.OW + 63) / 64) * ((p.OC + 63) / 64);
+  } else if (is_depthwise(p) && p.KH * p.KW <= DW_MAX_TAPS) {
+    plan.variant = WGX_CONV_DEPTHWISE;
+    plan.n_launches = 1;
+  } else {
+    plan.variant = WGX_CONV_DIRECT;
+    plan.n_launches = 1;
+  }
+  return plan;
+}
+
+uint64_t conv2d_packed_weight_bytes(const wgx_conv2d_params &p) {
+  if (plan_conv2d(p).variant != WGX_CONV_UMMA) return 0;
+  return umma_conv_packed_weight_bytes(p);
+}
+uint64_t conv2d_input_scratch_bytes(const wgx_conv2d_params &p) {
+  if (p.groups != 1 || p.dtype != WGX_FLOAT16 || !umma_conv_supported(p)) return 0;
+  return umma_conv_input_bytes(p);
+}
+uint64_t conv2d_scratch_bytes(const wgx_conv2d_params &p, bool include_packed) {
+  if (p.groups != 1 || p.dtype != WGX_FLOAT16 || !umma_conv_supported(p)) return 0;
+  uint64_t b = umma_conv_input_bytes(p);
+  if (include_packed) b += umma_conv_packed_weight_bytes(p);
+  return b;
+}
+int conv2d_kernel_launches(const wgx_conv2d_params &p, bool packed_ready) {
+  wgx_conv2d_plan plan = plan_conv2d(p);
+  if (plan.variant == WGX_CONV_UMMA) return packed_ready ? 2 : 3;
+  return plan.n_launches;
+}
+
+void conv2d_pack_weights(const wgx_conv2d_params &p, const void *w, void *packed,
+                         cudaStream_t stream) {
+  umma_conv_pack_weights(p, static_cast<const __half *>(w), packed, stream);
+}
+
+template <class T>
+static void launch_simt(const wgx_conv2d_params &p, int variant, const T *in, const T *w,
+                        const T *bias, T *out, cudaStream_t s) {
+  ConvGeom g = geom_of(p);
+  if (variant == WGX_CONV_SIMT_GEMM) {
+    long long N = (long long)p.B * p.OH * p.OW;
+    dim3 grid(unsigned((N + 63) / 64), unsigned((p.OC + 63) / 64));
+    if (grid.y > 65535) fail("conv2d: too many output channels for the FFMA path");
+    simt_gemm_conv<T><<<grid, 256, 0, s>>>(g, in, w, bias, out);
+  } else if (variant == WGX_CONV_POINTWISE1) {
+    long long hw = (long long)p.OH * p.OW;
+    if (p.B > 65535) fail("conv2d: batch too large for the single-channel kernel");
+    dim3 grid(unsigned((hw + 255) / 256), unsigned(p.B));
+    pointwise_single<T><<<grid, 256, 0, s>>>(g, in, w, bias, out);
+  } else if (variant == WGX_CONV_DEPTHWISE) {
+    // rows per CTA: keep the staged tile under ~40 KB
+    int TWs = p.IW + 2 * p.pW;
+    int TH = 32;
+    auto tile_bytes = [&](int th) {
+      return (uint64_t)((th - 1) * p.sH + (p.KH - 1) * p.dH + 1) * TWs * sizeof(T);
+    };
+    while (TH > 1 && tile_bytes(TH) > 40 * 1024) TH /= 2;
+    if (TH > p.OH) TH = p.OH;
+    uint64_t smem = DW_MAX_TAPS * sizeof(float) + tile_bytes(TH) + 16;
+    if (smem > 200 * 1024) fail("conv2d: depthwise plane too wide");
+    if (smem > 48 * 1024)
+      check_cuda(cudaFuncSetAttribute(depthwise_conv<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(smem)),
+                 "depthwise smem attr");
+    constexpr int V = 16 / sizeof(T);
+    int vec_in = (p.IW % V == 0) && ((reinterpret_cast<uintptr_t>(in) & 15) == 0) &&
+                 (((long long)p.IH * p.IW) % V == 0) && ((p.pW * sizeof(T)) % 1 == 0);
+    // the interior copy writes tile columns [pW, pW+IW): vector stores into
+    // smem need no alignment (element stores are used), so only global
+    // alignment matters.
+    int vec_out = (p.OW % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0) &&
+                  (((long long)p.OH * p.OW) % 8 == 0);
+    long long planes = (long long)p.B * p.OC;
+    if (planes > 65535) fail("conv2d: too many depthwise planes");
+    dim3 grid(unsigned((p.OH + TH - 1) / TH), unsigned(planes));
+    depthwise_conv<T><<<grid, DW_THREADS, smem, s>>>(g, TH, TWs, in, w, bias, out, vec_in,
+                                                      vec_out);
+  } else {
+    long long total = (long long)p.B * p.OC * p.OH * p.OW;
+    direct_conv<T><<<unsigned((total + 255) / 256), 256, 0, s>>>(g, in, w, bias, out, total);
+  }
+  check_cuda(cudaGetLastError(), "conv2d launch");
+}
+
+void launch_conv2d(const wgx_conv2d_params &p, const void *in, const void *w, const void *packed,
+                   const void *bias, void *out, void *scratch, uint64_t scratch_bytes,
+                   cudaStream_t stream) {
+  wgx_conv2d_plan plan = plan_conv2d(p);
+  if (!p.has_bias) bias = nullptr;
+  if (plan.variant == WGX_CONV_UMMA) {
+    uint64_t need = conv2d_scratch_bytes(p, packed == nullptr);
+    if (!scratch || scratch_bytes < need)
+      fail("conv2d: scratch too small (" + std::to_string(scratch_bytes) + " < " +
+           std::to_string(need) + " bytes)");
+    char *sp = static_cast<char *>(scratch);
+    void *xs = sp;
+    if (!packed) {
+      void *pw = sp + umma_conv_input_bytes(p);
+      umma_conv_pack_weights(p, static_cast<const __half *>(w), pw, stream);
+      packed = pw;
+    }
+    umma_conv_run(p, static_cast<const __half *>(in), packed, static_cast<const __half *>(bias),
+                  static_cast<__half *>(out), xs, stream);
+    return;
+  }
+  if (p.dtype == WGX_FLOAT16)
+    launch_simt<__half>(p, plan.variant, static_cast<const __half *>(in),
+                        static_cast<const __half *>(w), static_cast<const __half *>(bias),
+                        static_cast<__half *>(out), stream);
+  else
+    launch_simt<float>(p, plan.variant, static_cast<const float *>(in),
+                       static_cast<const float *>(w), static_cast<const float *>(bias),
+                       static_cast<float *>(out), stream);
+}
+
+void launch_conv_transpose2d(const wgx_conv2d_params &p, int, int, const void *in, const void *w,
+                             const void *bias, void *out, cudaStream_t s) {
+  ConvGeom g = geom_of(p);
+  if (!p.has_bias) bias = nullptr;
+  long long total = (long long)p.B * p.OC * p.OH * p.OW;
+  unsigned blocks = unsigned((total + 255) / 256);
+  if (p.dtype == WGX_FLOAT16)
+    conv_transpose_gather<__half><<<blocks, 256, 0, s>>>(
+        g, static_cast<const __half *>(in), static_cast<const __half *>(w),
+        static_cast<const __half *>(bias), static_cast<__half *>(out), total);
+  else
+    conv_transpose_gather<float><<<blocks, 256, 0, s>>>(
+        g, static_cast<const float *>(in), static_cast<const float *>(w),
+        static_cast<const float *>(bias), static_cast<float *>(out), total);
+  check_cuda(cudaGetLastError(), "conv_transpose2d launch");
+}
+
+// ------------------------------------------------------------------- mm
+// aten.mm is the 1x1 convolution W[OC=M, IC=K] x X[1, K, 1, N]: the same
+// kernels serve both (mm-64x64.wgsl.ts computes the identical GEMM).
+static wgx_conv2d_params mm_params(int64_t M, int64_t N, int64_t K, int dtype) {
+  if (M <= 0 || N <= 0 || K <= 0) fail("aten.mm.default: non-positive dimension");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) fail("aten.mm.default: dimension too large");
+  wgx_conv2d_params p{};
+  p.B = 1;
+  p.IC = int(K);
+  p.IH = 1;
+  p.IW = int(N);
+  p.OC = int(M);
+  p.OH = 1;
+  p.OW = int(N);
+  p.KH = p.KW = 1;
+  p.sH = p.sW = 1;
+  p.dH = p.dW = 1;
+  p.groups = 1;
+  p.dtype = dtype;
+  p.act = WGX_ACT_NONE;
+  p.out_min = -INFINITY;
+  p.out_max = INFINITY;
+  return p;
+}
+
+uint64_t mm_scratch_bytes(int64_t M, int64_t N, int64_t K, int dtype) {
+  return conv2d_scratch_bytes(mm_params(M, N, K, dtype), true);
+}
+
+void launch_mm(const void *a, const void *b, void *out, int64_t M, int64_t N, int64_t K,
+               int dtype, void *scratch, uint64_t scratch_bytes, cudaStream_t stream) {
+  wgx_conv2d_params p = mm_params(M, N, K, dtype);
+  launch_conv2d(p, b, a, nullptr, nullptr, out, scratch, scratch_bytes, stream);
+}
+
+}  // namespace wgx

@@ -1,0 +1,152 @@
+// Internal declarations shared by the runtime, the operator registry and the
+// kernels. Nothing here is part of the C ABI (that is include/wgx.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include <cmath>
+#include <cstdint>
+#include <functional>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "wgx.h"
+
+namespace wgx {
+
+// ---------------------------------------------------------------- errors
+// Thread-local last-error text (wgx_last_error). set_error returns its code
+// so call sites can write `return set_error(...)`.
+int set_error(int code, const std::string &msg);
+void clear_error();
+
+struct Error {
+  int code;
+  std::string msg;
+};
+// Validation helper used by the op recorders: throws Error, which the C ABI
+// entry points catch and turn into a status code + message.
+[[noreturn]] void fail(const std::string &msg, int code = WGX_ERR_INVALID);
+void check_cuda(cudaError_t e, const char *what);
+
+int dtype_size(int dtype);
+const char *dtype_name(int dtype);
+
+// Device-side error word. Kernels that wait on a barrier give up after a
+// bounded number of polls and OR a code in here instead of hanging.
+enum DeviceErrorBits : uint32_t {
+  kErrMmaTimeout = 1u << 0,
+  kErrLoadTimeout = 1u << 1,
+  kErrEpilogueTimeout = 1u << 2,
+  kErrTmemAlloc = 1u << 3,
+};
+uint32_t *device_error_word(int device);
+
+// ------------------------------------------------------------- objects
+struct Arena;
+
+}  // namespace wgx
+
+struct wgx_buffer {
+  wgx_context *ctx = nullptr;  // owner (null: external buffer)
+  void *dptr = nullptr;
+  uint64_t size = 0;
+  uint32_t usage = 0;
+  int device = 0;
+  bool owns_alloc = false;  // cudaFree(dptr) on destroy
+  bool destroyed = false;
+  bool constant = false;    // holds program weights (immutable after upload)
+};
+
+struct wgx_tensor {
+  wgx_buffer *buffer = nullptr;
+  int dtype = 0;
+  int ndim = 0;
+  int64_t shape[WGX_MAX_NDIM] = {0};
+  int64_t numel = 1;
+  uint64_t byte_length() const { return uint64_t(numel) * wgx::dtype_size(dtype); }
+  void *data() const { return buffer->dptr; }
+};
+
+namespace wgx {
+
+// Execution environment handed to every recorded command when it is
+// replayed (inside stream capture on the first submit).
+struct ExecEnv {
+  cudaStream_t stream;
+  void *workspace;        // shared scratch, sized to the max any command asked for
+  uint64_t workspace_bytes;
+};
+
+struct Command {
+  std::string name;
+  int kernel_launches = 0;
+  uint64_t workspace_bytes = 0;  // shared scratch this command needs
+  std::function<void(const ExecEnv &)> run;  // throws Error on failure
+};
+
+}  // namespace wgx
+
+struct wgx_context {
+  int device = 0;
+  bool destroyed = false;
+  cudaStream_t stream = nullptr;
+  std::vector<wgx_buffer *> owned;          // buffers freed on destroy
+  std::vector<void *> allocations;          // raw device allocations (arenas, caches)
+  std::vector<wgx::Command> commands;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t graph_exec = nullptr;
+  bool graph_valid = false;
+  void *workspace = nullptr;
+  uint64_t workspace_bytes = 0;
+  int64_t launches_per_submit = 0;
+  std::vector<std::unique_ptr<wgx_tensor>> program_tensors;  // views made by record_program
+
+  void *alloc_device(uint64_t bytes);  // tracked device allocation (freed on destroy)
+  void invalidate_graph();
+};
+
+namespace wgx {
+
+// ------------------------------------------------------ op registry
+// A recorder validates the resolved positional args exactly like the
+// reference operator's recordIn and appends one or more Commands.
+using OpRecorder = std::function<void(wgx_context *, const std::vector<wgx_arg> &)>;
+const std::unordered_map<std::string, OpRecorder> &op_registry();
+
+// ------------------------------------------------------ kernel front-ends
+// All of these enqueue work on `stream` and throw Error on bad input.
+struct ConvLaunch;  // defined in conv.cu
+
+void launch_mm(const void *a, const void *b, void *out, int64_t M, int64_t N, int64_t K,
+               int dtype, void *scratch, uint64_t scratch_bytes, cudaStream_t stream);
+uint64_t mm_scratch_bytes(int64_t M, int64_t N, int64_t K, int dtype);
+
+wgx_conv2d_plan plan_conv2d(const wgx_conv2d_params &p);
+// packed-weight layout size for the tcgen05 path (0 when the plan is not UMMA)
+uint64_t conv2d_packed_weight_bytes(const wgx_conv2d_params &p);
+uint64_t conv2d_input_scratch_bytes(const wgx_conv2d_params &p);
+// pack OIHW weights into the tcgen05 operand layout (one small kernel)
+void conv2d_pack_weights(const wgx_conv2d_params &p, const void *w, void *packed,
+                         cudaStream_t stream);
+// full convolution; `packed` may be null (then weights are packed into the
+// front of scratch first). scratch must hold conv2d_scratch_bytes(p, packed==null).
+uint64_t conv2d_scratch_bytes(const wgx_conv2d_params &p, bool include_packed_weights);
+void launch_conv2d(const wgx_conv2d_params &p, const void *in, const void *w, const void *packed,
+                   const void *bias, void *out, void *scratch, uint64_t scratch_bytes,
+                   cudaStream_t stream);
+int conv2d_kernel_launches(const wgx_conv2d_params &p, bool packed_ready);
+
+// transposed / grouped direct conv used by aten.convolution for shapes
+// outside the hot path
+void launch_conv_transpose2d(const wgx_conv2d_params &p, int opH, int opW, const void *in,
+                             const void *w, const void *bias, void *out, cudaStream_t stream);
+
+// conv recorder with a fused epilogue activation (program fusion pass):
+// args are aten.convolution's positional args.
+void record_convolution_act(wgx_context *ctx, const std::vector<wgx_arg> &args, int act);
+
+}  // namespace wgx

@@ -1,0 +1,424 @@
+// recordProgram: the Program JSON executor.
+//
+// Follows src/context.ts:219-317 step by step:
+//   1. argument count check                          (context.ts:226-230)
+//   2. one buffer per memoryPlan pool                 (context.ts:233-236)
+//   3. a tensor view for every tensor value: constant -> dedicated, memObjId
+//      -> the pool itself at offset 0, else dedicated (context.ts:239-261)
+//   4. weights upload into the constants              (context.ts:264-277)
+//   5. input copies user -> internal, non-Tensor inputs skipped (280-291)
+//   6. the op chain through the registry + resolveArgs (292-300,
+//      src/program.ts:188-224)
+//   7. output copies internal -> user                 (context.ts:303-314)
+//
+// B200 design:
+//   * pools, dedicated tensors and the weights image share ONE cudaMalloc
+//     arena; every slice starts on a 256-byte boundary.
+//   * constants alias their bytes inside a device copy of weights.bin that
+//     is uploaded with a single pinned, asynchronous host-to-device copy.
+//   * a fusion pass rewrites convolution -> sigmoid -> mul (SiLU) into one
+//     convolution with a SiLU epilogue when the intermediate values have no
+//     other reader.
+#include <cstring>
+#include <map>
+#include <set>
+
+#include "internal.h"
+#include "json.h"
+
+namespace wgx {
+
+namespace {
+
+struct PValue {
+  enum Kind { Tensor, Scalar, List, TensorList, Null } kind = Null;
+  // tensor
+  std::vector<int64_t> shape;
+  int dtype = 0;
+  bool has_mem = false, has_weights = false;
+  int64_t mem_obj = 0;
+  uint64_t w_off = 0, w_len = 0;
+  // scalar
+  enum SKind { SNum, SBool, SStr } skind = SNum;
+  double num = 0;
+  bool b = false;
+  std::string str;
+  // list / tensorlist
+  std::vector<int64_t> items;
+};
+
+struct POp {
+  std::string name;
+  std::vector<int64_t> args;
+};
+
+int parse_dtype(const std::string &s) {
+  static const char *names[] = {"float32", "float16", "int32", "int8",
+                                "uint8",   "bool",    "float64", "int64"};
+  for (int i = 0; i < 8; ++i)
+    if (s == names[i]) return i;
+  fail("program: unknown dtype '" + s + "'");
+}
+
+const json::Value &need(const json::Value &o, const char *k) {
+  const json::Value *v = o.get(k);
+  if (!v) fail(std::string("program: missing field '") + k + "'");
+  return *v;
+}
+
+int64_t as_int(const json::Value &v) {
+  if (v.kind != json::Value::Number) fail("program: expected a number");
+  return int64_t(v.num);
+}
+
+std::vector<int64_t> int_array(const json::Value &v) {
+  if (v.kind != json::Value::Array) fail("program: expected an array");
+  std::vector<int64_t> out;
+  for (auto &e : v.arr) out.push_back(as_int(e));
+  return out;
+}
+
+struct Program {
+  std::vector<PValue> values;
+  std::vector<POp> chain;
+  std::vector<int64_t> input_ids, output_ids;
+  std::vector<std::pair<int64_t, uint64_t>> pools;
+};
+
+Program parse_program(const char *text, uint64_t len) {
+  json::Value root;
+  try {
+    root = json::parse(text, len);
+  } catch (const std::runtime_error &e) {
+    fail(e.what());
+  }
+  Program P;
+  for (auto &v : need(root, "values").arr) {
+    PValue pv;
+    const std::string &t = need(v, "type").str;
+    if (t == "tensor") {
+      pv.kind = PValue::Tensor;
+      pv.shape = int_array(need(v, "shape"));
+      pv.dtype = parse_dtype(need(v, "dtype").str);
+      if (auto *m = v.get("memObjId"); m && m->kind == json::Value::Number) {
+        pv.has_mem = true;
+        pv.mem_obj = as_int(*m);
+      }
+      auto *wo = v.get("weightsOffset");
+      auto *wl = v.get("weightsLength");
+      if (wo && wl && wo->kind == json::Value::Number && wl->kind == json::Value::Number) {
+        pv.has_weights = true;
+        pv.w_off = uint64_t(wo->num);
+        pv.w_len = uint64_t(wl->num);
+      }
+    } else if (t == "scalar") {
+      pv.kind = PValue::Scalar;
+      const json::Value &val = need(v, "value");
+      if (val.kind == json::Value::Bool) {
+        pv.skind = PValue::SBool;
+        pv.b = val.b;
+      } else if (val.kind == json::Value::String) {
+        pv.skind = PValue::SStr;
+        pv.str = val.str;
+      } else {
+        pv.skind = PValue::SNum;
+        pv.num = val.num;
+      }
+    } else if (t == "list") {
+      pv.kind = PValue::List;
+      pv.items = int_array(need(v, "items"));
+    } else if (t == "tensorlist") {
+      pv.kind = PValue::TensorList;
+      pv.items = int_array(need(v, "items"));
+    } else {
+      pv.kind = PValue::Null;
+    }
+    P.values.push_back(std::move(pv));
+  }
+  for (auto &op : need(root, "chain").arr) {
+    POp o;
+    o.name = need(op, "name").str;
+    o.args = int_array(need(op, "args"));
+    P.chain.push_back(std::move(o));
+  }
+  P.input_ids = int_array(need(root, "inputIds"));
+  P.output_ids = int_array(need(root, "outputIds"));
+  for (auto &pl : need(need(root, "memoryPlan"), "pools").arr)
+    P.pools.emplace_back(as_int(need(pl, "id")), uint64_t(as_int(need(pl, "size"))));
+  return P;
+}
+
+uint64_t align256(uint64_t x) { return (x + 255) / 256 * 256; }
+
+// SiLU fusion: conv(v) ; sigmoid(v)->s ; mul(v,s)->y  ==>  conv_silu -> y
+// Returns, per chain index, 0 = record as is, 1 = fused conv head (record
+// with SiLU into the mul's output), 2 = skip (absorbed).
+std::vector<int> plan_fusion(const Program &P, const std::map<int64_t, wgx_tensor *> &tensors) {
+  std::vector<int> mark(P.chain.size(), 0);
+  std::map<int64_t, int> readers;
+  for (auto &op : P.chain)
+    for (auto a : op.args) {
+      if (a < 0 || size_t(a) >= P.values.size()) continue;
+      readers[a]++;
+      if (P.values[a].kind == PValue::TensorList)
+        for (auto t : P.values[a].items) readers[t]++;
+    }
+  std::set<int64_t> outputs(P.output_ids.begin(), P.output_ids.end());
+  for (size_t i = 0; i + 2 < P.chain.size(); ++i) {
+    const POp &c = P.chain[i], &s = P.chain[i + 1], &m = P.chain[i + 2];
+    if (c.name != "aten.convolution.default" || c.args.size() != 10) continue;
+    if (s.name != "aten.sigmoid.default" || s.args.size() != 2) continue;
+    if (m.name != "aten.mul.Tensor" || m.args.size() != 3) continue;
+    int64_t v = c.args[9], sv = s.args[1], y = m.args[2];
+    if (s.args[0] != v) continue;
+    if (!((m.args[0] == v && m.args[1] == sv) || (m.args[0] == sv && m.args[1] == v))) continue;
+    // v read by conv(out) + sigmoid + mul, s by sigmoid(out) + mul
+    if (readers[v] != 3 || readers[sv] != 2) continue;
+    if (outputs.count(v) || outputs.count(sv)) continue;
+    const PValue &tr = P.values[P.values[c.args[6]].kind == PValue::Scalar ? c.args[6] : 0];
+    if (tr.kind == PValue::Scalar && tr.b) continue;  // transposed
+    auto tv = tensors.find(v), ty = tensors.find(y), tx = tensors.find(c.args[0]);
+    if (tv == tensors.end() || ty == tensors.end() || tx == tensors.end()) continue;
+    if (tv->second->numel != ty->second->numel || tv->second->dtype != ty->second->dtype)
+      continue;
+    // the fused conv writes y directly: never fuse in place
+    if (ty->second->buffer->dptr == tx->second->buffer->dptr) continue;
+    mark[i] = 1;
+    mark[i + 1] = 2;
+    mark[i + 2] = 2;
+    i += 2;
+  }
+  return mark;
+}
+
+}  // namespace
+
+static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len,
+                                const void *weights, uint64_t wlen, const wgx_arg *args,
+                                int nargs) {
+  Program P = parse_program(text, len);
+  size_t n_in = P.input_ids.size(), n_out = P.output_ids.size();
+  if (size_t(nargs) != n_in + n_out)
+    fail("program: expected " + std::to_string(n_in + n_out) + " args, got " +
+         std::to_string(nargs));
+
+  // ---- arena layout: pools, dedicated tensors, weights image
+  std::map<int64_t, uint64_t> pool_off, pool_size;
+  uint64_t off = 0;
+  for (auto &pl : P.pools) {
+    uint64_t sz = pl.second < 4 ? 4 : (pl.second + 3) / 4 * 4;
+    pool_off[pl.first] = off;
+    pool_size[pl.first] = sz;
+    off = align256(off + sz);
+  }
+  std::map<size_t, uint64_t> dedicated_off;
+  for (size_t i = 0; i < P.values.size(); ++i) {
+    const PValue &v = P.values[i];
+    if (v.kind != PValue::Tensor) continue;
+    if (v.has_weights) continue;
+    if (v.has_mem) {
+      if (!pool_off.count(v.mem_obj))
+        fail("program: no memory pool " + std::to_string(v.mem_obj) + " for value " +
+             std::to_string(i));
+      continue;
+    }
+    int64_t numel = 1;
+    for (auto d : v.shape) numel *= d;
+    uint64_t sz = uint64_t(numel) * dtype_size(v.dtype);
+    sz = sz < 4 ? 4 : (sz + 3) / 4 * 4;
+    dedicated_off[i] = off;
+    off = align256(off + sz);
+  }
+  uint64_t weights_off = off;
+  bool any_const = false;
+  for (auto &v : P.values)
+    if (v.kind == PValue::Tensor && v.has_weights) {
+      any_const = true;
+      if (v.w_off + v.w_len > wlen)
+        fail("program: constant [" + std::to_string(v.w_off) + ", +" + std::to_string(v.w_len) +
+             ") lies outside weights.bin (" + std::to_string(wlen) + " bytes)");
+    }
+  uint64_t total = weights_off + (any_const ? align256(wlen + 4) : 0);
+  char *arena = static_cast<char *>(ctx->alloc_device(total));
+
+  const uint32_t usage = WGX_USAGE_STORAGE | WGX_USAGE_COPY_SRC | WGX_USAGE_COPY_DST;
+  auto slice = [&](uint64_t o, uint64_t sz, bool constant) {
+    auto *b = new wgx_buffer();
+    b->ctx = ctx;
+    b->dptr = arena + o;
+    b->size = sz;
+    b->usage = usage;
+    b->device = ctx->device;
+    b->owns_alloc = false;
+    b->constant = constant;
+    ctx->owned.push_back(b);
+    return b;
+  };
+  std::map<int64_t, wgx_buffer *> pool_buf;
+  for (auto &pl : P.pools) pool_buf[pl.first] = slice(pool_off[pl.first], pool_size[pl.first], false);
+
+  // ---- weights: one pinned staging copy, one async H2D
+  if (any_const && wlen) {
+    void *pinned = nullptr;
+    check_cuda(cudaHostAlloc(&pinned, wlen, cudaHostAllocDefault), "cudaHostAlloc(weights)");
+    std::memcpy(pinned, weights, wlen);
+    cudaError_t e = cudaMemcpyAsync(arena + weights_off, pinned, wlen, cudaMemcpyHostToDevice,
+                                    ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    cudaFreeHost(pinned);
+    check_cuda(e, "weights upload");
+  }
+
+  // ---- tensor views
+  std::map<int64_t, wgx_tensor *> tensors;
+  for (size_t i = 0; i < P.values.size(); ++i) {
+    const PValue &v = P.values[i];
+    if (v.kind != PValue::Tensor) continue;
+    wgx_buffer *buf;
+    if (v.has_weights) {
+      uint64_t sz = v.w_len < 4 ? 4 : (v.w_len + 3) / 4 * 4;
+      buf = slice(weights_off + v.w_off, sz, true);
+    } else if (v.has_mem) {
+      buf = pool_buf[v.mem_obj];
+    } else {
+      int64_t numel = 1;
+      for (auto d : v.shape) numel *= d;
+      uint64_t sz = uint64_t(numel) * dtype_size(v.dtype);
+      buf = slice(dedicated_off[i], sz < 4 ? 4 : (sz + 3) / 4 * 4, false);
+    }
+    wgx_tensor *t = nullptr;
+    if (wgx_tensor_create(ctx, v.dtype, v.shape.data(), int(v.shape.size()), buf, &t) != WGX_OK)
+      fail(std::string("program: value ") + std::to_string(i) + ": " + wgx_last_error());
+    ctx->program_tensors.emplace_back(t);
+    tensors[int64_t(i)] = t;
+  }
+
+  // ---- input copies
+  for (size_t i = 0; i < n_in; ++i) {
+    if (args[i].kind != WGX_ARG_TENSOR) continue;  // non-Tensor inputs are skipped
+    auto it = tensors.find(P.input_ids[i]);
+    if (it == tensors.end())
+      fail("program: no tensor for input value " + std::to_string(P.input_ids[i]));
+    if (wgx_copy(ctx, args[i].v.tensor, it->second) != WGX_OK) fail(wgx_last_error());
+  }
+
+  // ---- chain
+  const auto &reg = op_registry();
+  std::vector<int> fusion = plan_fusion(P, tensors);
+  for (size_t oi = 0; oi < P.chain.size(); ++oi) {
+    if (fusion[oi] == 2) continue;
+    const POp &op = P.chain[oi];
+    auto rit = reg.find(op.name);
+    if (rit == reg.end()) fail("program: unknown operator '" + op.name + "'");
+    // resolveArgs (src/program.ts:188-224)
+    std::vector<wgx_arg> a(op.args.size());
+    std::vector<std::vector<int64_t>> lists(op.args.size());
+    std::vector<std::vector<wgx_tensor *>> tlists(op.args.size());
+    for (size_t k = 0; k < op.args.size(); ++k) {
+      int64_t idx = op.args[k];
+      if (idx < 0 || size_t(idx) >= P.values.size())
+        fail("program: value index " + std::to_string(idx) + " out of range in '" + op.name + "'");
+      const PValue &v = P.values[idx];
+      wgx_arg &x = a[k];
+      std::memset(&x, 0, sizeof(x));
+      switch (v.kind) {
+        case PValue::Tensor: {
+          auto it = tensors.find(idx);
+          if (it == tensors.end())
+            fail("program: no tensor for value " + std::to_string(idx) + " referenced by '" +
+                 op.name + "'");
+          x.kind = WGX_ARG_TENSOR;
+          x.v.tensor = it->second;
+          break;
+        }
+        case PValue::Scalar:
+          if (v.skind == PValue::SBool) {
+            x.kind = WGX_ARG_BOOL;
+            x.v.boolean = v.b;
+          } else if (v.skind == PValue::SStr) {
+            x.kind = WGX_ARG_STRING;
+            x.v.string = v.str.c_str();
+          } else {
+            x.kind = WGX_ARG_NUMBER;
+            x.v.number = v.num;
+          }
+          break;
+        case PValue::List:
+          lists[k] = v.items;
+          x.kind = WGX_ARG_INT_LIST;
+          x.count = int32_t(lists[k].size());
+          x.v.ints = lists[k].data();
+          break;
+        case PValue::TensorList:
+          for (auto t : v.items) {
+            if (t < 0 || size_t(t) >= P.values.size() || P.values[t].kind != PValue::Tensor)
+              fail("program: tensorlist item " + std::to_string(t) + " is not a tensor (" +
+                   op.name + ")");
+            auto it = tensors.find(t);
+            if (it == tensors.end())
+              fail("program: no tensor for value " + std::to_string(t) + " referenced by '" +
+                   op.name + "'");
+            tlists[k].push_back(it->second);
+          }
+          x.kind = WGX_ARG_TENSOR_LIST;
+          x.count = int32_t(tlists[k].size());
+          x.v.tensors = tlists[k].data();
+          break;
+        case PValue::Null:
+          x.kind = WGX_ARG_NULL;
+          break;
+      }
+    }
+    size_t before = ctx->commands.size();
+    try {
+      if (fusion[oi] == 1) {
+        // fused conv + SiLU writes straight into the mul's output
+        a[9].v.tensor = tensors[P.chain[oi + 2].args[2]];
+        record_convolution_act(ctx, a, WGX_ACT_SILU);
+      } else {
+        rit->second(ctx, a);
+      }
+    } catch (...) {
+      ctx->commands.resize(before);
+      throw;
+    }
+  }
+
+  // ---- output copies
+  for (size_t i = 0; i < n_out; ++i) {
+    const wgx_arg &dst = args[n_in + i];
+    auto it = tensors.find(P.output_ids[i]);
+    if (dst.kind != WGX_ARG_TENSOR) fail("program: output " + std::to_string(i) + " must be a Tensor");
+    if (it == tensors.end())
+      fail("program: no tensor for output value " + std::to_string(P.output_ids[i]));
+    if (wgx_copy(ctx, it->second, dst.v.tensor) != WGX_OK) fail(wgx_last_error());
+  }
+}
+
+}  // namespace wgx
+
+extern "C" int wgx_record_program(wgx_context *ctx, const char *json, uint64_t json_len,
+                                  const void *weights, uint64_t weights_len, const wgx_arg *args,
+                                  int nargs) {
+  using namespace wgx;
+  try {
+    clear_error();
+    if (!ctx) fail("null context");
+    if (ctx->destroyed) fail("WgpuExecutionContext is destroyed", WGX_ERR_DESTROYED);
+    check_cuda(cudaSetDevice(ctx->device), "cudaSetDevice");
+    size_t before = ctx->commands.size();
+    try {
+      record_program_impl(ctx, json, json_len, weights, weights_len, args, nargs);
+    } catch (...) {
+      ctx->commands.resize(before);
+      ctx->invalidate_graph();
+      throw;
+    }
+    ctx->invalidate_graph();
+    return WGX_OK;
+  } catch (const Error &e) {
+    return set_error(e.code, e.msg);
+  } catch (const std::exception &e) {
+    return set_error(WGX_ERR_INVALID, e.what());
+  }
+}
