@@ -207,6 +207,16 @@ WGX_API int wgx_conv2d(const wgx_conv2d_params *p, const void *in, const void *w
                void *out, void *scratch, uint64_t scratch_bytes, void *stream);
 
 /* ------------------------------------------------------------------ */
+/* kernel timing: when enabled, the hot-path kernels launched outside a */
+/* CUDA graph record a CUDA-event pair on their own stream around the   */
+/* main kernel. read() waits for the recorded pairs and returns the     */
+/* summed milliseconds and launch count for `kernel` (e.g.              */
+/* "umma_conv_kernel"); reset=1 clears the totals.                      */
+/* ------------------------------------------------------------------ */
+WGX_API int wgx_kernel_timing(int enable);
+WGX_API int wgx_kernel_timing_read(const char *kernel, double *total_ms, int64_t *count, int reset);
+
+/* ------------------------------------------------------------------ */
 /* device error word: kernels with bounded waits set it instead of      */
 /* hanging; wgx_sync reports it.                                        */
 /* ------------------------------------------------------------------ */

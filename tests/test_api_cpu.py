@@ -74,8 +74,8 @@ def test_plan_selects_tensor_core_path_for_dense_fp16():
     # [8,64,160,160] x [128,64,3,3], s1 p1
     p = plan(B=8, IC=64, IH=160, IW=160, OC=128, OH=160, OW=160, KH=3, KW=3, pH=1, pW=1)
     assert p.variant == _lib.CONV_UMMA
-    # 128 output channels x 512 positions per CTA: 51 tiles per image
-    assert p.grid_ctas == 8 * 51
+    # tiles of 128 output channels x 256 positions: 102 per image
+    assert p.grid_ctas == 8 * 102
     assert p.scratch_bytes > 8 * 64 * 162 * 162 * 2
 
 

@@ -85,6 +85,8 @@ DENSE_F16 = [
     (1, 256, 20, 20, 256, 3, 3, 1, 1),
     (1, 8, 1, 600, 8, 1, 3, 0, 1),        # 1-row image, KH != KW
     (1, 96, 40, 40, 96, 3, 3, 1, 1),
+    (8, 64, 48, 48, 192, 3, 3, 1, 1),     # streamed weights, >1 tile per CTA
+    (3, 16, 30, 30, 24, 5, 3, 2, 1),      # KH != KW with padding
 ]
 
 
@@ -94,7 +96,7 @@ def test_dense_f16_tensor_core(ctx, geom):
     (x,) = oracle.make_inputs([(B, IC, H, W)], seed=10)
     w = kaiming((OC, IC, KH, KW), 11)
     (b,) = oracle.make_inputs([(OC,)], seed=12, scale=0.01)
-    pads = (pad if KH > 1 else 0, pad)
+    pads = (pad if KH > 1 else 0, pad if KW > 1 else 0) if KH != KW else (pad, pad)
     y = engine_conv(ctx, x, w, b, 1, pads, dil, 1)
     check_f16(y, x, w, b, 1, pads, dil, 1)
 

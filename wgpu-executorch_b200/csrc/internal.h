@@ -45,6 +45,11 @@ enum DeviceErrorBits : uint32_t {
 };
 uint32_t *device_error_word(int device);
 
+// Opt-in CUDA-event timing of individual kernels (wgx_kernel_timing). Both
+// are no-ops unless timing is enabled and the stream is not capturing.
+int timer_begin(const char *kernel, cudaStream_t stream);
+void timer_end(int handle, cudaStream_t stream);
+
 // ------------------------------------------------------------- objects
 struct Arena;
 

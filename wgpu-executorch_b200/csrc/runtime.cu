@@ -83,6 +83,49 @@ uint32_t *device_error_word(int device) {
   return static_cast<uint32_t *>(p);
 }
 
+// ------------------------------------------------------- kernel timing
+struct TimedLaunch {
+  std::string kernel;
+  cudaEvent_t start, stop;
+  bool closed;
+};
+struct TimingState {
+  std::mutex mu;
+  bool enabled = false;
+  std::vector<TimedLaunch> pending;
+  std::unordered_map<std::string, std::pair<double, int64_t>> totals;
+};
+static TimingState &timing() {
+  static TimingState t;
+  return t;
+}
+
+int timer_begin(const char *kernel, cudaStream_t stream) {
+  TimingState &t = timing();
+  std::lock_guard<std::mutex> lock(t.mu);
+  if (!t.enabled) return -1;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return -1;
+  }
+  TimedLaunch l{kernel, nullptr, nullptr, false};
+  check_cuda(cudaEventCreate(&l.start), "timer event");
+  check_cuda(cudaEventCreate(&l.stop), "timer event");
+  check_cuda(cudaEventRecord(l.start, stream), "timer record");
+  t.pending.push_back(l);
+  return int(t.pending.size()) - 1;
+}
+
+void timer_end(int handle, cudaStream_t stream) {
+  if (handle < 0) return;
+  TimingState &t = timing();
+  std::lock_guard<std::mutex> lock(t.mu);
+  if (handle >= int(t.pending.size())) return;
+  check_cuda(cudaEventRecord(t.pending[handle].stop, stream), "timer record");
+  t.pending[handle].closed = true;
+}
+
 }  // namespace wgx
 
 using namespace wgx;
@@ -501,6 +544,38 @@ int wgx_device_error(int device, uint32_t *code, int clear) {
       uint32_t zero = 0;
       check_cuda(cudaMemcpy(w, &zero, 4, cudaMemcpyHostToDevice), "clear device error word");
     }
+  });
+}
+
+int wgx_kernel_timing(int enable) {
+  return guarded([&] {
+    TimingState &t = timing();
+    std::lock_guard<std::mutex> lock(t.mu);
+    t.enabled = enable != 0;
+  });
+}
+
+int wgx_kernel_timing_read(const char *kernel, double *total_ms, int64_t *count, int reset) {
+  return guarded([&] {
+    TimingState &t = timing();
+    std::lock_guard<std::mutex> lock(t.mu);
+    for (auto &l : t.pending) {
+      if (l.closed) {
+        check_cuda(cudaEventSynchronize(l.stop), "timer sync");
+        float ms = 0;
+        check_cuda(cudaEventElapsedTime(&ms, l.start, l.stop), "timer elapsed");
+        auto &tot = t.totals[l.kernel];
+        tot.first += ms;
+        tot.second += 1;
+      }
+      cudaEventDestroy(l.start);
+      cudaEventDestroy(l.stop);
+    }
+    t.pending.clear();
+    auto it = t.totals.find(kernel ? kernel : "");
+    if (total_ms) *total_ms = it == t.totals.end() ? 0.0 : it->second.first;
+    if (count) *count = it == t.totals.end() ? 0 : it->second.second;
+    if (reset) t.totals.clear();
   });
 }
 

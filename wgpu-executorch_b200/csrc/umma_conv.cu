@@ -24,11 +24,16 @@
 //  * weights packed by pack_weights into [oc_tile][kh][cblk][kw][chunk][128][8]
 //    so the A operand of one pipeline stage is one contiguous bulk copy.
 //
-// CTA = 128 output channels x 512 positions (two N=256 accumulators, 512
-// TMEM columns). Pipeline stage = (kh, 32-channel block): A = KW x 128 x 32,
-// B = (512 + (KW-1)*dW) rows x 32 channels. Warp roles: warp 0 issues the
-// bulk copies, warp 1 owns TMEM and issues tcgen05.mma, warps 4-7 drain TMEM
-// (tcgen05.ld) through bias + activation to global memory.
+// Persistent kernel: one CTA per SM loops over tiles of 128 output channels
+// x 256 positions. Pipeline stage = (kh, 32-channel block): A = KW x 128 x 32
+// weights, B = (256 + (KW-1)*dW) activation rows x 32 channels. When all
+// weights of the (single) output-channel tile fit next to the pipeline they
+// are loaded once per CTA and stay resident; otherwise each stage streams
+// its A block. Two TMEM accumulators of 256 columns ping-pong, so the
+// epilogue of tile i overlaps the MMAs of tile i+1.
+// Warp roles: warp 0 issues bulk copies, warp 1 owns TMEM and issues
+// tcgen05.mma, warps 4-19 drain TMEM (four warps per TMEM lane quadrant,
+// 64 columns each) through bias + activation to NCHW global memory.
 //
 // Every mbarrier wait is bounded (about 2 s of %globaltimer); on expiry the
 // waiting role sets a bit in the device error word and stops, so a broken
@@ -37,26 +42,36 @@
 
 namespace wgx {
 
-constexpr int UM = 128;        // MMA M (output channels per CTA)
-constexpr int UN = 256;        // MMA N per instruction
-constexpr int NACC = 2;        // accumulators per CTA
-constexpr int NT = UN * NACC;  // positions per CTA
-constexpr int BK = 32;         // channels per pipeline stage
-constexpr int CHUNKS = BK / 8;
-constexpr int THREADS = 256;
-constexpr uint32_t TMEM_COLS = 512;
+constexpr int UM = 128;          // MMA M: output channels per tile
+constexpr int UN = 256;          // MMA N: positions per tile
+constexpr int BK = 32;           // channels per pipeline stage
+constexpr int CHUNKS = BK / 8;   // 16-byte channel chunks per stage
+constexpr int EPI_WARP0 = 4;     // first epilogue warp
+constexpr int EPI_WARPS = 16;    // four per TMEM lane quadrant
+constexpr int THREADS = 32 * (EPI_WARP0 + EPI_WARPS);
+constexpr uint32_t TMEM_COLS = 512;  // two accumulators of UN fp32 columns
 constexpr int MAX_KW = 7;
 constexpr uint64_t WAIT_NS = 2000000000ull;
+constexpr int EPI_COLS = 16;     // positions per staged epilogue block
+constexpr int EPI_ROWB = 48;     // staged channel row: 16 fp16 + 16 B pad
+constexpr uint32_t EPI_BYTES = EPI_WARPS * 32 * EPI_ROWB;
+constexpr uint32_t SMEM_MAX = 227u * 1024u;
 
 struct UmmaGeom {
   int B, IC, IH, IW, OC, OH, OW, KH, KW, dH, dW, pH, pW;
-  int Hp, Wp, C8, ncb, n_oct, tiles_per_img, R, R_alloc, stages, n_kstages;
-  long long plane_rows;  // Hp*Wp
-  uint32_t a_stage_bytes, b_stage_bytes;
+  int Hp, Wp, C8, ncb, n_oct, tiles_per_img, total_tiles, R, R_alloc, stages, n_kstages;
+  int resident;                      // all weights of the oc tile stay in smem
+  long long plane_rows;              // Hp*Wp
+  uint32_t a_stage_bytes, b_stage_bytes, w_region_bytes;
   int has_bias, act;
   float lo, hi;
   uint32_t *err;
 };
+
+static uint32_t smem_need(const UmmaGeom &g) {
+  return g.w_region_bytes + uint32_t(g.stages) * g.b_stage_bytes + EPI_BYTES +
+         (2 * g.stages + 5) * 8 + 16 + 128;
+}
 
 static UmmaGeom make_geom(const wgx_conv2d_params &p) {
   UmmaGeom g{};
@@ -80,18 +95,43 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p) {
   g.n_oct = (p.OC + UM - 1) / UM;
   g.plane_rows = (long long)g.Hp * g.Wp;
   long long p_out = (long long)(p.OH - 1) * g.Wp + p.OW;
-  g.tiles_per_img = int((p_out + NT - 1) / NT);
-  g.R = NT + (p.KW - 1) * p.dW;
+  g.tiles_per_img = int((p_out + UN - 1) / UN);
+  g.total_tiles = g.tiles_per_img * g.n_oct * g.B;
+  g.R = UN + (p.KW - 1) * p.dW;
   g.R_alloc = (g.R + 7) / 8 * 8;
   g.a_stage_bytes = uint32_t(p.KW) * CHUNKS * UM * 16;
   g.b_stage_bytes = uint32_t(CHUNKS) * g.R_alloc * 16;
   g.n_kstages = p.KH * g.ncb;
-  uint32_t stage = g.a_stage_bytes + g.b_stage_bytes;
-  int st = int((220u * 1024u) / stage);
-  if (st > 6) st = 6;
-  if (st > g.n_kstages) st = g.n_kstages;
-  if (st < 1) st = 1;
-  g.stages = st;
+  // resident weights: one oc tile, all stages' A blocks plus >= 2 B stages
+  uint64_t w_all = uint64_t(g.n_kstages) * g.a_stage_bytes;
+  g.resident = 0;
+  if (g.n_oct == 1) {
+    g.w_region_bytes = uint32_t(w_all);
+    g.stages = 2;
+    if (w_all < SMEM_MAX && smem_need(g) <= SMEM_MAX) {
+      g.resident = 1;
+      while (g.stages < 6 && (g.stages + 1) <= g.n_kstages) {
+        ++g.stages;
+        if (smem_need(g) > SMEM_MAX) {
+          --g.stages;
+          break;
+        }
+      }
+    }
+  }
+  if (!g.resident) {
+    g.stages = 2;
+    g.w_region_bytes = 2 * g.a_stage_bytes;
+    while (g.stages < 6) {
+      g.stages += 1;
+      g.w_region_bytes = uint32_t(g.stages) * g.a_stage_bytes;
+      if (smem_need(g) > SMEM_MAX) {
+        g.stages -= 1;
+        g.w_region_bytes = uint32_t(g.stages) * g.a_stage_bytes;
+        break;
+      }
+    }
+  }
   g.has_bias = p.has_bias;
   g.act = p.act;
   g.lo = p.out_min;
@@ -99,12 +139,10 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p) {
   return g;
 }
 
-// Dynamic shared memory of one CTA. Never below 120 KB, so that at most
-// one CTA is resident per SM and the 512-column TMEM allocation of a CTA
-// never waits on another CTA of the same kernel.
+// Dynamic shared memory of one CTA; never below 120 KB so that exactly one
+// CTA is resident per SM (the 512-column TMEM allocation never waits).
 static uint32_t smem_bytes(const UmmaGeom &g) {
-  uint32_t need = uint32_t(g.stages) * (g.a_stage_bytes + g.b_stage_bytes) +
-                  (2 * g.stages + 1) * 8 + 16 + 128;
+  uint32_t need = smem_need(g);
   return need < 120u * 1024u ? 120u * 1024u : need;
 }
 
@@ -117,16 +155,23 @@ bool umma_conv_supported(const wgx_conv2d_params &p) {
   if (p.OH != p.IH + 2 * p.pH - p.dH * (p.KH - 1)) return false;
   if (p.OW != p.IW + 2 * p.pW - p.dW * (p.KW - 1)) return false;
   UmmaGeom g = make_geom(p);
-  if (g.stages < 2 && g.n_kstages > 1) return false;
-  if (smem_bytes(g) > 227u * 1024u) return false;
+  if (g.stages < 2) return false;
+  if (smem_need(g) > SMEM_MAX) return false;
   if (g.R_alloc * 16 >= (1 << 18)) return false;  // LBO field range
-  if (g.B > 65535 || g.n_oct > 65535) return false;
+  if (g.total_tiles < 1) return false;
   return true;
+}
+
+static int sm_count() {
+  int dev = 0, n = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  check_cuda(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev), "SM count");
+  return n;
 }
 
 uint64_t umma_conv_grid(const wgx_conv2d_params &p) {
   UmmaGeom g = make_geom(p);
-  return uint64_t(g.tiles_per_img) * g.n_oct * g.B;
+  return uint64_t(g.total_tiles);
 }
 
 uint64_t umma_conv_packed_weight_bytes(const wgx_conv2d_params &p) {
@@ -135,11 +180,11 @@ uint64_t umma_conv_packed_weight_bytes(const wgx_conv2d_params &p) {
 }
 
 // Rows the main kernel may read: the last tile's B stage of the last filter
-// row starts at (tiles*NT - NT) + (KH-1)*dH*Wp and spans R rows. Rows past
-// the image only feed output positions that are discarded.
+// row starts at (tiles-1)*UN + (KH-1)*dH*Wp and spans R rows. Rows past the
+// image only feed output positions that are discarded.
 static uint64_t input_rows_total(const UmmaGeom &g) {
   uint64_t planes = uint64_t(g.B) * (g.C8 / 8);
-  uint64_t last_end = uint64_t(g.tiles_per_img - 1) * NT + uint64_t(g.KH - 1) * g.dH * g.Wp + g.R;
+  uint64_t last_end = uint64_t(g.tiles_per_img - 1) * UN + uint64_t(g.KH - 1) * g.dH * g.Wp + g.R;
   uint64_t slack = last_end > uint64_t(g.plane_rows) ? last_end - g.plane_rows : 0;
   return planes * g.plane_rows + slack;
 }
@@ -175,6 +220,62 @@ __global__ void pack_input(UmmaGeom g, const __half *__restrict__ x, uint4 *__re
     v[e] = (inside && c < g.IC) ? src[e * cstride] : __float2half_rn(0.f);
   }
   xs[i] = *reinterpret_cast<const uint4 *>(v);
+}
+
+// Vector form of pack_input for IW % 4 == 0: one thread re-lays 4
+// consecutive padded positions of one 8-channel block. The first position
+// wp0 = 4t + (pW % 4) - 4 is chosen so that its input column iw0 = wp0 - pW
+// is a multiple of 4: each channel row contributes one aligned 8-byte load,
+// the 8x4 block is transposed in registers (prmt) and written as four
+// 16-byte slots (64 contiguous bytes). Positions outside [0, Wp) are
+// skipped; padding positions and channels >= IC are written as zeros.
+__global__ void pack_input_v4(UmmaGeom g, const __half *__restrict__ x, uint4 *__restrict__ xs,
+                              int groups_per_row, long long n_threads) {
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_threads) return;
+  const int t = int(i % groups_per_row);
+  long long r = i / groups_per_row;
+  const int hp = int(r % g.Hp);
+  r /= g.Hp;
+  const int cb = int(r % (g.C8 / 8));
+  const long long b = r / (g.C8 / 8);
+  const int wp0 = 4 * t + (g.pW & 3) - 4;
+  const int iw0 = wp0 - g.pW;
+  const int ih = hp - g.pH;
+  const bool row_in = ih >= 0 && ih < g.IH;
+  uint2 ch[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int c = cb * 8 + e;
+    ch[e] = make_uint2(0u, 0u);
+    if (row_in && c < g.IC) {
+      const __half *src = x + ((b * g.IC + c) * g.IH + ih) * (long long)g.IW;
+      if (iw0 >= 0 && iw0 + 3 < g.IW) {
+        ch[e] = *reinterpret_cast<const uint2 *>(src + iw0);
+      } else {
+        __align__(8) __half v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int iw = iw0 + k;
+          v[k] = (iw >= 0 && iw < g.IW) ? src[iw] : __float2half_rn(0.f);
+        }
+        ch[e] = *reinterpret_cast<const uint2 *>(v);
+      }
+    }
+  }
+  uint4 *dst = xs + ((b * (g.C8 / 8) + cb) * g.Hp + hp) * (long long)g.Wp;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int wp = wp0 + k;
+    if (wp < 0 || wp >= g.Wp) continue;
+    // halves of position k: low (k even) or high (k odd) half of word k/2
+    const uint32_t sel = (k & 1) ? 0x7632u : 0x5410u;
+    const bool lo = k < 2;
+    dst[wp] = make_uint4(__byte_perm(lo ? ch[0].x : ch[0].y, lo ? ch[1].x : ch[1].y, sel),
+                         __byte_perm(lo ? ch[2].x : ch[2].y, lo ? ch[3].x : ch[3].y, sel),
+                         __byte_perm(lo ? ch[4].x : ch[4].y, lo ? ch[5].x : ch[5].y, sel),
+                         __byte_perm(lo ? ch[6].x : ch[6].y, lo ? ch[7].x : ch[7].y, sel));
+  }
 }
 
 // packed[oct][kh][cbk][kw][chunk][row 0..127][8] <- w[oc][c][kh][kw]
@@ -289,10 +390,50 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *r) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ float epi_act(float v, int act, float lo, float hi) {
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *r) {
+  uint32_t *u = reinterpret_cast<uint32_t *>(r);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]),
+        "=r"(u[7]), "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]),
+        "=r"(u[14]), "=r"(u[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// bias + activation of one accumulator value. SiLU(v) = v*sigmoid(v) is
+// evaluated as h + h*tanh(h) with h = v/2 (the identity
+// sigmoid(v) = (1 + tanh(v/2)) / 2): two FMAs and one MUFU op; the bias is
+// folded into the first FMA (hb = bias/2).
+__device__ __forceinline__ float epi_act(float acc, float bias, float hb, int act, float lo,
+                                         float hi) {
+  if (act == WGX_ACT_SILU) {
+    const float h = fmaf(acc, 0.5f, hb);
+    return fmaf(h, tanh_approx(h), h);
+  }
+  const float v = acc + bias;
   if (act == WGX_ACT_CLAMP) return fminf(fmaxf(v, lo), hi);
-  if (act == WGX_ACT_SILU) return v / (1.0f + __expf(-v));
   return v;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// tile index -> (image, first position, output-channel tile); oc tile
+// fastest so that CTAs working on the same positions run together.
+__device__ __forceinline__ void tile_coords(const UmmaGeom &g, int t, int &b, long long &p0,
+                                            int &oct) {
+  oct = t % g.n_oct;
+  const int rest = t / g.n_oct;
+  b = rest / g.tiles_per_img;
+  p0 = (long long)(rest % g.tiles_per_img) * UN;
 }
 
 // ------------------------------------------------------------ main kernel
@@ -304,20 +445,25 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
                                               ~uintptr_t(127));
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int tile = blockIdx.x, oct = blockIdx.y, b = blockIdx.z;
   const int S = g.stages;
-  uint8_t *sA = smem;
-  uint8_t *sB = smem + size_t(S) * g.a_stage_bytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + size_t(S) * g.b_stage_bytes);
-  uint64_t *full = bars, *empty = bars + S, *accf = bars + 2 * S;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accf + 1);
+  uint8_t *sW = smem;                                  // weights (resident or per stage)
+  uint8_t *sB = sW + g.w_region_bytes;                 // activation stages
+  uint8_t *sE = sB + size_t(S) * g.b_stage_bytes;      // epilogue staging
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sE + EPI_BYTES);
+  uint64_t *full = bars, *empty = bars + S;
+  uint64_t *accf = bars + 2 * S, *acce = accf + 2, *wbar = acce + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(wbar + 1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
-    mbar_init(smem_u32(accf), 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&accf[a]), 1);
+      mbar_init(smem_u32(&acce[a]), EPI_WARPS);
+    }
+    mbar_init(smem_u32(wbar), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -332,29 +478,42 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const long long p0 = (long long)tile * NT;
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- producer: bulk copies of weights + activation rows
-      const uint32_t b_bytes_copied = uint32_t(g.R) * 16;
-      for (int s = 0; s < g.n_kstages; ++s) {
-        const int slot = s % S, use = s / S;
-        if (use > 0 && !mbar_wait(smem_u32(&empty[slot]), (use - 1) & 1)) {
-          atomicOr(g.err, kErrLoadTimeout);
-          break;
-        }
-        const int kh = s / g.ncb, cbk = s % g.ncb;
-        const uint32_t fb = smem_u32(&full[slot]);
-        mbar_expect_tx(fb, g.a_stage_bytes + CHUNKS * b_bytes_copied);
-        const uint8_t *asrc = wpk + ((size_t(oct) * g.KH + kh) * g.ncb + cbk) * g.a_stage_bytes;
-        bulk_g2s(smem_u32(sA + size_t(slot) * g.a_stage_bytes), asrc, g.a_stage_bytes, fb);
-        const long long row0 = p0 + (long long)kh * g.dH * g.Wp;
-        for (int ch = 0; ch < CHUNKS; ++ch) {
-          const long long plane = (long long)b * (g.C8 / 8) + cbk * CHUNKS + ch;
-          const uint8_t *bsrc = xs + (plane * g.plane_rows + row0) * 16;
-          bulk_g2s(smem_u32(sB + size_t(slot) * g.b_stage_bytes + size_t(ch) * g.R_alloc * 16),
-                   bsrc, b_bytes_copied, fb);
+      const uint32_t b_copy = uint32_t(g.R) * 16;
+      if (g.resident) {
+        const uint32_t wb = smem_u32(wbar);
+        mbar_expect_tx(wb, g.w_region_bytes);
+        bulk_g2s(smem_u32(sW), wpk, g.w_region_bytes, wb);
+      }
+      int gs = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x) {
+        int b, oct;
+        long long p0;
+        tile_coords(g, t, b, p0, oct);
+        for (int s = 0; s < g.n_kstages; ++s, ++gs) {
+          const int slot = gs % S, use = gs / S;
+          if (use > 0 && !mbar_wait(smem_u32(&empty[slot]), (use - 1) & 1)) {
+            atomicOr(g.err, kErrLoadTimeout);
+            ok = false;
+            break;
+          }
+          const int kh = s / g.ncb, cbk = s % g.ncb;
+          const uint32_t fb = smem_u32(&full[slot]);
+          mbar_expect_tx(fb, (g.resident ? 0u : g.a_stage_bytes) + CHUNKS * b_copy);
+          if (!g.resident)
+            bulk_g2s(smem_u32(sW + size_t(slot) * g.a_stage_bytes),
+                     wpk + ((size_t(oct) * g.KH + kh) * g.ncb + cbk) * g.a_stage_bytes,
+                     g.a_stage_bytes, fb);
+          const long long row0 = p0 + (long long)kh * g.dH * g.Wp;
+          for (int ch = 0; ch < CHUNKS; ++ch) {
+            const long long plane = (long long)b * (g.C8 / 8) + cbk * CHUNKS + ch;
+            bulk_g2s(smem_u32(sB + size_t(slot) * g.b_stage_bytes + size_t(ch) * g.R_alloc * 16),
+                     xs + (plane * g.plane_rows + row0) * 16, b_copy, fb);
+          }
         }
       }
     }
@@ -367,60 +526,126 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t a_lbo = UM * 16;                       // chunk plane of A
       const uint32_t b_lbo = uint32_t(g.R_alloc) * 16;      // chunk plane of B
       bool ok = true;
-      for (int s = 0; s < g.n_kstages && ok; ++s) {
-        const int slot = s % S, use = s / S;
-        if (!mbar_wait(smem_u32(&full[slot]), use & 1)) {
+      if (g.resident && !mbar_wait(smem_u32(wbar), 0)) {
+        atomicOr(g.err, kErrMmaTimeout);
+        ok = false;
+      }
+      int gs = 0, it = 0;
+      for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1, use_acc = it >> 1;
+        if (use_acc > 0 && !mbar_wait(smem_u32(&acce[acc]), (use_acc - 1) & 1)) {
           atomicOr(g.err, kErrMmaTimeout);
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t a_base = smem_u32(sA + size_t(slot) * g.a_stage_bytes);
-        const uint32_t b_base = smem_u32(sB + size_t(slot) * g.b_stage_bytes);
-        for (int kw = 0; kw < g.KW; ++kw) {
+        const uint32_t d = tmem + uint32_t(acc * UN);
+        for (int s = 0; s < g.n_kstages; ++s, ++gs) {
+          const int slot = gs % S, use = gs / S;
+          if (!mbar_wait(smem_u32(&full[slot]), use & 1)) {
+            atomicOr(g.err, kErrMmaTimeout);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base =
+              smem_u32(sW + size_t(g.resident ? s : slot) * g.a_stage_bytes);
+          const uint32_t b_base = smem_u32(sB + size_t(slot) * g.b_stage_bytes);
+          for (int kw = 0; kw < g.KW; ++kw) {
 #pragma unroll
-          for (int ks = 0; ks < BK / 16; ++ks) {
-            const uint64_t adesc =
-                kmajor_desc(a_base + uint32_t(kw) * CHUNKS * UM * 16 + ks * 2 * a_lbo, a_lbo);
-#pragma unroll
-            for (int h = 0; h < NACC; ++h) {
-              const uint64_t bdesc = kmajor_desc(
-                  b_base + uint32_t(h * UN + kw * g.dW) * 16 + ks * 2 * b_lbo, b_lbo);
-              mma_f16(tmem + h * UN, adesc, bdesc, idesc, (s | kw | ks) != 0);
+            for (int ks = 0; ks < BK / 16; ++ks) {
+              const uint64_t adesc =
+                  kmajor_desc(a_base + uint32_t(kw) * CHUNKS * UM * 16 + ks * 2 * a_lbo, a_lbo);
+              const uint64_t bdesc =
+                  kmajor_desc(b_base + uint32_t(kw * g.dW) * 16 + ks * 2 * b_lbo, b_lbo);
+              mma_f16(d, adesc, bdesc, idesc, (s | kw | ks) != 0);
             }
           }
+          mma_commit(smem_u32(&empty[slot]));
         }
-        mma_commit(smem_u32(&empty[slot]));
+        if (ok) mma_commit(smem_u32(&accf[acc]));
       }
-      mma_commit(smem_u32(accf));
     }
-  } else if (warp >= 4) {
-    // ---------------- epilogue: TMEM -> bias + activation -> NCHW fp16
-    const int q = warp & 3;
-    const int oc = oct * UM + q * 32 + lane;
-    const bool ok = mbar_wait(smem_u32(accf), 0);
-    if (!ok && lane == 0) atomicOr(g.err, kErrEpilogueTimeout);
-    tc_fence_after();
-    const float bv = (g.has_bias && oc < g.OC) ? __half2float(bias[oc]) : 0.f;
-    __half *obase = out + ((long long)b * g.OC + (oc < g.OC ? oc : 0)) * g.OH * (long long)g.OW;
-    float r[32];
-    for (int h = 0; h < NACC; ++h) {
-      for (int c = 0; c < UN / 32; ++c) {
-        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + h * UN + c * 32, r);
-        long long pb = p0 + h * UN + c * 32;
-        int oh = int(pb / g.Wp), ow = int(pb % g.Wp);
-        if (ok && oc < g.OC) {
+  } else if (warp >= EPI_WARP0) {
+    // ---------------- epilogue: TMEM -> bias + activation -> NCHW fp16.
+    // Warp w reads TMEM lane quadrant w % 4 (32 output channels) and one
+    // quarter (64 columns) of the accumulator. Per block of 16 positions it
+    // converts its 32x16 tile to fp16 into its private staging rows (48 B,
+    // conflict-free row writes), then stores four channel rows per
+    // instruction: 8 lanes x 2 positions = one full 32-byte sector per row
+    // when OW and Wp are even (pairs never straddle an output row), 2-byte
+    // stores otherwise.
+    const int ew = warp - EPI_WARP0;
+    constexpr int WCOLS = UN / (EPI_WARPS / 4);  // accumulator columns per warp
+    const int q = warp & 3, colh = ew / 4;
+    uint8_t *stage = sE + size_t(ew) * 32 * EPI_ROWB;
+    const bool pairs = ((g.OW | g.Wp) & 1) == 0;
+    const long long plane = (long long)g.OH * g.OW;
+    const int sub = lane & 7, rsel = lane >> 3;  // position pair, row within 4
+    float r[EPI_COLS];
+    int it = 0;
+    for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++it) {
+      const int acc = it & 1, use_acc = it >> 1;
+      int b, oct;
+      long long p0;
+      tile_coords(g, t, b, p0, oct);
+      const bool ok = mbar_wait(smem_u32(&accf[acc]), use_acc & 1);
+      if (!ok) {
+        if (lane == 0) atomicOr(g.err, kErrEpilogueTimeout);
+        break;
+      }
+      tc_fence_after();
+      const int oc_lane = oct * UM + q * 32 + lane;
+      const float bv = (g.has_bias && oc_lane < g.OC) ? __half2float(bias[oc_lane]) : 0.f;
+      const float hb = 0.5f * bv;
+      __half *obase = out + (long long)b * g.OC * plane;
+      constexpr int NBLK = WCOLS / EPI_COLS;
+      for (int blk = 0; blk < NBLK; ++blk) {
+        const int col0 = colh * WCOLS + blk * EPI_COLS;
+        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * UN + col0), r);
+        if (blk == NBLK - 1) {
+          // all TMEM reads of this accumulator are done: hand it back
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
+        }
+        uint32_t pw[EPI_COLS / 2];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (oh < g.OH && ow < g.OW)
-              obase[(long long)oh * g.OW + ow] =
-                  __float2half_rn(epi_act(r[j] + bv, g.act, g.lo, g.hi));
-            if (++ow == g.Wp) {
-              ow = 0;
-              ++oh;
+        for (int j = 0; j < EPI_COLS / 2; ++j) {
+          __half2 h2 = __floats2half2_rn(epi_act(r[2 * j], bv, hb, g.act, g.lo, g.hi),
+                                         epi_act(r[2 * j + 1], bv, hb, g.act, g.lo, g.hi));
+          pw[j] = *reinterpret_cast<uint32_t *>(&h2);
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(stage + lane * EPI_ROWB);
+        dst[0] = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+        dst[1] = make_uint4(pw[4], pw[5], pw[6], pw[7]);
+        __syncwarp();
+        const long long p = p0 + col0 + 2 * sub;
+        const int oh = int(p / g.Wp), ow = int(p % g.Wp);
+        const bool v0 = oh < g.OH && ow < g.OW;
+        const long long off0 = (long long)oh * g.OW + ow;
+        // second position: next column, or the first column of the next row
+        const bool wrap = ow + 1 >= g.Wp;
+        const bool v1 = wrap ? (oh + 1 < g.OH) : (oh < g.OH && ow + 1 < g.OW);
+        const long long off1 = wrap ? (long long)(oh + 1) * g.OW : off0 + 1;
+#pragma unroll
+        for (int r4 = 0; r4 < 8; ++r4) {
+          const int rr = 4 * r4 + rsel;
+          const int oc = oct * UM + q * 32 + rr;
+          const uint32_t val =
+              *reinterpret_cast<const uint32_t *>(stage + rr * EPI_ROWB + 4 * sub);
+          if (oc < g.OC) {
+            __half *orow = obase + (long long)oc * plane;
+            if (pairs) {
+              if (v0) *reinterpret_cast<uint32_t *>(orow + off0) = val;
+            } else {
+              const __half2 h2 = *reinterpret_cast<const __half2 *>(&val);
+              if (v0) orow[off0] = __low2half(h2);
+              if (v1) orow[off1] = __high2half(h2);
             }
           }
         }
+        __syncwarp();
       }
     }
   }
@@ -452,23 +677,35 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, const void *pac
   g.err = device_error_word(dev);
   if ((reinterpret_cast<uintptr_t>(xs) & 15) || (reinterpret_cast<uintptr_t>(packed) & 15))
     fail("conv2d: scratch must be 16-byte aligned");
-  long long n_slots = (long long)g.B * (g.C8 / 8) * g.plane_rows;
-  pack_input<<<unsigned((n_slots + 255) / 256), 256, 0, stream>>>(g, in, static_cast<uint4 *>(xs),
-                                                                 n_slots);
+  if (g.IW % 4 == 0 && (reinterpret_cast<uintptr_t>(in) & 7) == 0) {
+    const int groups_per_row = (g.Wp - (g.pW & 3) + 4 + 3) / 4;
+    long long n = (long long)g.B * (g.C8 / 8) * g.Hp * groups_per_row;
+    pack_input_v4<<<unsigned((n + 255) / 256), 256, 0, stream>>>(
+        g, in, static_cast<uint4 *>(xs), groups_per_row, n);
+  } else {
+    long long n_slots = (long long)g.B * (g.C8 / 8) * g.plane_rows;
+    pack_input<<<unsigned((n_slots + 255) / 256), 256, 0, stream>>>(
+        g, in, static_cast<uint4 *>(xs), n_slots);
+  }
   check_cuda(cudaGetLastError(), "pack_input launch");
   uint32_t smem = smem_bytes(g);
   static bool attr_set[64] = {};
   if (dev < 64 && !attr_set[dev]) {
     check_cuda(cudaFuncSetAttribute(umma_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    227 * 1024),
+                                    int(SMEM_MAX)),
                "umma_conv smem attr");
     attr_set[dev] = true;
   }
-  dim3 grid(unsigned(g.tiles_per_img), unsigned(g.n_oct), unsigned(g.B));
+  static int sms[64] = {};
+  if (dev < 64 && !sms[dev]) sms[dev] = sm_count();
+  const int n_sm = dev < 64 ? sms[dev] : sm_count();
+  const int grid = g.total_tiles < n_sm ? g.total_tiles : n_sm;
+  int th = timer_begin("umma_conv_kernel", stream);
   umma_conv_kernel<<<grid, THREADS, smem, stream>>>(g, static_cast<const uint8_t *>(xs),
                                                     static_cast<const uint8_t *>(packed), bias,
                                                     out);
   check_cuda(cudaGetLastError(), "umma_conv launch");
+  timer_end(th, stream);
 }
 
 }  // namespace wgx
