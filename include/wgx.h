@@ -205,6 +205,18 @@ WGX_API int wgx_conv2d_plan_for(const wgx_conv2d_params *p, wgx_conv2d_plan *out
  * out: NCHW [B,OC,OH,OW]. The packed-weight cache lives in scratch. */
 WGX_API int wgx_conv2d(const wgx_conv2d_params *p, const void *in, const void *w, const void *bias,
                void *out, void *scratch, uint64_t scratch_bytes, void *stream);
+/* Same convolution for callers that cannot allocate device memory (inside
+ * a stream capture, under a foreign allocator, or in loops that cannot
+ * afford cudaFree's synchronisation). No counterpart in the reference.
+ * Scratch comes from a fixed 32 MiB buffer built into the library instead
+ * of from the caller; the call allocates nothing. Convolutions needing more
+ * than 32 MiB of scratch (wgx_conv2d_plan_for: scratch_bytes) are rejected.
+ * The first call on a device looks the buffer up (once per device); make
+ * that first call before any stream capture. All calls on a device share
+ * the buffer: calls that overlap on the GPU race, so order them on one
+ * stream. */
+WGX_API int wgx_conv2d_noalloc(const wgx_conv2d_params *p, const void *in, const void *w,
+                               const void *bias, void *out, void *stream);
 
 /* ------------------------------------------------------------------ */
 /* kernel timing: when enabled, the hot-path kernels launched outside a */

@@ -88,6 +88,8 @@ SIGNATURES = {
     "wgx_conv2d_plan_for": ([POINTER(ConvParams), POINTER(ConvPlan)], c_int),
     "wgx_conv2d": ([POINTER(ConvParams), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                     c_uint64, c_void_p], c_int),
+    "wgx_conv2d_noalloc": ([POINTER(ConvParams), c_void_p, c_void_p, c_void_p, c_void_p,
+                            c_void_p], c_int),
     "wgx_device_error": ([c_int, POINTER(c_uint32), c_int], c_int),
     "wgx_kernel_timing": ([c_int], c_int),
     "wgx_kernel_timing_read": ([c_char_p, POINTER(c_double), POINTER(c_int64), c_int], c_int),
