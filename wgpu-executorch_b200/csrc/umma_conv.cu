@@ -44,8 +44,6 @@ namespace wgx {
 
 constexpr int UM = 128;          // MMA M: output channels per tile
 constexpr int UN = 256;          // MMA N: positions per tile
-constexpr int BK = 32;           // channels per pipeline stage
-constexpr int CHUNKS = BK / 8;   // 16-byte channel chunks per stage
 constexpr int EPI_WARP0 = 4;     // first epilogue warp
 constexpr int EPI_WARPS = 16;    // four per TMEM lane quadrant
 constexpr int THREADS = 32 * (EPI_WARP0 + EPI_WARPS);
@@ -59,6 +57,8 @@ constexpr uint32_t SMEM_MAX = 227u * 1024u;
 
 struct UmmaGeom {
   int B, IC, IH, IW, OC, OH, OW, KH, KW, dH, dW, pH, pW;
+  int bk, chunks;                    // channels per stage, 16-byte chunks per stage
+  int khs, n_khg;                    // filter rows per stage, filter-row groups
   int Hp, Wp, C8, ncb, n_oct, tiles_per_img, total_tiles, R, R_alloc, stages, n_kstages;
   int resident;                      // all weights of the oc tile stay in smem
   long long plane_rows;              // Hp*Wp
@@ -73,7 +73,10 @@ static uint32_t smem_need(const UmmaGeom &g) {
          (2 * g.stages + 5) * 8 + 16 + 128;
 }
 
-static UmmaGeom make_geom(const wgx_conv2d_params &p) {
+// Geometry for one staging choice: each pipeline stage carries `bk` input
+// channels and `khs` filter rows (khs = 1: one stage per filter row;
+// khs = KH: the whole filter, so one staged activation tile feeds every tap).
+static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk) {
   UmmaGeom g{};
   g.B = p.B;
   g.IC = p.IC;
@@ -88,27 +91,33 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p) {
   g.dW = p.dW;
   g.pH = p.pH;
   g.pW = p.pW;
+  g.bk = bk;
+  g.chunks = bk / 8;
+  g.khs = khs;
+  g.n_khg = p.KH / khs;
   g.Hp = p.IH + 2 * p.pH;
   g.Wp = p.IW + 2 * p.pW;
-  g.C8 = (p.IC + BK - 1) / BK * BK;
-  g.ncb = g.C8 / BK;
+  g.C8 = (p.IC + bk - 1) / bk * bk;
+  g.ncb = g.C8 / bk;
   g.n_oct = (p.OC + UM - 1) / UM;
   g.plane_rows = (long long)g.Hp * g.Wp;
   long long p_out = (long long)(p.OH - 1) * g.Wp + p.OW;
   g.tiles_per_img = int((p_out + UN - 1) / UN);
   g.total_tiles = g.tiles_per_img * g.n_oct * g.B;
-  g.R = UN + (p.KW - 1) * p.dW;
+  long long r = UN + (long long)(khs - 1) * p.dH * g.Wp + (long long)(p.KW - 1) * p.dW;
+  g.R = r > (1 << 20) ? (1 << 20) : int(r);
   g.R_alloc = (g.R + 7) / 8 * 8;
-  g.a_stage_bytes = uint32_t(p.KW) * CHUNKS * UM * 16;
-  g.b_stage_bytes = uint32_t(CHUNKS) * g.R_alloc * 16;
-  g.n_kstages = p.KH * g.ncb;
+  g.a_stage_bytes = uint32_t(khs * p.KW) * g.chunks * UM * 16;
+  g.b_stage_bytes = uint32_t(g.chunks) * g.R_alloc * 16;
+  g.n_kstages = g.n_khg * g.ncb;
   // resident weights: one oc tile, all stages' A blocks plus >= 2 B stages
   uint64_t w_all = uint64_t(g.n_kstages) * g.a_stage_bytes;
   g.resident = 0;
-  if (g.n_oct == 1) {
+  g.stages = 0;
+  if (g.n_oct == 1 && w_all < SMEM_MAX) {
     g.w_region_bytes = uint32_t(w_all);
     g.stages = 2;
-    if (w_all < SMEM_MAX && smem_need(g) <= SMEM_MAX) {
+    if (smem_need(g) <= SMEM_MAX) {
       g.resident = 1;
       while (g.stages < 6 && (g.stages + 1) <= g.n_kstages) {
         ++g.stages;
@@ -120,8 +129,8 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p) {
     }
   }
   if (!g.resident) {
-    g.stages = 2;
-    g.w_region_bytes = 2 * g.a_stage_bytes;
+    g.stages = 1;
+    g.w_region_bytes = g.a_stage_bytes;
     while (g.stages < 6) {
       g.stages += 1;
       g.w_region_bytes = uint32_t(g.stages) * g.a_stage_bytes;
@@ -137,6 +146,29 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p) {
   g.lo = p.out_min;
   g.hi = p.out_max;
   return g;
+}
+
+// Pick the staging: per-filter-row stages of 32 channels measured fastest
+// on config 2 (41 % tensor-pipe activity against 30 % for whole-filter
+// stages of 16 channels); whole-filter and 16-channel stages are the
+// fallbacks for shapes where fewer than three 32-channel stages fit.
+static UmmaGeom make_geom(const wgx_conv2d_params &p) {
+  const int cand[3][2] = {{1, 32}, {p.KH, 16}, {1, 16}};
+  UmmaGeom best{};
+  bool have = false;
+  for (int min_stages : {3, 2}) {
+    for (auto &c : cand) {
+      UmmaGeom g = geom_for(p, c[0], c[1]);
+      if (g.stages >= min_stages && smem_need(g) <= SMEM_MAX && g.R_alloc * 16 < (1 << 18)) {
+        return g;
+      }
+      if (!have) {
+        best = g;
+        have = true;
+      }
+    }
+  }
+  return best;
 }
 
 // Dynamic shared memory of one CTA; never below 120 KB so that exactly one
@@ -159,6 +191,9 @@ bool umma_conv_supported(const wgx_conv2d_params &p) {
   if (smem_need(g) > SMEM_MAX) return false;
   if (g.R_alloc * 16 >= (1 << 18)) return false;  // LBO field range
   if (g.total_tiles < 1) return false;
+  // positions and per-image output offsets are handled in 32-bit integers
+  if ((long long)g.tiles_per_img * UN + g.plane_rows >= (1ll << 31)) return false;
+  if ((long long)g.OH * g.OW >= (1ll << 31)) return false;
   return true;
 }
 
@@ -176,7 +211,7 @@ uint64_t umma_conv_grid(const wgx_conv2d_params &p) {
 
 uint64_t umma_conv_packed_weight_bytes(const wgx_conv2d_params &p) {
   UmmaGeom g = make_geom(p);
-  return uint64_t(g.n_oct) * g.KH * g.ncb * g.a_stage_bytes;
+  return uint64_t(g.n_oct) * g.n_kstages * g.a_stage_bytes;
 }
 
 // Rows the main kernel may read: the last tile's B stage of the last filter
@@ -184,7 +219,8 @@ uint64_t umma_conv_packed_weight_bytes(const wgx_conv2d_params &p) {
 // image only feed output positions that are discarded.
 static uint64_t input_rows_total(const UmmaGeom &g) {
   uint64_t planes = uint64_t(g.B) * (g.C8 / 8);
-  uint64_t last_end = uint64_t(g.tiles_per_img - 1) * UN + uint64_t(g.KH - 1) * g.dH * g.Wp + g.R;
+  uint64_t last_end = uint64_t(g.tiles_per_img - 1) * UN +
+                      uint64_t(g.n_khg - 1) * g.khs * g.dH * g.Wp + g.R;
   uint64_t slack = last_end > uint64_t(g.plane_rows) ? last_end - g.plane_rows : 0;
   return planes * g.plane_rows + slack;
 }
@@ -278,27 +314,31 @@ __global__ void pack_input_v4(UmmaGeom g, const __half *__restrict__ x, uint4 *_
   }
 }
 
-// packed[oct][kh][cbk][kw][chunk][row 0..127][8] <- w[oc][c][kh][kw]
+// packed[oct][khg][cb][kh_local][kw][chunk][row 0..127][8] <- w[oc][c][kh][kw]
+// (kh = khg*khs + kh_local): one pipeline stage's A operand is contiguous.
 __global__ void pack_weights(UmmaGeom g, const __half *__restrict__ w, uint4 *__restrict__ packed,
-                             long long n_slots) {
-  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+                             int n_slots) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n_slots) return;
-  int row = int(i % UM);
-  long long t = i / UM;
-  int chunk = int(t % CHUNKS);
-  t /= CHUNKS;
-  int kw = int(t % g.KW);
+  const int row = i % UM;
+  int t = i / UM;
+  const int chunk = t % g.chunks;
+  t /= g.chunks;
+  const int kw = t % g.KW;
   t /= g.KW;
-  int cbk = int(t % g.ncb);
+  const int khl = t % g.khs;
+  t /= g.khs;
+  const int cb = t % g.ncb;
   t /= g.ncb;
-  int kh = int(t % g.KH);
-  int oct = int(t / g.KH);
-  int oc = oct * UM + row;
+  const int khg = t % g.n_khg;
+  const int oct = t / g.n_khg;
+  const int kh = khg * g.khs + khl;
+  const int oc = oct * UM + row;
   __align__(16) __half v[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    int c = cbk * BK + chunk * 8 + e;
-    v[e] = (oc < g.OC && c < g.IC) ? w[(((long long)oc * g.IC + c) * g.KH + kh) * g.KW + kw]
+    const int c = cb * g.bk + chunk * 8 + e;
+    v[e] = (oc < g.OC && c < g.IC) ? w[((size_t(oc) * g.IC + c) * g.KH + kh) * g.KW + kw]
                                    : __float2half_rn(0.f);
   }
   packed[i] = *reinterpret_cast<const uint4 *>(v);
@@ -411,15 +451,16 @@ __device__ __forceinline__ float tanh_approx(float x) {
 // evaluated as h + h*tanh(h) with h = v/2 (the identity
 // sigmoid(v) = (1 + tanh(v/2)) / 2): two FMAs and one MUFU op; the bias is
 // folded into the first FMA (hb = bias/2).
-__device__ __forceinline__ float epi_act(float acc, float bias, float hb, int act, float lo,
-                                         float hi) {
-  if (act == WGX_ACT_SILU) {
+template <int ACT>
+__device__ __forceinline__ float epi_act(float acc, float bias, float hb, float lo, float hi) {
+  if constexpr (ACT == WGX_ACT_SILU) {
     const float h = fmaf(acc, 0.5f, hb);
     return fmaf(h, tanh_approx(h), h);
+  } else if constexpr (ACT == WGX_ACT_CLAMP) {
+    return fminf(fmaxf(acc + bias, lo), hi);
+  } else {
+    return acc + bias;
   }
-  const float v = acc + bias;
-  if (act == WGX_ACT_CLAMP) return fminf(fmaxf(v, lo), hi);
-  return v;
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
@@ -437,6 +478,10 @@ __device__ __forceinline__ void tile_coords(const UmmaGeom &g, int t, int &b, lo
 }
 
 // ------------------------------------------------------------ main kernel
+// KW_T > 0: compile-time filter width with one filter row and 32 channels
+// per stage (the common staging); the MMA issue loop is then fully unrolled
+// over precomputed descriptor offsets. KW_T == 0: any staging, runtime loops.
+template <int KW_T, int ACT_T>
 __global__ void __launch_bounds__(THREADS, 1)
     umma_conv_kernel(const UmmaGeom g, const uint8_t *__restrict__ xs,
                      const uint8_t *__restrict__ wpk, const __half *__restrict__ bias,
@@ -501,16 +546,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             ok = false;
             break;
           }
-          const int kh = s / g.ncb, cbk = s % g.ncb;
+          const int khg = s / g.ncb, cbk = s % g.ncb;
           const uint32_t fb = smem_u32(&full[slot]);
-          mbar_expect_tx(fb, (g.resident ? 0u : g.a_stage_bytes) + CHUNKS * b_copy);
+          mbar_expect_tx(fb, (g.resident ? 0u : g.a_stage_bytes) + g.chunks * b_copy);
           if (!g.resident)
             bulk_g2s(smem_u32(sW + size_t(slot) * g.a_stage_bytes),
-                     wpk + ((size_t(oct) * g.KH + kh) * g.ncb + cbk) * g.a_stage_bytes,
-                     g.a_stage_bytes, fb);
-          const long long row0 = p0 + (long long)kh * g.dH * g.Wp;
-          for (int ch = 0; ch < CHUNKS; ++ch) {
-            const long long plane = (long long)b * (g.C8 / 8) + cbk * CHUNKS + ch;
+                     wpk + (size_t(oct) * g.n_kstages + s) * g.a_stage_bytes, g.a_stage_bytes,
+                     fb);
+          const long long row0 = p0 + (long long)khg * g.khs * g.dH * g.Wp;
+          for (int ch = 0; ch < g.chunks; ++ch) {
+            const long long plane = (long long)b * (g.C8 / 8) + cbk * g.chunks + ch;
             bulk_g2s(smem_u32(sB + size_t(slot) * g.b_stage_bytes + size_t(ch) * g.R_alloc * 16),
                      xs + (plane * g.plane_rows + row0) * 16, b_copy, fb);
           }
@@ -529,6 +574,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (g.resident && !mbar_wait(smem_u32(wbar), 0)) {
         atomicOr(g.err, kErrMmaTimeout);
         ok = false;
+      }
+      // per-MMA start-address offsets (16-byte units) of the specialised path:
+      // MMA i = (kw, ks) reads A tap kw chunk pair ks, B shifted kw*dW rows
+      uint32_t a_off[KW_T > 0 ? 2 * KW_T : 1], b_off[KW_T > 0 ? 2 * KW_T : 1];
+      if constexpr (KW_T > 0) {
+#pragma unroll
+        for (int kw = 0; kw < KW_T; ++kw)
+#pragma unroll
+          for (int ks = 0; ks < 2; ++ks) {
+            a_off[2 * kw + ks] = (uint32_t(kw) * 4 * UM * 16 + uint32_t(ks) * 2 * a_lbo) >> 4;
+            b_off[2 * kw + ks] = (uint32_t(kw * g.dW) * 16 + uint32_t(ks) * 2 * b_lbo) >> 4;
+          }
       }
       int gs = 0, it = 0;
       for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x, ++it) {
@@ -551,14 +608,28 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t a_base =
               smem_u32(sW + size_t(g.resident ? s : slot) * g.a_stage_bytes);
           const uint32_t b_base = smem_u32(sB + size_t(slot) * g.b_stage_bytes);
-          for (int kw = 0; kw < g.KW; ++kw) {
+          if constexpr (KW_T > 0) {
+            // descriptors differ from the stage's base descriptors only in
+            // the start-address field: add precomputed (offset >> 4) values
+            const uint64_t a0 = kmajor_desc(a_base, a_lbo), b0 = kmajor_desc(b_base, b_lbo);
 #pragma unroll
-            for (int ks = 0; ks < BK / 16; ++ks) {
-              const uint64_t adesc =
-                  kmajor_desc(a_base + uint32_t(kw) * CHUNKS * UM * 16 + ks * 2 * a_lbo, a_lbo);
-              const uint64_t bdesc =
-                  kmajor_desc(b_base + uint32_t(kw * g.dW) * 16 + ks * 2 * b_lbo, b_lbo);
-              mma_f16(d, adesc, bdesc, idesc, (s | kw | ks) != 0);
+            for (int i = 0; i < 2 * KW_T; ++i)
+              mma_f16(d, a0 + a_off[i], b0 + b_off[i], idesc, (s | i) != 0);
+            mma_commit(smem_u32(&empty[slot]));
+            continue;
+          }
+          const int ksteps = g.bk / 16;
+          for (int khl = 0; khl < g.khs; ++khl) {
+            for (int kw = 0; kw < g.KW; ++kw) {
+              const uint32_t tap = uint32_t(khl * g.KW + kw);
+              const uint32_t shift = uint32_t(khl * g.dH * g.Wp + kw * g.dW);  // B row shift
+              for (int ks = 0; ks < ksteps; ++ks) {
+                const uint64_t adesc = kmajor_desc(
+                    a_base + tap * uint32_t(g.chunks) * UM * 16 + ks * 2 * a_lbo, a_lbo);
+                const uint64_t bdesc =
+                    kmajor_desc(b_base + shift * 16 + ks * 2 * b_lbo, b_lbo);
+                mma_f16(d, adesc, bdesc, idesc, (s | khl | kw | ks) != 0);
+              }
             }
           }
           mma_commit(smem_u32(&empty[slot]));
@@ -580,7 +651,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int q = warp & 3, colh = ew / 4;
     uint8_t *stage = sE + size_t(ew) * 32 * EPI_ROWB;
     const bool pairs = ((g.OW | g.Wp) & 1) == 0;
-    const long long plane = (long long)g.OH * g.OW;
+    const size_t plane = size_t(g.OH) * g.OW;
     const int sub = lane & 7, rsel = lane >> 3;  // position pair, row within 4
     float r[EPI_COLS];
     int it = 0;
@@ -595,10 +666,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
-      const int oc_lane = oct * UM + q * 32 + lane;
+      const int oc0 = oct * UM + q * 32;  // first channel of this quadrant
+      const int oc_lane = oc0 + lane;
       const float bv = (g.has_bias && oc_lane < g.OC) ? __half2float(bias[oc_lane]) : 0.f;
       const float hb = 0.5f * bv;
-      __half *obase = out + (long long)b * g.OC * plane;
+      const int nrows = min(32, g.OC - oc0);  // valid channel rows of the quadrant
+      // this lane stores rows rsel, rsel+4, ..., rsel+28 of the quadrant
+      __half *rowp = out + (size_t(b) * g.OC + oc0 + rsel) * plane;
+      // (oh, ow) of this lane's first position pair; advanced per block
+      const int pos0 = int(p0) + colh * WCOLS + 2 * sub;
+      int oh = pos0 / g.Wp, ow = pos0 - oh * g.Wp;
       constexpr int NBLK = WCOLS / EPI_COLS;
       for (int blk = 0; blk < NBLK; ++blk) {
         const int col0 = colh * WCOLS + blk * EPI_COLS;
@@ -612,30 +689,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t pw[EPI_COLS / 2];
 #pragma unroll
         for (int j = 0; j < EPI_COLS / 2; ++j) {
-          __half2 h2 = __floats2half2_rn(epi_act(r[2 * j], bv, hb, g.act, g.lo, g.hi),
-                                         epi_act(r[2 * j + 1], bv, hb, g.act, g.lo, g.hi));
+          __half2 h2 = __floats2half2_rn(epi_act<ACT_T>(r[2 * j], bv, hb, g.lo, g.hi),
+                                         epi_act<ACT_T>(r[2 * j + 1], bv, hb, g.lo, g.hi));
           pw[j] = *reinterpret_cast<uint32_t *>(&h2);
         }
         uint4 *dst = reinterpret_cast<uint4 *>(stage + lane * EPI_ROWB);
         dst[0] = make_uint4(pw[0], pw[1], pw[2], pw[3]);
         dst[1] = make_uint4(pw[4], pw[5], pw[6], pw[7]);
         __syncwarp();
-        const long long p = p0 + col0 + 2 * sub;
-        const int oh = int(p / g.Wp), ow = int(p % g.Wp);
         const bool v0 = oh < g.OH && ow < g.OW;
-        const long long off0 = (long long)oh * g.OW + ow;
+        const int off0 = oh * g.OW + ow;
         // second position: next column, or the first column of the next row
         const bool wrap = ow + 1 >= g.Wp;
         const bool v1 = wrap ? (oh + 1 < g.OH) : (oh < g.OH && ow + 1 < g.OW);
-        const long long off1 = wrap ? (long long)(oh + 1) * g.OW : off0 + 1;
+        const int off1 = wrap ? (oh + 1) * g.OW : off0 + 1;
+        const uint8_t *src = stage + rsel * EPI_ROWB + 4 * sub;
 #pragma unroll
         for (int r4 = 0; r4 < 8; ++r4) {
-          const int rr = 4 * r4 + rsel;
-          const int oc = oct * UM + q * 32 + rr;
-          const uint32_t val =
-              *reinterpret_cast<const uint32_t *>(stage + rr * EPI_ROWB + 4 * sub);
-          if (oc < g.OC) {
-            __half *orow = obase + (long long)oc * plane;
+          const uint32_t val = *reinterpret_cast<const uint32_t *>(src + r4 * 4 * EPI_ROWB);
+          if (4 * r4 + rsel < nrows) {
+            __half *orow = rowp + size_t(r4) * 4 * plane;
             if (pairs) {
               if (v0) *reinterpret_cast<uint32_t *>(orow + off0) = val;
             } else {
@@ -646,6 +719,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         __syncwarp();
+        ow += EPI_COLS;
+        while (ow >= g.Wp) {
+          ow -= g.Wp;
+          ++oh;
+        }
       }
     }
   }
@@ -662,9 +740,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 void umma_conv_pack_weights(const wgx_conv2d_params &p, const __half *w, void *packed,
                             cudaStream_t stream) {
   UmmaGeom g = make_geom(p);
-  long long n = (long long)(umma_conv_packed_weight_bytes(p) / 16);
+  const uint64_t n = umma_conv_packed_weight_bytes(p) / 16;
+  if (n >= (1ull << 31)) fail("conv2d: weights too large for the tensor-core path");
   pack_weights<<<unsigned((n + 255) / 256), 256, 0, stream>>>(g, w, static_cast<uint4 *>(packed),
-                                                              n);
+                                                              int(n));
   check_cuda(cudaGetLastError(), "pack_weights launch");
 }
 
@@ -689,21 +768,36 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, const void *pac
   }
   check_cuda(cudaGetLastError(), "pack_input launch");
   uint32_t smem = smem_bytes(g);
-  static bool attr_set[64] = {};
-  if (dev < 64 && !attr_set[dev]) {
-    check_cuda(cudaFuncSetAttribute(umma_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  using KernelFn = void (*)(const UmmaGeom, const uint8_t *, const uint8_t *, const __half *,
+                           __half *);
+  // specialisations: filter width (1/3/5/7, per-row 32-channel staging) x
+  // epilogue activation
+  static const KernelFn table[5][3] = {
+      {umma_conv_kernel<0, 0>, umma_conv_kernel<0, 1>, umma_conv_kernel<0, 2>},
+      {umma_conv_kernel<1, 0>, umma_conv_kernel<1, 1>, umma_conv_kernel<1, 2>},
+      {umma_conv_kernel<3, 0>, umma_conv_kernel<3, 1>, umma_conv_kernel<3, 2>},
+      {umma_conv_kernel<5, 0>, umma_conv_kernel<5, 1>, umma_conv_kernel<5, 2>},
+      {umma_conv_kernel<7, 0>, umma_conv_kernel<7, 1>, umma_conv_kernel<7, 2>}};
+  int kw_idx = 0;
+  if (g.khs == 1 && g.bk == 32)
+    kw_idx = g.KW == 1 ? 1 : g.KW == 3 ? 2 : g.KW == 5 ? 3 : g.KW == 7 ? 4 : 0;
+  const int act_idx = (g.act >= 0 && g.act <= 2) ? g.act : 0;
+  KernelFn kern = table[kw_idx][act_idx];
+  const int kidx = kw_idx * 3 + act_idx;
+  static bool attr_set[64][15] = {};
+  if (dev < 64 && !attr_set[dev][kidx]) {
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(SMEM_MAX)),
                "umma_conv smem attr");
-    attr_set[dev] = true;
+    attr_set[dev][kidx] = true;
   }
   static int sms[64] = {};
   if (dev < 64 && !sms[dev]) sms[dev] = sm_count();
   const int n_sm = dev < 64 ? sms[dev] : sm_count();
   const int grid = g.total_tiles < n_sm ? g.total_tiles : n_sm;
   int th = timer_begin("umma_conv_kernel", stream);
-  umma_conv_kernel<<<grid, THREADS, smem, stream>>>(g, static_cast<const uint8_t *>(xs),
-                                                    static_cast<const uint8_t *>(packed), bias,
-                                                    out);
+  kern<<<grid, THREADS, smem, stream>>>(g, static_cast<const uint8_t *>(xs),
+                                        static_cast<const uint8_t *>(packed), bias, out);
   check_cuda(cudaGetLastError(), "umma_conv launch");
   timer_end(th, stream);
 }
