@@ -359,7 +359,7 @@ wgx_conv2d_plan plan_conv2d(const wgx_conv2d_params &p) {
     plan.variant = WGX_CONV_UMMA;
     plan.scratch_bytes = conv2d_scratch_bytes(p, true);
     plan.grid_ctas = umma_conv_grid(p);
-    plan.n_launches = 3;
+    plan.n_launches = 2;
   } else if (p.groups == 1 && p.OC == 1 && unit1x1) {
     plan.variant = WGX_CONV_POINTWISE1;
     plan.n_launches = 1;
@@ -394,7 +394,7 @@ uint64_t conv2d_scratch_bytes(const wgx_conv2d_params &p, bool include_packed) {
 }
 int conv2d_kernel_launches(const wgx_conv2d_params &p, bool packed_ready) {
   wgx_conv2d_plan plan = plan_conv2d(p);
-  if (plan.variant == WGX_CONV_UMMA) return packed_ready ? 2 : 3;
+  if (plan.variant == WGX_CONV_UMMA) return 2;
   return plan.n_launches;
 }
 
@@ -465,12 +465,14 @@ void launch_conv2d(const wgx_conv2d_params &p, const void *in, const void *w, co
     char *sp = static_cast<char *>(scratch);
     void *xs = sp;
     if (!packed) {
-      void *pw = sp + umma_conv_input_bytes(p);
-      umma_conv_pack_weights(p, static_cast<const __half *>(w), pw, stream);
-      packed = pw;
+      // pack the weights into the scratch behind the input re-layout
+      umma_conv_run(p, static_cast<const __half *>(in), sp + umma_conv_input_bytes(p),
+                    static_cast<const __half *>(w), static_cast<const __half *>(bias),
+                    static_cast<__half *>(out), xs, stream);
+    } else {
+      umma_conv_run(p, static_cast<const __half *>(in), const_cast<void *>(packed), nullptr,
+                    static_cast<const __half *>(bias), static_cast<__half *>(out), xs, stream);
     }
-    umma_conv_run(p, static_cast<const __half *>(in), packed, static_cast<const __half *>(bias),
-                  static_cast<__half *>(out), xs, stream);
     return;
   }
   if (p.dtype == WGX_FLOAT16)

@@ -85,7 +85,7 @@ static void record_mm(wgx_context *ctx, const std::vector<wgx_arg> &args) {
   Command c;
   c.name = name;
   c.workspace_bytes = mm_scratch_bytes(m, n, k1, dtype);
-  c.kernel_launches = c.workspace_bytes ? 3 : 1;
+  c.kernel_launches = c.workspace_bytes ? 2 : 1;
   c.run = [=](const ExecEnv &env) {
     launch_mm(pa, pb, po, m, n, k1, dtype, env.workspace, env.workspace_bytes, env.stream);
   };
@@ -126,10 +126,10 @@ static void append_conv(wgx_context *ctx, const char *name, const wgx_conv2d_par
       check_cuda(cudaStreamSynchronize(ctx->stream), "pack weights");
     }
     c.workspace_bytes = umma_conv_input_bytes(p);
-    c.kernel_launches = constant ? 2 : 3;
+    c.kernel_launches = 2;
     c.run = [=](const ExecEnv &env) {
-      if (!constant) umma_conv_pack_weights(p, static_cast<const __half *>(pw), packed, env.stream);
       umma_conv_run(p, static_cast<const __half *>(pin), packed,
+                    constant ? nullptr : static_cast<const __half *>(pw),
                     static_cast<const __half *>(pbias), static_cast<__half *>(pout),
                     env.workspace, env.stream);
     };

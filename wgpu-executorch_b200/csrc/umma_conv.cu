@@ -314,12 +314,88 @@ __global__ void pack_input_v4(UmmaGeom g, const __half *__restrict__ x, uint4 *_
   }
 }
 
+// Vector form of pack_input for IW % 8 == 0: one thread re-lays 8
+// consecutive padded positions of one 8-channel block. The first position
+// wp0 = 8t + (pW % 8) - 8 is chosen so that its input column iw0 = wp0 - pW
+// is a multiple of 8: each channel row contributes one aligned 16-byte load,
+// the 8x8 block is transposed in registers (prmt) and written as eight
+// 16-byte slots (128 contiguous bytes). Positions outside [0, Wp) are
+// skipped; padding positions and channels >= IC are written as zeros.
+__device__ __forceinline__ void pack_input_v8_body(const UmmaGeom &g,
+                                                   const __half *__restrict__ x,
+                                                   uint4 *__restrict__ xs, int groups_per_row,
+                                                   long long i) {
+  const int t = int(i % groups_per_row);
+  long long r = i / groups_per_row;
+  const int hp = int(r % g.Hp);
+  r /= g.Hp;
+  const int cb = int(r % (g.C8 / 8));
+  const long long b = r / (g.C8 / 8);
+  const int wp0 = 8 * t + (g.pW & 7) - 8;
+  const int iw0 = wp0 - g.pW;
+  const int ih = hp - g.pH;
+  const bool row_in = ih >= 0 && ih < g.IH;
+  uint4 ch[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int c = cb * 8 + e;
+    ch[e] = make_uint4(0u, 0u, 0u, 0u);
+    if (row_in && c < g.IC) {
+      const __half *src = x + ((b * g.IC + c) * g.IH + ih) * (long long)g.IW;
+      if (iw0 >= 0 && iw0 + 7 < g.IW) {
+        ch[e] = *reinterpret_cast<const uint4 *>(src + iw0);
+      } else {
+        __align__(16) __half v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int iw = iw0 + k;
+          v[k] = (iw >= 0 && iw < g.IW) ? src[iw] : __float2half_rn(0.f);
+        }
+        ch[e] = *reinterpret_cast<const uint4 *>(v);
+      }
+    }
+  }
+  uint4 *dst = xs + ((b * (g.C8 / 8) + cb) * g.Hp + hp) * (long long)g.Wp;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int wp = wp0 + k;
+    if (wp < 0 || wp >= g.Wp) continue;
+    // position k sits in word k/2 of every channel vector, low or high half
+    const uint32_t sel = (k & 1) ? 0x7632u : 0x5410u;
+    auto word = [&](const uint4 &v) -> uint32_t {
+      const int w = k >> 1;
+      return w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
+    };
+    dst[wp] = make_uint4(__byte_perm(word(ch[0]), word(ch[1]), sel),
+                         __byte_perm(word(ch[2]), word(ch[3]), sel),
+                         __byte_perm(word(ch[4]), word(ch[5]), sel),
+                         __byte_perm(word(ch[6]), word(ch[7]), sel));
+  }
+}
+
+__device__ __forceinline__ void pack_weights_body(const UmmaGeom &g, const __half *__restrict__ w,
+                                                  uint4 *__restrict__ packed, int i);
+
+
+
+// One launch re-lays the input (first n_in threads) and, when `w` is not
+// null, packs the weights (next n_w threads): the small weight packing no
+// longer costs a launch of its own on the per-call path.
+__global__ void pack_input_v8(UmmaGeom g, const __half *__restrict__ x, uint4 *__restrict__ xs,
+                              int groups_per_row, long long n_in, const __half *__restrict__ w,
+                              uint4 *__restrict__ packed, int n_w) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n_in) {
+    pack_input_v8_body(g, x, xs, groups_per_row, i);
+  } else if (w && i - n_in < n_w) {
+    pack_weights_body(g, w, packed, int(i - n_in));
+  }
+}
+
 // packed[oct][khg][cb][kh_local][kw][chunk][row 0..127][8] <- w[oc][c][kh][kw]
 // (kh = khg*khs + kh_local): one pipeline stage's A operand is contiguous.
-__global__ void pack_weights(UmmaGeom g, const __half *__restrict__ w, uint4 *__restrict__ packed,
-                             int n_slots) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n_slots) return;
+__device__ __forceinline__ void pack_weights_body(const UmmaGeom &g, const __half *__restrict__ w,
+                                                  uint4 *__restrict__ packed, int i) {
   const int row = i % UM;
   int t = i / UM;
   const int chunk = t % g.chunks;
@@ -342,6 +418,12 @@ __global__ void pack_weights(UmmaGeom g, const __half *__restrict__ w, uint4 *__
                                    : __float2half_rn(0.f);
   }
   packed[i] = *reinterpret_cast<const uint4 *>(v);
+}
+
+__global__ void pack_weights(UmmaGeom g, const __half *__restrict__ w, uint4 *__restrict__ packed,
+                             int n_slots) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n_slots) pack_weights_body(g, w, packed, i);
 }
 
 // ------------------------------------------------------------ PTX helpers
@@ -747,8 +829,9 @@ void umma_conv_pack_weights(const wgx_conv2d_params &p, const __half *w, void *p
   check_cuda(cudaGetLastError(), "pack_weights launch");
 }
 
-void umma_conv_run(const wgx_conv2d_params &p, const __half *in, const void *packed,
-                   const __half *bias, __half *out, void *xs, cudaStream_t stream) {
+void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
+                   const __half *w_to_pack, const __half *bias, __half *out, void *xs,
+                   cudaStream_t stream) {
   if (!umma_conv_supported(p)) fail("conv2d: shape not supported by the tensor-core path");
   UmmaGeom g = make_geom(p);
   int dev = 0;
@@ -756,15 +839,31 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, const void *pac
   g.err = device_error_word(dev);
   if ((reinterpret_cast<uintptr_t>(xs) & 15) || (reinterpret_cast<uintptr_t>(packed) & 15))
     fail("conv2d: scratch must be 16-byte aligned");
-  if (g.IW % 4 == 0 && (reinterpret_cast<uintptr_t>(in) & 7) == 0) {
-    const int groups_per_row = (g.Wp - (g.pW & 3) + 4 + 3) / 4;
-    long long n = (long long)g.B * (g.C8 / 8) * g.Hp * groups_per_row;
-    pack_input_v4<<<unsigned((n + 255) / 256), 256, 0, stream>>>(
-        g, in, static_cast<uint4 *>(xs), groups_per_row, n);
+  const uint64_t n_w64 = w_to_pack ? umma_conv_packed_weight_bytes(p) / 16 : 0;
+  if (n_w64 >= (1ull << 31)) fail("conv2d: weights too large for the tensor-core path");
+  const int n_w = int(n_w64);
+  if (g.IW % 8 == 0 && (reinterpret_cast<uintptr_t>(in) & 15) == 0) {
+    // input re-layout and weight packing in one launch
+    const int groups_per_row = (g.Wp - (g.pW & 7) + 8 + 7) / 8;
+    const long long n_in = (long long)g.B * (g.C8 / 8) * g.Hp * groups_per_row;
+    const long long n = n_in + n_w;
+    pack_input_v8<<<unsigned((n + 255) / 256), 256, 0, stream>>>(
+        g, in, static_cast<uint4 *>(xs), groups_per_row, n_in, w_to_pack,
+        static_cast<uint4 *>(packed), n_w);
   } else {
-    long long n_slots = (long long)g.B * (g.C8 / 8) * g.plane_rows;
-    pack_input<<<unsigned((n_slots + 255) / 256), 256, 0, stream>>>(
-        g, in, static_cast<uint4 *>(xs), n_slots);
+    if (w_to_pack)
+      pack_weights<<<unsigned((n_w + 255) / 256), 256, 0, stream>>>(
+          g, w_to_pack, static_cast<uint4 *>(packed), n_w);
+    if (g.IW % 4 == 0 && (reinterpret_cast<uintptr_t>(in) & 7) == 0) {
+      const int groups_per_row = (g.Wp - (g.pW & 3) + 4 + 3) / 4;
+      long long n = (long long)g.B * (g.C8 / 8) * g.Hp * groups_per_row;
+      pack_input_v4<<<unsigned((n + 255) / 256), 256, 0, stream>>>(
+          g, in, static_cast<uint4 *>(xs), groups_per_row, n);
+    } else {
+      long long n_slots = (long long)g.B * (g.C8 / 8) * g.plane_rows;
+      pack_input<<<unsigned((n_slots + 255) / 256), 256, 0, stream>>>(
+          g, in, static_cast<uint4 *>(xs), n_slots);
+    }
   }
   check_cuda(cudaGetLastError(), "pack_input launch");
   uint32_t smem = smem_bytes(g);
