@@ -321,74 +321,75 @@ __global__ void pack_input_v4(UmmaGeom g, const __half *__restrict__ x, uint4 *_
 // the 8x8 block is transposed in registers (prmt) and written as eight
 // 16-byte slots (128 contiguous bytes). Positions outside [0, Wp) are
 // skipped; padding positions and channels >= IC are written as zeros.
-__device__ __forceinline__ void pack_input_v8_body(const UmmaGeom &g,
-                                                   const __half *__restrict__ x,
-                                                   uint4 *__restrict__ xs, int groups_per_row,
-                                                   long long i) {
-  const int t = int(i % groups_per_row);
-  long long r = i / groups_per_row;
-  const int hp = int(r % g.Hp);
-  r /= g.Hp;
-  const int cb = int(r % (g.C8 / 8));
-  const long long b = r / (g.C8 / 8);
-  const int wp0 = 8 * t + (g.pW & 7) - 8;
-  const int iw0 = wp0 - g.pW;
-  const int ih = hp - g.pH;
-  const bool row_in = ih >= 0 && ih < g.IH;
-  uint4 ch[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const int c = cb * 8 + e;
-    ch[e] = make_uint4(0u, 0u, 0u, 0u);
-    if (row_in && c < g.IC) {
-      const __half *src = x + ((b * g.IC + c) * g.IH + ih) * (long long)g.IW;
-      if (iw0 >= 0 && iw0 + 7 < g.IW) {
-        ch[e] = *reinterpret_cast<const uint4 *>(src + iw0);
-      } else {
-        __align__(16) __half v[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int iw = iw0 + k;
-          v[k] = (iw >= 0 && iw < g.IW) ? src[iw] : __float2half_rn(0.f);
-        }
-        ch[e] = *reinterpret_cast<const uint4 *>(v);
-      }
-    }
-  }
-  uint4 *dst = xs + ((b * (g.C8 / 8) + cb) * g.Hp + hp) * (long long)g.Wp;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int wp = wp0 + k;
-    if (wp < 0 || wp >= g.Wp) continue;
-    // position k sits in word k/2 of every channel vector, low or high half
-    const uint32_t sel = (k & 1) ? 0x7632u : 0x5410u;
-    auto word = [&](const uint4 &v) -> uint32_t {
-      const int w = k >> 1;
-      return w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
-    };
-    dst[wp] = make_uint4(__byte_perm(word(ch[0]), word(ch[1]), sel),
-                         __byte_perm(word(ch[2]), word(ch[3]), sel),
-                         __byte_perm(word(ch[4]), word(ch[5]), sel),
-                         __byte_perm(word(ch[6]), word(ch[7]), sel));
-  }
-}
-
 __device__ __forceinline__ void pack_weights_body(const UmmaGeom &g, const __half *__restrict__ w,
                                                   uint4 *__restrict__ packed, int i);
 
-
-
-// One launch re-lays the input (first n_in threads) and, when `w` is not
-// null, packs the weights (next n_w threads): the small weight packing no
-// longer costs a launch of its own on the per-call path.
-__global__ void pack_input_v8(UmmaGeom g, const __half *__restrict__ x, uint4 *__restrict__ xs,
-                              int groups_per_row, long long n_in, const __half *__restrict__ w,
-                              uint4 *__restrict__ packed, int n_w) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n_in) {
-    pack_input_v8_body(g, x, xs, groups_per_row, i);
-  } else if (w && i - n_in < n_w) {
-    pack_weights_body(g, w, packed, int(i - n_in));
+// One launch re-lays the input and, when `w` is not null, packs the weights
+// (blocks past n_in_blocks): the small weight packing costs no launch of its
+// own on the per-call path. Each input thread handles one 8-position group
+// of one padded row (b, 8-channel block, hp); index math is 32-bit (the
+// host checks the ranges).
+__global__ void __launch_bounds__(256, 4)
+    pack_input_v8(UmmaGeom g, const __half *__restrict__ x, uint4 *__restrict__ xs,
+                  int groups_per_row, int n_items, int n_in_blocks,
+                  const __half *__restrict__ w, uint4 *__restrict__ packed, int n_w) {
+  if (int(blockIdx.x) >= n_in_blocks) {
+    const int i = (int(blockIdx.x) - n_in_blocks) * 256 + threadIdx.x;
+    if (w && i < n_w) pack_weights_body(g, w, packed, i);
+    return;
+  }
+  const int item = blockIdx.x * 256 + threadIdx.x;
+  if (item >= n_items) return;
+  const int row = item / groups_per_row;
+  const int t = item - row * groups_per_row;
+  const int ncb = g.C8 / 8;
+  const int hp = row % g.Hp;
+  const int rest = row / g.Hp;
+  const int cb = rest % ncb, b = rest / ncb;
+  const int ih = hp - g.pH;
+  const bool row_in = ih >= 0 && ih < g.IH;
+  const int nch = min(8, g.IC - cb * 8);
+  const size_t cstride = size_t(g.IH) * g.IW;
+  const __half *src0 = x + ((size_t(b) * g.IC + cb * 8) * g.IH + (row_in ? ih : 0)) * g.IW;
+  uint4 *dst = xs + size_t(row) * g.Wp;
+  {
+    const int wp0 = 8 * t + (g.pW & 7) - 8;
+    const int iw0 = wp0 - g.pW;  // a multiple of 8
+    const bool full = row_in && iw0 >= 0 && iw0 + 7 < g.IW;
+    uint4 ch[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      ch[e] = make_uint4(0u, 0u, 0u, 0u);
+      if (e < nch && row_in) {
+        const __half *src = src0 + e * cstride;
+        if (full) {
+          ch[e] = *reinterpret_cast<const uint4 *>(src + iw0);
+        } else {
+          __align__(16) __half v[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int iw = iw0 + k;
+            v[k] = (iw >= 0 && iw < g.IW) ? src[iw] : __float2half_rn(0.f);
+          }
+          ch[e] = *reinterpret_cast<const uint4 *>(v);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int wp = wp0 + k;
+      if (wp < 0 || wp >= g.Wp) continue;
+      // position k sits in word k/2 of every channel vector, low or high half
+      const uint32_t sel = (k & 1) ? 0x7632u : 0x5410u;
+      uint32_t wd[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint4 &v = ch[e];
+        wd[e] = (k >> 1) == 0 ? v.x : (k >> 1) == 1 ? v.y : (k >> 1) == 2 ? v.z : v.w;
+      }
+      dst[wp] = make_uint4(__byte_perm(wd[0], wd[1], sel), __byte_perm(wd[2], wd[3], sel),
+                           __byte_perm(wd[4], wd[5], sel), __byte_perm(wd[6], wd[7], sel));
+    }
   }
 }
 
@@ -845,10 +846,12 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   if (g.IW % 8 == 0 && (reinterpret_cast<uintptr_t>(in) & 15) == 0) {
     // input re-layout and weight packing in one launch
     const int groups_per_row = (g.Wp - (g.pW & 7) + 8 + 7) / 8;
-    const long long n_in = (long long)g.B * (g.C8 / 8) * g.Hp * groups_per_row;
-    const long long n = n_in + n_w;
-    pack_input_v8<<<unsigned((n + 255) / 256), 256, 0, stream>>>(
-        g, in, static_cast<uint4 *>(xs), groups_per_row, n_in, w_to_pack,
+    const long long n_items = (long long)g.B * (g.C8 / 8) * g.Hp * groups_per_row;
+    if (n_items >= (1ll << 31) - 256) fail("conv2d: input too large for the re-layout kernel");
+    const int n_in_blocks = int((n_items + 255) / 256);
+    const int n_wblk = (n_w + 255) / 256;
+    pack_input_v8<<<unsigned(n_in_blocks + n_wblk), 256, 0, stream>>>(
+        g, in, static_cast<uint4 *>(xs), groups_per_row, int(n_items), n_in_blocks, w_to_pack,
         static_cast<uint4 *>(packed), n_w);
   } else {
     if (w_to_pack)
