@@ -355,26 +355,14 @@ __global__ void __launch_bounds__(256, 4)
   {
     const int wp0 = 8 * t + (g.pW & 7) - 8;
     const int iw0 = wp0 - g.pW;  // a multiple of 8
-    const bool full = row_in && iw0 >= 0 && iw0 + 7 < g.IW;
+    // IW % 8 == 0 and iw0 % 8 == 0: the 16-byte chunk [iw0, iw0 + 8) lies
+    // either entirely inside the input row or entirely in the padding
+    const bool inside = row_in && iw0 >= 0 && iw0 < g.IW;
     uint4 ch[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      ch[e] = make_uint4(0u, 0u, 0u, 0u);
-      if (e < nch && row_in) {
-        const __half *src = src0 + e * cstride;
-        if (full) {
-          ch[e] = *reinterpret_cast<const uint4 *>(src + iw0);
-        } else {
-          __align__(16) __half v[8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int iw = iw0 + k;
-            v[k] = (iw >= 0 && iw < g.IW) ? src[iw] : __float2half_rn(0.f);
-          }
-          ch[e] = *reinterpret_cast<const uint4 *>(v);
-        }
-      }
-    }
+    for (int e = 0; e < 8; ++e)
+      ch[e] = (inside && e < nch) ? *reinterpret_cast<const uint4 *>(src0 + e * cstride + iw0)
+                                  : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int wp = wp0 + k;
