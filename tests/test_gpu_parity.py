@@ -256,13 +256,15 @@ def test_config2_full_batch_properties(ctx):
 
 
 # --------------------------------------------------- program fusion
-@pytest.mark.parametrize("out_pool,commands", [(3, 3), (0, 5)])
-def test_program_conv_sigmoid_mul_fusion(ctx, out_pool, commands):
+@pytest.mark.parametrize("out_pool,ic,commands", [(3, 32, 3), (0, 32, 3), (0, 4, 5)])
+def test_program_conv_sigmoid_mul_fusion(ctx, out_pool, ic, commands):
     """conv -> sigmoid -> mul becomes one conv with a SiLU epilogue (input
-    copy + conv + output copy = 3 commands); when the mul's output shares the
-    conv input's pool the ops stay separate (5 commands)."""
-    (x,) = oracle.make_inputs([(2, 32, 24, 24)], seed=100)
-    w = kaiming((48, 32, 3, 3), 101)
+    copy + conv + output copy = 3 commands). When the mul's output shares the
+    conv input's pool, only a tensor-core conv fuses (it stages the whole
+    input in scratch before writing); a CUDA-core conv (IC=4) keeps the ops
+    separate (5 commands)."""
+    (x,) = oracle.make_inputs([(2, ic, 24, 24)], seed=100)
+    w = kaiming((48, ic, 3, 3), 101)
     (b,) = oracle.make_inputs([(48,)], seed=102, scale=0.01)
     wbytes = w.tobytes() + b.tobytes()
     prog = {
@@ -273,8 +275,8 @@ def test_program_conv_sigmoid_mul_fusion(ctx, out_pool, commands):
             {"name": "aten.mul.Tensor", "args": [9, 10, 11]},
         ],
         "values": [
-            {"type": "tensor", "shape": [2, 32, 24, 24], "dtype": "float16", "memObjId": 0},
-            {"type": "tensor", "shape": [48, 32, 3, 3], "dtype": "float16", "weightsOffset": 0,
+            {"type": "tensor", "shape": [2, ic, 24, 24], "dtype": "float16", "memObjId": 0},
+            {"type": "tensor", "shape": [48, ic, 3, 3], "dtype": "float16", "weightsOffset": 0,
              "weightsLength": w.nbytes},
             {"type": "tensor", "shape": [48], "dtype": "float16", "weightsOffset": w.nbytes,
              "weightsLength": b.nbytes},

@@ -1,0 +1,768 @@
+// Data-movement, pooling, reduction and resampling operators that the
+// shipped YOLO26-N / DepthART / selfie-segmentation programs chain around
+// their convolutions. Each recorder follows the reference operator's
+// argument layout and validation (file:line per op); arithmetic is fp32 with
+// one rounding to the storage type.
+//
+//   aten.view_copy / clone / squeeze_copy.dims / unsqueeze_copy,
+//   et_vk.prepack       flat byte copies   (src/shaders/utils/flat-copy.ts:31-60)
+//   aten.cat            pitched copies     (src/shaders/cat/index.ts:27-113)
+//   aten.split_with_sizes_copy  pitched    (src/shaders/split-with-sizes/index.ts:30-82)
+//   aten.permute_copy   index remap        (src/shaders/permute/index.ts:34-73)
+//   aten.bmm            batched GEMM       (src/shaders/bmm/index.ts:33-55)
+//   aten.max_pool2d_with_indices           (src/shaders/max-pool-2d/index.ts:36-94)
+//   aten._softmax                          (src/shaders/softmax/index.ts:60-90)
+//   aten.upsample_nearest2d.vec            (src/shaders/upsample-nearest-2d/index.ts:30-54)
+//   aten.upsample_bilinear2d.vec           (src/shaders/upsample-bilinear2d/index.ts:28-60)
+//   aten.mean.dim                          (src/shaders/mean-dim/index.ts:26-112)
+//   aten.constant_pad_nd                   (src/shaders/constant-pad-nd/index.ts:20-76)
+#include <algorithm>
+#include <cmath>
+
+#include "internal.h"
+
+namespace wgx {
+
+namespace {
+
+const wgx_arg &at(const std::vector<wgx_arg> &a, size_t i, const char *op) {
+  if (i >= a.size()) fail(std::string(op) + ": missing argument " + std::to_string(i));
+  return a[i];
+}
+wgx_tensor *tensor_at(const std::vector<wgx_arg> &a, size_t i, const char *op) {
+  const wgx_arg &x = at(a, i, op);
+  if (x.kind != WGX_ARG_TENSOR || !x.v.tensor)
+    fail(std::string(op) + ": argument " + std::to_string(i) + " must be a Tensor");
+  return x.v.tensor;
+}
+std::vector<wgx_tensor *> tensors_at(const std::vector<wgx_arg> &a, size_t i, const char *op) {
+  const wgx_arg &x = at(a, i, op);
+  if (x.kind == WGX_ARG_TENSOR) return {x.v.tensor};
+  if (x.kind != WGX_ARG_TENSOR_LIST)
+    fail(std::string(op) + ": argument " + std::to_string(i) + " must be a Tensor list");
+  return std::vector<wgx_tensor *>(x.v.tensors, x.v.tensors + x.count);
+}
+double num_at(const std::vector<wgx_arg> &a, size_t i, const char *op) {
+  const wgx_arg &x = at(a, i, op);
+  if (x.kind == WGX_ARG_NUMBER) return x.v.number;
+  if (x.kind == WGX_ARG_BOOL) return x.v.boolean;
+  fail(std::string(op) + ": argument " + std::to_string(i) + " must be a number");
+}
+std::vector<int64_t> list_at(const std::vector<wgx_arg> &a, size_t i, const char *op) {
+  const wgx_arg &x = at(a, i, op);
+  if (x.kind == WGX_ARG_NULL) return {};
+  if (x.kind == WGX_ARG_NUMBER) return {int64_t(x.v.number)};
+  if (x.kind != WGX_ARG_INT_LIST)
+    fail(std::string(op) + ": argument " + std::to_string(i) + " must be an int list");
+  return std::vector<int64_t>(x.v.ints, x.v.ints + x.count);
+}
+bool is_float(int dt) { return dt == WGX_FLOAT32 || dt == WGX_FLOAT16; }
+void require_float_pair(const wgx_tensor *a, const wgx_tensor *b, const char *op) {
+  if (!is_float(a->dtype) || b->dtype != a->dtype)
+    fail(std::string(op) + ": Tensors must have matching float32 or float16 dtype");
+}
+
+template <class T>
+__device__ __forceinline__ float lf(T v) {
+  return float(v);
+}
+template <>
+__device__ __forceinline__ float lf<__half>(__half v) {
+  return __half2float(v);
+}
+template <class T>
+__device__ __forceinline__ T sf(float v) {
+  return T(v);
+}
+template <>
+__device__ __forceinline__ __half sf<__half>(float v) {
+  return __float2half_rn(v);
+}
+
+unsigned blocks_for(long long n, int threads = 256) {
+  long long b = (n + threads - 1) / threads;
+  return unsigned(std::min<long long>(std::max<long long>(b, 1), 148LL * 64));
+}
+
+void push(wgx_context *ctx, const char *name, int launches, std::function<void(const ExecEnv &)> f) {
+  Command c;
+  c.name = name;
+  c.kernel_launches = launches;
+  c.run = std::move(f);
+  ctx->commands.push_back(std::move(c));
+}
+
+// ------------------------------------------------------------ flat copies
+void record_flat_copy(wgx_context *ctx, const std::vector<wgx_arg> &a, const char *name,
+                      size_t in_idx, size_t out_idx) {
+  wgx_tensor *in = tensor_at(a, in_idx, name), *out = tensor_at(a, out_idx, name);
+  if (in->dtype != out->dtype)
+    fail(std::string(name) + ": dtype mismatch (" + dtype_name(in->dtype) + " != " +
+         dtype_name(out->dtype) + ")");
+  if (in->numel != out->numel)
+    fail(std::string(name) + ": numel mismatch (" + std::to_string(in->numel) + " != " +
+         std::to_string(out->numel) + ")");
+  if (in->buffer == out->buffer) return;  // aliased: already in place (flat-copy.ts:46-48)
+  const void *s = in->data();
+  void *d = out->data();
+  const uint64_t bytes = in->byte_length();
+  push(ctx, name, 0, [=](const ExecEnv &env) {
+    check_cuda(cudaMemcpyAsync(d, s, bytes, cudaMemcpyDeviceToDevice, env.stream), name);
+  });
+}
+
+// --------------------------------------------------------- cat / split
+// outer x (extent along dim x inner) blocks: one pitched 2-D copy per input
+struct Blocks {
+  int64_t outer = 1, inner = 1;
+};
+Blocks blocks_of(const wgx_tensor *t, int dim) {
+  Blocks b;
+  for (int i = 0; i < dim; ++i) b.outer *= t->shape[i];
+  for (int i = dim + 1; i < t->ndim; ++i) b.inner *= t->shape[i];
+  return b;
+}
+
+void record_cat(wgx_context *ctx, const std::vector<wgx_arg> &a) {
+  const char *name = "aten.cat.default";
+  std::vector<wgx_tensor *> ins = tensors_at(a, 0, name);
+  int dim = int(num_at(a, 1, name));
+  wgx_tensor *out = tensor_at(a, 2, name);
+  if (ins.empty()) fail(std::string(name) + ": empty input list");
+  const int ndim = out->ndim;
+  if (dim < 0) dim += ndim;
+  if (dim < 0 || dim >= ndim) fail(std::string(name) + ": dim out of range");
+  int64_t total = 0;
+  for (auto *t : ins) {
+    if (!is_float(t->dtype) || t->dtype != out->dtype)
+      fail(std::string(name) + ": Tensors must have matching float32 or float16 dtype");
+    if (t->ndim != ndim) fail(std::string(name) + ": input rank != output rank");
+    for (int d = 0; d < ndim; ++d)
+      if (d != dim && t->shape[d] != out->shape[d])
+        fail(std::string(name) + ": non-concat dim " + std::to_string(d) + " size mismatch");
+    total += t->shape[dim];
+  }
+  if (total != out->shape[dim]) fail(std::string(name) + ": concat dim sizes do not sum to output");
+  const int es = dtype_size(out->dtype);
+  const Blocks ob = blocks_of(out, dim);
+  const size_t dpitch = size_t(out->shape[dim] * ob.inner) * es;
+  struct Piece {
+    const void *src;
+    char *dst;
+    size_t width;
+  };
+  std::vector<Piece> pieces;
+  int64_t off = 0;
+  for (auto *t : ins) {
+    const size_t width = size_t(t->shape[dim] * ob.inner) * es;
+    pieces.push_back({t->data(), static_cast<char *>(out->data()) + size_t(off * ob.inner) * es,
+                      width});
+    off += t->shape[dim];
+  }
+  const size_t rows = size_t(ob.outer);
+  push(ctx, name, 0, [=](const ExecEnv &env) {
+    for (auto &p : pieces)
+      if (p.width)
+        check_cuda(cudaMemcpy2DAsync(p.dst, dpitch, p.src, p.width, p.width, rows,
+                                     cudaMemcpyDeviceToDevice, env.stream),
+                   "cat copy");
+  });
+}
+
+void record_split(wgx_context *ctx, const std::vector<wgx_arg> &a) {
+  const char *name = "aten.split_with_sizes_copy.default";
+  wgx_tensor *in = tensor_at(a, 0, name);
+  std::vector<int64_t> sizes = list_at(a, 1, name);
+  int dim = int(num_at(a, 2, name));
+  std::vector<wgx_tensor *> outs = tensors_at(a, 3, name);
+  const int ndim = in->ndim;
+  if (dim < 0) dim += ndim;
+  if (dim < 0 || dim >= ndim) fail(std::string(name) + ": dim out of range");
+  if (outs.size() != sizes.size())
+    fail(std::string(name) + ": outputs (" + std::to_string(outs.size()) + ") != sizes (" +
+         std::to_string(sizes.size()) + ")");
+  int64_t sum = 0;
+  for (auto s : sizes) {
+    if (s < 0) fail(std::string(name) + ": negative split size");
+    sum += s;
+  }
+  if (sum != in->shape[dim]) fail(std::string(name) + ": sizes must sum to the split dim extent");
+  for (size_t i = 0; i < outs.size(); ++i) {
+    if (!is_float(in->dtype) || outs[i]->dtype != in->dtype)
+      fail(std::string(name) + ": Tensors must have matching float32 or float16 dtype");
+    if (outs[i]->ndim != ndim || outs[i]->shape[dim] != sizes[i])
+      fail(std::string(name) + ": output " + std::to_string(i) + " dim " + std::to_string(dim) +
+           " != split size");
+  }
+  const int es = dtype_size(in->dtype);
+  const Blocks ib = blocks_of(in, dim);
+  const size_t spitch = size_t(in->shape[dim] * ib.inner) * es;
+  struct Piece {
+    const char *src;
+    void *dst;
+    size_t width;
+  };
+  std::vector<Piece> pieces;
+  int64_t off = 0;
+  for (size_t i = 0; i < outs.size(); ++i) {
+    pieces.push_back({static_cast<const char *>(in->data()) + size_t(off * ib.inner) * es,
+                      outs[i]->data(), size_t(sizes[i] * ib.inner) * es});
+    off += sizes[i];
+  }
+  const size_t rows = size_t(ib.outer);
+  push(ctx, name, 0, [=](const ExecEnv &env) {
+    for (auto &p : pieces)
+      if (p.width)
+        check_cuda(cudaMemcpy2DAsync(p.dst, p.width, p.src, spitch, p.width, rows,
+                                     cudaMemcpyDeviceToDevice, env.stream),
+                   "split copy");
+  });
+}
+
+// -------------------------------------------------------------- permute
+struct PermIdx {
+  int rank;
+  int64_t out_shape[8];
+  int64_t in_stride_of_out_dim[8];  // input element stride of output dim d
+};
+
+template <class T>
+__global__ void permute_kernel(PermIdx p, const T *__restrict__ x, T *__restrict__ y,
+                               long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long r = i, src = 0;
+    for (int d = p.rank - 1; d >= 0; --d) {
+      const long long c = r % p.out_shape[d];
+      r /= p.out_shape[d];
+      src += c * p.in_stride_of_out_dim[d];
+    }
+    y[i] = x[src];
+  }
+}
+
+void record_permute(wgx_context *ctx, const std::vector<wgx_arg> &a) {
+  const char *name = "aten.permute_copy.default";
+  wgx_tensor *in = tensor_at(a, 0, name);
+  std::vector<int64_t> dims = list_at(a, 1, name);
+  wgx_tensor *out = tensor_at(a, 2, name);
+  require_float_pair(in, out, name);
+  const int rank = in->ndim;
+  if (out->ndim != rank) fail(std::string(name) + ": output rank != input rank");
+  if (int(dims.size()) != rank)
+    fail(std::string(name) + ": dims count (" + std::to_string(dims.size()) + ") != input rank (" +
+         std::to_string(rank) + ")");
+  int perm[8];
+  bool seen[8] = {};
+  for (int d = 0; d < rank; ++d) {
+    int64_t q = dims[d] < 0 ? dims[d] + rank : dims[d];
+    if (q < 0 || q >= rank || seen[q]) fail(std::string(name) + ": invalid permute dims");
+    seen[q] = true;
+    perm[d] = int(q);
+  }
+  for (int d = 0; d < rank; ++d)
+    if (out->shape[d] != in->shape[perm[d]])
+      fail(std::string(name) + ": output shape does not match permuted input shape");
+  PermIdx p{};
+  p.rank = rank;
+  int64_t in_stride[8];
+  int64_t s = 1;
+  for (int d = rank - 1; d >= 0; --d) {
+    in_stride[d] = s;
+    s *= in->shape[d];
+  }
+  for (int d = 0; d < rank; ++d) {
+    p.out_shape[d] = out->shape[d];
+    p.in_stride_of_out_dim[d] = in_stride[perm[d]];
+  }
+  const void *px = in->data();
+  void *py = out->data();
+  const long long n = out->numel;
+  const int dt = in->dtype;
+  push(ctx, name, 1, [=](const ExecEnv &env) {
+    if (dt == WGX_FLOAT16)
+      permute_kernel<__half><<<blocks_for(n), 256, 0, env.stream>>>(p, (const __half *)px,
+                                                                    (__half *)py, n);
+    else
+      permute_kernel<float><<<blocks_for(n), 256, 0, env.stream>>>(p, (const float *)px,
+                                                                   (float *)py, n);
+    check_cuda(cudaGetLastError(), "permute launch");
+  });
+}
+
+// ------------------------------------------------------------------ bmm
+// out[b] = a[b] @ b[b]: 32x32 output tile per CTA, fp32 accumulation.
+template <class T>
+__global__ void __launch_bounds__(256) bmm_kernel(const T *__restrict__ A, const T *__restrict__ Bm,
+                                                  T *__restrict__ C, int M, int N, int K) {
+  __shared__ float As[32][33];
+  __shared__ float Bs[32][33];
+  const int bz = blockIdx.z;
+  const T *a = A + size_t(bz) * M * K;
+  const T *b = Bm + size_t(bz) * K * N;
+  T *c = C + size_t(bz) * M * N;
+  const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;  // 32 x 8
+  const int m0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = 0; k0 < K; k0 += 32) {
+    for (int r = ty; r < 32; r += 8) {
+      const int m = m0 + r, k = k0 + tx;
+      As[r][tx] = (m < M && k < K) ? lf(a[size_t(m) * K + k]) : 0.f;
+      const int kk = k0 + r, n = n0 + tx;
+      Bs[r][tx] = (kk < K && n < N) ? lf(b[size_t(kk) * N + n]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float bv = Bs[k][tx];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] = fmaf(As[ty + 8 * i][k], bv, acc[i]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty + 8 * i, n = n0 + tx;
+    if (m < M && n < N) c[size_t(m) * N + n] = sf<T>(acc[i]);
+  }
+}
+
+void record_bmm(wgx_context *ctx, const std::vector<wgx_arg> &a) {
+  const char *name = "aten.bmm.default";
+  wgx_tensor *A = tensor_at(a, 0, name), *B = tensor_at(a, 1, name), *out = tensor_at(a, 2, name);
+  if (!is_float(A->dtype) || B->dtype != A->dtype || out->dtype != A->dtype)
+    fail(std::string(name) + ": Tensors must have matching float32 or float16 dtype");
+  if (A->ndim != 3 || B->ndim != 3 || out->ndim != 3)
+    fail(std::string(name) + ": inputs and output must be 3D");
+  const int64_t batch = A->shape[0], m = A->shape[1], k = A->shape[2], n = B->shape[2];
+  if (B->shape[0] != batch || B->shape[1] != k)
+    fail(std::string(name) + ": batch/K mismatch between a and b");
+  if (out->shape[0] != batch || out->shape[1] != m || out->shape[2] != n)
+    fail(std::string(name) + ": output shape != [" + std::to_string(batch) + ", " +
+         std::to_string(m) + ", " + std::to_string(n) + "]");
+  if (batch > 65535 || (m + 31) / 32 > 65535) fail(std::string(name) + ": shape too large");
+  const void *pa = A->data(), *pb = B->data();
+  void *pc = out->data();
+  const int dt = A->dtype;
+  const dim3 grid(unsigned((n + 31) / 32), unsigned((m + 31) / 32), unsigned(batch));
+  push(ctx, name, 1, [=](const ExecEnv &env) {
+    if (dt == WGX_FLOAT16)
+      bmm_kernel<__half><<<grid, 256, 0, env.stream>>>((const __half *)pa, (const __half *)pb,
+                                                       (__half *)pc, int(m), int(n), int(k));
+    else
+      bmm_kernel<float><<<grid, 256, 0, env.stream>>>((const float *)pa, (const float *)pb,
+                                                      (float *)pc, int(m), int(n), int(k));
+    check_cuda(cudaGetLastError(), "bmm launch");
+  });
+}
+
+// ------------------------------------------------------------- max pool
+struct PoolGeom {
+  int N, C, IH, IW, OH, OW, kH, kW, sH, sW, pH, pW, dH, dW;
+};
+
+template <class T>
+__global__ void maxpool_kernel(PoolGeom g, const T *__restrict__ x, T *__restrict__ y,
+                               int32_t *__restrict__ idx, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int ow = int(i % g.OW);
+    long long t = i / g.OW;
+    const int oh = int(t % g.OH);
+    const long long plane = t / g.OH;
+    const T *xp = x + plane * g.IH * (long long)g.IW;
+    // -65504 / -FLT_MAX start and strict '>' like max-pool-2d-f16.wgsl.ts:52-72
+    float best = sizeof(T) == 2 ? -65504.0f : -3.402823466e38f;
+    int best_idx = 0;
+    for (int kh = 0; kh < g.kH; ++kh) {
+      const int ih = oh * g.sH - g.pH + kh * g.dH;
+      if (ih < 0 || ih >= g.IH) continue;
+      for (int kw = 0; kw < g.kW; ++kw) {
+        const int iw = ow * g.sW - g.pW + kw * g.dW;
+        if (iw < 0 || iw >= g.IW) continue;
+        const float v = lf(xp[(long long)ih * g.IW + iw]);
+        if (v > best) {
+          best = v;
+          best_idx = ih * g.IW + iw;
+        }
+      }
+    }
+    y[i] = sf<T>(best);
+    if (idx) idx[i] = best_idx;
+  }
+}
+
+void parse_hw(const std::vector<int64_t> &v, const char *name, const char *what, int *h, int *w) {
+  if (v.size() == 1) {
+    *h = *w = int(v[0]);
+  } else if (v.size() == 2) {
+    *h = int(v[0]);
+    *w = int(v[1]);
+  } else {
+    fail(std::string(name) + ": " + what + " must be 1 or 2 elements");
+  }
+}
+
+void record_maxpool(wgx_context *ctx, const std::vector<wgx_arg> &a) {
+  const char *name = "aten.max_pool2d_with_indices.default";
+  wgx_tensor *in = tensor_at(a, 0, name);
+  PoolGeom g{};
+  parse_hw(list_at(a, 1, name), name, "kernel_size", &g.kH, &g.kW);
+  std::vector<int64_t> st = list_at(a, 2, name);
+  if (st.empty()) st = {g.kH, g.kW};  // stride defaults to the kernel size
+  parse_hw(st, name, "stride", &g.sH, &g.sW);
+  parse_hw(list_at(a, 3, name), name, "padding", &g.pH, &g.pW);
+  parse_hw(list_at(a, 4, name), name, "dilation", &g.dH, &g.dW);
+  const bool ceil_mode = num_at(a, 5, name) != 0;
+  std::vector<wgx_tensor *> outs = tensors_at(a, 6, name);
+  if (outs.size() != 2)
+    fail(std::string(name) + ": expected 2 outputs [values, indices], got " +
+         std::to_string(outs.size()));
+  wgx_tensor *vals = outs[0], *idx = outs[1];
+  if (!is_float(in->dtype) || vals->dtype != in->dtype)
+    fail(std::string(name) + ": values tensors must have matching float32 or float16 dtype");
+  if (idx->dtype != WGX_INT32) fail(std::string(name) + ": indices output must be int32");
+  if (in->ndim != 4) fail(std::string(name) + ": input must be 4D NCHW");
+  g.N = int(in->shape[0]);
+  g.C = int(in->shape[1]);
+  g.IH = int(in->shape[2]);
+  g.IW = int(in->shape[3]);
+  const int ohn = g.IH + 2 * g.pH - (g.dH * (g.kH - 1) + 1);
+  const int own = g.IW + 2 * g.pW - (g.dW * (g.kW - 1) + 1);
+  // max-pool-2d/index.ts:72-75: floor or ceil of the real quotient
+  auto div = [&](int num, int s) {
+    const double q = double(num) / double(s);
+    return int(ceil_mode ? std::ceil(q) : std::floor(q));
+  };
+  g.OH = std::max(0, div(ohn, g.sH) + 1);
+  g.OW = std::max(0, div(own, g.sW) + 1);
+  for (auto *t : {vals, idx})
+    if (t->ndim != 4 || t->shape[0] != g.N || t->shape[1] != g.C || t->shape[2] != g.OH ||
+        t->shape[3] != g.OW)
+      fail(std::string(name) + (t == vals ? ": values" : ": indices") + " output shape != [" +
+           std::to_string(g.N) + ", " + std::to_string(g.C) + ", " + std::to_string(g.OH) +
+           ", " + std::to_string(g.OW) + "]");
+  const void *px = in->data();
+  void *py = vals->data();
+  int32_t *pi = static_cast<int32_t *>(idx->data());
+  const long long n = vals->numel;
+  const int dt = in->dtype;
+  push(ctx, name, 1, [=](const ExecEnv &env) {
+    if (dt == WGX_FLOAT16)
+      maxpool_kernel<__half><<<blocks_for(n), 256, 0, env.stream>>>(g, (const __half *)px,
+                                                                    (__half *)py, pi, n);
+    else
+      maxpool_kernel<float><<<blocks_for(n), 256, 0, env.stream>>>(g, (const float *)px,
+                                                                   (float *)py, pi, n);
+    check_cuda(cudaGetLastError(), "maxpool launch");
+  });
+}
+
+// -------------------------------------------------------------- softmax
+// One warp per (outer, inner) line of length R: max, sum of exp, normalise.
+template <class T>
+__global__ void softmax_kernel(const T *__restrict__ x, T *__restrict__ y, long long lines, int R,
+                               long long inner) {
+  const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (warp >= lines) return;
+  const long long o = warp / inner, in = warp % inner;
+  const T *xp = x + o * R * inner + in;
+  T *yp = y + o * R * inner + in;
+  float mx = -INFINITY;
+  for (int r = lane; r < R; r += 32) mx = fmaxf(mx, lf(xp[r * inner]));
+  for (int s = 16; s > 0; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
+  float sum = 0.f;
+  for (int r = lane; r < R; r += 32) sum += __expf(lf(xp[r * inner]) - mx);
+  for (int s = 16; s > 0; s >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, s);
+  const float inv = 1.0f / sum;
+  for (int r = lane; r < R; r += 32) yp[r * inner] = sf<T>(__expf(lf(xp[r * inner]) - mx) * inv);
+}
+
+void record_softmax(wgx_context *ctx, const std::vector<wgx_arg> &a) {
+  const char *name = "aten._softmax.default";
+  wgx_tensor *in = tensor_at(a, 0, name);
+  int dim = int(num_at(a, 1, name));
+  wgx_tensor *out = tensor_at(a, 3, name);
+  require_float_pair(in, out, name);
+  if (in->ndim == 0) fail(std::string(name) + ": scalar input unsupported");
+  if (in->numel != out->numel) fail(std::string(name) + ": input/output numel mismatch");
+  if (dim < 0) dim += in->ndim;
+  if (dim < 0 || dim >= in->ndim) fail(std::string(name) + ": dim out of range");
+  int64_t outer = 1, inner = 1;
+  for (int i = 0; i < dim; ++i) outer *= in->shape[i];
+  for (int i = dim + 1; i < in->ndim; ++i) inner *= in->shape[i];
+  const int R = int(in->shape[dim]);
+  if (outer == 0 || R == 0 || inner == 0) fail(std::string(name) + ": zero-sized reduction");
+  const void *px = in->data();
+  void *py = out->data();
+  const long long lines = outer * inner;
+  const int dt = in->dtype;
+  const unsigned blocks = unsigned((lines * 32 + 255) / 256);
+  push(ctx, name, 1, [=](const ExecEnv &env) {
+    if (dt == WGX_FLOAT16)
+      softmax_kernel<__half><<<blocks, 256, 0, env.stream>>>((const __half *)px, (__half *)py,
+                                                             lines, R, inner);
+    else
+      softmax_kernel<float><<<blocks, 256, 0, env.stream>>>((const float *)px, (float *)py, lines,
+                                                            R, inner);
+    check_cuda(cudaGetLastError(), "softmax launch");
+  });
+}
+
+// ------------------------------------------------------------ resampling
+struct Resample {
+  int N, C, IH, IW, OH, OW, align;
+};
+
+template <class T>
+__global__ void nearest_kernel(Resample r, const T *__restrict__ x, T *__restrict__ y, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int ow = int(i % r.OW);
+    long long t = i / r.OW;
+    const int oh = int(t % r.OH);
+    const long long plane = t / r.OH;
+    // source index (dst * in) / out, upsample-nearest-2d-f16.wgsl.ts:40-42
+    const int ih = int((long long)oh * r.IH / r.OH), iw = int((long long)ow * r.IW / r.OW);
+    y[i] = x[(plane * r.IH + ih) * r.IW + iw];
+  }
+}
+
+__device__ __forceinline__ float src_index(int dst, int insz, int outsz, int align) {
+  if (align) return outsz <= 1 ? 0.f : float(dst) * float(insz - 1) / float(outsz - 1);
+  return (float(dst) + 0.5f) * float(insz) / float(outsz) - 0.5f;
+}
+
+template <class T>
+__global__ void bilinear_kernel(Resample r, const T *__restrict__ x, T *__restrict__ y,
+                                long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int ow = int(i % r.OW);
+    long long t = i / r.OW;
+    const int oh = int(t % r.OH);
+    const long long plane = t / r.OH;
+    // upsample-bilinear2d-f16.wgsl.ts:28-77 (interpolation here in fp32)
+    const float sh = src_index(oh, r.IH, r.OH, r.align), sw = src_index(ow, r.IW, r.OW, r.align);
+    const int h0 = int(floorf(sh)), w0 = int(floorf(sw));
+    const float lh = sh - float(h0), lw = sw - float(w0);
+    const int h0c = min(max(h0, 0), r.IH - 1), h1c = min(max(h0 + 1, 0), r.IH - 1);
+    const int w0c = min(max(w0, 0), r.IW - 1), w1c = min(max(w0 + 1, 0), r.IW - 1);
+    const T *p = x + plane * r.IH * (long long)r.IW;
+    const float v00 = lf(p[h0c * (long long)r.IW + w0c]), v01 = lf(p[h0c * (long long)r.IW + w1c]);
+    const float v10 = lf(p[h1c * (long long)r.IW + w0c]), v11 = lf(p[h1c * (long long)r.IW + w1c]);
+    const float top = v00 + (v01 - v00) * lw, bot = v10 + (v11 - v10) * lw;
+    y[i] = sf<T>(top + (bot - top) * lh);
+  }
+}
+
+void record_nearest(wgx_context *ctx, const std::vector<wgx_arg> &a) {
+  const char *name = "aten.upsample_nearest2d.vec";
+  wgx_tensor *in = tensor_at(a, 0, name), *out = tensor_at(a, 3, name);
+  require_float_pair(in, out, name);
+  if (in->ndim != 4 || out->ndim != 4) fail(std::string(name) + ": input and output must be 4D NCHW");
+  if (out->shape[0] != in->shape[0] || out->shape[1] != in->shape[1])
+    fail(std::string(name) + ": output batch/channels must match input");
+  if (out->shape[2] < in->shape[2] || out->shape[3] < in->shape[3])
+    fail(std::string(name) + ": output spatial dims must be >= input spatial dims");
+  Resample r{int(in->shape[0]), int(in->shape[1]), int(in->shape[2]), int(in->shape[3]),
+             int(out->shape[2]), int(out->shape[3]), 0};
+  const void *px = in->data();
+  void *py = out->data();
+  const long long n = out->numel;
+  const int dt = in->dtype;
+  push(ctx, name, 1, [=](const ExecEnv &env) {
+    if (dt == WGX_FLOAT16)
+      nearest_kernel<__half><<<blocks_for(n), 256, 0, env.stream>>>(r, (const __half *)px,
+                                                                    (__half *)py, n);
+    else
+      nearest_kernel<float><<<blocks_for(n), 256, 0, env.stream>>>(r, (const float *)px,
+                                                                   (float *)py, n);
+    check_cuda(cudaGetLastError(), "upsample launch");
+  });
+}
+
+void record_bilinear(wgx_context *ctx, const std::vector<wgx_arg> &a) {
+  const char *name = "aten.upsample_bilinear2d.vec";
+  wgx_tensor *in = tensor_at(a, 0, name), *out = tensor_at(a, 4, name);
+  const bool align = num_at(a, 2, name) != 0;
+  require_float_pair(in, out, name);
+  if (in->ndim != 4 || out->ndim != 4) fail(std::string(name) + ": expected 4D in/out tensors");
+  if (out->shape[0] != in->shape[0] || out->shape[1] != in->shape[1])
+    fail(std::string(name) + ": N/C mismatch");
+  Resample r{int(in->shape[0]), int(in->shape[1]), int(in->shape[2]), int(in->shape[3]),
+             int(out->shape[2]), int(out->shape[3]), align ? 1 : 0};
+  const void *px = in->data();
+  void *py = out->data();
+  const long long n = out->numel;
+  const int dt = in->dtype;
+  push(ctx, name, 1, [=](const ExecEnv &env) {
+    if (dt == WGX_FLOAT16)
+      bilinear_kernel<__half><<<blocks_for(n), 256, 0, env.stream>>>(r, (const __half *)px,
+                                                                     (__half *)py, n);
+    else
+      bilinear_kernel<float><<<blocks_for(n), 256, 0, env.stream>>>(r, (const float *)px,
+                                                                    (float *)py, n);
+    check_cuda(cudaGetLastError(), "upsample launch");
+  });
+}
+
+// ---------------------------------------------------------- mean.dim
+template <class T>
+__global__ void mean_kernel(const T *__restrict__ x, T *__restrict__ y, long long lines, long long R,
+                            long long inner) {
+  const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (warp >= lines) return;
+  const long long o = warp / inner, in = warp % inner;
+  const T *xp = x + o * R * inner + in;
+  float sum = 0.f;
+  for (long long r = lane; r < R; r += 32) sum += lf(xp[r * inner]);
+  for (int s = 16; s > 0; s >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, s);
+  if (lane == 0) y[warp] = sf<T>(sum / float(R));
+}
+
+void record_mean(wgx_context *ctx, const std::vector<wgx_arg> &a) {
+  const char *name = "aten.mean.dim";
+  wgx_tensor *in = tensor_at(a, 0, name), *out = tensor_at(a, 4, name);
+  std::vector<int64_t> dims = list_at(a, 1, name);
+  const int nd = in->ndim;
+  if (nd == 0 || dims.empty()) fail(std::string(name) + ": dim out of range");
+  for (auto &d : dims) {
+    if (d < 0) d += nd;
+    if (d < 0 || d >= nd) fail(std::string(name) + ": dim out of range");
+  }
+  std::sort(dims.begin(), dims.end());
+  for (size_t i = 1; i < dims.size(); ++i) {
+    if (dims[i] == dims[i - 1]) fail(std::string(name) + ": duplicate reduced dim");
+    if (dims[i] != dims[i - 1] + 1) fail(std::string(name) + ": only contiguous reduced dims supported");
+  }
+  require_float_pair(in, out, name);
+  int64_t outer = 1, R = 1, inner = 1;
+  for (int i = 0; i < dims.front(); ++i) outer *= in->shape[i];
+  for (int64_t i = dims.front(); i <= dims.back(); ++i) R *= in->shape[i];
+  for (int i = int(dims.back()) + 1; i < nd; ++i) inner *= in->shape[i];
+  if (R == 0) fail(std::string(name) + ": zero-sized reduction");
+  if (outer * inner != out->numel) fail(std::string(name) + ": output numel mismatch");
+  const void *px = in->data();
+  void *py = out->data();
+  const long long lines = outer * inner;
+  const int dt = in->dtype;
+  const unsigned blocks = unsigned((lines * 32 + 255) / 256);
+  push(ctx, name, 1, [=](const ExecEnv &env) {
+    if (dt == WGX_FLOAT16)
+      mean_kernel<__half><<<blocks, 256, 0, env.stream>>>((const __half *)px, (__half *)py, lines,
+                                                          R, inner);
+    else
+      mean_kernel<float><<<blocks, 256, 0, env.stream>>>((const float *)px, (float *)py, lines, R,
+                                                         inner);
+    check_cuda(cudaGetLastError(), "mean launch");
+  });
+}
+
+// ------------------------------------------------------ constant_pad_nd
+struct Pad4 {
+  int64_t in[4], out[4], left[4];
+  float value;
+};
+
+template <class T>
+__global__ void pad_kernel(Pad4 p, const T *__restrict__ x, T *__restrict__ y, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long r = i, src = 0, stride = 1;
+    bool inside = true;
+    for (int d = 3; d >= 0; --d) {
+      const long long c = r % p.out[d] - p.left[d];
+      r /= p.out[d];
+      if (c < 0 || c >= p.in[d]) inside = false;
+      src += c * stride;
+      stride *= p.in[d];
+    }
+    y[i] = inside ? x[src] : sf<T>(p.value);
+  }
+}
+
+void record_pad(wgx_context *ctx, const std::vector<wgx_arg> &a) {
+  const char *name = "aten.constant_pad_nd.default";
+  wgx_tensor *in = tensor_at(a, 0, name);
+  std::vector<int64_t> pad = list_at(a, 1, name);
+  double value = 0.0;
+  wgx_tensor *out;
+  if (a.size() == 4) {
+    value = num_at(a, 2, name);
+    out = tensor_at(a, 3, name);
+  } else {
+    out = tensor_at(a, 2, name);
+  }
+  require_float_pair(in, out, name);
+  const int nd = in->ndim;
+  if (nd == 0 || nd > 4) fail(std::string(name) + ": rank must be 1..4 (got " + std::to_string(nd) + ")");
+  if (out->ndim != nd)
+    fail(std::string(name) + ": in/out rank mismatch (" + std::to_string(nd) + " !== " +
+         std::to_string(out->ndim) + ")");
+  if (pad.size() % 2) fail(std::string(name) + ": pad must be even-length");
+  const int npad = int(pad.size() / 2);
+  if (npad > nd) fail(std::string(name) + ": pad longer than rank");
+  Pad4 p{};
+  int64_t left[4] = {0, 0, 0, 0}, right[4] = {0, 0, 0, 0};
+  for (int k = 0; k < npad; ++k) {
+    left[nd - 1 - k] = pad[2 * k];
+    right[nd - 1 - k] = pad[2 * k + 1];
+  }
+  for (int d = 0; d < nd; ++d) {
+    if (left[d] < 0 || right[d] < 0) fail(std::string(name) + ": negative pad (cropping) not supported");
+    const int64_t e = in->shape[d] + left[d] + right[d];
+    if (out->shape[d] != e)
+      fail(std::string(name) + ": output dim " + std::to_string(d) + " mismatch (" +
+           std::to_string(e) + " != " + std::to_string(out->shape[d]) + ")");
+  }
+  for (int d = 0; d < 4; ++d) {  // right-align into 4-D
+    const int sd = d - (4 - nd);
+    p.in[d] = sd >= 0 ? in->shape[sd] : 1;
+    p.out[d] = sd >= 0 ? out->shape[sd] : 1;
+    p.left[d] = sd >= 0 ? left[sd] : 0;
+  }
+  p.value = float(value);
+  const void *px = in->data();
+  void *py = out->data();
+  const long long n = out->numel;
+  const int dt = in->dtype;
+  push(ctx, name, 1, [=](const ExecEnv &env) {
+    if (dt == WGX_FLOAT16)
+      pad_kernel<__half><<<blocks_for(n), 256, 0, env.stream>>>(p, (const __half *)px,
+                                                                (__half *)py, n);
+    else
+      pad_kernel<float><<<blocks_for(n), 256, 0, env.stream>>>(p, (const float *)px, (float *)py,
+                                                               n);
+    check_cuda(cudaGetLastError(), "pad launch");
+  });
+}
+
+}  // namespace
+
+void register_data_ops(std::unordered_map<std::string, OpRecorder> &r) {
+  auto flat = [](const char *name) {
+    return [name](wgx_context *c, const std::vector<wgx_arg> &a) {
+      record_flat_copy(c, a, name, 0, a.size() - 1);
+    };
+  };
+  r["aten.view_copy.default"] = flat("aten.view_copy.default");
+  r["aten.clone.default"] = flat("aten.clone.default");
+  r["aten.squeeze_copy.dims"] = flat("aten.squeeze_copy.dims");
+  r["aten.unsqueeze_copy.default"] = flat("aten.unsqueeze_copy.default");
+  r["et_vk.prepack.default"] = flat("et_vk.prepack.default");
+  r["aten.cat.default"] = record_cat;
+  r["aten.split_with_sizes_copy.default"] = record_split;
+  r["aten.permute_copy.default"] = record_permute;
+  r["aten.bmm.default"] = record_bmm;
+  r["aten.max_pool2d_with_indices.default"] = record_maxpool;
+  r["aten._softmax.default"] = record_softmax;
+  r["aten.upsample_nearest2d.vec"] = record_nearest;
+  r["aten.upsample_bilinear2d.vec"] = record_bilinear;
+  r["aten.mean.dim"] = record_mean;
+  r["aten.constant_pad_nd.default"] = record_pad;
+}
+
+}  // namespace wgx

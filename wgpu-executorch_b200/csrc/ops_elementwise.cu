@@ -220,6 +220,5 @@ void register_elementwise_ops(std::unordered_map<std::string, OpRecorder> &r) {
   };
 }
 
-void register_data_ops(std::unordered_map<std::string, OpRecorder> &) {}
 
 }  // namespace wgx

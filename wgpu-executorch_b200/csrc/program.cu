@@ -150,6 +150,45 @@ Program parse_program(const char *text, uint64_t len) {
 
 uint64_t align256(uint64_t x) { return (x + 255) / 256 * 256; }
 
+// True when the convolution `c` (aten.convolution positional args) takes
+// the tensor-core path, which stages its whole input in scratch first.
+bool conv_in_place_safe(const Program &P, const POp &c,
+                        const std::map<int64_t, wgx_tensor *> &tensors) {
+  auto in = tensors.find(c.args[0]), w = tensors.find(c.args[1]), out = tensors.find(c.args[9]);
+  if (in == tensors.end() || w == tensors.end() || out == tensors.end()) return false;
+  auto hw = [&](int64_t idx, int *h, int *wv) {
+    const PValue &v = P.values[idx];
+    if (v.kind != PValue::List || v.items.empty() || v.items.size() > 2) return false;
+    *h = int(v.items[0]);
+    *wv = int(v.items.size() == 2 ? v.items[1] : v.items[0]);
+    return true;
+  };
+  wgx_conv2d_params p{};
+  const wgx_tensor *x = in->second, *wt = w->second, *y = out->second;
+  if (x->ndim != 4 || wt->ndim != 4 || y->ndim != 4) return false;
+  p.B = int(x->shape[0]);
+  p.IC = int(x->shape[1]);
+  p.IH = int(x->shape[2]);
+  p.IW = int(x->shape[3]);
+  p.OC = int(wt->shape[0]);
+  p.KH = int(wt->shape[2]);
+  p.KW = int(wt->shape[3]);
+  p.OH = int(y->shape[2]);
+  p.OW = int(y->shape[3]);
+  if (!hw(c.args[3], &p.sH, &p.sW) || !hw(c.args[4], &p.pH, &p.pW) ||
+      !hw(c.args[5], &p.dH, &p.dW))
+    return false;
+  const PValue &g = P.values[c.args[8]];
+  p.groups = g.kind == PValue::Scalar ? int(g.num) : 0;
+  p.dtype = x->dtype;
+  p.act = WGX_ACT_SILU;
+  try {
+    return plan_conv2d(p).variant == WGX_CONV_UMMA;
+  } catch (const Error &) {
+    return false;
+  }
+}
+
 // SiLU fusion: conv(v) ; sigmoid(v)->s ; mul(v,s)->y  ==>  conv_silu -> y
 // Returns, per chain index, 0 = record as is, 1 = fused conv head (record
 // with SiLU into the mul's output), 2 = skip (absorbed).
@@ -175,14 +214,20 @@ std::vector<int> plan_fusion(const Program &P, const std::map<int64_t, wgx_tenso
     // v read by conv(out) + sigmoid + mul, s by sigmoid(out) + mul
     if (readers[v] != 3 || readers[sv] != 2) continue;
     if (outputs.count(v) || outputs.count(sv)) continue;
-    const PValue &tr = P.values[P.values[c.args[6]].kind == PValue::Scalar ? c.args[6] : 0];
+    const PValue &tr = P.values[c.args[6]];
     if (tr.kind == PValue::Scalar && tr.b) continue;  // transposed
     auto tv = tensors.find(v), ty = tensors.find(y), tx = tensors.find(c.args[0]);
     if (tv == tensors.end() || ty == tensors.end() || tx == tensors.end()) continue;
     if (tv->second->numel != ty->second->numel || tv->second->dtype != ty->second->dtype)
       continue;
-    // the fused conv writes y directly: never fuse in place
-    if (ty->second->buffer->dptr == tx->second->buffer->dptr) continue;
+    // The fused conv writes y directly. When y shares the conv input's
+    // buffer, only the tensor-core path is safe (its first kernel copies the
+    // whole input into scratch before the second writes the output); the
+    // CUDA-core variants read the input while writing, so they never fuse
+    // in place.
+    if (ty->second->buffer->dptr == tx->second->buffer->dptr &&
+        !conv_in_place_safe(P, c, tensors))
+      continue;
     mark[i] = 1;
     mark[i + 1] = 2;
     mark[i + 2] = 2;
