@@ -152,6 +152,16 @@ WGX_API int wgx_sync(wgx_context *ctx);
 WGX_API int wgx_reset(wgx_context *ctx);
 /* number of recorded commands and of kernel launches one submit replays */
 WGX_API int wgx_context_stats(const wgx_context *ctx, int64_t *n_commands, int64_t *n_kernel_launches);
+/* Replays the recorded commands eagerly (outside the captured graph)
+ * `repeats` times with a CUDA event pair around each command and writes the
+ * mean milliseconds of command i to ms[i] (at most `capacity` entries);
+ * *count receives the number of commands. The reference times whole
+ * submits only (utils/benchmark/main.ts:60-77); this is the per-command
+ * breakdown of that figure. */
+WGX_API int wgx_context_profile(wgx_context *ctx, int repeats, double *ms, int capacity, int *count);
+/* the op name of recorded command `index` (NULL when out of range); the
+ * string lives until the context is reset or destroyed */
+WGX_API const char *wgx_context_command_name(const wgx_context *ctx, int index);
 /* the context's CUDA stream (cudaStream_t) for callers that interleave work */
 WGX_API int wgx_context_stream(const wgx_context *ctx, void **stream);
 

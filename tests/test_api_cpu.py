@@ -91,9 +91,26 @@ def test_plan_fallbacks():
     assert plan(dtype=0, B=1, IC=64, IH=8, IW=8, OC=64, OH=8, OW=8).variant == _lib.CONV_SIMT_GEMM
     assert plan(IC=3, OC=1, IH=4, IW=4, OH=4, OW=4).variant == _lib.CONV_POINTWISE1
     assert plan(IC=4, OC=4, groups=2, IH=2, IW=2, OH=2, OW=2).variant == _lib.CONV_DIRECT
-    # YOLO stem: IC=3, stride 2 -> CUDA-core implicit GEMM
-    assert plan(IC=3, IH=640, IW=640, OC=16, OH=320, OW=320, KH=3, KW=3, sH=2, sW=2, pH=1,
+    # stride 2 with one input channel: 4 space-to-depth channels -> CUDA cores
+    assert plan(IC=1, IH=64, IW=64, OC=16, OH=32, OW=32, KH=3, KW=3, sH=2, sW=2, pH=1,
                 pW=1).variant == _lib.CONV_SIMT_GEMM
+    # stride above 4 -> CUDA cores
+    assert plan(IC=16, IH=20, IW=20, OC=16, OH=4, OW=4, KH=3, KW=3, sH=5, sW=5, pH=1,
+                pW=1).variant == _lib.CONV_SIMT_GEMM
+
+
+def test_plan_strided_convs_use_tensor_cores():
+    # YOLO stem: IC=3, 3x3 stride 2 pad 1 -> 2x2 stride-1 conv over 12 channels
+    stem = plan(B=64, IC=3, IH=640, IW=640, OC=16, OH=320, OW=320, KH=3, KW=3, sH=2, sW=2,
+                pH=1, pW=1)
+    assert stem.variant == _lib.CONV_UMMA
+    # 321 x 321 virtual positions per image (OW + 1 columns), 256 per tile
+    assert stem.grid_ctas == 64 * ((319 * 321 + 320 + 255) // 256)
+    down = plan(B=64, IC=128, IH=80, IW=80, OC=128, OH=40, OW=40, KH=3, KW=3, sH=2, sW=2,
+                pH=1, pW=1)
+    assert down.variant == _lib.CONV_UMMA
+    # re-laid input: 4 phases x 128 channels x 41 x 41 positions (+ slack)
+    assert down.scratch_bytes >= 64 * 512 * 41 * 41 * 2
 
 
 def test_plan_rejects_bad_geometry():

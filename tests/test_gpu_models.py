@@ -120,3 +120,54 @@ def test_yolo26n_fp16_replay_is_stable(ctx):
     # 397 ops in the chain; the conv->sigmoid->mul triples (87) fuse into one
     # conv each, including those whose output reuses the conv input's pool
     assert st["commands"] <= 397 + 2 - 2 * 80
+
+
+def test_yolo26n_batch_lift_matches_per_image(ctx):
+    """A batch-3 lift of the fp16 detector gives, image by image, exactly
+    the batch-1 program's output (every kernel treats images independently
+    and keeps its per-output accumulation order)."""
+    from wgx import programs
+    prog, w = load("yolo26n", True)
+    n = 3 * 640 * 640
+    base = ((np.arange(n) % 251) / 250.0 - 0.5).astype(np.float16)
+    imgs = [base, (base * 0.5).astype(np.float16), base[::-1].copy()]
+    singles = []
+    for im in imgs:
+        c = wgx.WgpuExecutionContext(0)
+        try:
+            inp = c.tensor("float16", [1, 3, 640, 640]).setData(im)
+            out = c.tensor("float16", [1, 84, 8400])
+            c.recordProgram(prog, w, [inp, out])
+            c.submit()
+            c.sync()
+            singles.append(out.numpy().copy())
+        finally:
+            c.destroy()
+    lifted = programs.batch_lift(prog, 3)
+    inp = ctx.tensor("float16", [3, 3, 640, 640]).setData(np.concatenate(imgs))
+    out = ctx.tensor("float16", [3, 84, 8400])
+    ctx.recordProgram(lifted, w, [inp, out])
+    ctx.submit()
+    ctx.sync()
+    y = out.numpy()
+    for i in range(3):
+        np.testing.assert_array_equal(y[i], singles[i][0])
+
+
+def test_depthart_256_batch_lift_runs(ctx):
+    """DepthART re-shaped to 256x256 and lifted to batch 4 (the benchmark's
+    program form) runs and gives the same output for identical images."""
+    from wgx import programs
+    prog, w = load("depthart", True)
+    p = programs.batch_lift(programs.respatial(prog, 256, 256), 4)
+    n = 3 * 256 * 256
+    x = ((np.arange(n) % 251) / 250.0 - 0.5).astype(np.float16)
+    inp = ctx.tensor("float16", [4, 3, 256, 256]).setData(np.tile(x, 4))
+    out = ctx.tensor("float16", [4, 1, 256, 256])
+    ctx.recordProgram(p, w, [inp, out])
+    ctx.submit()
+    ctx.sync()
+    y = out.numpy()
+    assert np.all(np.isfinite(y))
+    for i in range(1, 4):
+        np.testing.assert_array_equal(y[i], y[0])

@@ -110,10 +110,57 @@ def test_dense_f16_no_bias_and_clamp(ctx):
     check_f16(y, x, w, None, 1, 1, 1, 1, act=oracle.ACT_CLAMP, lo=0.0, hi=np.inf, clamp_op=True)
 
 
+# strided convolutions on the tensor cores (space-to-depth re-layout):
+# (B, IC, H, W, OC, K, stride, pad)
+STRIDED_F16 = [
+    (1, 3, 64, 64, 16, 3, 2, 1),      # YOLO stem shape (IC = 3: 12 virtual channels)
+    (2, 16, 40, 40, 32, 3, 2, 1),     # vectorised re-layout (IC % 8 == 0, W % 8 == 0)
+    (2, 32, 21, 19, 64, 3, 2, 1),     # odd sizes: per-slot re-layout
+    (1, 64, 48, 48, 160, 3, 2, 1),    # two output-channel tiles
+    (2, 32, 20, 24, 48, 5, 2, 2),     # 5x5 -> 3x3 virtual filter
+    (1, 16, 30, 30, 32, 1, 2, 0),     # 1x1 stride 2: one input phase
+    (1, 16, 33, 33, 24, 3, 2, 0),     # no padding
+    (1, 8, 28, 28, 16, 7, 2, 3),      # 7x7 -> 4x4 virtual filter
+    (1, 16, 27, 27, 16, 3, 3, 1),     # stride 3
+    (2, 128, 80, 80, 128, 3, 2, 1),   # YOLO26-N downsampling shape
+]
+
+
+@pytest.mark.parametrize("geom", STRIDED_F16, ids=[str(g) for g in STRIDED_F16])
+def test_strided_f16_tensor_core(ctx, geom):
+    B, IC, H, W, OC, K, s, p = geom
+    OH, OW = oracle.conv_out_hw(H, W, K, K, (s, s), (p, p), (1, 1))
+    params = _lib.ConvParams(B, IC, H, W, OC, OH, OW, K, K, s, s, p, p, 1, 1, 1, 1, 1,
+                             _lib.ACT_NONE, -np.inf, np.inf)
+    plan = _lib.ConvPlan()
+    _lib.check(_lib.lib.wgx_conv2d_plan_for(ctypes.byref(params), ctypes.byref(plan)))
+    assert plan.variant == _lib.CONV_UMMA
+    (x,) = oracle.make_inputs([(B, IC, H, W)], seed=35)
+    w = kaiming((OC, IC, K, K), 36)
+    (b,) = oracle.make_inputs([(OC,)], seed=37, scale=0.01)
+    y = engine_conv(ctx, x, w, b, s, p, 1, 1)
+    check_f16(y, x, w, b, s, p, 1, 1)
+
+
+def test_strided_f16_without_bias(ctx):
+    """A stride-2 tensor-core convolution with no bias tensor."""
+    (x,) = oracle.make_inputs([(2, 32, 40, 40)], seed=38)
+    w = kaiming((64, 32, 3, 3), 39)
+    tx = ctx.tensor("float16", x.shape).setData(x)
+    tw = ctx.tensor("float16", w.shape).setData(w)
+    out = ctx.tensor("float16", [2, 64, 20, 20])
+    ctx.recordShader(wgx.shaders.convolution,
+                     [tx, tw, None, [2, 2], [1, 1], [1, 1], False, [0, 0], 1, out])
+    ctx.submit()
+    ctx.sync()
+    check_f16(out.numpy(), x, w, None, 2, 1, 1, 1)
+    ctx.reset()
+
+
 @pytest.mark.parametrize("geom", [
-    (1, 3, 64, 64, 16, 3, 2, 1),     # YOLO stem shape (stride 2, IC = 3)
-    (2, 32, 21, 19, 64, 3, 2, 1),    # stride-2 downsampling conv
+    (1, 1, 33, 35, 8, 3, 2, 1),      # stride 2 with IC = 1 (4 virtual channels < 8)
     (1, 5, 7, 7, 3, 3, 1, 1),        # IC < 8
+    (1, 16, 20, 20, 16, 3, 5, 1),    # stride 5
 ])
 def test_dense_f16_cuda_core_fallback(ctx, geom):
     B, IC, H, W, OC, K, s, p = geom

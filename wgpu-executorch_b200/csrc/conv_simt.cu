@@ -241,9 +241,9 @@ __global__ void __launch_bounds__(DW_THREADS)
   extern __shared__ __align__(16) unsigned char dw_smem[];
   float *wsm = reinterpret_cast<float *>(dw_smem);  // KH*KW weights
   T *tile = reinterpret_cast<T *>(dw_smem + DW_MAX_TAPS * sizeof(float));
-  const int plane = blockIdx.y;  // b*C + c
+  const int plane = blockIdx.x;  // b*C + c
   const int c = plane % g.OC;
-  const int oh0 = blockIdx.x * TH;
+  const int oh0 = blockIdx.y * TH;
   const int taps = g.KH * g.KW;
   for (int i = threadIdx.x; i < taps; i += blockDim.x) wsm[i] = ld_f(&w[(long long)c * taps + i]);
   const int rows = (TH - 1) * g.sH + (g.KH - 1) * g.dH + 1;
@@ -441,8 +441,10 @@ static void launch_simt(const wgx_conv2d_params &p, int variant, const T *in, co
     int vec_out = (p.OW % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0) &&
                   (((long long)p.OH * p.OW) % 8 == 0);
     long long planes = (long long)p.B * p.OC;
-    if (planes > 65535) fail("conv2d: too many depthwise planes");
-    dim3 grid(unsigned((p.OH + TH - 1) / TH), unsigned(planes));
+    if (planes > 0x7fffffffLL) fail("conv2d: too many depthwise planes");
+    if ((p.OH + TH - 1) / TH > 65535) fail("conv2d: depthwise plane too tall");
+    // planes on x (up to 2^31-1 blocks), row bands on y
+    dim3 grid(unsigned(planes), unsigned((p.OH + TH - 1) / TH));
     depthwise_conv<T><<<grid, DW_THREADS, smem, s>>>(g, TH, TWs, in, w, bias, out, vec_in,
                                                       vec_out);
   } else {

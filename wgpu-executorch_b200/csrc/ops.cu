@@ -105,6 +105,17 @@ static void parse_hw(const std::vector<int64_t> &v, const char *name, const char
   }
 }
 
+// "<op>/<variant> B,IC,HxW->OC,OHxOW kKHxKW sS gG": the per-command label
+// that profiling reports.
+static std::string conv_label(const char *name, const wgx_conv2d_params &p, int variant) {
+  static const char *variants[] = {"?", "umma", "gemm", "depthwise", "direct", "pointwise1"};
+  char buf[192];
+  snprintf(buf, sizeof buf, "%s/%s %d,%d,%dx%d->%d,%dx%d k%dx%d s%d g%d%s", name,
+           variants[(variant >= 1 && variant <= 5) ? variant : 0], p.B, p.IC, p.IH, p.IW, p.OC,
+           p.OH, p.OW, p.KH, p.KW, p.sH, p.groups, p.act == WGX_ACT_SILU ? " silu" : "");
+  return buf;
+}
+
 // Append the command(s) of one forward convolution. Weights held by a
 // program constant are packed once now; user weights are re-packed inside
 // the graph on every submit so later setData calls are honoured (the
@@ -116,7 +127,7 @@ static void append_conv(wgx_context *ctx, const char *name, const wgx_conv2d_par
   const void *pbias = bias ? bias->data() : nullptr;
   void *pout = out->data();
   Command c;
-  c.name = name;
+  c.name = conv_label(name, p, plan.variant);
   if (plan.variant == WGX_CONV_UMMA) {
     uint64_t wbytes = umma_conv_packed_weight_bytes(p);
     void *packed = persistent_alloc(ctx, wbytes);

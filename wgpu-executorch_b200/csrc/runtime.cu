@@ -447,27 +447,30 @@ static void replay(wgx_context *ctx, const ExecEnv &env) {
   for (auto &c : ctx->commands) c.run(env);
 }
 
+// Grows the context's shared workspace to what the largest command needs.
+static ExecEnv ensure_workspace(wgx_context *ctx) {
+  uint64_t ws = 0;
+  for (auto &c : ctx->commands) ws = std::max(ws, c.workspace_bytes);
+  if (ws > ctx->workspace_bytes) {
+    check_cuda(cudaStreamSynchronize(ctx->stream), "workspace sync");
+    if (ctx->workspace) cudaFree(ctx->workspace);
+    ctx->workspace = nullptr;
+    ctx->workspace_bytes = 0;
+    check_cuda(cudaMalloc(&ctx->workspace, ws), "cudaMalloc(workspace)");
+    ctx->workspace_bytes = ws;
+  }
+  return ExecEnv{ctx->stream, ctx->workspace, ctx->workspace_bytes};
+}
+
 int wgx_submit(wgx_context *ctx) {
   return guarded([&] {
     assert_alive(ctx);
     if (ctx->commands.empty()) return;  // context.ts:325-327
     set_device(ctx->device);
     if (!ctx->graph_valid) {
-      uint64_t ws = 0;
       int64_t launches = 0;
-      for (auto &c : ctx->commands) {
-        ws = std::max(ws, c.workspace_bytes);
-        launches += c.kernel_launches;
-      }
-      if (ws > ctx->workspace_bytes) {
-        check_cuda(cudaStreamSynchronize(ctx->stream), "workspace sync");
-        if (ctx->workspace) cudaFree(ctx->workspace);
-        ctx->workspace = nullptr;
-        ctx->workspace_bytes = 0;
-        check_cuda(cudaMalloc(&ctx->workspace, ws), "cudaMalloc(workspace)");
-        ctx->workspace_bytes = ws;
-      }
-      ExecEnv env{ctx->stream, ctx->workspace, ctx->workspace_bytes};
+      for (auto &c : ctx->commands) launches += c.kernel_launches;
+      ExecEnv env = ensure_workspace(ctx);
       check_cuda(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal),
                  "cudaStreamBeginCapture");
       try {
@@ -524,6 +527,50 @@ int wgx_context_stats(const wgx_context *ctx, int64_t *n_commands, int64_t *n_ke
     if (n_commands) *n_commands = int64_t(ctx->commands.size());
     if (n_kernel_launches) *n_kernel_launches = launches;
   });
+}
+
+int wgx_context_profile(wgx_context *ctx, int repeats, double *ms, int capacity, int *count) {
+  return guarded([&] {
+    assert_alive(ctx);
+    if (repeats < 1) fail("profile: repeats must be >= 1");
+    set_device(ctx->device);
+    const int n = int(ctx->commands.size());
+    if (count) *count = n;
+    if (n == 0) return;
+    ExecEnv env = ensure_workspace(ctx);
+    std::vector<cudaEvent_t> ev(size_t(n) + 1, nullptr);
+    std::vector<double> total(size_t(n), 0.0);
+    auto release = [&] {
+      for (auto e : ev)
+        if (e) cudaEventDestroy(e);
+    };
+    try {
+      for (auto &e : ev) check_cuda(cudaEventCreate(&e), "profile event");
+      for (int r = 0; r < repeats; ++r) {
+        check_cuda(cudaEventRecord(ev[0], ctx->stream), "profile record");
+        for (int i = 0; i < n; ++i) {
+          ctx->commands[size_t(i)].run(env);
+          check_cuda(cudaEventRecord(ev[size_t(i) + 1], ctx->stream), "profile record");
+        }
+        check_cuda(cudaEventSynchronize(ev[size_t(n)]), "profile sync");
+        for (int i = 0; i < n; ++i) {
+          float t = 0.f;
+          check_cuda(cudaEventElapsedTime(&t, ev[size_t(i)], ev[size_t(i) + 1]), "profile time");
+          total[size_t(i)] += t;
+        }
+      }
+    } catch (...) {
+      release();
+      throw;
+    }
+    release();
+    for (int i = 0; i < n && i < capacity; ++i) ms[i] = total[size_t(i)] / repeats;
+  });
+}
+
+const char *wgx_context_command_name(const wgx_context *ctx, int index) {
+  if (!ctx || index < 0 || size_t(index) >= ctx->commands.size()) return nullptr;
+  return ctx->commands[size_t(index)].name.c_str();
 }
 
 int wgx_context_stream(const wgx_context *ctx, void **stream) {

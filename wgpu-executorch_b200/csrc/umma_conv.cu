@@ -16,6 +16,14 @@
 //    Flattening (hp, wp) to p = hp*Wp + wp turns a stride-1 convolution into
 //    out[p] = sum_taps W_tap . xs[p + kh*dH*Wp + kw*dW]: every tap is a pure
 //    row shift.
+//  * a stride-s convolution (dilation 1) is run as a stride-1 convolution
+//    over a space-to-depth view of its input: writing each tap offset
+//    kh - pH = s*d + ph (0 <= ph < s), input row s*oh + kh - pH is row
+//    oh + d of phase ph. The re-layout stores phase (ph, pw) of input
+//    channel c as virtual channel (phase index)*IC + c, the virtual filter
+//    spans the d range (3x3 / stride 2 / pad 1 -> 2x2 over 4*IC channels)
+//    and the packed weights hold w[oc][c][s*d + ph + pH][...] at virtual
+//    tap d, zero where that tap falls outside the real filter.
 //  * operands in shared memory use the canonical K-major no-swizzle layout
 //    (core matrix = 8 rows x 16 bytes, rows 16 bytes apart, 8-channel chunks
 //    one plane apart). A row shift is then just a 16-byte move of the
@@ -56,7 +64,12 @@ constexpr uint32_t EPI_BYTES = EPI_WARPS * 32 * EPI_ROWB;
 constexpr uint32_t SMEM_MAX = 227u * 1024u;
 
 struct UmmaGeom {
+  // IC, KH, KW, dH, dW, pH, pW describe the stride-1 convolution the MMA
+  // pipeline runs (for a strided convolution: the space-to-depth view);
+  // the x* fields and the phase tables describe the real one.
   int B, IC, IH, IW, OC, OH, OW, KH, KW, dH, dW, pH, pW;
+  int sH, sW, xIC, xKH, xKW, xpH, xpW;
+  int nphH, nphW, phH[4], phW[4];    // input phases the filter touches
   int bk, chunks;                    // channels per stage, 16-byte chunks per stage
   int khs, n_khg;                    // filter rows per stage, filter-row groups
   int Hp, Wp, C8, ncb, n_oct, tiles_per_img, total_tiles, R, R_alloc, stages, n_kstages;
@@ -76,38 +89,75 @@ static uint32_t smem_need(const UmmaGeom &g) {
 // Geometry for one staging choice: each pipeline stage carries `bk` input
 // channels and `khs` filter rows (khs = 1: one stage per filter row;
 // khs = KH: the whole filter, so one staged activation tile feeds every tap).
+static int floor_div(int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
+
+// Phases ph in [0, s) with (kh - pad) mod s == ph for some filter tap kh,
+// and the range [d0, d1] of (kh - pad - ph) / s.
+static void phases(int K, int pad, int s, int &n, int *ph, int &d0, int &d1) {
+  bool used[4] = {false, false, false, false};
+  for (int k = 0; k < K; ++k) used[(((k - pad) % s) + s) % s] = true;
+  n = 0;
+  for (int q = 0; q < s; ++q)
+    if (used[q]) ph[n++] = q;
+  d0 = floor_div(-pad, s);
+  d1 = floor_div(K - 1 - pad, s);
+}
+
 static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk) {
   UmmaGeom g{};
   g.B = p.B;
-  g.IC = p.IC;
   g.IH = p.IH;
   g.IW = p.IW;
   g.OC = p.OC;
   g.OH = p.OH;
   g.OW = p.OW;
-  g.KH = p.KH;
-  g.KW = p.KW;
-  g.dH = p.dH;
-  g.dW = p.dW;
-  g.pH = p.pH;
-  g.pW = p.pW;
+  g.sH = p.sH;
+  g.sW = p.sW;
+  g.xIC = p.IC;
+  g.xKH = p.KH;
+  g.xKW = p.KW;
+  g.xpH = p.pH;
+  g.xpW = p.pW;
+  if (p.sH == 1 && p.sW == 1) {
+    g.IC = p.IC;
+    g.KH = p.KH;
+    g.KW = p.KW;
+    g.dH = p.dH;
+    g.dW = p.dW;
+    g.pH = p.pH;
+    g.pW = p.pW;
+    g.nphH = g.nphW = 1;
+    g.Hp = p.IH + 2 * p.pH;
+    g.Wp = p.IW + 2 * p.pW;
+  } else {
+    int d0h, d1h, d0w, d1w;
+    phases(p.KH, p.pH, p.sH, g.nphH, g.phH, d0h, d1h);
+    phases(p.KW, p.pW, p.sW, g.nphW, g.phW, d0w, d1w);
+    g.IC = g.nphH * g.nphW * p.IC;
+    g.KH = d1h - d0h + 1;
+    g.KW = d1w - d0w + 1;
+    g.dH = g.dW = 1;
+    g.pH = -d0h;
+    g.pW = -d0w;
+    g.Hp = p.OH + g.KH - 1;
+    g.Wp = p.OW + g.KW - 1;
+  }
+  if (khs <= 0) khs = g.KH;
   g.bk = bk;
   g.chunks = bk / 8;
   g.khs = khs;
-  g.n_khg = p.KH / khs;
-  g.Hp = p.IH + 2 * p.pH;
-  g.Wp = p.IW + 2 * p.pW;
-  g.C8 = (p.IC + bk - 1) / bk * bk;
+  g.n_khg = g.KH / khs;
+  g.C8 = (g.IC + bk - 1) / bk * bk;
   g.ncb = g.C8 / bk;
   g.n_oct = (p.OC + UM - 1) / UM;
   g.plane_rows = (long long)g.Hp * g.Wp;
   long long p_out = (long long)(p.OH - 1) * g.Wp + p.OW;
   g.tiles_per_img = int((p_out + UN - 1) / UN);
   g.total_tiles = g.tiles_per_img * g.n_oct * g.B;
-  long long r = UN + (long long)(khs - 1) * p.dH * g.Wp + (long long)(p.KW - 1) * p.dW;
+  long long r = UN + (long long)(khs - 1) * g.dH * g.Wp + (long long)(g.KW - 1) * g.dW;
   g.R = r > (1 << 20) ? (1 << 20) : int(r);
   g.R_alloc = (g.R + 7) / 8 * 8;
-  g.a_stage_bytes = uint32_t(khs * p.KW) * g.chunks * UM * 16;
+  g.a_stage_bytes = uint32_t(khs * g.KW) * g.chunks * UM * 16;
   g.b_stage_bytes = uint32_t(g.chunks) * g.R_alloc * 16;
   g.n_kstages = g.n_khg * g.ncb;
   // resident weights: one oc tile, all stages' A blocks plus >= 2 B stages
@@ -153,7 +203,13 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk) {
 // stages of 16 channels); whole-filter and 16-channel stages are the
 // fallbacks for shapes where fewer than three 32-channel stages fit.
 static UmmaGeom make_geom(const wgx_conv2d_params &p) {
-  const int cand[3][2] = {{1, 32}, {p.KH, 16}, {1, 16}};
+  // (khs, bk); khs 0 = the whole filter. Below 16 (virtual) channels,
+  // 16-channel stages halve the zero padding of the K dimension.
+  int cand[3][2] = {{1, 32}, {0, 16}, {1, 16}};
+  if (geom_for(p, 1, 32).IC <= 16) {
+    cand[0][1] = 16;
+    cand[2][1] = 32;
+  }
   UmmaGeom best{};
   bool have = false;
   for (int min_stages : {3, 2}) {
@@ -180,13 +236,22 @@ static uint32_t smem_bytes(const UmmaGeom &g) {
 
 bool umma_conv_supported(const wgx_conv2d_params &p) {
   if (p.dtype != WGX_FLOAT16 || p.groups != 1) return false;
-  if (p.sH != 1 || p.sW != 1) return false;
-  if (p.KW > MAX_KW || p.IC < 8) return false;
-  if (p.dH < 1 || p.dW < 1) return false;
-  // stride-1 geometry must be consistent with the padded flattening
-  if (p.OH != p.IH + 2 * p.pH - p.dH * (p.KH - 1)) return false;
-  if (p.OW != p.IW + 2 * p.pW - p.dW * (p.KW - 1)) return false;
+  if (p.sH < 1 || p.sW < 1 || p.sH > 4 || p.sW > 4) return false;
+  if (p.dH < 1 || p.dW < 1 || p.pH < 0 || p.pW < 0) return false;
+  if (p.sH == 1 && p.sW == 1) {
+    if (p.IC < 8) return false;
+    // stride-1 geometry must be consistent with the padded flattening
+    if (p.OH != p.IH + 2 * p.pH - p.dH * (p.KH - 1)) return false;
+    if (p.OW != p.IW + 2 * p.pW - p.dW * (p.KW - 1)) return false;
+  } else {
+    // strided: space-to-depth view, dilation 1
+    if (p.dH != 1 || p.dW != 1) return false;
+    if (p.IH + 2 * p.pH < p.KH || p.IW + 2 * p.pW < p.KW) return false;
+    if (p.OH != (p.IH + 2 * p.pH - p.KH) / p.sH + 1) return false;
+    if (p.OW != (p.IW + 2 * p.pW - p.KW) / p.sW + 1) return false;
+  }
   UmmaGeom g = make_geom(p);
+  if (g.KW > MAX_KW || g.IC < 8) return false;
   if (g.stages < 2) return false;
   if (smem_need(g) > SMEM_MAX) return false;
   if (g.R_alloc * 16 >= (1 << 18)) return false;  // LBO field range
@@ -402,11 +467,109 @@ __device__ __forceinline__ void pack_weights_body(const UmmaGeom &g, const __hal
   __align__(16) __half v[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    const int c = cb * g.bk + chunk * 8 + e;
-    v[e] = (oc < g.OC && c < g.IC) ? w[((size_t(oc) * g.IC + c) * g.KH + kh) * g.KW + kw]
-                                   : __float2half_rn(0.f);
+    const int cv = cb * g.bk + chunk * 8 + e;  // virtual channel
+    __half val = __float2half_rn(0.f);
+    if (oc < g.OC && cv < g.IC) {
+      // virtual channel -> (phase, real channel); virtual tap -> real tap
+      // (stride 1: one phase, identity)
+      const int phase = cv / g.xIC, c = cv - phase * g.xIC;
+      const int ph = g.phH[phase / g.nphW], pw = g.phW[phase % g.nphW];
+      const int rkh = g.sH * (kh - g.pH) + ph + g.xpH;
+      const int rkw = g.sW * (kw - g.pW) + pw + g.xpW;
+      if (rkh >= 0 && rkh < g.xKH && rkw >= 0 && rkw < g.xKW)
+        val = w[((size_t(oc) * g.xIC + c) * g.xKH + rkh) * g.xKW + rkw];
+    }
+    v[e] = val;
   }
   packed[i] = *reinterpret_cast<const uint4 *>(v);
+}
+
+// ------------------------------------------------- space-to-depth re-layout
+// xs[b][cb][hp][wp][8] <- phase (ph, pw) of input channel c at
+// x[b][c][sH*(hp-pH)+ph][sW*(wp-pW)+pw] for virtual channel
+// cv = (phase index)*IC + c, zero outside the image and for cv >= the
+// virtual channel count. One thread per 16-byte slot (any shape).
+__global__ void pack_input_s2d(UmmaGeom g, const __half *__restrict__ x, uint4 *__restrict__ xs,
+                               long long n_slots) {
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_slots) return;
+  const int wp = int(i % g.Wp);
+  long long t = i / g.Wp;
+  const int hp = int(t % g.Hp);
+  t /= g.Hp;
+  const int cb = int(t % (g.C8 / 8));
+  const long long b = t / (g.C8 / 8);
+  __align__(16) __half v[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int cv = cb * 8 + e;
+    __half val = __float2half_rn(0.f);
+    if (cv < g.IC) {
+      const int phase = cv / g.xIC, c = cv - phase * g.xIC;
+      const int ih = g.sH * (hp - g.pH) + g.phH[phase / g.nphW];
+      const int iw = g.sW * (wp - g.pW) + g.phW[phase % g.nphW];
+      if (ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW)
+        val = x[((b * g.xIC + c) * g.IH + ih) * (long long)g.IW + iw];
+    }
+    v[e] = val;
+  }
+  xs[i] = *reinterpret_cast<const uint4 *>(v);
+}
+
+// Vector form for stride 2 across with both column phases used, IC % 8 == 0
+// and IW % 8 == 0 (then the virtual channel count is a multiple of 8 and
+// every 8-channel block of xs holds one phase). One thread takes one
+// 8-channel block of one input row (phase ph of virtual row hp) and 8
+// consecutive input columns iw0 = 2*q0 (q0 a multiple of 4): eight aligned
+// 16-byte loads, a register transpose, and four 16-byte slots for each of
+// the two column phases (64 contiguous bytes each).
+__global__ void __launch_bounds__(256)
+    pack_input_s2d_v8(UmmaGeom g, const __half *__restrict__ x, uint4 *__restrict__ xs,
+                      int groups_per_row, int qbase, int n_items) {
+  const int item = blockIdx.x * 256 + threadIdx.x;
+  if (item >= n_items) return;
+  const int t = item % groups_per_row;
+  int r = item / groups_per_row;
+  const int iph = r % g.nphH;
+  r /= g.nphH;
+  const int hp = r % g.Hp;
+  r /= g.Hp;
+  const int nb = g.xIC / 8;
+  const int cb = r % nb, b = r / nb;
+  const int ih = g.sH * (hp - g.pH) + g.phH[iph];
+  const int q0 = 4 * t + qbase;
+  const int iw0 = 2 * q0;  // a multiple of 8: the 8 columns are all in or all out
+  const bool inside = ih >= 0 && ih < g.IH && iw0 >= 0 && iw0 < g.IW;
+  uint4 ch[8];
+  const size_t cstride = size_t(g.IH) * g.IW;
+  const __half *src0 = x + ((size_t(b) * g.xIC + cb * 8) * g.IH + (inside ? ih : 0)) * g.IW +
+                       (inside ? iw0 : 0);
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    ch[e] = inside ? *reinterpret_cast<const uint4 *>(src0 + e * cstride)
+                   : make_uint4(0u, 0u, 0u, 0u);
+  const size_t plane_rows = size_t(g.Hp) * g.Wp;
+#pragma unroll
+  for (int pw = 0; pw < 2; ++pw) {
+    // virtual block of phase (iph, pw), real block cb
+    const int vb = (iph * 2 + pw) * nb + cb;
+    uint4 *dst = xs + (size_t(b) * (g.C8 / 8) + vb) * plane_rows + size_t(hp) * g.Wp;
+    const uint32_t sel = pw ? 0x7632u : 0x5410u;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int wp = q0 + k + g.pW;
+      if (wp < 0 || wp >= g.Wp) continue;
+      // column 2k+pw of each channel: half pw of word k
+      uint32_t wd[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint4 &v = ch[e];
+        wd[e] = k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
+      }
+      dst[wp] = make_uint4(__byte_perm(wd[0], wd[1], sel), __byte_perm(wd[2], wd[3], sel),
+                           __byte_perm(wd[4], wd[5], sel), __byte_perm(wd[6], wd[7], sel));
+    }
+  }
 }
 
 __global__ void pack_weights(UmmaGeom g, const __half *__restrict__ w, uint4 *__restrict__ packed,
@@ -831,7 +994,26 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   const uint64_t n_w64 = w_to_pack ? umma_conv_packed_weight_bytes(p) / 16 : 0;
   if (n_w64 >= (1ull << 31)) fail("conv2d: weights too large for the tensor-core path");
   const int n_w = int(n_w64);
-  if (g.IW % 8 == 0 && (reinterpret_cast<uintptr_t>(in) & 15) == 0) {
+  const bool strided = g.sH != 1 || g.sW != 1;
+  if (strided) {
+    if (w_to_pack)
+      pack_weights<<<unsigned((n_w + 255) / 256), 256, 0, stream>>>(
+          g, w_to_pack, static_cast<uint4 *>(packed), n_w);
+    if (g.sW == 2 && g.nphW == 2 && g.phW[0] == 0 && g.phW[1] == 1 && g.xIC % 8 == 0 &&
+        g.IW % 8 == 0 && g.C8 == g.IC && (reinterpret_cast<uintptr_t>(in) & 15) == 0) {
+      const int qbase = -4 * ((g.pW + 3) / 4);
+      const int groups_per_row = (g.Wp - g.pW - qbase + 3) / 4;
+      const long long n_items =
+          (long long)g.B * (g.xIC / 8) * g.Hp * g.nphH * groups_per_row;
+      if (n_items >= (1ll << 31) - 256) fail("conv2d: input too large for the re-layout kernel");
+      pack_input_s2d_v8<<<unsigned((n_items + 255) / 256), 256, 0, stream>>>(
+          g, in, static_cast<uint4 *>(xs), groups_per_row, qbase, int(n_items));
+    } else {
+      const long long n_slots = (long long)g.B * (g.C8 / 8) * g.plane_rows;
+      pack_input_s2d<<<unsigned((n_slots + 255) / 256), 256, 0, stream>>>(
+          g, in, static_cast<uint4 *>(xs), n_slots);
+    }
+  } else if (g.IW % 8 == 0 && (reinterpret_cast<uintptr_t>(in) & 15) == 0) {
     // input re-layout and weight packing in one launch
     const int groups_per_row = (g.Wp - (g.pW & 7) + 8 + 7) / 8;
     const long long n_items = (long long)g.B * (g.C8 / 8) * g.Hp * groups_per_row;
@@ -862,19 +1044,21 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
                            __half *);
   // specialisations: filter width (1/3/5/7, per-row 32-channel staging) x
   // epilogue activation
-  static const KernelFn table[5][3] = {
+  static const KernelFn table[7][3] = {
       {umma_conv_kernel<0, 0>, umma_conv_kernel<0, 1>, umma_conv_kernel<0, 2>},
       {umma_conv_kernel<1, 0>, umma_conv_kernel<1, 1>, umma_conv_kernel<1, 2>},
+      {umma_conv_kernel<2, 0>, umma_conv_kernel<2, 1>, umma_conv_kernel<2, 2>},
       {umma_conv_kernel<3, 0>, umma_conv_kernel<3, 1>, umma_conv_kernel<3, 2>},
+      {umma_conv_kernel<4, 0>, umma_conv_kernel<4, 1>, umma_conv_kernel<4, 2>},
       {umma_conv_kernel<5, 0>, umma_conv_kernel<5, 1>, umma_conv_kernel<5, 2>},
       {umma_conv_kernel<7, 0>, umma_conv_kernel<7, 1>, umma_conv_kernel<7, 2>}};
   int kw_idx = 0;
   if (g.khs == 1 && g.bk == 32)
-    kw_idx = g.KW == 1 ? 1 : g.KW == 3 ? 2 : g.KW == 5 ? 3 : g.KW == 7 ? 4 : 0;
+    kw_idx = g.KW == 7 ? 6 : (g.KW >= 1 && g.KW <= 5) ? g.KW : 0;
   const int act_idx = (g.act >= 0 && g.act <= 2) ? g.act : 0;
   KernelFn kern = table[kw_idx][act_idx];
   const int kidx = kw_idx * 3 + act_idx;
-  static bool attr_set[64][15] = {};
+  static bool attr_set[64][21] = {};
   if (dev < 64 && !attr_set[dev][kidx]) {
     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(SMEM_MAX)),

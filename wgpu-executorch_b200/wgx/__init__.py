@@ -361,6 +361,18 @@ class WgpuExecutionContext:
         check(lib.wgx_context_stats(self._h, byref(n), byref(k)))
         return {"commands": n.value, "kernel_launches": k.value}
 
+    def profile(self, repeats: int = 1) -> list:
+        """Per-command device time: the recorded commands replayed eagerly
+        ``repeats`` times with CUDA events around each one. Returns
+        ``[(op_name, mean_ms), ...]`` in recording order."""
+        self._assert_alive()
+        n = c_int(self.stats()["commands"])
+        if n.value == 0:
+            return []
+        ms = (ctypes.c_double * n.value)()
+        check(lib.wgx_context_profile(self._h, int(repeats), ms, n.value, byref(n)))
+        return [(lib.wgx_context_command_name(self._h, i).decode(), ms[i]) for i in range(n.value)]
+
     @property
     def stream(self) -> int:
         s = c_void_p()
