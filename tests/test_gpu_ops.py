@@ -1,0 +1,209 @@
+"""The program-executor operators around the convolutions (cat, split,
+permute, bmm, max-pool, upsampling, softmax, mean, pad, flat copies),
+recorded one by one through the ``shaders`` registry and compared with
+numpy restatements of the reference kernels' arithmetic
+(src/shaders/<op>/*.wgsl.ts): data movement bit-exact, arithmetic in fp32
+with one rounding (fp16: within one fp16 ulp of the fp64 result)."""
+import numpy as np
+import pytest
+
+import wgx
+
+pytestmark = pytest.mark.gpu
+
+RNG = np.random.default_rng(7)
+
+
+def T(ctx, a):
+    return ctx.tensor("float16" if a.dtype == np.float16 else
+                      "int32" if a.dtype == np.int32 else "float32", list(a.shape)).setData(a)
+
+
+def empty(ctx, shape, dt):
+    return ctx.tensor(dt, list(shape))
+
+
+def run(ctx, shader, args):
+    ctx.recordShader(shader, args)
+    ctx.submit()
+    ctx.sync()
+    ctx.reset()
+
+
+def rnd(shape, dt=np.float16):
+    return RNG.standard_normal(shape).astype(dt)
+
+
+@pytest.mark.parametrize("dt", [np.float16, np.float32])
+@pytest.mark.parametrize("shapes,dim", [
+    ([(4, 16, 20, 20), (4, 16, 20, 20), (4, 32, 20, 20)], 1),    # 16-byte pieces
+    ([(2, 3, 5, 7), (2, 1, 5, 7)], 1),                           # unaligned pieces
+    ([(3, 4, 6400), (3, 4, 1600), (3, 4, 400)], -1),
+    ([(2, 8, 8)] * 10, 1),                                       # more than 8 pieces
+])
+def test_cat(ctx, shapes, dim, dt):
+    xs = [rnd(s, dt) for s in shapes]
+    ref = np.concatenate(xs, axis=dim)
+    out = empty(ctx, ref.shape, "float16" if dt == np.float16 else "float32")
+    run(ctx, wgx.shaders.cat, [[T(ctx, x) for x in xs], dim, out])
+    np.testing.assert_array_equal(out.numpy(), ref)
+
+
+@pytest.mark.parametrize("shape,sizes,dim", [
+    ((4, 64, 20, 20), [32, 32], 1),
+    ((3, 2, 128, 40), [32, 32, 64], 2),
+    ((2, 5, 3), [2, 3], 1),
+])
+def test_split(ctx, shape, sizes, dim):
+    x = rnd(shape)
+    outs = [empty(ctx, tuple(s if d == dim else shape[d] for d in range(len(shape))), "float16")
+            for s in sizes]
+    run(ctx, wgx.shaders.splitWithSizesCopy, [T(ctx, x), sizes, dim, outs])
+    refs = np.split(x, np.cumsum(sizes)[:-1], axis=dim)
+    for o, r in zip(outs, refs):
+        np.testing.assert_array_equal(o.numpy(), r)
+
+
+@pytest.mark.parametrize("shape,perm", [
+    ((3, 2, 400, 400), [0, 1, 3, 2]),   # tiled transpose
+    ((2, 2, 32, 400), [0, 1, 3, 2]),
+    ((5, 33, 17), [0, 2, 1]),
+    ((2, 3, 4, 5), [2, 0, 3, 1]),       # generic index remap
+])
+def test_permute(ctx, shape, perm):
+    x = rnd(shape)
+    ref = np.transpose(x, perm)
+    out = empty(ctx, ref.shape, "float16")
+    run(ctx, wgx.shaders.permuteCopy, [T(ctx, x), perm, out])
+    np.testing.assert_array_equal(out.numpy(), ref)
+
+
+@pytest.mark.parametrize("dt", [np.float16, np.float32])
+@pytest.mark.parametrize("bmkn", [(8, 400, 32, 400), (8, 64, 400, 400), (3, 5, 7, 9),
+                                  (2, 65, 17, 130)])
+def test_bmm(ctx, bmkn, dt):
+    b, m, k, n = bmkn
+    a, bb = rnd((b, m, k), dt), rnd((b, k, n), dt)
+    out = empty(ctx, (b, m, n), "float16" if dt == np.float16 else "float32")
+    run(ctx, wgx.shaders.bmm, [T(ctx, a), T(ctx, bb), out])
+    ref = np.matmul(a.astype(np.float64), bb.astype(np.float64))
+    err = np.abs(out.numpy().astype(np.float64) - ref).max() / np.abs(ref).max()
+    assert err <= (2e-3 if dt == np.float16 else 1e-5)
+
+
+def maxpool_ref(x, k, s, p, d, ceil_mode, f16):
+    N, C, H, W = x.shape
+    def osz(n, kk, ss, pp, dd):
+        num = n + 2 * pp - (dd * (kk - 1) + 1)
+        q = num / ss
+        return int(np.ceil(q) if ceil_mode else np.floor(q)) + 1
+    OH, OW = osz(H, k[0], s[0], p[0], d[0]), osz(W, k[1], s[1], p[1], d[1])
+    y = np.empty((N, C, OH, OW), np.float32)
+    idx = np.zeros((N, C, OH, OW), np.int32)
+    start = -65504.0 if f16 else -3.4028234663852886e38
+    xf = x.astype(np.float32)
+    for oh in range(OH):
+        for ow in range(OW):
+            best = np.full((N, C), start, np.float32)
+            bi = np.zeros((N, C), np.int32)
+            for kh in range(k[0]):
+                ih = oh * s[0] - p[0] + kh * d[0]
+                if ih < 0 or ih >= H:
+                    continue
+                for kw in range(k[1]):
+                    iw = ow * s[1] - p[1] + kw * d[1]
+                    if iw < 0 or iw >= W:
+                        continue
+                    v = xf[:, :, ih, iw]
+                    m = v > best
+                    best = np.where(m, v, best)
+                    bi = np.where(m, ih * W + iw, bi)
+            y[:, :, oh, ow] = best
+            idx[:, :, oh, ow] = bi
+    return y, idx
+
+
+@pytest.mark.parametrize("geom", [
+    ((3, 16, 20, 20), (5, 5), (1, 1), (2, 2), (1, 1), False),   # YOLO SPPF, plane kernel
+    ((2, 4, 9, 11), (3, 3), (2, 2), (1, 1), (1, 1), True),      # ceil mode
+    ((1, 2, 70, 70), (2, 2), (2, 2), (0, 0), (1, 1), False),    # plane > 4096: generic
+    ((1, 3, 12, 12), (3, 3), (1, 1), (0, 0), (2, 2), False),    # dilation
+])
+def test_maxpool(ctx, geom):
+    shape, k, s, p, d, ceil_mode = geom
+    x = rnd(shape)
+    y, idx = maxpool_ref(x, k, s, p, d, ceil_mode, True)
+    vals = empty(ctx, y.shape, "float16")
+    ind = empty(ctx, y.shape, "int32")
+    run(ctx, wgx.shaders.maxPool2d, [T(ctx, x), list(k), list(s), list(p), list(d), ceil_mode,
+                                     [vals, ind]])
+    np.testing.assert_array_equal(vals.numpy().astype(np.float32), y)
+    np.testing.assert_array_equal(ind.numpy(), idx)
+
+
+@pytest.mark.parametrize("shape,out_hw", [((2, 16, 20, 20), (40, 40)), ((1, 3, 5, 7), (11, 13)),
+                                          ((2, 8, 40, 40), (80, 80))])
+def test_upsample_nearest(ctx, shape, out_hw):
+    x = rnd(shape)
+    N, C, H, W = shape
+    ih = (np.arange(out_hw[0]) * H) // out_hw[0]
+    iw = (np.arange(out_hw[1]) * W) // out_hw[1]
+    ref = x[:, :, ih][:, :, :, iw]
+    out = empty(ctx, (N, C) + out_hw, "float16")
+    run(ctx, wgx.shaders.upsampleNearest2d, [T(ctx, x), list(out_hw), None, out])
+    np.testing.assert_array_equal(out.numpy(), ref)
+
+
+@pytest.mark.parametrize("align", [True, False])
+def test_upsample_bilinear(ctx, align):
+    x = rnd((2, 5, 14, 14), np.float32)
+    OH, OW = 28, 21
+    def src(o, n_in, n_out):
+        o = np.arange(o, dtype=np.float64)
+        if align:
+            return o * (n_in - 1) / (n_out - 1)
+        return (o + 0.5) * n_in / n_out - 0.5
+    sh, sw = src(OH, 14, OH), src(OW, 14, OW)
+    h0, w0 = np.floor(sh).astype(int), np.floor(sw).astype(int)
+    lh, lw = sh - h0, sw - w0
+    c = lambda v, n: np.clip(v, 0, n - 1)
+    xd = x.astype(np.float64)
+    v00 = xd[:, :, c(h0, 14)][:, :, :, c(w0, 14)]
+    v01 = xd[:, :, c(h0, 14)][:, :, :, c(w0 + 1, 14)]
+    v10 = xd[:, :, c(h0 + 1, 14)][:, :, :, c(w0, 14)]
+    v11 = xd[:, :, c(h0 + 1, 14)][:, :, :, c(w0 + 1, 14)]
+    top = v00 + (v01 - v00) * lw
+    bot = v10 + (v11 - v10) * lw
+    ref = top + (bot - top) * lh[:, None]
+    out = empty(ctx, (2, 5, OH, OW), "float32")
+    run(ctx, wgx.shaders.upsampleBilinear2d, [T(ctx, x), [OH, OW], align, None, out])
+    assert np.abs(out.numpy() - ref).max() <= 1e-5
+
+
+def test_softmax_and_mean(ctx):
+    x = rnd((2, 2, 40, 400))
+    out = empty(ctx, x.shape, "float16")
+    run(ctx, wgx.shaders.softmax, [T(ctx, x), -1, False, out])
+    xd = x.astype(np.float64)
+    e = np.exp(xd - xd.max(-1, keepdims=True))
+    ref = e / e.sum(-1, keepdims=True)
+    assert np.abs(out.numpy().astype(np.float64) - ref).max() <= 1e-3
+    m = empty(ctx, (2, 2, 1, 1), "float16")
+    run(ctx, wgx.shaders.meanDim, [T(ctx, x), [2, 3], True, None, m])
+    np.testing.assert_allclose(m.numpy().astype(np.float64), xd.mean((2, 3), keepdims=True),
+                               atol=2e-3)
+
+
+def test_constant_pad_and_flat_copies(ctx):
+    x = rnd((1, 3, 5, 6))
+    out = empty(ctx, (1, 3, 6, 9), "float16")
+    run(ctx, wgx.shaders.constantPadNd, [T(ctx, x), [1, 2, 0, 1], 0.5, out])
+    ref = np.pad(x.astype(np.float32), ((0, 0), (0, 0), (0, 1), (1, 2)), constant_values=0.5)
+    np.testing.assert_array_equal(out.numpy().astype(np.float32), ref)
+    for shader, args_tail in [(wgx.shaders.viewCopy, [[3, 30]]), (wgx.shaders.clone, [None]),
+                              (wgx.shaders.squeezeCopy, [[0]])]:
+        shape = (3, 30) if shader is wgx.shaders.viewCopy else (3, 5, 6) if shader is \
+            wgx.shaders.squeezeCopy else (1, 3, 5, 6)
+        o = empty(ctx, shape, "float16")
+        run(ctx, shader, [T(ctx, x)] + args_tail + [o])
+        np.testing.assert_array_equal(o.numpy().reshape(-1), x.reshape(-1))

@@ -112,6 +112,78 @@ void record_flat_copy(wgx_context *ctx, const std::vector<wgx_arg> &a, const cha
 }
 
 // --------------------------------------------------------- cat / split
+// Up to kMaxPieces pitched 2-D copies in one launch: piece p copies `rows`
+// rows of width[p] bytes from src[p] (row pitch spitch[p]) to dst[p] (row
+// pitch dpitch[p]). The pieces tile one virtual row of `row16` 16-byte
+// vectors (col0 = first vector of each piece); every pointer, pitch and
+// width is a multiple of 16 bytes (the host falls back to pitched memcpy
+// otherwise), so each thread moves whole 16-byte vectors.
+constexpr int kMaxPieces = 8;
+struct MultiCopy {
+  int n;
+  long long rows, row16;
+  const char *src[kMaxPieces];
+  char *dst[kMaxPieces];
+  long long spitch[kMaxPieces], dpitch[kMaxPieces], col0[kMaxPieces + 1];
+};
+
+__global__ void __launch_bounds__(256) multi_copy_kernel(MultiCopy m) {
+  const long long total = m.rows * m.row16;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
+    const long long row = i / m.row16, c = i - row * m.row16;
+    int p = 0;
+#pragma unroll
+    for (int q = 1; q < kMaxPieces; ++q)
+      if (q < m.n && c >= m.col0[q]) p = q;
+    const long long off = (c - m.col0[p]) * 16;
+    const uint4 v = *reinterpret_cast<const uint4 *>(m.src[p] + row * m.spitch[p] + off);
+    *reinterpret_cast<uint4 *>(m.dst[p] + row * m.dpitch[p] + off) = v;
+  }
+}
+
+struct CopyPiece {
+  const char *src;
+  char *dst;
+  size_t spitch, dpitch, width;
+};
+
+// Launch pitched copies: whole-vector pieces through multi_copy_kernel (in
+// groups of kMaxPieces), anything unaligned through cudaMemcpy2DAsync.
+void run_pieces(const std::vector<CopyPiece> &pieces, size_t rows, cudaStream_t stream,
+                const char *what) {
+  auto aligned = [](const CopyPiece &p) {
+    return ((reinterpret_cast<uintptr_t>(p.src) | reinterpret_cast<uintptr_t>(p.dst) | p.spitch |
+             p.dpitch | p.width) &
+            15) == 0;
+  };
+  MultiCopy m{};
+  auto flush = [&] {
+    if (m.n == 0) return;
+    m.rows = (long long)rows;
+    m.row16 = m.col0[m.n];
+    const long long total = m.rows * m.row16;
+    multi_copy_kernel<<<blocks_for(total), 256, 0, stream>>>(m);
+    check_cuda(cudaGetLastError(), what);
+    m = MultiCopy{};
+  };
+  for (const CopyPiece &p : pieces) {
+    if (!p.width || !rows) continue;
+    if (!aligned(p)) {
+      check_cuda(cudaMemcpy2DAsync(p.dst, p.dpitch, p.src, p.spitch, p.width, rows,
+                                   cudaMemcpyDeviceToDevice, stream),
+                 what);
+      continue;
+    }
+    m.src[m.n] = p.src;
+    m.dst[m.n] = p.dst;
+    m.spitch[m.n] = (long long)p.spitch;
+    m.dpitch[m.n] = (long long)p.dpitch;
+    m.col0[m.n + 1] = m.col0[m.n] + (long long)(p.width / 16);
+    if (++m.n == kMaxPieces) flush();
+  }
+  flush();
+}
+
 // outer x (extent along dim x inner) blocks: one pitched 2-D copy per input
 struct Blocks {
   int64_t outer = 1, inner = 1;
@@ -146,27 +218,17 @@ void record_cat(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   const int es = dtype_size(out->dtype);
   const Blocks ob = blocks_of(out, dim);
   const size_t dpitch = size_t(out->shape[dim] * ob.inner) * es;
-  struct Piece {
-    const void *src;
-    char *dst;
-    size_t width;
-  };
-  std::vector<Piece> pieces;
+  std::vector<CopyPiece> pieces;
   int64_t off = 0;
   for (auto *t : ins) {
     const size_t width = size_t(t->shape[dim] * ob.inner) * es;
-    pieces.push_back({t->data(), static_cast<char *>(out->data()) + size_t(off * ob.inner) * es,
-                      width});
+    pieces.push_back({static_cast<const char *>(t->data()),
+                      static_cast<char *>(out->data()) + size_t(off * ob.inner) * es, width,
+                      dpitch, width});
     off += t->shape[dim];
   }
   const size_t rows = size_t(ob.outer);
-  push(ctx, name, 0, [=](const ExecEnv &env) {
-    for (auto &p : pieces)
-      if (p.width)
-        check_cuda(cudaMemcpy2DAsync(p.dst, dpitch, p.src, p.width, p.width, rows,
-                                     cudaMemcpyDeviceToDevice, env.stream),
-                   "cat copy");
-  });
+  push(ctx, name, 1, [=](const ExecEnv &env) { run_pieces(pieces, rows, env.stream, "cat copy"); });
 }
 
 void record_split(wgx_context *ctx, const std::vector<wgx_arg> &a) {
@@ -197,26 +259,17 @@ void record_split(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   const int es = dtype_size(in->dtype);
   const Blocks ib = blocks_of(in, dim);
   const size_t spitch = size_t(in->shape[dim] * ib.inner) * es;
-  struct Piece {
-    const char *src;
-    void *dst;
-    size_t width;
-  };
-  std::vector<Piece> pieces;
+  std::vector<CopyPiece> pieces;
   int64_t off = 0;
   for (size_t i = 0; i < outs.size(); ++i) {
+    const size_t width = size_t(sizes[i] * ib.inner) * es;
     pieces.push_back({static_cast<const char *>(in->data()) + size_t(off * ib.inner) * es,
-                      outs[i]->data(), size_t(sizes[i] * ib.inner) * es});
+                      static_cast<char *>(outs[i]->data()), spitch, width, width});
     off += sizes[i];
   }
   const size_t rows = size_t(ib.outer);
-  push(ctx, name, 0, [=](const ExecEnv &env) {
-    for (auto &p : pieces)
-      if (p.width)
-        check_cuda(cudaMemcpy2DAsync(p.dst, p.width, p.src, spitch, p.width, rows,
-                                     cudaMemcpyDeviceToDevice, env.stream),
-                   "split copy");
-  });
+  push(ctx, name, 1,
+       [=](const ExecEnv &env) { run_pieces(pieces, rows, env.stream, "split copy"); });
 }
 
 // -------------------------------------------------------------- permute
@@ -238,6 +291,24 @@ __global__ void permute_kernel(PermIdx p, const T *__restrict__ x, T *__restrict
       src += c * p.in_stride_of_out_dim[d];
     }
     y[i] = x[src];
+  }
+}
+
+// y[b][c][r] = x[b][r][c] for an R x C matrix per batch: 32x32 tiles staged
+// in shared memory (one padding column against bank conflicts).
+template <class T>
+__global__ void transpose_kernel(const T *__restrict__ x, T *__restrict__ y, int R, int C) {
+  __shared__ T tile[32][33];
+  const size_t base = size_t(blockIdx.z) * R * C;
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int r = r0 + i, c = c0 + threadIdx.x;
+    if (r < R && c < C) tile[i][threadIdx.x] = x[base + size_t(r) * C + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int c = c0 + i, r = r0 + threadIdx.x;
+    if (r < R && c < C) y[base + size_t(c) * R + r] = tile[threadIdx.x][i];
   }
 }
 
@@ -279,6 +350,27 @@ void record_permute(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   void *py = out->data();
   const long long n = out->numel;
   const int dt = in->dtype;
+  // swap of the last two dims with the leading dims in place: a batched
+  // transpose through shared-memory tiles (coalesced on both sides)
+  bool last_two = rank >= 2 && perm[rank - 1] == rank - 2 && perm[rank - 2] == rank - 1;
+  for (int d = 0; d < rank - 2; ++d) last_two = last_two && perm[d] == d;
+  if (last_two && n > 0) {
+    const long long R = in->shape[rank - 2], C = in->shape[rank - 1];
+    const long long batch = n / (R * C);
+    if (batch <= 65535 && (R + 31) / 32 <= 65535) {
+      const dim3 grid(unsigned((C + 31) / 32), unsigned((R + 31) / 32), unsigned(batch));
+      push(ctx, name, 1, [=](const ExecEnv &env) {
+        if (dt == WGX_FLOAT16)
+          transpose_kernel<__half><<<grid, dim3(32, 8), 0, env.stream>>>(
+              (const __half *)px, (__half *)py, int(R), int(C));
+        else
+          transpose_kernel<float><<<grid, dim3(32, 8), 0, env.stream>>>(
+              (const float *)px, (float *)py, int(R), int(C));
+        check_cuda(cudaGetLastError(), "permute launch");
+      });
+      return;
+    }
+  }
   push(ctx, name, 1, [=](const ExecEnv &env) {
     if (dt == WGX_FLOAT16)
       permute_kernel<__half><<<blocks_for(n), 256, 0, env.stream>>>(p, (const __half *)px,
@@ -291,39 +383,56 @@ void record_permute(wgx_context *ctx, const std::vector<wgx_arg> &a) {
 }
 
 // ------------------------------------------------------------------ bmm
-// out[b] = a[b] @ b[b]: 32x32 output tile per CTA, fp32 accumulation.
+// out[b] = a[b] @ b[b]: 64x64 output tile per CTA, each of the 256 threads
+// accumulates a 4x4 block in fp32 over K steps of 16 staged in shared
+// memory (A stored k-major so both operands are read as float4).
 template <class T>
 __global__ void __launch_bounds__(256) bmm_kernel(const T *__restrict__ A, const T *__restrict__ Bm,
                                                   T *__restrict__ C, int M, int N, int K) {
-  __shared__ float As[32][33];
-  __shared__ float Bs[32][33];
+  __shared__ __align__(16) float As[16][64 + 4];  // As[k][m]
+  __shared__ __align__(16) float Bs[16][64 + 4];  // Bs[k][n]
   const int bz = blockIdx.z;
   const T *a = A + size_t(bz) * M * K;
   const T *b = Bm + size_t(bz) * K * N;
   T *c = C + size_t(bz) * M * N;
-  const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;  // 32 x 8
-  const int m0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int k0 = 0; k0 < K; k0 += 32) {
-    for (int r = ty; r < 32; r += 8) {
-      const int m = m0 + r, k = k0 + tx;
-      As[r][tx] = (m < M && k < K) ? lf(a[size_t(m) * K + k]) : 0.f;
-      const int kk = k0 + r, n = n0 + tx;
-      Bs[r][tx] = (kk < K && n < N) ? lf(b[size_t(kk) * N + n]) : 0.f;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int k0 = 0; k0 < K; k0 += 16) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = threadIdx.x + 256 * r;
+      const int am = i / 16, ak = i % 16;
+      As[ak][am] = (m0 + am < M && k0 + ak < K) ? lf(a[size_t(m0 + am) * K + k0 + ak]) : 0.f;
+      const int bk = i / 64, bn = i % 64;
+      Bs[bk][bn] = (k0 + bk < K && n0 + bn < N) ? lf(b[size_t(k0 + bk) * N + n0 + bn]) : 0.f;
     }
     __syncthreads();
-#pragma unroll 8
-    for (int k = 0; k < 32; ++k) {
-      const float bv = Bs[k][tx];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[i] = fmaf(As[ty + 8 * i][k], bv, acc[i]);
+    for (int k = 0; k < 16; ++k) {
+      const float4 av = *reinterpret_cast<const float4 *>(&As[k][ty * 4]);
+      const float4 bv = *reinterpret_cast<const float4 *>(&Bs[k][tx * 4]);
+      const float ar[4] = {av.x, av.y, av.z, av.w}, br[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
     }
     __syncthreads();
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int m = m0 + ty + 8 * i, n = n0 + tx;
-    if (m < M && n < N) c[size_t(m) * N + n] = sf<T>(acc[i]);
+    const int m = m0 + ty * 4 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx * 4 + j;
+      if (n < N) c[size_t(m) * N + n] = sf<T>(acc[i][j]);
+    }
   }
 }
 
@@ -340,11 +449,11 @@ void record_bmm(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   if (out->shape[0] != batch || out->shape[1] != m || out->shape[2] != n)
     fail(std::string(name) + ": output shape != [" + std::to_string(batch) + ", " +
          std::to_string(m) + ", " + std::to_string(n) + "]");
-  if (batch > 65535 || (m + 31) / 32 > 65535) fail(std::string(name) + ": shape too large");
+  if (batch > 65535 || (m + 63) / 64 > 65535) fail(std::string(name) + ": shape too large");
   const void *pa = A->data(), *pb = B->data();
   void *pc = out->data();
   const int dt = A->dtype;
-  const dim3 grid(unsigned((n + 31) / 32), unsigned((m + 31) / 32), unsigned(batch));
+  const dim3 grid(unsigned((n + 63) / 64), unsigned((m + 63) / 64), unsigned(batch));
   push(ctx, name, 1, [=](const ExecEnv &env) {
     if (dt == WGX_FLOAT16)
       bmm_kernel<__half><<<grid, 256, 0, env.stream>>>((const __half *)pa, (const __half *)pb,
@@ -389,6 +498,42 @@ __global__ void maxpool_kernel(PoolGeom g, const T *__restrict__ x, T *__restric
     }
     y[i] = sf<T>(best);
     if (idx) idx[i] = best_idx;
+  }
+}
+
+// Small planes (IH*IW <= 4096): one CTA per plane stages the plane in
+// shared memory, then each thread reduces its windows from there. Same
+// start value, strict '>' and index rule as maxpool_kernel.
+template <class T>
+__global__ void __launch_bounds__(256) maxpool_plane_kernel(PoolGeom g, const T *__restrict__ x,
+                                                            T *__restrict__ y,
+                                                            int32_t *__restrict__ idx) {
+  __shared__ float tile[4096];
+  const long long plane = blockIdx.x;
+  const int hw = g.IH * g.IW;
+  const T *xp = x + plane * hw;
+  for (int i = threadIdx.x; i < hw; i += 256) tile[i] = lf(xp[i]);
+  __syncthreads();
+  const int ohw = g.OH * g.OW;
+  for (int o = threadIdx.x; o < ohw; o += 256) {
+    const int oh = o / g.OW, ow = o - oh * g.OW;
+    float best = sizeof(T) == 2 ? -65504.0f : -3.402823466e38f;
+    int best_idx = 0;
+    for (int kh = 0; kh < g.kH; ++kh) {
+      const int ih = oh * g.sH - g.pH + kh * g.dH;
+      if (ih < 0 || ih >= g.IH) continue;
+      for (int kw = 0; kw < g.kW; ++kw) {
+        const int iw = ow * g.sW - g.pW + kw * g.dW;
+        if (iw < 0 || iw >= g.IW) continue;
+        const float v = tile[ih * g.IW + iw];
+        if (v > best) {
+          best = v;
+          best_idx = ih * g.IW + iw;
+        }
+      }
+    }
+    y[plane * ohw + o] = sf<T>(best);
+    if (idx) idx[plane * ohw + o] = best_idx;
   }
 }
 
@@ -447,6 +592,19 @@ void record_maxpool(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   int32_t *pi = static_cast<int32_t *>(idx->data());
   const long long n = vals->numel;
   const int dt = in->dtype;
+  const long long planes = (long long)g.N * g.C;
+  if ((long long)g.IH * g.IW <= 4096 && planes > 0 && planes < (1ll << 31)) {
+    push(ctx, name, 1, [=](const ExecEnv &env) {
+      if (dt == WGX_FLOAT16)
+        maxpool_plane_kernel<__half><<<unsigned(planes), 256, 0, env.stream>>>(
+            g, (const __half *)px, (__half *)py, pi);
+      else
+        maxpool_plane_kernel<float><<<unsigned(planes), 256, 0, env.stream>>>(
+            g, (const float *)px, (float *)py, pi);
+      check_cuda(cudaGetLastError(), "maxpool launch");
+    });
+    return;
+  }
   push(ctx, name, 1, [=](const ExecEnv &env) {
     if (dt == WGX_FLOAT16)
       maxpool_kernel<__half><<<blocks_for(n), 256, 0, env.stream>>>(g, (const __half *)px,
@@ -557,6 +715,26 @@ __global__ void bilinear_kernel(Resample r, const T *__restrict__ x, T *__restri
   }
 }
 
+// fp16, OW % 8 == 0: each thread writes 8 consecutive outputs of one row
+// with one 16-byte store (the 8 source reads hit the same cache lines).
+__global__ void nearest_v8_kernel(Resample r, const __half *__restrict__ x, uint4 *__restrict__ y,
+                                  long long n8) {
+  const int ow8 = r.OW / 8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int g = int(i % ow8);
+    const long long t = i / ow8;
+    const int oh = int(t % r.OH);
+    const long long plane = t / r.OH;
+    const int ih = int((long long)oh * r.IH / r.OH);
+    const __half *row = x + (plane * r.IH + ih) * r.IW;
+    __align__(16) __half v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = row[int((long long)(8 * g + k) * r.IW / r.OW)];
+    y[i] = *reinterpret_cast<const uint4 *>(v);
+  }
+}
+
 void record_nearest(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   const char *name = "aten.upsample_nearest2d.vec";
   wgx_tensor *in = tensor_at(a, 0, name), *out = tensor_at(a, 3, name);
@@ -572,6 +750,15 @@ void record_nearest(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   void *py = out->data();
   const long long n = out->numel;
   const int dt = in->dtype;
+  if (dt == WGX_FLOAT16 && r.OW % 8 == 0 && (reinterpret_cast<uintptr_t>(py) & 15) == 0) {
+    const long long n8 = n / 8;
+    push(ctx, name, 1, [=](const ExecEnv &env) {
+      nearest_v8_kernel<<<blocks_for(n8), 256, 0, env.stream>>>(r, (const __half *)px,
+                                                                (uint4 *)py, n8);
+      check_cuda(cudaGetLastError(), "upsample launch");
+    });
+    return;
+  }
   push(ctx, name, 1, [=](const ExecEnv &env) {
     if (dt == WGX_FLOAT16)
       nearest_kernel<__half><<<blocks_for(n), 256, 0, env.stream>>>(r, (const __half *)px,

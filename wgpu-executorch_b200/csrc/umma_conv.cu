@@ -995,6 +995,7 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   if (n_w64 >= (1ull << 31)) fail("conv2d: weights too large for the tensor-core path");
   const int n_w = int(n_w64);
   const bool strided = g.sH != 1 || g.sW != 1;
+  const int th_pack = timer_begin("umma_conv_pack", stream);
   if (strided) {
     if (w_to_pack)
       pack_weights<<<unsigned((n_w + 255) / 256), 256, 0, stream>>>(
@@ -1039,6 +1040,7 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
     }
   }
   check_cuda(cudaGetLastError(), "pack_input launch");
+  timer_end(th_pack, stream);
   uint32_t smem = smem_bytes(g);
   using KernelFn = void (*)(const UmmaGeom, const uint8_t *, const uint8_t *, const __half *,
                            __half *);

@@ -251,7 +251,8 @@ _CONV_VARIANTS = {
 
 
 class _Shaders:
-    """``shaders`` namespace (src/shaders/index.ts:39-55)."""
+    """``shaders`` namespace (src/shaders/index.ts:39-60): every operator of
+    the reference's registry, recorded through wgx_record_op."""
     mm = _native_shader("aten.mm.default", {"umma": "tcgen05 GEMM (fp16)",
                                             "simt": "FFMA GEMM (fp32)"})
     convolution = _native_shader("aten.convolution.default", _CONV_VARIANTS)
@@ -262,6 +263,28 @@ class _Shaders:
     sigmoid = _native_shader("aten.sigmoid.default", {"elementwise": ""})
     relu = _native_shader("aten.relu.default", {"elementwise": ""})
     hardswish = _native_shader("aten.hardswish.default", {"elementwise": ""})
+    # linear algebra & reductions
+    bmm = _native_shader("aten.bmm.default", {"simt64": "64x64 FFMA tiles"})
+    meanDim = _native_shader("aten.mean.dim", {"warpPerLine": ""})
+    softmax = _native_shader("aten._softmax.default", {"warpPerLine": ""})
+    # pooling & resampling
+    maxPool2d = _native_shader("aten.max_pool2d_with_indices.default",
+                               {"plane": "whole plane in shared memory", "generic": ""})
+    upsampleBilinear2d = _native_shader("aten.upsample_bilinear2d.vec", {"generic": ""})
+    upsampleNearest2d = _native_shader("aten.upsample_nearest2d.vec",
+                                       {"vec8": "16-byte stores", "generic": ""})
+    # shape & data movement
+    cat = _native_shader("aten.cat.default", {"multiCopy": "one 16-byte gather launch"})
+    constantPadNd = _native_shader("aten.constant_pad_nd.default", {"generic": ""})
+    splitWithSizesCopy = _native_shader("aten.split_with_sizes_copy.default",
+                                        {"multiCopy": "one 16-byte gather launch"})
+    permuteCopy = _native_shader("aten.permute_copy.default",
+                                 {"transpose": "32x32 shared-memory tiles", "generic": ""})
+    viewCopy = _native_shader("aten.view_copy.default", {"flatCopy": ""})
+    clone = _native_shader("aten.clone.default", {"flatCopy": ""})
+    squeezeCopy = _native_shader("aten.squeeze_copy.dims", {"flatCopy": ""})
+    unsqueezeCopy = _native_shader("aten.unsqueeze_copy.default", {"flatCopy": ""})
+    prepack = _native_shader("et_vk.prepack.default", {"flatCopy": ""})
 
     def __iter__(self):
         for k, v in vars(type(self)).items():
