@@ -87,6 +87,12 @@ DENSE_F16 = [
     (1, 96, 40, 40, 96, 3, 3, 1, 1),
     (8, 64, 48, 48, 192, 3, 3, 1, 1),     # streamed weights, >1 tile per CTA
     (3, 16, 30, 30, 24, 5, 3, 2, 1),      # KH != KW with padding
+    # OC <= 64: positions on the MMA M side (N = 16 / 32 / 64)
+    (2, 64, 40, 40, 64, 3, 3, 1, 1),
+    (2, 48, 33, 35, 17, 1, 1, 0, 1),
+    (1, 32, 24, 40, 1, 1, 1, 0, 1),       # one output channel
+    (2, 16, 26, 26, 8, 3, 3, 1, 1),       # 16-channel stages, 8 M blocks per tile
+    (1, 96, 20, 20, 40, 5, 5, 2, 1),
 ]
 
 

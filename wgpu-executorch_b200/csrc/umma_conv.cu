@@ -70,6 +70,13 @@ struct UmmaGeom {
   int B, IC, IH, IW, OC, OH, OW, KH, KW, dH, dW, pH, pW;
   int sH, sW, xIC, xKH, xKW, xpH, xpW;
   int nphH, nphW, phH[4], phW[4];    // input phases the filter touches
+  // trans = 1: positions on the MMA M side (128 per MMA, G M-blocks per
+  // tile), output channels on N (NT = OC rounded up to 16/32/64). Used for
+  // OC <= 64, where channels on M would leave TMEM lane quadrants idle.
+  int trans, NT, G, lgNT;
+  int tile_pos;                      // output positions per tile
+  int wrows;                         // packed weight rows per oc tile (UM or NT)
+  int acc_cols;                      // TMEM columns per accumulator
   int bk, chunks;                    // channels per stage, 16-byte chunks per stage
   int khs, n_khg;                    // filter rows per stage, filter-row groups
   int Hp, Wp, C8, ncb, n_oct, tiles_per_img, total_tiles, R, R_alloc, stages, n_kstages;
@@ -103,8 +110,25 @@ static void phases(int K, int pad, int s, int &n, int *ph, int &d0, int &d1) {
   d1 = floor_div(K - 1 - pad, s);
 }
 
-static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk) {
+static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans) {
   UmmaGeom g{};
+  g.trans = trans;
+  if (trans) {
+    // G M blocks per tile, interleaved MMA by MMA: 8 for N = 16 / 32, 4 for
+    // N = 64 (a tile's accumulator then spans 128 or 256 TMEM columns)
+    g.NT = p.OC <= 16 ? 16 : p.OC <= 32 ? 32 : 64;
+    g.lgNT = g.NT == 16 ? 4 : g.NT == 32 ? 5 : 6;
+    g.G = g.NT == 64 ? 4 : 8;
+    g.tile_pos = 128 * g.G;
+    g.wrows = g.NT;
+    g.acc_cols = g.G * g.NT;
+  } else {
+    g.NT = UN;
+    g.G = 1;
+    g.tile_pos = UN;
+    g.wrows = UM;
+    g.acc_cols = UN;
+  }
   g.B = p.B;
   g.IH = p.IH;
   g.IW = p.IW;
@@ -149,15 +173,15 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk) {
   g.n_khg = g.KH / khs;
   g.C8 = (g.IC + bk - 1) / bk * bk;
   g.ncb = g.C8 / bk;
-  g.n_oct = (p.OC + UM - 1) / UM;
+  g.n_oct = (p.OC + g.wrows - 1) / g.wrows;
   g.plane_rows = (long long)g.Hp * g.Wp;
   long long p_out = (long long)(p.OH - 1) * g.Wp + p.OW;
-  g.tiles_per_img = int((p_out + UN - 1) / UN);
+  g.tiles_per_img = int((p_out + g.tile_pos - 1) / g.tile_pos);
   g.total_tiles = g.tiles_per_img * g.n_oct * g.B;
-  long long r = UN + (long long)(khs - 1) * g.dH * g.Wp + (long long)(g.KW - 1) * g.dW;
+  long long r = g.tile_pos + (long long)(khs - 1) * g.dH * g.Wp + (long long)(g.KW - 1) * g.dW;
   g.R = r > (1 << 20) ? (1 << 20) : int(r);
   g.R_alloc = (g.R + 7) / 8 * 8;
-  g.a_stage_bytes = uint32_t(khs * g.KW) * g.chunks * UM * 16;
+  g.a_stage_bytes = uint32_t(khs * g.KW) * g.chunks * g.wrows * 16;
   g.b_stage_bytes = uint32_t(g.chunks) * g.R_alloc * 16;
   g.n_kstages = g.n_khg * g.ncb;
   // resident weights: one oc tile, all stages' A blocks plus >= 2 B stages
@@ -206,7 +230,8 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p) {
   // (khs, bk); khs 0 = the whole filter. Below 16 (virtual) channels,
   // 16-channel stages halve the zero padding of the K dimension.
   int cand[3][2] = {{1, 32}, {0, 16}, {1, 16}};
-  if (geom_for(p, 1, 32).IC <= 16) {
+  const int trans = p.OC <= 64 ? 1 : 0;
+  if (geom_for(p, 1, 32, trans).IC <= 16) {
     cand[0][1] = 16;
     cand[2][1] = 32;
   }
@@ -214,7 +239,7 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p) {
   bool have = false;
   for (int min_stages : {3, 2}) {
     for (auto &c : cand) {
-      UmmaGeom g = geom_for(p, c[0], c[1]);
+      UmmaGeom g = geom_for(p, c[0], c[1], trans);
       if (g.stages >= min_stages && smem_need(g) <= SMEM_MAX && g.R_alloc * 16 < (1 << 18)) {
         return g;
       }
@@ -257,7 +282,7 @@ bool umma_conv_supported(const wgx_conv2d_params &p) {
   if (g.R_alloc * 16 >= (1 << 18)) return false;  // LBO field range
   if (g.total_tiles < 1) return false;
   // positions and per-image output offsets are handled in 32-bit integers
-  if ((long long)g.tiles_per_img * UN + g.plane_rows >= (1ll << 31)) return false;
+  if ((long long)g.tiles_per_img * g.tile_pos + g.plane_rows >= (1ll << 31)) return false;
   if ((long long)g.OH * g.OW >= (1ll << 31)) return false;
   return true;
 }
@@ -280,11 +305,11 @@ uint64_t umma_conv_packed_weight_bytes(const wgx_conv2d_params &p) {
 }
 
 // Rows the main kernel may read: the last tile's B stage of the last filter
-// row starts at (tiles-1)*UN + (KH-1)*dH*Wp and spans R rows. Rows past the
+// row starts at (tiles-1)*tile_pos + (KH-1)*dH*Wp and spans R rows. Rows past the
 // image only feed output positions that are discarded.
 static uint64_t input_rows_total(const UmmaGeom &g) {
   uint64_t planes = uint64_t(g.B) * (g.C8 / 8);
-  uint64_t last_end = uint64_t(g.tiles_per_img - 1) * UN +
+  uint64_t last_end = uint64_t(g.tiles_per_img - 1) * g.tile_pos +
                       uint64_t(g.n_khg - 1) * g.khs * g.dH * g.Wp + g.R;
   uint64_t slack = last_end > uint64_t(g.plane_rows) ? last_end - g.plane_rows : 0;
   return planes * g.plane_rows + slack;
@@ -446,12 +471,12 @@ __global__ void __launch_bounds__(256, 4)
   }
 }
 
-// packed[oct][khg][cb][kh_local][kw][chunk][row 0..127][8] <- w[oc][c][kh][kw]
+// packed[oct][khg][cb][kh_local][kw][chunk][row < wrows][8] <- w[oc][c][kh][kw]
 // (kh = khg*khs + kh_local): one pipeline stage's A operand is contiguous.
 __device__ __forceinline__ void pack_weights_body(const UmmaGeom &g, const __half *__restrict__ w,
                                                   uint4 *__restrict__ packed, int i) {
-  const int row = i % UM;
-  int t = i / UM;
+  const int row = i % g.wrows;
+  int t = i / g.wrows;
   const int chunk = t % g.chunks;
   t /= g.chunks;
   const int kw = t % g.KW;
@@ -463,7 +488,7 @@ __device__ __forceinline__ void pack_weights_body(const UmmaGeom &g, const __hal
   const int khg = t % g.n_khg;
   const int oct = t / g.n_khg;
   const int kh = khg * g.khs + khl;
-  const int oc = oct * UM + row;
+  const int oc = oct * g.wrows + row;
   __align__(16) __half v[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
@@ -697,6 +722,28 @@ __device__ __forceinline__ float epi_act(float acc, float bias, float hb, float 
   }
 }
 
+// Two epilogue values (with their biases) -> packed fp16x2. SiLU runs in
+// half precision after one rounding of h = (acc + bias)/2: one
+// tanh.approx.f16x2 for both values and y = h + h*tanh(h) as one HFMA2
+// (the output is fp16, so the half-precision tail adds at most about one
+// fp16 rounding); the other activations round once from fp32.
+template <int ACT>
+__device__ __forceinline__ uint32_t epi_act2(float a0, float a1, float b0, float b1, float lo,
+                                             float hi) {
+  if constexpr (ACT == WGX_ACT_SILU) {
+    const __half2 h = __floats2half2_rn(fmaf(a0, 0.5f, 0.5f * b0), fmaf(a1, 0.5f, 0.5f * b1));
+    const uint32_t hu = *reinterpret_cast<const uint32_t *>(&h);
+    uint32_t tu;
+    asm("tanh.approx.f16x2 %0, %1;" : "=r"(tu) : "r"(hu));
+    const __half2 y = __hfma2(h, *reinterpret_cast<const __half2 *>(&tu), h);
+    return *reinterpret_cast<const uint32_t *>(&y);
+  } else {
+    const __half2 y = __floats2half2_rn(epi_act<ACT>(a0, b0, 0.f, lo, hi),
+                                        epi_act<ACT>(a1, b1, 0.f, lo, hi));
+    return *reinterpret_cast<const uint32_t *>(&y);
+  }
+}
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -708,14 +755,17 @@ __device__ __forceinline__ void tile_coords(const UmmaGeom &g, int t, int &b, lo
   oct = t % g.n_oct;
   const int rest = t / g.n_oct;
   b = rest / g.tiles_per_img;
-  p0 = (long long)(rest % g.tiles_per_img) * UN;
+  p0 = (long long)(rest % g.tiles_per_img) * g.tile_pos;
 }
 
 // ------------------------------------------------------------ main kernel
 // KW_T > 0: compile-time filter width with one filter row and 32 channels
 // per stage (the common staging); the MMA issue loop is then fully unrolled
 // over precomputed descriptor offsets. KW_T == 0: any staging, runtime loops.
-template <int KW_T, int ACT_T>
+// TRANS (geometry trans = 1): positions are the MMA's M rows and output
+// channels its N columns; the staged activation rows become the A operand
+// and the packed weights the B operand, with no change to either layout.
+template <int KW_T, int ACT_T, int TRANS>
 __global__ void __launch_bounds__(THREADS, 1)
     umma_conv_kernel(const UmmaGeom g, const uint8_t *__restrict__ xs,
                      const uint8_t *__restrict__ wpk, const __half *__restrict__ bias,
@@ -799,11 +849,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
-      const uint32_t idesc = (1u << 4)                      // D = f32
-                             | (uint32_t(UN >> 3) << 17)    // N
-                             | (uint32_t(UM >> 4) << 24);   // M; A,B f16 K-major
-      const uint32_t a_lbo = UM * 16;                       // chunk plane of A
-      const uint32_t b_lbo = uint32_t(g.R_alloc) * 16;      // chunk plane of B
+      // (a = packed weights, b = staged activation rows, whichever MMA
+      // operand slot they take)
+      const uint32_t idesc = (1u << 4)                                  // D = f32
+                             | (uint32_t((TRANS ? g.NT : UN) >> 3) << 17)  // N
+                             | (uint32_t(128 >> 4) << 24);              // M; f16 K-major
+      const uint32_t a_lbo = uint32_t(g.wrows) * 16;        // chunk plane of the weights
+      const uint32_t b_lbo = uint32_t(g.R_alloc) * 16;      // chunk plane of the activations
       bool ok = true;
       if (g.resident && !mbar_wait(smem_u32(wbar), 0)) {
         atomicOr(g.err, kErrMmaTimeout);
@@ -817,7 +869,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int kw = 0; kw < KW_T; ++kw)
 #pragma unroll
           for (int ks = 0; ks < 2; ++ks) {
-            a_off[2 * kw + ks] = (uint32_t(kw) * 4 * UM * 16 + uint32_t(ks) * 2 * a_lbo) >> 4;
+            a_off[2 * kw + ks] = (uint32_t(kw) * 4 * a_lbo + uint32_t(ks) * 2 * a_lbo) >> 4;
             b_off[2 * kw + ks] = (uint32_t(kw * g.dW) * 16 + uint32_t(ks) * 2 * b_lbo) >> 4;
           }
       }
@@ -830,7 +882,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + uint32_t(acc * UN);
+        const uint32_t d = tmem + uint32_t(acc * g.acc_cols);
         for (int s = 0; s < g.n_kstages; ++s, ++gs) {
           const int slot = gs % S, use = gs / S;
           if (!mbar_wait(smem_u32(&full[slot]), use & 1)) {
@@ -846,9 +898,21 @@ __global__ void __launch_bounds__(THREADS, 1)
             // descriptors differ from the stage's base descriptors only in
             // the start-address field: add precomputed (offset >> 4) values
             const uint64_t a0 = kmajor_desc(a_base, a_lbo), b0 = kmajor_desc(b_base, b_lbo);
+            if constexpr (TRANS) {
+              // M-block mb: activation rows mb*128.., accumulator columns
+              // mb*NT..; M blocks innermost so that consecutive MMAs feed
+              // different accumulators (a short MMA would otherwise wait on
+              // the previous one's accumulation)
 #pragma unroll
-            for (int i = 0; i < 2 * KW_T; ++i)
-              mma_f16(d, a0 + a_off[i], b0 + b_off[i], idesc, (s | i) != 0);
+              for (int i = 0; i < 2 * KW_T; ++i)
+                for (int mb = 0; mb < g.G; ++mb)
+                  mma_f16(d + uint32_t(mb * g.NT), b0 + uint64_t(mb * 128) + b_off[i],
+                          a0 + a_off[i], idesc, (s | i) != 0);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 2 * KW_T; ++i)
+                mma_f16(d, a0 + a_off[i], b0 + b_off[i], idesc, (s | i) != 0);
+            }
             mma_commit(smem_u32(&empty[slot]));
             continue;
           }
@@ -856,19 +920,90 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int khl = 0; khl < g.khs; ++khl) {
             for (int kw = 0; kw < g.KW; ++kw) {
               const uint32_t tap = uint32_t(khl * g.KW + kw);
-              const uint32_t shift = uint32_t(khl * g.dH * g.Wp + kw * g.dW);  // B row shift
+              // activation row shift of this tap
+              const uint32_t shift = uint32_t(khl * g.dH * g.Wp + kw * g.dW);
               for (int ks = 0; ks < ksteps; ++ks) {
-                const uint64_t adesc = kmajor_desc(
-                    a_base + tap * uint32_t(g.chunks) * UM * 16 + ks * 2 * a_lbo, a_lbo);
-                const uint64_t bdesc =
-                    kmajor_desc(b_base + shift * 16 + ks * 2 * b_lbo, b_lbo);
-                mma_f16(d, adesc, bdesc, idesc, (s | khl | kw | ks) != 0);
+                const uint64_t wdesc = kmajor_desc(
+                    a_base + tap * uint32_t(g.chunks) * a_lbo + ks * 2 * a_lbo, a_lbo);
+                const uint64_t xdesc = kmajor_desc(b_base + shift * 16 + ks * 2 * b_lbo, b_lbo);
+                const uint32_t acc_flag = (s | khl | kw | ks) != 0;
+                if constexpr (TRANS) {
+                  // M blocks innermost (see the specialised path)
+                  for (int mb = 0; mb < g.G; ++mb)
+                    mma_f16(d + uint32_t(mb * g.NT), xdesc + uint64_t(mb * 128), wdesc, idesc,
+                            acc_flag);
+                } else {
+                  mma_f16(d, wdesc, xdesc, idesc, acc_flag);
+                }
               }
             }
           }
           mma_commit(smem_u32(&empty[slot]));
         }
         if (ok) mma_commit(smem_u32(&accf[acc]));
+      }
+    }
+  } else if (warp >= EPI_WARP0 && TRANS) {
+    // ---------------- epilogue (positions on TMEM lanes): warp w reads lane
+    // quadrant w % 4 (32 positions of every M block) and 32 of the 128
+    // accumulator columns; column c is channel c % NT of M block c / NT.
+    // For each channel the warp stores 32 consecutive positions (64 bytes
+    // of one output row unless the block wraps a row).
+    const int ew = warp - EPI_WARP0;
+    const int q = warp & 3, cq = ew / 4;
+    const size_t plane = size_t(g.OH) * g.OW;
+    // bias (and its half, for SiLU) of the NT channels, staged once in the
+    // otherwise unused epilogue staging area
+    float *sbias = reinterpret_cast<float *>(sE);
+    for (int i = threadIdx.x - EPI_WARP0 * 32; i < g.NT; i += EPI_WARPS * 32)
+      sbias[i] = (g.has_bias && i < g.OC) ? __half2float(bias[i]) : 0.f;
+    asm volatile("bar.sync 1, %0;" ::"r"(EPI_WARPS * 32) : "memory");
+    float r[32];
+    int it = 0;
+    for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++it) {
+      const int acc = it & 1, use_acc = it >> 1;
+      int b, oct;
+      long long p0;
+      tile_coords(g, t, b, p0, oct);
+      if (!mbar_wait(smem_u32(&accf[acc]), use_acc & 1)) {
+        if (lane == 0) atomicOr(g.err, kErrEpilogueTimeout);
+        break;
+      }
+      tc_fence_after();
+      // the warp's acc_cols / 4 columns, in chunks of 32
+      const int nchunk = g.acc_cols / 128;
+      __half *base = out + size_t(b) * g.OC * plane;
+      for (int h = 0; h < nchunk; ++h) {
+        const int c0 = cq * (g.acc_cols / 4) + h * 32;
+        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * g.acc_cols + c0), r);
+        if (h == nchunk - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
+        }
+        // 32 columns cover one M block (NT >= 32) or two (NT = 16)
+        const int mb0 = c0 >> g.lgNT, mb1 = (c0 + 31) >> g.lgNT;
+        const int pos_a = int(p0) + mb0 * 128 + q * 32 + lane;
+        const int pos_b = int(p0) + mb1 * 128 + q * 32 + lane;
+        const int oh_a = pos_a / g.Wp, ow_a = pos_a - oh_a * g.Wp;
+        const int oh_b = pos_b / g.Wp, ow_b = pos_b - oh_b * g.Wp;
+        const bool ok_a = oh_a < g.OH && ow_a < g.OW, ok_b = oh_b < g.OH && ow_b < g.OW;
+        __half *dst_a = base + size_t(oh_a) * g.OW + ow_a;
+        __half *dst_b = base + size_t(oh_b) * g.OW + ow_b;
+        // columns j, j+1: channels oc, oc+1 of the same position (NT is even)
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const int c = c0 + j;
+          const int oc = c & (g.NT - 1);
+          const bool second = (c >> g.lgNT) != mb0;
+          const uint32_t pr = epi_act2<ACT_T>(r[j], r[j + 1], sbias[oc], sbias[oc + 1], g.lo, g.hi);
+          const __half2 h2 = *reinterpret_cast<const __half2 *>(&pr);
+          if (second ? ok_b : ok_a) {
+            __half *d = (second ? dst_b : dst_a) + size_t(oc) * plane;
+            if (oc < g.OC) d[0] = __low2half(h2);
+            if (oc + 1 < g.OC) d[plane] = __high2half(h2);
+          }
+        }
       }
     }
   } else if (warp >= EPI_WARP0) {
@@ -903,7 +1038,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int oc0 = oct * UM + q * 32;  // first channel of this quadrant
       const int oc_lane = oc0 + lane;
       const float bv = (g.has_bias && oc_lane < g.OC) ? __half2float(bias[oc_lane]) : 0.f;
-      const float hb = 0.5f * bv;
       const int nrows = min(32, g.OC - oc0);  // valid channel rows of the quadrant
       // this lane stores rows rsel, rsel+4, ..., rsel+28 of the quadrant
       __half *rowp = out + (size_t(b) * g.OC + oc0 + rsel) * plane;
@@ -913,7 +1047,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       constexpr int NBLK = WCOLS / EPI_COLS;
       for (int blk = 0; blk < NBLK; ++blk) {
         const int col0 = colh * WCOLS + blk * EPI_COLS;
-        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * UN + col0), r);
+        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * g.acc_cols + col0), r);
         if (blk == NBLK - 1) {
           // all TMEM reads of this accumulator are done: hand it back
           tc_fence_before();
@@ -922,11 +1056,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         uint32_t pw[EPI_COLS / 2];
 #pragma unroll
-        for (int j = 0; j < EPI_COLS / 2; ++j) {
-          __half2 h2 = __floats2half2_rn(epi_act<ACT_T>(r[2 * j], bv, hb, g.lo, g.hi),
-                                         epi_act<ACT_T>(r[2 * j + 1], bv, hb, g.lo, g.hi));
-          pw[j] = *reinterpret_cast<uint32_t *>(&h2);
-        }
+        for (int j = 0; j < EPI_COLS / 2; ++j)
+          pw[j] = epi_act2<ACT_T>(r[2 * j], r[2 * j + 1], bv, bv, g.lo, g.hi);
         uint4 *dst = reinterpret_cast<uint4 *>(stage + lane * EPI_ROWB);
         dst[0] = make_uint4(pw[0], pw[1], pw[2], pw[3]);
         dst[1] = make_uint4(pw[4], pw[5], pw[6], pw[7]);
@@ -1046,21 +1177,22 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
                            __half *);
   // specialisations: filter width (1/3/5/7, per-row 32-channel staging) x
   // epilogue activation
-  static const KernelFn table[7][3] = {
-      {umma_conv_kernel<0, 0>, umma_conv_kernel<0, 1>, umma_conv_kernel<0, 2>},
-      {umma_conv_kernel<1, 0>, umma_conv_kernel<1, 1>, umma_conv_kernel<1, 2>},
-      {umma_conv_kernel<2, 0>, umma_conv_kernel<2, 1>, umma_conv_kernel<2, 2>},
-      {umma_conv_kernel<3, 0>, umma_conv_kernel<3, 1>, umma_conv_kernel<3, 2>},
-      {umma_conv_kernel<4, 0>, umma_conv_kernel<4, 1>, umma_conv_kernel<4, 2>},
-      {umma_conv_kernel<5, 0>, umma_conv_kernel<5, 1>, umma_conv_kernel<5, 2>},
-      {umma_conv_kernel<7, 0>, umma_conv_kernel<7, 1>, umma_conv_kernel<7, 2>}};
+#define WGX_UMMA_ROW(KW, T) \
+  { umma_conv_kernel<KW, 0, T>, umma_conv_kernel<KW, 1, T>, umma_conv_kernel<KW, 2, T> }
+  static const KernelFn table[2][7][3] = {
+      {WGX_UMMA_ROW(0, 0), WGX_UMMA_ROW(1, 0), WGX_UMMA_ROW(2, 0), WGX_UMMA_ROW(3, 0),
+       WGX_UMMA_ROW(4, 0), WGX_UMMA_ROW(5, 0), WGX_UMMA_ROW(7, 0)},
+      {WGX_UMMA_ROW(0, 1), WGX_UMMA_ROW(1, 1), WGX_UMMA_ROW(2, 1), WGX_UMMA_ROW(3, 1),
+       WGX_UMMA_ROW(0, 1), WGX_UMMA_ROW(0, 1), WGX_UMMA_ROW(0, 1)}};
+#undef WGX_UMMA_ROW
   int kw_idx = 0;
   if (g.khs == 1 && g.bk == 32)
     kw_idx = g.KW == 7 ? 6 : (g.KW >= 1 && g.KW <= 5) ? g.KW : 0;
+  if (g.trans && kw_idx > 3) kw_idx = 0;  // transposed: specialised for KW <= 3 only
   const int act_idx = (g.act >= 0 && g.act <= 2) ? g.act : 0;
-  KernelFn kern = table[kw_idx][act_idx];
-  const int kidx = kw_idx * 3 + act_idx;
-  static bool attr_set[64][21] = {};
+  KernelFn kern = table[g.trans][kw_idx][act_idx];
+  const int kidx = (g.trans * 7 + kw_idx) * 3 + act_idx;
+  static bool attr_set[64][42] = {};
   if (dev < 64 && !attr_set[dev][kidx]) {
     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(SMEM_MAX)),
