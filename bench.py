@@ -1,30 +1,38 @@
 #!/usr/bin/env python3
-"""Benchmark of the B200 hot path (one JSON line on rank 0).
+"""Benchmark of the B200 engine (one JSON line on rank 0).
 
-Workload: BASELINE config 2, the single fp16 aten.convolution with fused
-SiLU: input [8,64,160,160] N(0,1), weight [128,64,3,3] Kaiming-normal, bias
-N(0,0.01), stride 1, pad 1; 8 images per GPU (weak scaling, batch-sharded,
-no collective on the data path).
+Headline workload: the YOLO26-N-shaped detector, fp16,
+640x640 input, 64 images per GPU (weak scaling: the batch is sharded across
+GPUs, one process and one CUDA graph per GPU, no collective on the data
+path). The program is the reference's shipped YOLO26-N export converted to
+fp16 (its convert_model_to_fp16 output), lifted to batch 64
+(wgx.programs.batch_lift) and given seeded Kaiming-normal random-init
+weights (wgx.programs.random_init, seed 0); inputs are seeded U[0,1) images.
 
-* ``value``: TFLOP/s of the whole job with inputs resident in HBM. One step =
-  one call of the C-ABI entry point ``wgx_conv2d`` (weight packing, input
-  re-layout, tcgen05 implicit GEMM + bias + SiLU epilogue). Before every
-  step, outside the per-step CUDA events, L2 is flushed: a 256 MiB buffer is
-  written (evicting the step's data) and a second 256 MiB buffer is read
-  (forcing the write-back of those dirty lines), so the step starts with an
-  L2 that holds none of its inputs and owes no write-back.
-* ``e2e``: the same metric through the public API a user calls: a Program
-  (convolution -> sigmoid -> mul, fused by the engine into one kernel)
-  recorded with recordProgram; every step uploads the input from pinned
-  host memory (setData), submits, and reads the output back (getData).
-* ``roofline``: the tcgen05 conv kernel's own CUDA-event time inside the
-  timed region against the measured dense bf16 peak.
-* ``cpu_baseline``: the CPU port of the reference's WGSL arithmetic
-  (oracle/, fp16 per-operation rounding, all host threads) on a bounded
-  sample of the same workload, rank 0 at N = 1 only.
+* ``value``: images/s of the whole job with the input resident in HBM. One
+  step = one ``submit()`` of the recorded program (one CUDA-graph launch of
+  every kernel of the model). The step's input (157 MB) and its working set
+  (GBs of activations) exceed L2, so no flush is needed between steps.
+* ``e2e``: the same metric through the public API with host buffers: every
+  step uploads the batch from pinned host memory (``setData``), submits and
+  reads the detections back (``getDataInto``).
+* ``roofline``: the tcgen05 convolution kernel (umma_conv_kernel), which
+  runs every dense convolution of the model: algorithmic bytes of those
+  convolutions (input + weights + bias + output, fp16) over that kernel's
+  CUDA-event time, measured by replaying the same recorded program eagerly
+  with events around every launch; YOLO-shaped convolutions sit below the
+  fp16 ridge, so the bound is HBM bandwidth.
+* ``cpu_baseline``: the CPU program oracle (oracle/program_oracle.py: the
+  reference operators restated in C and numpy, all host threads) on one
+  image of the same program, rank 0 at N = 1 only.
+* ``kernels``: the single-kernel configurations of the metric's
+  "conv/mm TFLOP/s vs roofline" part: configs[1] (fp16 conv + SiLU),
+  configs[2] (depthwise 5x5 + 1x1 pointwise) and configs[0] (fp32 mm), each
+  timed with CUDA events with L2 flushed between steps.
 
-``--impl reference`` times only that CPU port of the reference
-implementation (rank 0; other ranks exit), on the same metric and config.
+``--impl reference`` times only the CPU program oracle (rank 0; other ranks
+exit) on the same metric and config; WebGPU is unavailable on this box, so
+that CPU restatement stands in for the reference's own path.
 """
 from __future__ import annotations
 
@@ -44,29 +52,19 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "wgpu-executorch_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
-METRIC = None
 with open(os.path.join(ROOT, "BASELINE.json")) as _f:
     METRIC = json.load(_f)["metric"]
 
-B, IC, H, W, OC, K, PAD = 8, 64, 160, 160, 128, 3, 1
-FLOP_PER_IMAGE = 2.0 * OC * H * W * IC * K * K
-FLOP_PER_STEP = FLOP_PER_IMAGE * B
-IN_BYTES, OUT_BYTES = B * IC * H * W * 2, B * OC * H * W * 2
-W_BYTES, BIAS_BYTES = OC * IC * K * K * 2, OC * 2
-WORKLOAD = ("BASELINE configs[1]: aten.convolution fp16 NCHW [8,64,160,160] x [128,64,3,3] "
-            "stride 1 pad 1 + bias + fused SiLU, 8 images per GPU")
-DATA = "synthetic: seeded N(0,1) input, Kaiming-normal weight, N(0,0.01) bias (numpy PCG64)"
+PER_GPU = 64
+HW = 640
+MODEL_DIR = os.path.join(ROOT, "tests", "golden", "_assets", "yolo26n")
+WORKLOAD = ("BASELINE configs[3]: YOLO26-N-shaped detector fp16, input [64,3,640,640] per GPU "
+            "(shipped export converted to fp16, batch-lifted, seeded random-init weights)")
+DATA = ("synthetic: seeded U[0,1) images, seeded Kaiming-normal conv weights / N(0,0.01) biases "
+        "(no checkpoint)")
 FLUSH_BYTES = 256 << 20
-
-
-def synthetic_inputs(seed: int):
-    rng = np.random.default_rng(seed)
-    x = rng.standard_normal((B, IC, H, W), dtype=np.float32).astype(np.float16)
-    w = (rng.standard_normal((OC, IC, K, K), dtype=np.float32) *
-         np.sqrt(2.0 / (IC * K * K))).astype(np.float16)
-    b = (rng.standard_normal((OC,), dtype=np.float32) * 0.01).astype(np.float16)
-    return x, w, b
 
 
 def peaks():
@@ -77,13 +75,61 @@ def peaks():
     return 1590.0, 6650.0, "fallback"
 
 
-def profiled_traffic():
-    """Per-launch DRAM bytes of the conv kernel from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "umma_conv_kernel_config2.md")
+def profiled(name, key):
+    """A number recorded in a committed ncu summary under profiles/."""
+    p = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(p):
         return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(p).read())
-    return int(m.group(1)) if m else None
+    m = re.search(key + r":\s*([0-9.]+)", open(p).read())
+    return float(m.group(1)) if m else None
+
+
+# ------------------------------------------------------------ model
+def load_model(batch):
+    """(batch-1 program, batch-`batch` program, weights image)."""
+    from wgx import programs
+    prog_path = os.path.join(MODEL_DIR, "program-fp16.json")
+    if not os.path.exists(prog_path):
+        sys.path.insert(0, ROOT)
+        import __graft_entry__
+        __graft_entry__.copy_assets()
+    if not os.path.exists(prog_path):
+        raise SystemExit(f"{prog_path} missing: run __graft_entry__.build() where the reference "
+                         "checkout is available")
+    prog = json.load(open(prog_path))
+    w = open(os.path.join(MODEL_DIR, "weights-fp16.bin"), "rb").read()
+    w = programs.random_init(prog, w, seed=0)
+    return prog, programs.batch_lift(prog, batch), w
+
+
+def images(seed, shape):
+    rng = np.random.default_rng(seed)
+    return rng.random(shape, dtype=np.float32).astype(np.float16)
+
+
+def conv_work(prog):
+    """Algorithmic (flops, bytes) of the dense (groups == 1) convolutions and
+    bytes of the depthwise ones: inputs, weights, bias and output touched
+    once, fp16."""
+    v = prog["values"]
+    dense_f = dense_b = dw_b = 0.0
+    n_dense = n_dw = 0
+    for op in prog["chain"]:
+        if op["name"] not in ("aten.convolution.default", "et_vk.conv_with_clamp.default"):
+            continue
+        a = op["args"]
+        x, w, out = v[a[0]]["shape"], v[a[1]]["shape"], v[a[-1]]["shape"]
+        b = v[a[2]]["shape"] if v[a[2]]["type"] == "tensor" else [0]
+        groups = int(v[a[8]]["value"])
+        nbytes = 2.0 * (np.prod(x) + np.prod(w) + np.prod(b) + np.prod(out))
+        if groups == 1:
+            dense_f += 2.0 * np.prod(out) * np.prod(w[1:])
+            dense_b += nbytes
+            n_dense += 1
+        else:
+            dw_b += nbytes
+            n_dw += 1
+    return dense_f, dense_b, n_dense, dw_b, n_dw
 
 
 # ------------------------------------------------------------ clocks
@@ -172,86 +218,193 @@ def barrier(ws):
     torch.cuda.synchronize()
 
 
-# ---------------------------------------------------- CPU baselines
-def cpu_port_sample(x, w, b, target_s: float):
-    """Times the CPU port of the reference WGSL arithmetic (fp16 rounding per
-    operation, the conv2d-tile64-f16 summation order, sigmoid+mul in f16) on
-    one image and a slice of output channels sized to ~target_s seconds.
-    Returns (flops, seconds, sample text, threads)."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+# ---------------------------------------------------- CPU program oracle
+def cpu_runner(prog1, w):
+    import program_oracle
+    x = images(0, prog1["values"][prog1["inputIds"][0]]["shape"])
+    return program_oracle.ProgramRunner(prog1, w, [x])
+
+
+def cpu_image_rate(prog1, w):
+    """Images/s of the CPU program oracle on one image (all host threads)."""
     import oracle
-    x1 = x[:1]
+    r = cpu_runner(prog1, w)
     t0 = time.perf_counter()
-    oracle.conv2d(x1, w[:8], b[:8], 1, PAD, 1, 1, act=oracle.ACT_SILU, mode="wgsl")
-    t8 = time.perf_counter() - t0
-    oc = int(max(1, min(OC, round(8 * target_s / max(t8, 1e-6)))))
-    t0 = time.perf_counter()
-    oracle.conv2d(x1, w[:oc], b[:oc], 1, PAD, 1, 1, act=oracle.ACT_SILU, mode="wgsl")
+    r.run()
     dt = time.perf_counter() - t0
-    flops = FLOP_PER_IMAGE * oc / OC
-    return flops, dt, f"1 image x {oc} of {OC} output channels of the config", \
-        oracle.num_threads()
+    return 1.0 / dt, dt, oracle.num_threads()
 
 
 def run_reference(args, ws, rank):
+    """The CPU program oracle as the reference arm. Each step is a bounded
+    sample: the chain's ops are split into S groups of about equal CPU time
+    (S chosen so that warm-up + steps fit in about two minutes) and step i
+    re-runs group i mod S of one image on its recorded inputs; S steps make
+    one image."""
     if rank != 0:
         return 0
-    x, w, b = synthetic_inputs(0)
-    per_step = max(0.02, min(1.0, 90.0 / max(1, args.steps + args.warmup)))
-    total_f, total_t, sample, threads = 0.0, 0.0, "", 1
-    for i in range(args.warmup + args.steps):
-        f, t, sample, threads = cpu_port_sample(x, w, b, per_step)
-        if i >= args.warmup:
-            total_f += f
-            total_t += t
-    v = total_f / total_t / 1e12
+    import oracle
+    prog1, _, w = load_model(1)
+    r = cpu_runner(prog1, w)
+    n_ops = len(prog1["chain"])
+    op_t = []
+    for i in range(n_ops):
+        t0 = time.perf_counter()
+        r.run_op(i)
+        op_t.append(time.perf_counter() - t0)
+    t_img = sum(op_t)
+    n_steps = args.warmup + args.steps
+    S = max(1, min(n_ops, int(np.ceil(t_img * n_steps / 120.0))))
+    groups = [[] for _ in range(S)]
+    loads = [0.0] * S
+    for i in sorted(range(n_ops), key=lambda k: -op_t[k]):
+        g = int(np.argmin(loads))
+        groups[g].append(i)
+        loads[g] += op_t[i]
+    for g in groups:
+        g.sort()
+    total = 0.0
+    for s in range(n_steps):
+        t0 = time.perf_counter()
+        for i in groups[s % S]:
+            r.run_op(i)
+        dt = time.perf_counter() - t0
+        if s >= args.warmup:
+            total += dt
+    imgs = args.steps / S
+    v = imgs / total
+    sample = (f"1 image of the batch-1 program split into {S} op groups of equal CPU time; "
+              f"each step re-runs one group (the CPU program oracle: reference operators "
+              f"restated in C/numpy, fp64 accumulation; WebGPU/SwiftShader unavailable on this "
+              f"box)")
     line = {
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": ws,
-        "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": total_t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16", "data": DATA,
-        "config": {"workload": WORKLOAD, "global_batch": B, "per_gpu_batch": B,
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "imgs/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": DATA,
+        "config": {"workload": WORKLOAD, "global_batch": PER_GPU * ws, "per_gpu_batch": PER_GPU,
                    "parallelism": "host cores of rank 0"},
-        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                         "sample": sample + " per step (the reference's WGSL arithmetic "
-                                            "restated in C; WebGPU is unavailable on this box)"},
-        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": v, "unit": "imgs/s", "cores": oracle.num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "imgs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
+# ------------------------------------------------- single-kernel configs
+def kernel_configs(ctx, local, steps, peak_tf, peak_hbm):
+    """configs[1] conv+SiLU, configs[2] depthwise + pointwise, configs[0]
+    fp32 mm: CUDA events per launch on the context stream, L2 flushed
+    (256 MiB write + 256 MiB read) before every step, untimed."""
+    import torch
+
+    from wgx import _lib
+    dev = f"cuda:{local}"
+    ext = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    flush_rd = torch.ones(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    rng = np.random.default_rng(0)
+    out = {}
+
+    def timed(launch, n):
+        s = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        for i in range(3):
+            launch()
+        for i in range(n):
+            with torch.cuda.stream(ext):
+                flush.fill_(i)
+                flush_rd.max()
+                s[i].record(ext)
+            launch()
+            e[i].record(ext)
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in zip(s, e)) / n
+
+    def conv(B, IC, H, Wd, OC, K, s, p, g, act):
+        OH, OW = (H + 2 * p - K) // s + 1, (Wd + 2 * p - K) // s + 1
+        prm = _lib.ConvParams(B, IC, H, Wd, OC, OH, OW, K, K, s, s, p, p, 1, 1, g, 1, 1, act,
+                              -np.inf, np.inf)
+        plan = _lib.ConvPlan()
+        _lib.check(_lib.lib.wgx_conv2d_plan_for(ctypes.byref(prm), ctypes.byref(plan)))
+        x = torch.from_numpy(rng.standard_normal((B, IC, H, Wd), dtype=np.float32)).half().to(dev)
+        std = np.sqrt(2.0 / (IC // g * K * K)) if g == 1 else 0.1
+        wt = (torch.randn(OC, IC // g, K, K, device=dev) * std).half()
+        b = (torch.randn(OC, device=dev) * 0.01).half()
+        y = torch.empty(B, OC, OH, OW, device=dev, dtype=torch.float16)
+        scr = torch.empty(max(plan.scratch_bytes, 16), device=dev, dtype=torch.uint8)
+        args_c = (ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(wt.data_ptr()),
+                  ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(y.data_ptr()),
+                  ctypes.c_void_p(scr.data_ptr()), ctypes.c_uint64(plan.scratch_bytes),
+                  ctypes.c_void_p(ctx.stream))
+        pp = ctypes.byref(prm)
+        launch = lambda: _lib.check(_lib.lib.wgx_conv2d(pp, *args_c))
+        flops = 2.0 * B * OC * OH * OW * (IC // g) * K * K
+        nbytes = 2.0 * (x.numel() + wt.numel() + b.numel() + y.numel())
+        return launch, flops, nbytes, plan, (x, wt, b, y, scr)
+
+    # configs[1]: [8,64,160,160] x [128,64,3,3], s1 p1, SiLU; tensor-core bound
+    launch, flops, nbytes, plan, keep = conv(8, 64, 160, 160, 128, 3, 1, 1, 1, _lib.ACT_SILU)
+    _lib.check(_lib.lib.wgx_kernel_timing(1))
+    _lib.check(_lib.lib.wgx_kernel_timing_read(b"", None, None, 1))
+    ms = timed(launch, steps)
+    kms, kcnt = ctypes.c_double(), ctypes.c_int64()
+    _lib.check(_lib.lib.wgx_kernel_timing_read(b"umma_conv_kernel", ctypes.byref(kms),
+                                                ctypes.byref(kcnt), 1))
+    _lib.check(_lib.lib.wgx_kernel_timing(0))
+    k_ms = kms.value / max(1, kcnt.value)
+    ach = flops / (k_ms * 1e-3) / 1e12
+    out["configs[1]_conv_silu"] = {
+        "workload": "fp16 conv [8,64,160,160] x [128,64,3,3] s1 p1 + bias + SiLU",
+        "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_call": ms,
+        "roofline": {"bound": "tensor", "kernel": "umma_conv_kernel", "achieved": ach,
+                     "peak": peak_tf, "unit": "TFLOP/s", "frac": ach / peak_tf,
+                     "avg_launch_ms": k_ms, "flop_per_launch": flops,
+                     "algorithmic_bytes_per_launch": nbytes,
+                     "traffic": profiled("umma_conv_kernel_config2.md",
+                                         "traffic_bytes_per_launch")}}
+    del keep
+
+    # configs[2]: depthwise 5x5 on [16,256,80,80] then 1x1 256 -> 256
+    l_dw, f_dw, b_dw, _, keep_dw = conv(16, 256, 80, 80, 256, 5, 1, 2, 256, _lib.ACT_NONE)
+    l_pw, f_pw, b_pw, _, keep_pw = conv(16, 256, 80, 80, 256, 1, 1, 0, 1, _lib.ACT_NONE)
+    ms_dw = timed(l_dw, steps)
+    ms_pw = timed(l_pw, steps)
+    dw_gbs = b_dw / (ms_dw * 1e-3) / 1e9
+    pw_gbs = b_pw / (ms_pw * 1e-3) / 1e9
+    out["configs[2]_depthwise_pointwise"] = {
+        "workload": "fp16 depthwise [16,256,80,80] x [256,1,5,5] s1 p2 g256, then 1x1 256->256",
+        "depthwise": {"ms_per_call": ms_dw, "roofline": {
+            "bound": "hbm", "kernel": "depthwise_conv", "achieved": dw_gbs, "peak": peak_hbm,
+            "unit": "GB/s", "frac": dw_gbs / peak_hbm, "algorithmic_bytes_per_launch": b_dw,
+            "traffic": profiled("depthwise_conv_config3.md", "traffic_bytes_per_launch")}},
+        "pointwise": {"ms_per_call": ms_pw, "tflops": f_pw / (ms_pw * 1e-3) / 1e12,
+                      "roofline": {"bound": "hbm", "achieved": pw_gbs, "peak": peak_hbm,
+                                   "unit": "GB/s", "frac": pw_gbs / peak_hbm,
+                                   "algorithmic_bytes_per_launch": b_pw}}}
+    del keep_dw, keep_pw
+
+    # configs[0]: fp32 mm 512^3 (latency-bound: 268 MFLOP)
+    M = N = Kd = 512
+    a = torch.rand(M, Kd, device=dev) * 2 - 1
+    bm = torch.rand(Kd, N, device=dev) * 2 - 1
+    c = torch.empty(M, N, device=dev)
+    need = ctypes.c_uint64()
+    _lib.check(_lib.lib.wgx_mm_scratch_bytes(M, N, Kd, 0, ctypes.byref(need)))
+    scr = torch.empty(max(need.value, 16), device=dev, dtype=torch.uint8)
+    mm_args = (ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(bm.data_ptr()),
+               ctypes.c_void_p(c.data_ptr()), M, N, Kd, 0, ctypes.c_void_p(scr.data_ptr()),
+               ctypes.c_uint64(need.value), ctypes.c_void_p(ctx.stream))
+    ms_mm = timed(lambda: _lib.check(_lib.lib.wgx_mm(*mm_args)), steps)
+    out["configs[0]_mm_fp32"] = {"workload": "fp32 mm [512,512] @ [512,512]",
+                                 "value": 2.0 * M * N * Kd / (ms_mm * 1e-3) / 1e12,
+                                 "unit": "TFLOP/s", "ms_per_call": ms_mm,
+                                 "path": "FFMA (fp32 accumulate)"}
+    return out
+
+
 # ------------------------------------------------------- our engine
-def program_json():
-    """conv -> sigmoid -> mul over config 2 (the reference's SiLU spelling)."""
-    shape_out = [B, OC, H, W]
-    nbytes = B * OC * H * W * 2
-    return {
-        "version": "1",
-        "chain": [
-            {"name": "aten.convolution.default", "args": [0, 1, 2, 3, 4, 5, 6, 7, 8, 9]},
-            {"name": "aten.sigmoid.default", "args": [9, 10]},
-            {"name": "aten.mul.Tensor", "args": [9, 10, 11]},
-        ],
-        "values": [
-            {"type": "tensor", "shape": [B, IC, H, W], "dtype": "float16", "memObjId": 0},
-            {"type": "tensor", "shape": [OC, IC, K, K], "dtype": "float16", "weightsOffset": 0,
-             "weightsLength": W_BYTES},
-            {"type": "tensor", "shape": [OC], "dtype": "float16", "weightsOffset": W_BYTES,
-             "weightsLength": BIAS_BYTES},
-            {"type": "list", "items": [1, 1]}, {"type": "list", "items": [PAD, PAD]},
-            {"type": "list", "items": [1, 1]}, {"type": "scalar", "value": False},
-            {"type": "list", "items": [0, 0]}, {"type": "scalar", "value": 1},
-            {"type": "tensor", "shape": shape_out, "dtype": "float16", "memObjId": 1},
-            {"type": "tensor", "shape": shape_out, "dtype": "float16", "memObjId": 2},
-            {"type": "tensor", "shape": shape_out, "dtype": "float16", "memObjId": 3},
-        ],
-        "inputIds": [0], "outputIds": [11],
-        "memoryPlan": {"pools": [{"id": 0, "size": IN_BYTES}, {"id": 1, "size": nbytes},
-                                 {"id": 2, "size": nbytes}, {"id": 3, "size": nbytes}]},
-    }
-
-
 def run_ours(args, ws, rank, local):
     import torch
 
@@ -259,55 +412,31 @@ def run_ours(args, ws, rank, local):
     from wgx import _lib
 
     torch.cuda.set_device(local)
-    x, w, b = synthetic_inputs(rank)
+    prog1, progb, w = load_model(PER_GPU)
+    v_in = progb["values"][progb["inputIds"][0]]
+    v_out = progb["values"][progb["outputIds"][0]]
+    x = images(1000 + rank, v_in["shape"])
+    in_bytes = x.nbytes
+    out_bytes = int(np.prod(v_out["shape"])) * 2
+
     ctx = wgx.WgpuExecutionContext(local)
     ext = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
-
-    # ---- device-resident stateless path
-    prm = _lib.ConvParams(B, IC, H, W, OC, H, W, K, K, 1, 1, PAD, PAD, 1, 1, 1, 1, 1,
-                          _lib.ACT_SILU, -np.inf, np.inf)
-    plan = _lib.ConvPlan()
-    _lib.check(_lib.lib.wgx_conv2d_plan_for(ctypes.byref(prm), ctypes.byref(plan)))
-    tx = ctx.tensor("float16", x.shape).setData(x)
-    tw = ctx.tensor("float16", w.shape).setData(w)
-    tb = ctx.tensor("float16", b.shape).setData(b)
-    tout = ctx.tensor("float16", [B, OC, H, W])
-    scratch = ctx.storageBuffer(plan.scratch_bytes)
-    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=f"cuda:{local}")
-    flush_rd = torch.ones(FLUSH_BYTES // 4, dtype=torch.int32, device=f"cuda:{local}")
-
-    def flush_l2(i):
-        flush.fill_(i)
-        flush_rd.max()
-    pp = ctypes.byref(prm)
-    args_c = (tx.data_ptr, tw.data_ptr, tb.data_ptr, tout.data_ptr, scratch.device_ptr,
-              scratch.size, ctx.stream)
-
-    def step():
-        _lib.check(_lib.lib.wgx_conv2d(pp, *args_c))
-
-    # ---- public API path (Program, host buffers)
-    e2e_ctx = wgx.WgpuExecutionContext(local)
-    weights = w.tobytes() + b.tobytes()
-    pin_in = torch.empty(IN_BYTES, dtype=torch.uint8, pin_memory=True).numpy()
-    pin_out = torch.empty(OUT_BYTES, dtype=torch.uint8, pin_memory=True).numpy()
+    inp = ctx.tensor("float16", v_in["shape"]).setData(x)
+    out = ctx.tensor("float16", v_out["shape"])
+    ctx.recordProgram(progb, w, [inp, out])
+    st = ctx.stats()
+    pin_in = torch.empty(in_bytes, dtype=torch.uint8, pin_memory=True).numpy()
+    pin_out = torch.empty(out_bytes, dtype=torch.uint8, pin_memory=True).numpy()
     pin_in[:] = x.view(np.uint8).reshape(-1)
-    ein = e2e_ctx.tensor("float16", [B, IC, H, W])
-    eout = e2e_ctx.tensor("float16", [B, OC, H, W])
-    e2e_ctx.recordProgram(program_json(), weights, [ein, eout])
-    e2e_launches = e2e_ctx.stats()["kernel_launches"]
 
     def e2e_step():
-        ein.setData(pin_in)
-        e2e_ctx.submit()
-        eout.getDataInto(pin_out)
+        inp.setData(pin_in)
+        ctx.submit()
+        out.getDataInto(pin_out)
 
-    # ---- warm-up
-    for i in range(args.warmup):
-        with torch.cuda.stream(ext):
-            flush_l2(i)
-        step()
-        e2e_step()
+    for _ in range(args.warmup):
+        ctx.submit()
+    e2e_step()
     torch.cuda.synchronize()
 
     gpus = [int(g) for g in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if g.strip()]
@@ -316,26 +445,18 @@ def run_ours(args, ws, rank, local):
         sampler.start()
         time.sleep(0.3)
 
-    # ---- timed: device-resident
+    # ---- timed: device-resident input, one graph launch per step
     barrier(ws)
-    _lib.check(_lib.lib.wgx_kernel_timing(1))
-    _lib.check(_lib.lib.wgx_kernel_timing_read(b"", None, None, 1))
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     for i in range(args.steps):
-        with torch.cuda.stream(ext):
-            flush_l2(i + 1)
-            starts[i].record(ext)
-        step()
+        starts[i].record(ext)
+        ctx.submit()
         ends[i].record(ext)
     barrier(ws)
     dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    kms, kcnt = ctypes.c_double(), ctypes.c_int64()
-    _lib.check(_lib.lib.wgx_kernel_timing_read(b"umma_conv_kernel", ctypes.byref(kms),
-                                                ctypes.byref(kcnt), 1))
-    _lib.check(_lib.lib.wgx_kernel_timing(0))
 
-    # ---- timed: end to end through the public API
+    # ---- timed: end to end through the public API (host buffers)
     barrier(ws)
     t0 = time.perf_counter()
     for _ in range(args.steps):
@@ -344,50 +465,73 @@ def run_ours(args, ws, rank, local):
     e2e_s = time.perf_counter() - t0
     clocks = sampler.stop() if sampler else None
 
-    dev_ms, e2e_s, k_ms = reduce_max([dev_ms, e2e_s, kms.value], ws)
-    total_flops = FLOP_PER_STEP * args.steps * ws
-    value = total_flops / (dev_ms * 1e-3) / 1e12
-    e2e_value = total_flops / e2e_s / 1e12
-    kernel_avg_ms = k_ms / max(1, kcnt.value)
-    peak_tf, peak_hbm, peak_kind = peaks()
-    achieved = FLOP_PER_STEP / (kernel_avg_ms * 1e-3) / 1e12
-    traffic = profiled_traffic()
+    # ---- per-kernel CUDA events: the same program replayed eagerly
+    _lib.check(_lib.lib.wgx_kernel_timing(1))
+    _lib.check(_lib.lib.wgx_kernel_timing_read(b"", None, None, 1))
+    prof_reps = max(3, min(20, args.steps // 5))
+    prof = ctx.profile(prof_reps)
+    kms, kcnt = ctypes.c_double(), ctypes.c_int64()
+    _lib.check(_lib.lib.wgx_kernel_timing_read(b"umma_conv_kernel", ctypes.byref(kms),
+                                                ctypes.byref(kcnt), 1))
+    _lib.check(_lib.lib.wgx_kernel_timing(0))
+    eager_ms = sum(t for _, t in prof)
+    conv_main_ms = kms.value / prof_reps       # per step
+    dw_ms = sum(t for n, t in prof if "/depthwise" in n)
 
+    dev_ms, e2e_s = reduce_max([dev_ms, e2e_s], ws)
+    imgs = PER_GPU * ws * args.steps
+    value = imgs / (dev_ms * 1e-3)
+    e2e_value = imgs / e2e_s
+    peak_tf, peak_hbm, peak_kind = peaks()
+    dense_f, dense_b, n_dense, dw_b, n_dw = conv_work(progb)
+    ach = dense_b / (conv_main_ms * 1e-3) / 1e9
+    kernels = kernel_configs(ctx, local, max(20, min(200, args.steps)), peak_tf, peak_hbm)
     if rank != 0:
+        ctx.destroy()
         return 0
     cpu = None
     if ws == 1:
-        f, t, sample, threads = cpu_port_sample(x, w, b, 10.0)
-        cpu = {"value": f / t / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-               "sample": sample + " (CPU port of the reference WGSL kernels, fp16 per-op "
-                                  "rounding; WebGPU/SwiftShader unavailable on this box)"}
+        rate, secs, threads = cpu_image_rate(prog1, w)
+        cpu = {"value": rate, "unit": "imgs/s", "cores": threads, "kind": "port",
+               "sample": f"1 image of the batch-1 program, {secs:.1f} s (CPU program oracle: "
+                         "reference operators restated in C/numpy, fp64 accumulation; "
+                         "WebGPU/SwiftShader unavailable on this box)"}
+    traffic_per_img = profiled("umma_conv_kernel_yolo26n.md", "traffic_bytes_per_image")
     line = {
-        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws,
+        "metric": METRIC, "value": value, "unit": "imgs/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": DATA,
-        "config": {"workload": WORKLOAD, "global_batch": B * ws, "per_gpu_batch": B,
-                   "accumulate": "fp32 (TMEM)",
-                   "l2": "flushed before every step (256 MiB write + 256 MiB read, untimed)",
+        "config": {"workload": WORKLOAD, "model": "yolo26n-fp16", "global_batch": PER_GPU * ws,
+                   "per_gpu_batch": PER_GPU, "image": [HW, HW], "accumulate": "fp32",
+                   "l2": "inputs larger than L2 (157 MB input, GBs of activations per step)",
                    "parallelism": f"dp{ws} (independent batch shards, no collective)",
-                   "value_path": "wgx_conv2d C-ABI call, device buffers",
-                   "e2e_path": "recordProgram(conv->sigmoid->mul) + setData/submit/getData, "
-                               "pinned host buffers"},
-        "roofline": {"bound": "tensor", "kernel": "umma_conv_kernel", "achieved": achieved,
-                     "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
-                     "peak_source": f"{peak_kind} bf16 dense (burst)",
-                     "flop_per_launch": FLOP_PER_STEP, "launches": kcnt.value,
-                     "avg_launch_ms": kernel_avg_ms,
-                     "algorithmic_bytes_per_launch": IN_BYTES + OUT_BYTES + W_BYTES + BIAS_BYTES,
-                     "traffic": traffic},
+                   "value_path": "recordProgram once, submit() per step (CUDA graph replay), "
+                                 "input resident in HBM",
+                   "e2e_path": "setData(pinned host) + submit() + getDataInto(pinned host)",
+                   "commands": st["commands"], "kernel_launches_per_step": st["kernel_launches"]},
+        "roofline": {"bound": "hbm", "kernel": "umma_conv_kernel", "achieved": ach,
+                     "peak": peak_hbm, "unit": "GB/s", "frac": ach / peak_hbm,
+                     "peak_source": f"{peak_kind} HBM copy bandwidth",
+                     "launches_per_step": n_dense,
+                     "algorithmic_bytes_per_launch": dense_b / n_dense,
+                     "avg_launch_ms": conv_main_ms / n_dense,
+                     "flop_rate_tflops": dense_f / (conv_main_ms * 1e-3) / 1e12,
+                     "tensor_peak_tflops": peak_tf,
+                     "traffic": (traffic_per_img * PER_GPU / n_dense) if traffic_per_img else None,
+                     "timing": f"eager replay of the recorded program, {prof_reps} reps, CUDA "
+                               "events around every launch",
+                     "step_share": conv_main_ms / eager_ms,
+                     "depthwise_ms_per_step": dw_ms,
+                     "depthwise_gbs": dw_b / (dw_ms * 1e-3) / 1e9 if dw_ms else None},
         "cpu_baseline": cpu,
-        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": IN_BYTES,
-                "d2h_bytes_per_step": OUT_BYTES, "ms_per_step": e2e_s / args.steps * 1e3},
-        "gpu_launches": args.steps * (plan.n_launches + e2e_launches) * ws,
+        "e2e": {"value": e2e_value, "unit": "imgs/s", "h2d_bytes_per_step": in_bytes,
+                "d2h_bytes_per_step": out_bytes, "ms_per_step": e2e_s / args.steps * 1e3},
+        "gpu_launches": 2 * args.steps * st["kernel_launches"] * ws,
         "clocks": clocks,
+        "kernels": kernels,
     }
     print(json.dumps(line), flush=True)
-    e2e_ctx.destroy()
     ctx.destroy()
     return 0
 
@@ -395,8 +539,8 @@ def run_ours(args, ws, rank, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     args = ap.parse_args()
     if args.warmup < 3:

@@ -171,3 +171,39 @@ def test_depthart_256_batch_lift_runs(ctx):
     assert np.all(np.isfinite(y))
     for i in range(1, 4):
         np.testing.assert_array_equal(y[i], y[0])
+
+
+@pytest.mark.parametrize("model,fp16,hw,batch", [
+    ("yolo26n", True, None, 2),
+    ("depthart", True, (256, 256), 2),
+    ("selfie-segmentation", True, None, 2),
+    ("yolo26n", False, None, 1),
+])
+def test_engine_matches_program_oracle(ctx, model, fp16, hw, batch):
+    """Whole programs against the CPU program oracle on seeded inputs (a
+    batch-lifted program, uniform [0, 1) images): both round once per op,
+    so they differ only by accumulation order inside each op."""
+    import program_oracle
+    from wgx import programs
+    prog, w = load(model, fp16)
+    if hw:
+        prog = programs.respatial(prog, *hw)
+    prog = programs.batch_lift(prog, batch)
+    v_in = prog["values"][prog["inputIds"][0]]
+    v_out = prog["values"][prog["outputIds"][0]]
+    dt = np.float16 if fp16 else np.float32
+    x = np.random.default_rng(5).random(v_in["shape"], dtype=np.float32).astype(dt)
+    inp = ctx.tensor("float16" if fp16 else "float32", v_in["shape"]).setData(x)
+    out = ctx.tensor("float16" if fp16 else "float32", v_out["shape"])
+    ctx.recordProgram(prog, w, [inp, out])
+    ctx.submit()
+    ctx.sync()
+    y = out.numpy().astype(np.float64)
+    (ref,) = program_oracle.run_program(prog, w.tobytes(), [x])
+    ref = ref.astype(np.float64)
+    assert np.all(np.isfinite(y))
+    err = np.abs(y - ref)
+    scale = np.abs(ref).max()
+    rel = err.max() / (scale if scale > 0 else 1.0)
+    print(f"{model} fp16={fp16}: max rel err {rel:.2e}, mean abs err {err.mean():.2e}")
+    assert rel <= (2e-2 if fp16 else 1e-3)
