@@ -58,7 +58,13 @@ def check_f16(y, x, w, b, stride, pad, dil, groups, act=oracle.ACT_NONE, lo=-np.
                        mode="exact", clamp_op=clamp_op)
     e1 = oracle.rel_err(y, ex)
     assert np.all(np.isfinite(y.astype(np.float32)))
-    assert e1 <= F16_EXACT, f"vs exact oracle: {e1}"
+    tol = F16_EXACT
+    if groups > 1 and groups == x.shape[1] == w.shape[0]:
+        # fp16 depthwise accumulates its KH*KW products in f16, as the
+        # reference's conv2d-depthwise-f16 kernel does: the running sum's
+        # rounding error grows with the number of taps
+        tol = F16_EXACT * max(1.0, w.shape[2] * w.shape[3] / 25.0)
+    assert e1 <= tol, f"vs exact oracle: {e1}"
     if act != oracle.ACT_SILU:
         wg = oracle.conv2d(x, w, b, stride, pad, dil, groups, act=act, out_min=lo, out_max=hi,
                            mode="wgsl", clamp_op=clamp_op)
@@ -179,6 +185,12 @@ def test_dense_f16_cuda_core_fallback(ctx, geom):
 
 @pytest.mark.parametrize("geom", [
     (1, 256, 80, 80, 5, 1, 2, 1),    # BASELINE config 3 depthwise, one image
+    (2, 80, 80, 80, 3, 1, 1, 1),     # YOLO shapes: one plane per CTA
+    (3, 64, 40, 40, 3, 1, 1, 1),     # several planes per CTA
+    (2, 24, 20, 20, 7, 1, 3, 1),
+    (1, 8, 300, 300, 3, 1, 1, 1),    # banded plane
+    (2, 5, 13, 21, 5, 1, 2, 1),      # unaligned rows: per-element staging
+    (1, 6, 17, 16, 3, 1, 0, 1),      # no padding
     (2, 8, 9, 13, 3, 2, 1, 1),
     (1, 16, 33, 31, 7, 1, 3, 1),
     (1, 12, 24, 24, 3, 1, 2, 2),

@@ -16,6 +16,8 @@
 //     (conv-with-clamp-1x1-single-channel*.wgsl.ts).
 // All of them apply bias, then the activation (clamp or SiLU) in fp32 and
 // round once to the storage type.
+#include <algorithm>
+
 #include "internal.h"
 #include "umma_conv.h"
 
@@ -343,6 +345,362 @@ __global__ void pointwise_single(ConvGeom g, const T *__restrict__ x, const T *_
   out[(long long)b * hw + p] = to_t<T>(apply_act(acc, g.act, g.lo, g.hi));
 }
 
+// ------------------------------------------- stride-1 depthwise, K x K
+// One CTA stages P whole planes, or a band of TH output rows of one plane,
+// in shared memory: staged row r of a plane is input row oh0 - pH + r and
+// staged column DW_PADL + iw holds input column iw (the interior starts on
+// a 16-byte boundary, the zero halo sits on both sides). Each thread owns
+// DW_R output rows x 8 output columns: it walks the DW_R + K - 1 input rows
+// once, holding the 8 + K - 1 values of the current row in registers and
+// adding them into every output row whose filter touches that row, then
+// writes each output row's 8 values with one 16-byte store.
+constexpr int DW_PADL = 8;  // staged columns left of the interior (>= pW)
+constexpr int DW_R = 4;     // output rows per thread
+constexpr int DW_SMEM = 46 * 1024;
+
+struct DwTile {
+  int P, TH, bands, rows, TWs, n_cg, n_rg;
+  long long planes;
+};
+
+// Stages np planes' rows [ih0, ih0 + rows) into the tiles with 16-byte
+// vectors: per staged row one zero vector left of the interior, IW / V
+// interior vectors, one zero vector right of it (rows outside the image are
+// zero). Each thread issues DW_STAGE_U loads before storing any of them, so
+// several loads are in flight per thread.
+constexpr int DW_STAGE_U = 4;
+template <class T>
+__device__ __forceinline__ void dw_stage_vec(const ConvGeom &g, const DwTile &d,
+                                             const T *__restrict__ x, T *tile, long long plane0,
+                                             int np, int ih0, size_t plane_tile) {
+  constexpr int V = 16 / sizeof(T);
+  const int vrow = g.IW / V + 2;
+  const int total = np * d.rows * vrow;
+  for (int base = threadIdx.x; base < total; base += blockDim.x * DW_STAGE_U) {
+    uint4 val[DW_STAGE_U];
+    T *dst[DW_STAGE_U];
+#pragma unroll
+    for (int u = 0; u < DW_STAGE_U; ++u) {
+      const int i = base + u * blockDim.x;
+      val[u] = make_uint4(0u, 0u, 0u, 0u);
+      dst[u] = nullptr;
+      if (i < total) {
+        const int v = i % vrow;
+        const int rr = i / vrow;
+        const int r = rr % d.rows, p = rr / d.rows;
+        const int ih = ih0 + r;
+        const int col = v == 0 ? DW_PADL - V : DW_PADL + (v - 1) * V;
+        dst[u] = tile + p * plane_tile + size_t(r) * d.TWs + col;
+        if (v > 0 && v < vrow - 1 && ih >= 0 && ih < g.IH)
+          val[u] = *reinterpret_cast<const uint4 *>(
+              x + ((plane0 + p) * g.IH + ih) * (long long)g.IW + (v - 1) * V);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < DW_STAGE_U; ++u)
+      if (dst[u]) *reinterpret_cast<uint4 *>(dst[u]) = val[u];
+  }
+}
+
+// Staging for rows that are not whole 16-byte vectors: a plane's row band
+// is one contiguous run of memory, so it is read as aligned 16-byte vectors
+// (the plane size is a multiple of the vector width) and each element is
+// scattered to its staged row and column; the tiles are zeroed first.
+template <class T>
+__device__ __forceinline__ void dw_stage_flat(const ConvGeom &g, const DwTile &d,
+                                              const T *__restrict__ x, T *tile, long long plane0,
+                                              int np, int ih0, size_t plane_tile) {
+  constexpr int V = 16 / sizeof(T);
+  const int zero_vecs = int(size_t(np) * plane_tile / V);
+  for (int i = threadIdx.x; i < zero_vecs; i += blockDim.x)
+    reinterpret_cast<uint4 *>(tile)[i] = make_uint4(0u, 0u, 0u, 0u);
+  __syncthreads();
+  const int r_lo = max(ih0, 0), r_hi = min(ih0 + d.rows, g.IH);
+  if (r_hi <= r_lo) return;
+  const int s = r_lo * g.IW, e = r_hi * g.IW;  // plane-local element range
+  const int v0 = s / V, nvec = (e + V - 1) / V - v0;
+  const int total = np * nvec;
+  for (int base = threadIdx.x; base < total; base += blockDim.x * DW_STAGE_U) {
+    uint4 val[DW_STAGE_U];
+#pragma unroll
+    for (int u = 0; u < DW_STAGE_U; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < total) {
+        const int p = i / nvec, v = v0 + i % nvec;
+        val[u] = *reinterpret_cast<const uint4 *>(x + (plane0 + p) * g.IH * (long long)g.IW +
+                                                  (long long)v * V);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < DW_STAGE_U; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i >= total) continue;
+      const int p = i / nvec, v = v0 + i % nvec;
+      const T *vals = reinterpret_cast<const T *>(&val[u]);
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const int idx = v * V + k;
+        if (idx < s || idx >= e) continue;
+        const int row = idx / g.IW, col = idx - row * g.IW;
+        tile[p * plane_tile + size_t(row - ih0) * d.TWs + DW_PADL + col] = vals[k];
+      }
+    }
+  }
+}
+
+template <class T, int K>
+__global__ void __launch_bounds__(256)
+    depthwise_tiled(ConvGeom g, DwTile d, const T *__restrict__ x, const T *__restrict__ w,
+                    const T *__restrict__ bias, T *__restrict__ out, int vec_in, int vec_out) {
+  extern __shared__ __align__(16) unsigned char dw_smem[];
+  T *tile = reinterpret_cast<T *>(dw_smem);
+  const long long cta = blockIdx.x;
+  const long long plane0 = (cta / d.bands) * d.P;
+  const int oh0 = int(cta % d.bands) * d.TH;
+  const int np = int(min((long long)d.P, d.planes - plane0));
+  const int ih0 = oh0 - g.pH;
+  const size_t plane_tile = size_t(d.rows) * d.TWs;
+  // ---- stage: interior (vectorised when rows are whole 16-byte vectors),
+  // zero halo columns on both sides, zero rows outside the image
+  constexpr int V = 16 / sizeof(T);
+  if (vec_in == 1) {
+    dw_stage_vec<T>(g, d, x, tile, plane0, np, ih0, plane_tile);
+  } else if (vec_in == 2) {
+    dw_stage_flat<T>(g, d, x, tile, plane0, np, ih0, plane_tile);
+  } else {
+    const int total = np * d.rows * d.TWs;
+    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+      const int col = i % d.TWs;
+      const int rr = i / d.TWs;
+      const int r = rr % d.rows, p = rr / d.rows;
+      const int ih = ih0 + r, iw = col - DW_PADL;
+      T v = to_t<T>(0.f);
+      if (ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW)
+        v = x[((plane0 + p) * g.IH + ih) * (long long)g.IW + iw];
+      tile[p * plane_tile + size_t(r) * d.TWs + col] = v;
+    }
+  }
+  __syncthreads();
+  // ---- compute
+  const int oh_end = min(oh0 + d.TH, g.OH);
+  const int items = np * d.n_rg * d.n_cg;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int cg = it % d.n_cg;
+    const int t = it / d.n_cg;
+    const int rg = t % d.n_rg, p = t / d.n_rg;
+    const long long plane = plane0 + p;
+    const int c = int(plane % g.OC);
+    float wr[K * K];
+#pragma unroll
+    for (int i = 0; i < K * K; ++i) wr[i] = ld_f(&w[size_t(c) * K * K + i]);
+    const float bv = g.has_bias ? ld_f(&bias[c]) : 0.f;
+    const int r0 = rg * DW_R, ow0 = cg * 8;
+    float acc[DW_R][8];
+#pragma unroll
+    for (int r = 0; r < DW_R; ++r)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[r][e] = bv;
+    const T *tb = tile + p * plane_tile + (DW_PADL - g.pW + ow0);
+#pragma unroll
+    for (int ir = 0; ir < DW_R + K - 1; ++ir) {
+      float v[8 + K - 1];
+      const T *src = tb + size_t(r0 + ir) * d.TWs;
+#pragma unroll
+      for (int j = 0; j < 8 + K - 1; ++j) v[j] = ld_f(&src[j]);
+#pragma unroll
+      for (int r = 0; r < DW_R; ++r) {
+        const int kh = ir - r;
+        if (kh < 0 || kh >= K) continue;
+#pragma unroll
+        for (int kw = 0; kw < K; ++kw)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[r][e] = fmaf(v[e + kw], wr[kh * K + kw], acc[r][e]);
+      }
+    }
+    T *op = out + plane * g.OH * (long long)g.OW;
+#pragma unroll
+    for (int r = 0; r < DW_R; ++r) {
+      const int oh = oh0 + r0 + r;
+      if (oh >= oh_end) break;
+      T *orow = op + (long long)oh * g.OW;
+      if (vec_out && ow0 + 8 <= g.OW) {
+        alignas(16) T res[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) res[e] = to_t<T>(apply_act(acc[r][e], g.act, g.lo, g.hi));
+#pragma unroll
+        for (int q = 0; q < 8 / V; ++q)
+          reinterpret_cast<uint4 *>(orow + ow0)[q] = reinterpret_cast<const uint4 *>(res)[q];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (ow0 + e < g.OW) orow[ow0 + e] = to_t<T>(apply_act(acc[r][e], g.act, g.lo, g.hi));
+      }
+    }
+  }
+}
+
+// fp16 form of depthwise_tiled for "same" padding (pW = (K-1)/2): packed
+// half2 arithmetic, accumulating in f16 from the bias like the reference's
+// f16 depthwise kernel (src/shaders/convolution/conv2d-depthwise-f16.wgsl.ts:
+// f16 accumulator initialised with the bias). Each staged input row is read
+// as three aligned 16-byte vectors (staged columns ow0-8 .. ow0+15 around
+// the thread's 8 outputs); the half2 pairs a filter tap needs are taken
+// from those words directly (even offset) or with one byte permute (odd).
+// The CTA's weights sit in shared memory behind the tiles as (w, w) pairs.
+template <int K>
+__global__ void __launch_bounds__(256)
+    depthwise_tiled_h2(ConvGeom g, DwTile d, const __half *__restrict__ x,
+                       const __half *__restrict__ w, const __half *__restrict__ bias,
+                       __half *__restrict__ out, int vec_in, int vec_out) {
+  constexpr int PW = (K - 1) / 2;
+  extern __shared__ __align__(16) unsigned char dw_smem[];
+  __half *tile = reinterpret_cast<__half *>(dw_smem);
+  const long long cta = blockIdx.x;
+  const long long plane0 = (cta / d.bands) * d.P;
+  const int oh0 = int(cta % d.bands) * d.TH;
+  const int np = int(min((long long)d.P, d.planes - plane0));
+  const int ih0 = oh0 - g.pH;
+  const size_t plane_tile = size_t(d.rows) * d.TWs;
+  __half2 *wsm = reinterpret_cast<__half2 *>(tile + size_t(d.P) * plane_tile);
+  for (int i = threadIdx.x; i < np * (K * K + 1); i += blockDim.x) {
+    const int p = i / (K * K + 1), t = i % (K * K + 1);
+    const int c = int((plane0 + p) % g.OC);
+    const __half v = t < K * K ? w[size_t(c) * K * K + t]
+                               : (g.has_bias ? bias[c] : __float2half_rn(0.f));
+    wsm[i] = __halves2half2(v, v);
+  }
+  if (vec_in == 1) {
+    dw_stage_vec<__half>(g, d, x, tile, plane0, np, ih0, plane_tile);
+  } else if (vec_in == 2) {
+    dw_stage_flat<__half>(g, d, x, tile, plane0, np, ih0, plane_tile);
+  } else {
+    const int total = np * d.rows * d.TWs;
+    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+      const int col = i % d.TWs;
+      const int rr = i / d.TWs;
+      const int r = rr % d.rows, p = rr / d.rows;
+      const int ih = ih0 + r, iw = col - DW_PADL;
+      __half v = __float2half_rn(0.f);
+      if (ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW)
+        v = x[((plane0 + p) * g.IH + ih) * (long long)g.IW + iw];
+      tile[p * plane_tile + size_t(r) * d.TWs + col] = v;
+    }
+  }
+  __syncthreads();
+  const int oh_end = min(oh0 + d.TH, g.OH);
+  const int items = np * d.n_rg * d.n_cg;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int cg = it % d.n_cg;
+    const int t = it / d.n_cg;
+    const int rg = t % d.n_rg, p = t / d.n_rg;
+    const long long plane = plane0 + p;
+    const __half2 *wp = wsm + p * (K * K + 1);
+    const int r0 = rg * DW_R, ow0 = cg * 8;
+    __half2 acc[DW_R][4];
+#pragma unroll
+    for (int r = 0; r < DW_R; ++r)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[r][j] = wp[K * K];
+    // staged columns ow0 - 8 + 8 .. : window start (16-byte aligned)
+    const __half *wbase = tile + p * plane_tile + (DW_PADL - 8 + ow0);
+#pragma unroll
+    for (int ir = 0; ir < DW_R + K - 1; ++ir) {
+      const uint4 *src = reinterpret_cast<const uint4 *>(wbase + size_t(r0 + ir) * d.TWs);
+      const uint4 a = src[0], b = src[1], c = src[2];
+      const uint32_t wd[12] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int r = 0; r < DW_R; ++r) {
+        const int kh = ir - r;
+        if (kh < 0 || kh >= K) continue;
+#pragma unroll
+        for (int kw = 0; kw < K; ++kw) {
+          const __half2 wv = wp[kh * K + kw];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            // outputs 2j, 2j+1 read window halves h, h+1 with h = 8 - PW + kw + 2j
+            const int h = 8 - PW + kw + 2 * j;
+            const uint32_t pr = (h & 1) ? __byte_perm(wd[h >> 1], wd[(h >> 1) + 1], 0x5432)
+                                        : wd[h >> 1];
+            acc[r][j] = __hfma2(*reinterpret_cast<const __half2 *>(&pr), wv, acc[r][j]);
+          }
+        }
+      }
+    }
+    __half *op = out + plane * g.OH * (long long)g.OW;
+#pragma unroll
+    for (int r = 0; r < DW_R; ++r) {
+      const int oh = oh0 + r0 + r;
+      if (oh >= oh_end) break;
+      __half *orow = op + (long long)oh * g.OW;
+      uint32_t res[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __half2 v = acc[r][j];
+        if (g.act == WGX_ACT_SILU) {
+          // v * sigmoid(v) = h + h * tanh(h), h = v / 2
+          const __half2 h = __hmul2(v, __float2half2_rn(0.5f));
+          const uint32_t hu = *reinterpret_cast<const uint32_t *>(&h);
+          uint32_t tu;
+          asm("tanh.approx.f16x2 %0, %1;" : "=r"(tu) : "r"(hu));
+          v = __hfma2(h, *reinterpret_cast<const __half2 *>(&tu), h);
+        } else if (g.act == WGX_ACT_CLAMP) {
+          const float2 f = __half22float2(v);
+          v = __floats2half2_rn(fminf(fmaxf(f.x, g.lo), g.hi), fminf(fmaxf(f.y, g.lo), g.hi));
+        }
+        res[j] = *reinterpret_cast<const uint32_t *>(&v);
+      }
+      if (vec_out && ow0 + 8 <= g.OW) {
+        *reinterpret_cast<uint4 *>(orow + ow0) = make_uint4(res[0], res[1], res[2], res[3]);
+      } else {
+        const __half *hv = reinterpret_cast<const __half *>(res);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (ow0 + e < g.OW) orow[ow0 + e] = hv[e];
+      }
+    }
+  }
+}
+
+// Tiling of depthwise_tiled for p (stride 1, dilation 1, square K in
+// {3,5,7}, pW <= DW_PADL), or false when it does not apply.
+static bool dw_tiling(const wgx_conv2d_params &p, int esize, DwTile &d) {
+  const int K = p.KH;
+  if (p.KW != K || (K != 3 && K != 5 && K != 7)) return false;
+  if (p.sH != 1 || p.sW != 1 || p.dH != 1 || p.dW != 1) return false;
+  // the zero halo on each side of a staged row is one 16-byte vector wide
+  if (p.pW > 16 / esize || p.pH < 0 || p.pW < 0) return false;
+  if (p.OH != p.IH + 2 * p.pH - K + 1 || p.OW != p.IW + 2 * p.pW - K + 1) return false;
+  const int V = 16 / esize;
+  d.n_cg = (p.OW + 7) / 8;
+  // staged row: zero halo vector + interior + zero halo vector, wide enough
+  // for every tap of the last column group and for the fp16 kernel's
+  // 24-column read window starting at staged column 8 * cg
+  const int right = std::max({p.IW + V, 8 * d.n_cg - p.pW + K - 1, 8 * d.n_cg + 8});
+  d.TWs = (DW_PADL + right + 7) / 8 * 8;
+  d.planes = (long long)p.B * p.OC;
+  // shared memory of one plane: its tile plus (fp16 kernel) K*K + 1 weight pairs
+  const size_t wbytes = esize == 2 ? size_t(K * K + 1) * 4 : 0;
+  auto tile_bytes = [&](int th) {
+    return size_t((th + DW_R - 1) / DW_R * DW_R + K - 1) * d.TWs * esize + wbytes;
+  };
+  int TH = p.OH;
+  while (TH > DW_R && tile_bytes(TH) > size_t(DW_SMEM)) TH = (TH / 2 + DW_R - 1) / DW_R * DW_R;
+  if (tile_bytes(TH) > size_t(DW_SMEM)) return false;
+  d.TH = TH;
+  d.bands = (p.OH + TH - 1) / TH;
+  d.n_rg = (TH + DW_R - 1) / DW_R;
+  d.rows = d.n_rg * DW_R + K - 1;
+  d.P = 1;
+  if (d.bands == 1) {
+    const int per_plane = d.n_rg * d.n_cg;
+    const int want = std::max(1, (256 + per_plane - 1) / per_plane);
+    const int fit = int(size_t(DW_SMEM) / tile_bytes(TH));
+    d.P = std::max(1, std::min(want, fit));
+  }
+  const long long ctas = (d.planes + d.P - 1) / d.P * d.bands;
+  return ctas < (1ll << 31);
+}
+
 // ---------------------------------------------------------------- dispatch
 static bool is_depthwise(const wgx_conv2d_params &p) {
   return p.groups == p.OC && p.IC == p.OC && p.groups > 1;
@@ -407,6 +765,7 @@ template <class T>
 static void launch_simt(const wgx_conv2d_params &p, int variant, const T *in, const T *w,
                         const T *bias, T *out, cudaStream_t s) {
   ConvGeom g = geom_of(p);
+  DwTile dt{};
   if (variant == WGX_CONV_SIMT_GEMM) {
     long long N = (long long)p.B * p.OH * p.OW;
     dim3 grid(unsigned((N + 63) / 64), unsigned((p.OC + 63) / 64));
@@ -417,6 +776,40 @@ static void launch_simt(const wgx_conv2d_params &p, int variant, const T *in, co
     if (p.B > 65535) fail("conv2d: batch too large for the single-channel kernel");
     dim3 grid(unsigned((hw + 255) / 256), unsigned(p.B));
     pointwise_single<T><<<grid, 256, 0, s>>>(g, in, w, bias, out);
+  } else if (variant == WGX_CONV_DEPTHWISE && dw_tiling(p, int(sizeof(T)), dt)) {
+    constexpr int V = 16 / sizeof(T);
+    // staging: 1 = whole-vector rows, 2 = vector reads of contiguous row
+    // bands scattered into the tile, 0 = per element
+    const bool aligned = (reinterpret_cast<uintptr_t>(in) & 15) == 0;
+    const int vec_in = !aligned ? 0
+                       : p.IW % V == 0 ? 1
+                       : (int64_t(p.IH) * p.IW) % V == 0 ? 2 : 0;
+    const int vec_out = (p.OW % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+    const size_t smem = size_t(dt.P) * dt.rows * dt.TWs * sizeof(T);
+    const unsigned grid = unsigned((dt.planes + dt.P - 1) / dt.P * dt.bands);
+    if constexpr (sizeof(T) == 2) {
+      if (p.pW == (p.KW - 1) / 2) {
+        const size_t smem_h2 = smem + size_t(dt.P) * (p.KH * p.KW + 1) * 4;
+        const __half *hin = reinterpret_cast<const __half *>(in);
+        const __half *hw = reinterpret_cast<const __half *>(w);
+        const __half *hb = reinterpret_cast<const __half *>(bias);
+        __half *hout = reinterpret_cast<__half *>(out);
+        if (p.KH == 3)
+          depthwise_tiled_h2<3><<<grid, 256, smem_h2, s>>>(g, dt, hin, hw, hb, hout, vec_in, vec_out);
+        else if (p.KH == 5)
+          depthwise_tiled_h2<5><<<grid, 256, smem_h2, s>>>(g, dt, hin, hw, hb, hout, vec_in, vec_out);
+        else
+          depthwise_tiled_h2<7><<<grid, 256, smem_h2, s>>>(g, dt, hin, hw, hb, hout, vec_in, vec_out);
+        check_cuda(cudaGetLastError(), "conv2d launch");
+        return;
+      }
+    }
+    if (p.KH == 3)
+      depthwise_tiled<T, 3><<<grid, 256, smem, s>>>(g, dt, in, w, bias, out, vec_in, vec_out);
+    else if (p.KH == 5)
+      depthwise_tiled<T, 5><<<grid, 256, smem, s>>>(g, dt, in, w, bias, out, vec_in, vec_out);
+    else
+      depthwise_tiled<T, 7><<<grid, 256, smem, s>>>(g, dt, in, w, bias, out, vec_in, vec_out);
   } else if (variant == WGX_CONV_DEPTHWISE) {
     // rows per CTA: keep the staged tile under ~40 KB
     int TWs = p.IW + 2 * p.pW;

@@ -130,7 +130,7 @@ class Tensor:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h:
+        if h and lib is not None:  # module globals may be gone at interpreter exit
             lib.wgx_tensor_release(h)
             self._h = None
 
@@ -309,7 +309,7 @@ class WgpuExecutionContext:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h:
+        if h and lib is not None:  # module globals may be gone at interpreter exit
             lib.wgx_context_release(h)
             self._h = None
 
