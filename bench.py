@@ -292,6 +292,34 @@ def run_reference(args, ws, rank):
     return 0
 
 
+def make_conv(ctx, dev, rng, B, IC, H, Wd, OC, K, s, p, g, act):
+    """A launch closure of the stateless wgx_conv2d entry on seeded device
+    tensors: (launch, algorithmic flops, algorithmic bytes, plan, buffers)."""
+    import torch
+
+    from wgx import _lib
+    OH, OW = (H + 2 * p - K) // s + 1, (Wd + 2 * p - K) // s + 1
+    prm = _lib.ConvParams(B, IC, H, Wd, OC, OH, OW, K, K, s, s, p, p, 1, 1, g, 1, 1, act,
+                          -np.inf, np.inf)
+    plan = _lib.ConvPlan()
+    _lib.check(_lib.lib.wgx_conv2d_plan_for(ctypes.byref(prm), ctypes.byref(plan)))
+    x = torch.from_numpy(rng.standard_normal((B, IC, H, Wd), dtype=np.float32)).half().to(dev)
+    std = np.sqrt(2.0 / (IC // g * K * K)) if g == 1 else 0.1
+    wt = (torch.randn(OC, IC // g, K, K, device=dev) * std).half()
+    b = (torch.randn(OC, device=dev) * 0.01).half()
+    y = torch.empty(B, OC, OH, OW, device=dev, dtype=torch.float16)
+    scr = torch.empty(max(plan.scratch_bytes, 16), device=dev, dtype=torch.uint8)
+    args_c = (ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(wt.data_ptr()),
+              ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(y.data_ptr()),
+              ctypes.c_void_p(scr.data_ptr()), ctypes.c_uint64(plan.scratch_bytes),
+              ctypes.c_void_p(ctx.stream))
+    pp = ctypes.byref(prm)
+    launch = lambda: _lib.check(_lib.lib.wgx_conv2d(pp, *args_c))
+    flops = 2.0 * B * OC * OH * OW * (IC // g) * K * K
+    nbytes = 2.0 * (x.numel() + wt.numel() + b.numel() + y.numel())
+    return launch, flops, nbytes, plan, (x, wt, b, y, scr, prm)
+
+
 # ------------------------------------------------- single-kernel configs
 def kernel_configs(ctx, local, steps, peak_tf, peak_hbm):
     """configs[1] conv+SiLU, configs[2] depthwise + pointwise, configs[0]
@@ -323,26 +351,7 @@ def kernel_configs(ctx, local, steps, peak_tf, peak_hbm):
         return sum(a.elapsed_time(b) for a, b in zip(s, e)) / n
 
     def conv(B, IC, H, Wd, OC, K, s, p, g, act):
-        OH, OW = (H + 2 * p - K) // s + 1, (Wd + 2 * p - K) // s + 1
-        prm = _lib.ConvParams(B, IC, H, Wd, OC, OH, OW, K, K, s, s, p, p, 1, 1, g, 1, 1, act,
-                              -np.inf, np.inf)
-        plan = _lib.ConvPlan()
-        _lib.check(_lib.lib.wgx_conv2d_plan_for(ctypes.byref(prm), ctypes.byref(plan)))
-        x = torch.from_numpy(rng.standard_normal((B, IC, H, Wd), dtype=np.float32)).half().to(dev)
-        std = np.sqrt(2.0 / (IC // g * K * K)) if g == 1 else 0.1
-        wt = (torch.randn(OC, IC // g, K, K, device=dev) * std).half()
-        b = (torch.randn(OC, device=dev) * 0.01).half()
-        y = torch.empty(B, OC, OH, OW, device=dev, dtype=torch.float16)
-        scr = torch.empty(max(plan.scratch_bytes, 16), device=dev, dtype=torch.uint8)
-        args_c = (ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(wt.data_ptr()),
-                  ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(y.data_ptr()),
-                  ctypes.c_void_p(scr.data_ptr()), ctypes.c_uint64(plan.scratch_bytes),
-                  ctypes.c_void_p(ctx.stream))
-        pp = ctypes.byref(prm)
-        launch = lambda: _lib.check(_lib.lib.wgx_conv2d(pp, *args_c))
-        flops = 2.0 * B * OC * OH * OW * (IC // g) * K * K
-        nbytes = 2.0 * (x.numel() + wt.numel() + b.numel() + y.numel())
-        return launch, flops, nbytes, plan, (x, wt, b, y, scr)
+        return make_conv(ctx, dev, rng, B, IC, H, Wd, OC, K, s, p, g, act)
 
     # [8,64,160,160] x [128,64,3,3], s1 p1, SiLU; tensor-core bound
     launch, flops, nbytes, plan, keep = conv(8, 64, 160, 160, 128, 3, 1, 1, 1, _lib.ACT_SILU)
@@ -536,15 +545,62 @@ def run_ours(args, ws, rank, local):
     return 0
 
 
+# Single workloads for profiling: the same launches as the bench, nothing
+# else (no timing, no other workload), on one GPU.
+ONLY_CONV = {
+    "conv2": (8, 64, 160, 160, 128, 3, 1, 1, 1, 2),     # configs[1] (SiLU epilogue)
+    "dw3": (16, 256, 80, 80, 256, 5, 1, 2, 256, 0),     # configs[2] depthwise
+    "pw3": (16, 256, 80, 80, 256, 1, 1, 0, 1, 0),       # configs[2] pointwise
+    "yolo_stem": (8, 3, 640, 640, 16, 3, 2, 1, 1, 2),   # YOLO26-N shapes, batch 8
+    "yolo_down": (8, 64, 160, 160, 64, 3, 2, 1, 1, 2),
+    "yolo_1x1": (8, 48, 160, 160, 64, 1, 1, 0, 1, 2),
+}
+
+
+def run_only(args):
+    import torch
+
+    import wgx
+    ctx = wgx.WgpuExecutionContext(0)
+    if args.only == "yolo":
+        _, progb, w = load_model(args.batch or PER_GPU)
+        v_in = progb["values"][progb["inputIds"][0]]
+        v_out = progb["values"][progb["outputIds"][0]]
+        inp = ctx.tensor("float16", v_in["shape"]).setData(images(1000, v_in["shape"]))
+        out = ctx.tensor("float16", v_out["shape"])
+        ctx.recordProgram(progb, w, [inp, out])
+        for _ in range(args.warmup + args.steps):
+            ctx.submit()
+        ctx.sync()
+        print(json.dumps({"only": "yolo", "steps": args.steps, "warmup": args.warmup,
+                          "kernel_launches_per_step": ctx.stats()["kernel_launches"]}))
+    else:
+        rng = np.random.default_rng(0)
+        launch, *_ = make_conv(ctx, "cuda:0", rng, *ONLY_CONV[args.only])
+        for _ in range(args.warmup + args.steps):
+            launch()
+        ctx.sync()
+        print(json.dumps({"only": args.only, "steps": args.steps, "warmup": args.warmup}))
+    torch.cuda.synchronize()
+    ctx.destroy()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--only", default=None, choices=["yolo"] + sorted(ONLY_CONV),
+                    help="run one workload's launches only (for profilers)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="images per GPU for --only yolo (default 64)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.only:
+        return run_only(args)
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         return run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)

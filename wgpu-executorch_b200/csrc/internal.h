@@ -93,6 +93,18 @@ struct Command {
   std::function<void(const ExecEnv &)> run;  // throws Error on failure
 };
 
+// Program-level connections of the convolution being recorded, set by the
+// program recorder around that one recording call (null otherwise).
+struct ConvRecordLink {
+  // write the output into this buffer: the re-laid input of `consumer`
+  void *out_xs = nullptr;
+  wgx_conv2d_params consumer{};
+  // the input has already been re-laid into this buffer by its producer
+  void *in_xs = nullptr;
+  // the input is the channel concatenation of these tensors
+  std::vector<wgx_tensor *> cat;
+};
+
 }  // namespace wgx
 
 struct wgx_context {
@@ -109,6 +121,7 @@ struct wgx_context {
   uint64_t workspace_bytes = 0;
   int64_t launches_per_submit = 0;
   std::vector<std::unique_ptr<wgx_tensor>> program_tensors;  // views made by record_program
+  const wgx::ConvRecordLink *conv_link = nullptr;  // see ConvRecordLink
 
   void *alloc_device(uint64_t bytes);  // tracked device allocation (freed on destroy)
   void invalidate_graph();

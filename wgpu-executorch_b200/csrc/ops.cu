@@ -136,13 +136,42 @@ static void append_conv(wgx_context *ctx, const char *name, const wgx_conv2d_par
       umma_conv_pack_weights(p, static_cast<const __half *>(pw), packed, ctx->stream);
       check_cuda(cudaStreamSynchronize(ctx->stream), "pack weights");
     }
-    c.workspace_bytes = umma_conv_input_bytes(p);
-    c.kernel_launches = 2;
+    // program-level links (see ConvRecordLink)
+    const ConvRecordLink *lk = ctx->conv_link;
+    UmmaLink link{};
+    bool linked = false, has_consumer = false;
+    wgx_conv2d_params consumer{};
+    void *in_xs = nullptr;
+    if (lk) {
+      if (lk->out_xs) {
+        consumer = lk->consumer;
+        link.consumer_xs = lk->out_xs;
+        has_consumer = linked = true;
+      }
+      if (lk->in_xs) {
+        if (!constant) fail(std::string(name) + ": linked input needs constant weights");
+        in_xs = lk->in_xs;
+        link.xs_ready = linked = true;
+      }
+      if (!lk->cat.empty()) {
+        if (lk->cat.size() > 8) fail(std::string(name) + ": too many concatenated inputs");
+        link.nsrc = int(lk->cat.size());
+        for (size_t k = 0; k < lk->cat.size(); ++k) {
+          link.src[k] = static_cast<const __half *>(lk->cat[k]->data());
+          link.src_ch[k] = int(lk->cat[k]->shape[1]);
+        }
+        linked = true;
+      }
+    }
+    c.workspace_bytes = in_xs ? 0 : umma_conv_input_bytes(p);
+    c.kernel_launches = in_xs ? 1 : 2;
     c.run = [=](const ExecEnv &env) {
+      UmmaLink l = link;
+      if (has_consumer) l.consumer = &consumer;
       umma_conv_run(p, static_cast<const __half *>(pin), packed,
                     constant ? nullptr : static_cast<const __half *>(pw),
                     static_cast<const __half *>(pbias), static_cast<__half *>(pout),
-                    env.workspace, env.stream);
+                    in_xs ? in_xs : env.workspace, env.stream, linked ? &l : nullptr);
     };
   } else {
     c.kernel_launches = plan.n_launches;

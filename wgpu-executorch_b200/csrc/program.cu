@@ -25,6 +25,7 @@
 
 #include "internal.h"
 #include "json.h"
+#include "umma_conv.h"
 
 namespace wgx {
 
@@ -150,11 +151,12 @@ Program parse_program(const char *text, uint64_t len) {
 
 uint64_t align256(uint64_t x) { return (x + 255) / 256 * 256; }
 
-// True when the convolution `c` (aten.convolution positional args) takes
-// the tensor-core path, which stages its whole input in scratch first.
-bool conv_in_place_safe(const Program &P, const POp &c,
-                        const std::map<int64_t, wgx_tensor *> &tensors) {
-  auto in = tensors.find(c.args[0]), w = tensors.find(c.args[1]), out = tensors.find(c.args[9]);
+// Kernel parameters of the aten.convolution `c` (positional args) writing
+// into value `out_id` with epilogue `act`; false when they cannot be formed.
+bool conv_params(const Program &P, const POp &c, const std::map<int64_t, wgx_tensor *> &tensors,
+                 int64_t out_id, int act, wgx_conv2d_params *pp) {
+  if (c.args.size() != 10) return false;
+  auto in = tensors.find(c.args[0]), w = tensors.find(c.args[1]), out = tensors.find(out_id);
   if (in == tensors.end() || w == tensors.end() || out == tensors.end()) return false;
   auto hw = [&](int64_t idx, int *h, int *wv) {
     const PValue &v = P.values[idx];
@@ -180,13 +182,31 @@ bool conv_in_place_safe(const Program &P, const POp &c,
     return false;
   const PValue &g = P.values[c.args[8]];
   p.groups = g.kind == PValue::Scalar ? int(g.num) : 0;
+  const PValue &tr = P.values[c.args[6]];
+  if (tr.kind == PValue::Scalar && tr.b) return false;  // transposed
+  p.has_bias = P.values[c.args[2]].kind == PValue::Tensor;
   p.dtype = x->dtype;
-  p.act = WGX_ACT_SILU;
+  p.act = act;
+  p.out_min = -INFINITY;
+  p.out_max = INFINITY;
+  *pp = p;
+  return true;
+}
+
+bool is_umma(const wgx_conv2d_params &p) {
   try {
     return plan_conv2d(p).variant == WGX_CONV_UMMA;
   } catch (const Error &) {
     return false;
   }
+}
+
+// True when the convolution `c` (aten.convolution positional args) takes
+// the tensor-core path, which stages its whole input in scratch first.
+bool conv_in_place_safe(const Program &P, const POp &c,
+                        const std::map<int64_t, wgx_tensor *> &tensors) {
+  wgx_conv2d_params p{};
+  return conv_params(P, c, tensors, c.args[9], WGX_ACT_SILU, &p) && is_umma(p);
 }
 
 // SiLU fusion: conv(v) ; sigmoid(v)->s ; mul(v,s)->y  ==>  conv_silu -> y
@@ -234,6 +254,97 @@ std::vector<int> plan_fusion(const Program &P, const std::map<int64_t, wgx_tenso
     i += 2;
   }
   return mark;
+}
+
+// Producer/consumer links between tensor-core convolutions (after SiLU
+// fusion), so intermediate activations skip their NCHW round trip:
+//  * conv -> conv: when a convolution's output has no other reader, the
+//    producer's epilogue writes the consumer's re-laid input (a dedicated
+//    buffer, zeroed once here so its padding and unused channels stay zero)
+//    and the consumer skips its re-layout kernel;
+//  * cat -> conv: a channel concatenation immediately followed by its only
+//    reader, a convolution, is not materialised; the consumer's re-layout
+//    reads the pieces directly.
+struct LinkPlan {
+  std::map<size_t, ConvRecordLink> conv;  // chain index -> links of that convolution
+  std::set<size_t> skip;                  // absorbed concatenations
+};
+
+LinkPlan plan_links(wgx_context *ctx, const Program &P,
+                    const std::map<int64_t, wgx_tensor *> &tensors, const std::vector<int> &fusion) {
+  LinkPlan L;
+  std::map<int64_t, int> readers;
+  for (size_t i = 0; i < P.chain.size(); ++i) {
+    if (fusion[i] == 2) continue;
+    const POp &op = P.chain[i];
+    for (size_t k = 0; k + 1 < op.args.size(); ++k) {
+      const int64_t a = op.args[k];
+      if (a < 0 || size_t(a) >= P.values.size()) continue;
+      readers[a]++;
+      if (P.values[a].kind == PValue::TensorList)
+        for (auto t : P.values[a].items) readers[t]++;
+    }
+  }
+  std::set<int64_t> boundary(P.output_ids.begin(), P.output_ids.end());
+  boundary.insert(P.input_ids.begin(), P.input_ids.end());
+  // value -> producing chain index; fused heads own the mul's output
+  std::map<int64_t, size_t> producer;
+  auto out_of = [&](size_t i) -> int64_t {
+    return fusion[i] == 1 ? P.chain[i + 2].args[2] : P.chain[i].args.back();
+  };
+  for (size_t i = 0; i < P.chain.size(); ++i)
+    if (fusion[i] != 2) producer[out_of(i)] = i;
+  auto conv_of = [&](size_t i, wgx_conv2d_params *pp) {
+    const POp &op = P.chain[i];
+    if (op.name != "aten.convolution.default" || fusion[i] == 2) return false;
+    return conv_params(P, op, tensors, out_of(i), fusion[i] == 1 ? WGX_ACT_SILU : WGX_ACT_NONE,
+                       pp) &&
+           is_umma(*pp);
+  };
+  for (size_t j = 0; j < P.chain.size(); ++j) {
+    wgx_conv2d_params pc{};
+    if (!conv_of(j, &pc)) continue;
+    const int64_t x = P.chain[j].args[0];
+    auto wt = tensors.find(P.chain[j].args[1]);
+    if (wt == tensors.end() || !wt->second->buffer->constant) continue;
+    if (readers[x] != 1 || boundary.count(x) || !producer.count(x)) continue;
+    const size_t k = producer[x];
+    wgx_conv2d_params pp{};
+    if (k < j && conv_of(k, &pp) && umma_conv_link_ok(pp, pc)) {
+      const uint64_t bytes = umma_conv_input_bytes(pc);
+      void *buf = ctx->alloc_device(bytes);
+      check_cuda(cudaMemsetAsync(buf, 0, bytes, ctx->stream), "link buffer");
+      L.conv[k].out_xs = buf;
+      L.conv[k].consumer = pc;
+      L.conv[j].in_xs = buf;
+      continue;
+    }
+    const POp &cat = P.chain[k];
+    if (cat.name == "aten.cat.default" && k + 1 == j && cat.args.size() == 3 &&
+        P.values[cat.args[0]].kind == PValue::TensorList) {
+      const PValue &dimv = P.values[cat.args[1]];
+      const int dim = dimv.kind == PValue::Scalar ? int(dimv.num) : -99;
+      if (dim != 1 && dim != -3) continue;
+      std::vector<wgx_tensor *> pieces;
+      bool ok = P.values[cat.args[0]].items.size() <= 8;
+      for (auto t : P.values[cat.args[0]].items) {
+        auto it = tensors.find(t);
+        if (it == tensors.end()) {
+          ok = false;
+          break;
+        }
+        const wgx_tensor *pt = it->second;
+        ok = ok && pt->dtype == WGX_FLOAT16 && pt->ndim == 4 && pt->shape[0] == pc.B &&
+             pt->shape[2] == pc.IH && pt->shape[3] == pc.IW && pt->shape[1] % 8 == 0;
+        pieces.push_back(it->second);
+      }
+      if (!ok) continue;
+      L.conv[j].cat = pieces;
+      L.skip.insert(k);
+    }
+  }
+  if (!L.conv.empty()) check_cuda(cudaStreamSynchronize(ctx->stream), "link buffers");
+  return L;
 }
 
 }  // namespace
@@ -350,8 +461,9 @@ static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len
   // ---- chain
   const auto &reg = op_registry();
   std::vector<int> fusion = plan_fusion(P, tensors);
+  const LinkPlan links = plan_links(ctx, P, tensors, fusion);
   for (size_t oi = 0; oi < P.chain.size(); ++oi) {
-    if (fusion[oi] == 2) continue;
+    if (fusion[oi] == 2 || links.skip.count(oi)) continue;
     const POp &op = P.chain[oi];
     auto rit = reg.find(op.name);
     if (rit == reg.end()) fail("program: unknown operator '" + op.name + "'");
@@ -415,6 +527,8 @@ static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len
       }
     }
     size_t before = ctx->commands.size();
+    auto lk = links.conv.find(oi);
+    ctx->conv_link = lk == links.conv.end() ? nullptr : &lk->second;
     try {
       if (fusion[oi] == 1) {
         // fused conv + SiLU writes straight into the mul's output
@@ -424,9 +538,11 @@ static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len
         rit->second(ctx, a);
       }
     } catch (...) {
+      ctx->conv_link = nullptr;
       ctx->commands.resize(before);
       throw;
     }
+    ctx->conv_link = nullptr;
   }
 
   // ---- output copies

@@ -63,6 +63,8 @@ constexpr int EPI_ROWB = 48;     // staged channel row: 16 fp16 + 16 B pad
 constexpr uint32_t EPI_BYTES = EPI_WARPS * 32 * EPI_ROWB;
 constexpr uint32_t SMEM_MAX = 227u * 1024u;
 
+constexpr int kMaxSrc = 8;
+
 struct UmmaGeom {
   // IC, KH, KW, dH, dW, pH, pW describe the stride-1 convolution the MMA
   // pipeline runs (for a strided convolution: the space-to-depth view);
@@ -86,6 +88,18 @@ struct UmmaGeom {
   int has_bias, act;
   float lo, hi;
   uint32_t *err;
+  // output layout: omode 0 = NCHW `out`; 1 = the re-laid input of a
+  // consuming tcgen05 convolution (its xs layout, described below), written
+  // 16 bytes (8 channels of one position) at a time
+  int omode;
+  int oHp, oWp, oplanes, opH, opW, osH, osW, onphW, oxIC;
+  int ophase_h[4], ophase_w[4];  // consumer phase index of (row mod osH), -1 when unused
+  uint4 *oxs;
+  // input: up to kMaxSrc channel ranges (a concatenation along channels),
+  // source s holding channels [src_c0[s], src_c0[s+1]) of the input
+  int nsrc;
+  int src_c0[kMaxSrc + 1];
+  const __half *src[kMaxSrc];
 };
 
 static uint32_t smem_need(const UmmaGeom &g) {
@@ -321,6 +335,17 @@ uint64_t umma_conv_input_bytes(const wgx_conv2d_params &p) {
 }
 
 // --------------------------------------------------------------- re-layout
+// Plane (b, c) of the (possibly concatenated) input: the source holding
+// channel c and c's channel within it.
+__device__ __forceinline__ const __half *src_plane(const UmmaGeom &g, long long b, int c) {
+  int s = 0;
+#pragma unroll
+  for (int k = 1; k < kMaxSrc; ++k)
+    if (k < g.nsrc && c >= g.src_c0[k]) s = k;
+  const int cs = g.src_c0[s + 1] - g.src_c0[s];
+  return g.src[s] + (b * cs + (c - g.src_c0[s])) * (long long)g.IH * g.IW;
+}
+
 // xs[b][cb][hp][wp][8] <- x[b][c][hp-pH][wp-pW], zero outside the image and
 // for channels >= IC. One thread per 16-byte row slot; consecutive threads
 // take consecutive wp, so the 2-byte gathers of one channel are coalesced
@@ -338,12 +363,11 @@ __global__ void pack_input(UmmaGeom g, const __half *__restrict__ x, uint4 *__re
   int ih = hp - g.pH, iw = wp - g.pW;
   __align__(16) __half v[8];
   bool inside = ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW;
-  const __half *src = x + ((b * g.IC + cb * 8) * g.IH + ih) * (long long)g.IW + iw;
-  long long cstride = (long long)g.IH * g.IW;
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     int c = cb * 8 + e;
-    v[e] = (inside && c < g.IC) ? src[e * cstride] : __float2half_rn(0.f);
+    v[e] = (inside && c < g.IC) ? src_plane(g, b, c)[(long long)ih * g.IW + iw]
+                                : __float2half_rn(0.f);
   }
   xs[i] = *reinterpret_cast<const uint4 *>(v);
 }
@@ -375,7 +399,7 @@ __global__ void pack_input_v4(UmmaGeom g, const __half *__restrict__ x, uint4 *_
     const int c = cb * 8 + e;
     ch[e] = make_uint2(0u, 0u);
     if (row_in && c < g.IC) {
-      const __half *src = x + ((b * g.IC + c) * g.IH + ih) * (long long)g.IW;
+      const __half *src = src_plane(g, b, c) + (long long)ih * g.IW;
       if (iw0 >= 0 && iw0 + 3 < g.IW) {
         ch[e] = *reinterpret_cast<const uint2 *>(src + iw0);
       } else {
@@ -440,7 +464,8 @@ __global__ void __launch_bounds__(256, 4)
   const bool row_in = ih >= 0 && ih < g.IH;
   const int nch = min(8, g.IC - cb * 8);
   const size_t cstride = size_t(g.IH) * g.IW;
-  const __half *src0 = x + ((size_t(b) * g.IC + cb * 8) * g.IH + (row_in ? ih : 0)) * g.IW;
+  // every 8-channel block lies in one source (source boundaries are multiples of 8)
+  const __half *src0 = (nch > 0 ? src_plane(g, b, cb * 8) : x) + size_t(row_in ? ih : 0) * g.IW;
   uint4 *dst = xs + size_t(row) * g.Wp;
   {
     const int wp0 = 8 * t + (g.pW & 7) - 8;
@@ -534,7 +559,7 @@ __global__ void pack_input_s2d(UmmaGeom g, const __half *__restrict__ x, uint4 *
       const int ih = g.sH * (hp - g.pH) + g.phH[phase / g.nphW];
       const int iw = g.sW * (wp - g.pW) + g.phW[phase % g.nphW];
       if (ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW)
-        val = x[((b * g.xIC + c) * g.IH + ih) * (long long)g.IW + iw];
+        val = src_plane(g, b, c)[(long long)ih * g.IW + iw];
     }
     v[e] = val;
   }
@@ -567,8 +592,7 @@ __global__ void __launch_bounds__(256)
   const bool inside = ih >= 0 && ih < g.IH && iw0 >= 0 && iw0 < g.IW;
   uint4 ch[8];
   const size_t cstride = size_t(g.IH) * g.IW;
-  const __half *src0 = x + ((size_t(b) * g.xIC + cb * 8) * g.IH + (inside ? ih : 0)) * g.IW +
-                       (inside ? iw0 : 0);
+  const __half *src0 = src_plane(g, b, cb * 8) + size_t(inside ? ih : 0) * g.IW + (inside ? iw0 : 0);
 #pragma unroll
   for (int e = 0; e < 8; ++e)
     ch[e] = inside ? *reinterpret_cast<const uint4 *>(src0 + e * cstride)
@@ -746,6 +770,27 @@ __device__ __forceinline__ uint32_t epi_act2(float a0, float a1, float b0, float
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// The consumer's re-layout slot (16 bytes: virtual channels vc..vc+7 of one
+// staged position) that holds output channels [c, c+8) of image b at output
+// position (oh, ow), or null when the consumer stages no such slot (an input
+// phase its filter never touches, or a row or column past its staged plane).
+__device__ __forceinline__ uint4 *xs_slot(const UmmaGeom &g, int b, int c, int oh, int ow) {
+  int hp, wp, vc;
+  if (g.osH == 1 && g.osW == 1) {
+    hp = oh + g.opH;
+    wp = ow + g.opW;
+    vc = c;
+  } else {
+    const int iph = g.ophase_h[oh % g.osH], ipw = g.ophase_w[ow % g.osW];
+    if (iph < 0 || ipw < 0) return nullptr;
+    vc = (iph * g.onphW + ipw) * g.oxIC + c;
+    hp = oh / g.osH + g.opH;
+    wp = ow / g.osW + g.opW;
+  }
+  if (hp >= g.oHp || wp >= g.oWp) return nullptr;
+  return g.oxs + ((size_t(b) * g.oplanes + (vc >> 3)) * g.oHp + hp) * g.oWp + wp;
 }
 
 // tile index -> (image, first position, output-channel tile); oc tile
@@ -991,17 +1036,36 @@ __global__ void __launch_bounds__(THREADS, 1)
         __half *dst_a = base + size_t(oh_a) * g.OW + ow_a;
         __half *dst_b = base + size_t(oh_b) * g.OW + ow_b;
         // columns j, j+1: channels oc, oc+1 of the same position (NT is even)
+        uint32_t pr[16];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
-          const int c = c0 + j;
-          const int oc = c & (g.NT - 1);
-          const bool second = (c >> g.lgNT) != mb0;
-          const uint32_t pr = epi_act2<ACT_T>(r[j], r[j + 1], sbias[oc], sbias[oc + 1], g.lo, g.hi);
-          const __half2 h2 = *reinterpret_cast<const __half2 *>(&pr);
-          if (second ? ok_b : ok_a) {
-            __half *d = (second ? dst_b : dst_a) + size_t(oc) * plane;
-            if (oc < g.OC) d[0] = __low2half(h2);
-            if (oc + 1 < g.OC) d[plane] = __high2half(h2);
+          const int oc = (c0 + j) & (g.NT - 1);
+          pr[j / 2] = epi_act2<ACT_T>(r[j], r[j + 1], sbias[oc], sbias[oc + 1], g.lo, g.hi);
+        }
+        if (g.omode) {
+          // 8 consecutive columns = 8 channels of one position: one 16-byte slot
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            const int c = c0 + 8 * q8;
+            const int oc = c & (g.NT - 1);
+            const bool second = (c >> g.lgNT) != mb0;
+            if (!(second ? ok_b : ok_a) || oc >= g.OC) continue;
+            uint4 *slot = xs_slot(g, b, oc, second ? oh_b : oh_a, second ? ow_b : ow_a);
+            if (slot)
+              *slot = make_uint4(pr[4 * q8], pr[4 * q8 + 1], pr[4 * q8 + 2], pr[4 * q8 + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const int c = c0 + j;
+            const int oc = c & (g.NT - 1);
+            const bool second = (c >> g.lgNT) != mb0;
+            const __half2 h2 = *reinterpret_cast<const __half2 *>(&pr[j / 2]);
+            if (second ? ok_b : ok_a) {
+              __half *d = (second ? dst_b : dst_a) + size_t(oc) * plane;
+              if (oc < g.OC) d[0] = __low2half(h2);
+              if (oc + 1 < g.OC) d[plane] = __high2half(h2);
+            }
           }
         }
       }
@@ -1062,6 +1126,38 @@ __global__ void __launch_bounds__(THREADS, 1)
         dst[0] = make_uint4(pw[0], pw[1], pw[2], pw[3]);
         dst[1] = make_uint4(pw[4], pw[5], pw[6], pw[7]);
         __syncwarp();
+        if (g.omode) {
+          // staged [32 channels][16 positions] -> 64 slots of 8 channels x 1
+          // position; lane k takes slots k and k + 32
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int id = lane + 32 * k;
+            const int pos = id & 15, grp = id >> 4;
+            const uint8_t *colp = stage + pos * 2;
+            uint32_t wv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t lo = *reinterpret_cast<const uint16_t *>(colp + (grp * 8 + 2 * e) * EPI_ROWB);
+              const uint32_t hi =
+                  *reinterpret_cast<const uint16_t *>(colp + (grp * 8 + 2 * e + 1) * EPI_ROWB);
+              wv[e] = lo | (hi << 16);
+            }
+            const int P = int(p0) + col0 + pos;
+            const int ohh = P / g.Wp, oww = P - ohh * g.Wp;
+            const int c = oc0 + grp * 8;
+            if (ohh < g.OH && oww < g.OW && c < g.OC) {
+              uint4 *slot = xs_slot(g, b, c, ohh, oww);
+              if (slot) *slot = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
+          }
+          __syncwarp();
+          ow += EPI_COLS;
+          while (ow >= g.Wp) {
+            ow -= g.Wp;
+            ++oh;
+          }
+          continue;
+        }
         const bool v0 = oh < g.OH && ow < g.OW;
         const int off0 = oh * g.OW + ow;
         // second position: next column, or the first column of the next row
@@ -1112,9 +1208,14 @@ void umma_conv_pack_weights(const wgx_conv2d_params &p, const __half *w, void *p
   check_cuda(cudaGetLastError(), "pack_weights launch");
 }
 
+bool umma_conv_link_ok(const wgx_conv2d_params &prod, const wgx_conv2d_params &cons) {
+  return umma_conv_supported(prod) && umma_conv_supported(cons) && prod.B == cons.B &&
+         prod.OC == cons.IC && prod.OH == cons.IH && prod.OW == cons.IW && prod.OC % 8 == 0;
+}
+
 void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
                    const __half *w_to_pack, const __half *bias, __half *out, void *xs,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, const UmmaLink *link) {
   if (!umma_conv_supported(p)) fail("conv2d: shape not supported by the tensor-core path");
   UmmaGeom g = make_geom(p);
   int dev = 0;
@@ -1122,17 +1223,66 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   g.err = device_error_word(dev);
   if ((reinterpret_cast<uintptr_t>(xs) & 15) || (reinterpret_cast<uintptr_t>(packed) & 15))
     fail("conv2d: scratch must be 16-byte aligned");
+  // ---- input sources
+  bool srcs_aligned = (reinterpret_cast<uintptr_t>(in) & 15) == 0;
+  if (link && link->nsrc > 0) {
+    if (link->nsrc > kMaxSrc) fail("conv2d: too many concatenated inputs");
+    g.nsrc = link->nsrc;
+    g.src_c0[0] = 0;
+    srcs_aligned = true;
+    for (int k = 0; k < link->nsrc; ++k) {
+      if (link->src_ch[k] % 8) fail("conv2d: concatenated input channels must be multiples of 8");
+      g.src[k] = link->src[k];
+      g.src_c0[k + 1] = g.src_c0[k] + link->src_ch[k];
+      srcs_aligned = srcs_aligned && (reinterpret_cast<uintptr_t>(link->src[k]) & 15) == 0;
+    }
+    if (g.src_c0[g.nsrc] != p.IC) fail("conv2d: concatenated inputs do not add up to IC");
+  } else {
+    g.nsrc = 1;
+    g.src[0] = in;
+    g.src_c0[0] = 0;
+    g.src_c0[1] = p.IC;
+  }
+  // ---- output into the consumer's re-laid input
+  if (link && link->consumer) {
+    if (!umma_conv_link_ok(p, *link->consumer)) fail("conv2d: invalid producer/consumer link");
+    if (reinterpret_cast<uintptr_t>(link->consumer_xs) & 15)
+      fail("conv2d: consumer buffer must be 16-byte aligned");
+    const UmmaGeom c = make_geom(*link->consumer);
+    g.omode = 1;
+    g.oHp = c.Hp;
+    g.oWp = c.Wp;
+    g.oplanes = c.C8 / 8;
+    g.opH = c.pH;
+    g.opW = c.pW;
+    g.osH = c.sH;
+    g.osW = c.sW;
+    g.onphW = c.nphW;
+    g.oxIC = c.xIC;
+    for (int k = 0; k < 4; ++k) g.ophase_h[k] = g.ophase_w[k] = -1;
+    if (c.sH == 1 && c.sW == 1) {
+      g.ophase_h[0] = g.ophase_w[0] = 0;
+    } else {
+      for (int k = 0; k < c.nphH; ++k) g.ophase_h[c.phH[k]] = k;
+      for (int k = 0; k < c.nphW; ++k) g.ophase_w[c.phW[k]] = k;
+    }
+    g.oxs = static_cast<uint4 *>(link->consumer_xs);
+  }
+  const bool xs_ready = link && link->xs_ready;
+  if (xs_ready && w_to_pack) fail("conv2d: weights must be packed before a linked launch");
   const uint64_t n_w64 = w_to_pack ? umma_conv_packed_weight_bytes(p) / 16 : 0;
   if (n_w64 >= (1ull << 31)) fail("conv2d: weights too large for the tensor-core path");
   const int n_w = int(n_w64);
   const bool strided = g.sH != 1 || g.sW != 1;
-  const int th_pack = timer_begin("umma_conv_pack", stream);
-  if (strided) {
+  const int th_pack = xs_ready ? -1 : timer_begin("umma_conv_pack", stream);
+  if (xs_ready) {
+    // re-laid by the producer
+  } else if (strided) {
     if (w_to_pack)
       pack_weights<<<unsigned((n_w + 255) / 256), 256, 0, stream>>>(
           g, w_to_pack, static_cast<uint4 *>(packed), n_w);
     if (g.sW == 2 && g.nphW == 2 && g.phW[0] == 0 && g.phW[1] == 1 && g.xIC % 8 == 0 &&
-        g.IW % 8 == 0 && g.C8 == g.IC && (reinterpret_cast<uintptr_t>(in) & 15) == 0) {
+        g.IW % 8 == 0 && g.C8 == g.IC && srcs_aligned) {
       const int qbase = -4 * ((g.pW + 3) / 4);
       const int groups_per_row = (g.Wp - g.pW - qbase + 3) / 4;
       const long long n_items =
@@ -1145,7 +1295,7 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
       pack_input_s2d<<<unsigned((n_slots + 255) / 256), 256, 0, stream>>>(
           g, in, static_cast<uint4 *>(xs), n_slots);
     }
-  } else if (g.IW % 8 == 0 && (reinterpret_cast<uintptr_t>(in) & 15) == 0) {
+  } else if (g.IW % 8 == 0 && srcs_aligned) {
     // input re-layout and weight packing in one launch
     const int groups_per_row = (g.Wp - (g.pW & 7) + 8 + 7) / 8;
     const long long n_items = (long long)g.B * (g.C8 / 8) * g.Hp * groups_per_row;
@@ -1159,7 +1309,7 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
     if (w_to_pack)
       pack_weights<<<unsigned((n_w + 255) / 256), 256, 0, stream>>>(
           g, w_to_pack, static_cast<uint4 *>(packed), n_w);
-    if (g.IW % 4 == 0 && (reinterpret_cast<uintptr_t>(in) & 7) == 0) {
+    if (g.IW % 4 == 0 && srcs_aligned) {
       const int groups_per_row = (g.Wp - (g.pW & 3) + 4 + 3) / 4;
       long long n = (long long)g.B * (g.C8 / 8) * g.Hp * groups_per_row;
       pack_input_v4<<<unsigned((n + 255) / 256), 256, 0, stream>>>(

@@ -10,12 +10,33 @@ uint64_t umma_conv_packed_weight_bytes(const wgx_conv2d_params &p);
 uint64_t umma_conv_input_bytes(const wgx_conv2d_params &p);
 void umma_conv_pack_weights(const wgx_conv2d_params &p, const __half *w, void *packed,
                             cudaStream_t stream);
+// How one tensor-core convolution connects to its neighbours in a program.
+struct UmmaLink {
+  // output: write the consumer convolution's re-laid input (its xs buffer,
+  // umma_conv_input_bytes(*consumer) bytes, padding and unused channels
+  // zeroed once by the caller) instead of NCHW `out`
+  const wgx_conv2d_params *consumer = nullptr;
+  void *consumer_xs = nullptr;
+  // input: `xs` already holds this convolution's re-laid input (written by
+  // its producer), so the re-layout kernel is skipped
+  bool xs_ready = false;
+  // input: the concatenation along channels of nsrc NCHW sources (channel
+  // counts src_ch, each a multiple of 8); 0 = the single tensor `in`
+  int nsrc = 0;
+  const __half *src[8] = {};
+  int src_ch[8] = {};
+};
+
+// True when `prod` can write its output straight into the re-laid input of
+// `cons` (both on the tensor-core path, matching shapes, OC % 8 == 0).
+bool umma_conv_link_ok(const wgx_conv2d_params &prod, const wgx_conv2d_params &cons);
+
 // in: NCHW fp16; packed: the operand-layout weights (umma_conv_pack_weights
 // output), or, when w_to_pack is not null, the buffer to pack w_to_pack
 // (OIHW) into first; xs: input scratch of umma_conv_input_bytes(p) bytes;
-// out: NCHW fp16.
+// out: NCHW fp16; link: see UmmaLink (null = a standalone convolution).
 void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
                    const __half *w_to_pack, const __half *bias, __half *out, void *xs,
-                   cudaStream_t stream);
+                   cudaStream_t stream, const UmmaLink *link = nullptr);
 
 }  // namespace wgx
