@@ -207,7 +207,9 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans)
     g.stages = 2;
     if (smem_need(g) <= SMEM_MAX) {
       g.resident = 1;
-      while (g.stages < 6 && (g.stages + 1) <= g.n_kstages) {
+      // stages are reused across tiles, so short filters (few stages per
+      // tile) still prefetch the next tiles' activations
+      while (g.stages < 6) {
         ++g.stages;
         if (smem_need(g) > SMEM_MAX) {
           --g.stages;
