@@ -126,6 +126,8 @@ def test_dense_f16_no_bias_and_clamp(ctx):
 # (B, IC, H, W, OC, K, stride, pad)
 STRIDED_F16 = [
     (1, 3, 64, 64, 16, 3, 2, 1),      # YOLO stem shape (IC = 3: 12 virtual channels)
+    (2, 5, 32, 40, 24, 3, 2, 1),      # few channels, vectorised re-layout (20 virtual)
+    (1, 2, 24, 24, 16, 3, 2, 0),      # 8 virtual channels, no padding
     (2, 16, 40, 40, 32, 3, 2, 1),     # vectorised re-layout (IC % 8 == 0, W % 8 == 0)
     (2, 32, 21, 19, 64, 3, 2, 1),     # odd sizes: per-slot re-layout
     (1, 64, 48, 48, 160, 3, 2, 1),    # two output-channel tiles

@@ -498,6 +498,69 @@ __global__ void __launch_bounds__(256, 4)
   }
 }
 
+// Space-to-depth re-layout for stride 2 with few input channels (XIC < 8,
+// e.g. an RGB stem): one thread takes staged row hp of image b and four
+// consecutive positions wp = q0 + pW .. q0 + pW + 3 (input columns 2*q0 ..
+// 2*q0 + 7, q0 a multiple of 4): one aligned 16-byte load per input channel
+// and row phase, then the C8/8 slots (8 virtual channels each) of the four
+// positions. Virtual channel vc = (2*ph + pw)*XIC + c, all index math
+// compile-time in XIC.
+template <int XIC>
+__global__ void __launch_bounds__(256)
+    pack_input_s2d_small(UmmaGeom g, uint4 *__restrict__ xs, int groups_per_row, int qbase,
+                         int n_items) {
+  const int item = blockIdx.x * 256 + threadIdx.x;
+  if (item >= n_items) return;
+  const int t = item % groups_per_row;
+  const int r = item / groups_per_row;
+  const int hp = r % g.Hp, b = r / g.Hp;
+  const int q0 = 4 * t + qbase;
+  const int iw0 = 2 * q0;  // a multiple of 8: the 8 columns are all in or all out
+  const bool col_in = iw0 >= 0 && iw0 < g.IW;
+  uint4 v[2][XIC];
+#pragma unroll
+  for (int ph = 0; ph < 2; ++ph) {
+    const int ih = 2 * (hp - g.pH) + ph;
+    const bool in = col_in && ih >= 0 && ih < g.IH;
+#pragma unroll
+    for (int c = 0; c < XIC; ++c)
+      v[ph][c] = in ? *reinterpret_cast<const uint4 *>(src_plane(g, b, c) + (long long)ih * g.IW + iw0)
+                    : make_uint4(0u, 0u, 0u, 0u);
+  }
+  const int planes = g.C8 / 8;
+  const size_t plane_rows = size_t(g.Hp) * g.Wp;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int wp = q0 + k + g.pW;
+    if (wp < 0 || wp >= g.Wp) continue;
+#pragma unroll
+    for (int pl = 0; pl < 4; ++pl) {
+      if (pl >= planes) break;
+      uint32_t w32[4];
+#pragma unroll
+      for (int e2 = 0; e2 < 4; ++e2) {
+        uint32_t h2 = 0;
+#pragma unroll
+        for (int hi = 0; hi < 2; ++hi) {
+          const int vc = pl * 8 + 2 * e2 + hi;
+          uint32_t hv = 0;
+          if (vc < 4 * XIC) {
+            const int phase = vc / XIC, c = vc % XIC;
+            const uint4 &src = v[phase >> 1][c];
+            // column 2k + pw of the 8 loaded: half pw of word k
+            const uint32_t word = k == 0 ? src.x : k == 1 ? src.y : k == 2 ? src.z : src.w;
+            hv = (phase & 1) ? (word >> 16) : (word & 0xffffu);
+          }
+          h2 |= hv << (16 * hi);
+        }
+        w32[e2] = h2;
+      }
+      xs[(size_t(b) * planes + pl) * plane_rows + size_t(hp) * g.Wp + wp] =
+          make_uint4(w32[0], w32[1], w32[2], w32[3]);
+    }
+  }
+}
+
 // packed[oct][khg][cb][kh_local][kw][chunk][row < wrows][8] <- w[oc][c][kh][kw]
 // (kh = khg*khs + kh_local): one pipeline stage's A operand is contiguous.
 __device__ __forceinline__ void pack_weights_body(const UmmaGeom &g, const __half *__restrict__ w,
@@ -1292,6 +1355,23 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
       if (n_items >= (1ll << 31) - 256) fail("conv2d: input too large for the re-layout kernel");
       pack_input_s2d_v8<<<unsigned((n_items + 255) / 256), 256, 0, stream>>>(
           g, in, static_cast<uint4 *>(xs), groups_per_row, qbase, int(n_items));
+    } else if (g.sH == 2 && g.sW == 2 && g.nphH == 2 && g.nphW == 2 && g.xIC < 8 &&
+               g.C8 <= 32 && g.IW % 8 == 0 && srcs_aligned) {
+      const int qbase = -4 * ((g.pW + 3) / 4);
+      const int groups_per_row = (g.Wp - g.pW - qbase + 3) / 4;
+      const long long n_items = (long long)g.B * g.Hp * groups_per_row;
+      if (n_items >= (1ll << 31) - 256) fail("conv2d: input too large for the re-layout kernel");
+      const unsigned blocks = unsigned((n_items + 255) / 256);
+      uint4 *o = static_cast<uint4 *>(xs);
+      switch (g.xIC) {
+        case 1: pack_input_s2d_small<1><<<blocks, 256, 0, stream>>>(g, o, groups_per_row, qbase, int(n_items)); break;
+        case 2: pack_input_s2d_small<2><<<blocks, 256, 0, stream>>>(g, o, groups_per_row, qbase, int(n_items)); break;
+        case 3: pack_input_s2d_small<3><<<blocks, 256, 0, stream>>>(g, o, groups_per_row, qbase, int(n_items)); break;
+        case 4: pack_input_s2d_small<4><<<blocks, 256, 0, stream>>>(g, o, groups_per_row, qbase, int(n_items)); break;
+        case 5: pack_input_s2d_small<5><<<blocks, 256, 0, stream>>>(g, o, groups_per_row, qbase, int(n_items)); break;
+        case 6: pack_input_s2d_small<6><<<blocks, 256, 0, stream>>>(g, o, groups_per_row, qbase, int(n_items)); break;
+        default: pack_input_s2d_small<7><<<blocks, 256, 0, stream>>>(g, o, groups_per_row, qbase, int(n_items)); break;
+      }
     } else {
       const long long n_slots = (long long)g.B * (g.C8 / 8) * g.plane_rows;
       pack_input_s2d<<<unsigned((n_slots + 255) / 256), 256, 0, stream>>>(
