@@ -501,35 +501,57 @@ __global__ void maxpool_kernel(PoolGeom g, const T *__restrict__ x, T *__restric
   }
 }
 
-// Small planes (IH*IW <= 4096): one CTA per plane stages the plane in
-// shared memory, then each thread reduces its windows from there. Same
-// start value, strict '>' and index rule as maxpool_kernel.
+// Small planes (IH*IW <= 4096, IH*OW <= 4096): one CTA per plane, separable
+// in shared memory. Pass 1 takes, for every input row and output column,
+// the maximum over the window's columns and the first column reaching it
+// (strict '>', left to right); pass 2 scans the window's rows top to bottom
+// over those row maxima with strict '>', so the winner is the first
+// maximum in the reference's row-major window order, with the same start
+// value and flat index ih*IW + iw as maxpool_kernel.
 template <class T>
 __global__ void __launch_bounds__(256) maxpool_plane_kernel(PoolGeom g, const T *__restrict__ x,
                                                             T *__restrict__ y,
                                                             int32_t *__restrict__ idx) {
-  __shared__ float tile[4096];
-  const long long plane = blockIdx.x;
+  extern __shared__ __align__(16) unsigned char mp_smem[];
   const int hw = g.IH * g.IW;
+  float *tile = reinterpret_cast<float *>(mp_smem);
+  float *rmax = tile + hw;
+  int16_t *rarg = reinterpret_cast<int16_t *>(rmax + g.IH * g.OW);
+  const long long plane = blockIdx.x;
   const T *xp = x + plane * hw;
   for (int i = threadIdx.x; i < hw; i += 256) tile[i] = lf(xp[i]);
+  __syncthreads();
+  const float start = sizeof(T) == 2 ? -65504.0f : -3.402823466e38f;
+  const int rw = g.IH * g.OW;
+  for (int i = threadIdx.x; i < rw; i += 256) {
+    const int ih = i / g.OW, ow = i - ih * g.OW;
+    float best = start;
+    int arg = -1;
+    for (int kw = 0; kw < g.kW; ++kw) {
+      const int iw = ow * g.sW - g.pW + kw * g.dW;
+      if (iw < 0 || iw >= g.IW) continue;
+      const float v = tile[ih * g.IW + iw];
+      if (v > best) {
+        best = v;
+        arg = iw;
+      }
+    }
+    rmax[i] = best;
+    rarg[i] = int16_t(arg);
+  }
   __syncthreads();
   const int ohw = g.OH * g.OW;
   for (int o = threadIdx.x; o < ohw; o += 256) {
     const int oh = o / g.OW, ow = o - oh * g.OW;
-    float best = sizeof(T) == 2 ? -65504.0f : -3.402823466e38f;
+    float best = start;
     int best_idx = 0;
     for (int kh = 0; kh < g.kH; ++kh) {
       const int ih = oh * g.sH - g.pH + kh * g.dH;
       if (ih < 0 || ih >= g.IH) continue;
-      for (int kw = 0; kw < g.kW; ++kw) {
-        const int iw = ow * g.sW - g.pW + kw * g.dW;
-        if (iw < 0 || iw >= g.IW) continue;
-        const float v = tile[ih * g.IW + iw];
-        if (v > best) {
-          best = v;
-          best_idx = ih * g.IW + iw;
-        }
+      const float v = rmax[ih * g.OW + ow];
+      if (v > best) {
+        best = v;
+        best_idx = ih * g.IW + rarg[ih * g.OW + ow];
       }
     }
     y[plane * ohw + o] = sf<T>(best);
@@ -593,13 +615,16 @@ void record_maxpool(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   const long long n = vals->numel;
   const int dt = in->dtype;
   const long long planes = (long long)g.N * g.C;
-  if ((long long)g.IH * g.IW <= 4096 && planes > 0 && planes < (1ll << 31)) {
+  if ((long long)g.IH * g.IW <= 4096 && (long long)g.IH * g.OW <= 4096 && g.IW <= 32767 &&
+      planes > 0 && planes < (1ll << 31)) {
     push(ctx, name, 1, [=](const ExecEnv &env) {
+      const size_t smem = (size_t(g.IH) * g.IW + size_t(g.IH) * g.OW) * 4 +
+                          size_t(g.IH) * g.OW * 2;
       if (dt == WGX_FLOAT16)
-        maxpool_plane_kernel<__half><<<unsigned(planes), 256, 0, env.stream>>>(
+        maxpool_plane_kernel<__half><<<unsigned(planes), 256, smem, env.stream>>>(
             g, (const __half *)px, (__half *)py, pi);
       else
-        maxpool_plane_kernel<float><<<unsigned(planes), 256, 0, env.stream>>>(
+        maxpool_plane_kernel<float><<<unsigned(planes), 256, smem, env.stream>>>(
             g, (const float *)px, (float *)py, pi);
       check_cuda(cudaGetLastError(), "maxpool launch");
     });
