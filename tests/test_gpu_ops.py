@@ -207,3 +207,60 @@ def test_constant_pad_and_flat_copies(ctx):
         o = empty(ctx, shape, "float16")
         run(ctx, shader, [T(ctx, x)] + args_tail + [o])
         np.testing.assert_array_equal(o.numpy().reshape(-1), x.reshape(-1))
+
+
+def attention_program(n, L, dq, dv):
+    """The PSA attention spelling of the YOLO26-N export: bmm(Q, K^T) ->
+    view -> softmax(-1) -> permute(0,1,3,2) -> squeeze -> bmm(V^T, P^T)."""
+    h = 2
+    b = n // h
+    vals = [
+        {"type": "tensor", "shape": [n, L, dq], "dtype": "float16", "memObjId": 0},      # 0 Q
+        {"type": "tensor", "shape": [n, dq, L], "dtype": "float16", "memObjId": 1},      # 1 K^T
+        {"type": "tensor", "shape": [n, dv, L], "dtype": "float16", "memObjId": 2},      # 2 V^T
+        {"type": "tensor", "shape": [n, L, L], "dtype": "float16", "memObjId": 3},       # 3 S
+        {"type": "list", "items": [b, h, L, L]},                                           # 4
+        {"type": "tensor", "shape": [b, h, L, L], "dtype": "float16", "memObjId": 4},    # 5
+        {"type": "scalar", "value": -1},                                                   # 6
+        {"type": "scalar", "value": False},                                                # 7
+        {"type": "tensor", "shape": [b, h, L, L], "dtype": "float16", "memObjId": 3},    # 8 P
+        {"type": "list", "items": [0, 1, 3, 2]},                                           # 9
+        {"type": "tensor", "shape": [b, h, L, L], "dtype": "float16", "memObjId": 4},    # 10 P^T
+        {"type": "list", "items": [0]},                                                    # 11
+        {"type": "tensor", "shape": [n, L, L], "dtype": "float16", "memObjId": 3},       # 12
+        {"type": "tensor", "shape": [n, dv, L], "dtype": "float16", "memObjId": 5},      # 13 O^T
+    ]
+    chain = [
+        {"name": "aten.bmm.default", "args": [0, 1, 3]},
+        {"name": "aten.view_copy.default", "args": [3, 4, 5]},
+        {"name": "aten._softmax.default", "args": [5, 6, 7, 8]},
+        {"name": "aten.permute_copy.default", "args": [8, 9, 10]},
+        {"name": "aten.view_copy.default", "args": [10, [n, L, L] and 4, 12]},
+        {"name": "aten.bmm.default", "args": [2, 12, 13]},
+    ]
+    vals.append({"type": "list", "items": [n, L, L]})                                    # 14
+    chain[4]["args"] = [10, 14, 12]
+    sizes = [n * L * dq * 2, n * dq * L * 2, n * dv * L * 2, n * L * L * 2, n * L * L * 2,
+             n * dv * L * 2]
+    return {"version": "1", "chain": chain, "values": vals, "inputIds": [0, 1, 2],
+            "outputIds": [13],
+            "memoryPlan": {"pools": [{"id": i, "size": sz} for i, sz in enumerate(sizes)]}}
+
+
+@pytest.mark.parametrize("n,L,dq,dv", [(4, 400, 32, 64), (2, 37, 16, 32), (6, 129, 32, 96)])
+def test_fused_attention_program(ctx, n, L, dq, dv):
+    q = (RNG.standard_normal((n, L, dq)) * 0.3).astype(np.float16)
+    kt = (RNG.standard_normal((n, dq, L)) * 0.3).astype(np.float16)
+    vt = RNG.standard_normal((n, dv, L)).astype(np.float16)
+    out = empty(ctx, (n, dv, L), "float16")
+    ctx.recordProgram(attention_program(n, L, dq, dv), b"", [T(ctx, q), T(ctx, kt), T(ctx, vt), out])
+    # input copies + one fused kernel + output copy
+    assert ctx.stats()["commands"] == 5
+    ctx.submit()
+    ctx.sync()
+    s = np.matmul(q.astype(np.float64), kt.astype(np.float64))
+    p = np.exp(s - s.max(-1, keepdims=True))
+    p /= p.sum(-1, keepdims=True)
+    ref = np.matmul(vt.astype(np.float64), np.swapaxes(p, 1, 2))
+    err = np.abs(out.numpy().astype(np.float64) - ref).max() / np.abs(ref).max()
+    assert err <= 5e-3, err

@@ -143,6 +143,13 @@ void launch_mm(const void *a, const void *b, void *out, int64_t M, int64_t N, in
                int dtype, void *scratch, uint64_t scratch_bytes, cudaStream_t stream);
 uint64_t mm_scratch_bytes(int64_t M, int64_t N, int64_t K, int dtype);
 
+// Fused attention O^T[c][i] = sum_j V^T[c][j] softmax_j(sum_d Q[i][d] K^T[d][j])
+// per head (csrc/attention.cu): Q [n, L, dq], K^T [n, dq, L], V^T [n, dv, L],
+// O^T [n, dv, L], all fp16.
+bool attention_supported(int64_t n, int64_t L, int64_t dq, int64_t dv);
+void launch_attention(const __half *Q, const __half *KT, const __half *VT, __half *OT, int64_t n,
+                      int64_t L, int64_t dq, int64_t dv, cudaStream_t stream);
+
 wgx_conv2d_plan plan_conv2d(const wgx_conv2d_params &p);
 // packed-weight layout size for the tcgen05 path (0 when the plan is not UMMA)
 uint64_t conv2d_packed_weight_bytes(const wgx_conv2d_params &p);

@@ -347,6 +347,125 @@ LinkPlan plan_links(wgx_context *ctx, const Program &P,
   return L;
 }
 
+// Attention fusion: bmm(Q, K^T) -> view -> softmax(-1) -> permute(last two)
+// -> squeeze/view -> bmm(V^T, .) (the PSA block of YOLO26-N) becomes one
+// fused tcgen05 kernel recorded where the second bmm stood. Every
+// intermediate must have exactly one reader and not be a program output, and
+// no op left between the two bmm's may write into the buffers of Q or K^T
+// (the fused kernel reads them later than the first bmm did).
+struct AttnPlan {
+  struct Site {
+    int64_t q, kt, vt, ot;
+    // when an op left between the two bmm's reuses the memory of Q or K^T,
+    // both are copied into these buffers where the first bmm stood
+    void *q_snap = nullptr, *kt_snap = nullptr;
+  };
+  std::map<size_t, Site> at;        // chain index of the second bmm -> operands
+  std::map<size_t, size_t> snap_at; // chain index of the first bmm -> its second bmm
+  std::set<size_t> skip;
+};
+
+AttnPlan plan_attention(wgx_context *ctx, const Program &P,
+                        const std::map<int64_t, wgx_tensor *> &tensors,
+                        const std::vector<int> &fusion, const std::set<size_t> &already_skipped) {
+  AttnPlan A;
+  std::map<int64_t, std::vector<size_t>> readers;
+  for (size_t i = 0; i < P.chain.size(); ++i) {
+    if (fusion[i] == 2 || already_skipped.count(i)) continue;
+    const POp &op = P.chain[i];
+    for (size_t k = 0; k + 1 < op.args.size(); ++k) {
+      const int64_t a = op.args[k];
+      if (a < 0 || size_t(a) >= P.values.size()) continue;
+      readers[a].push_back(i);
+      if (P.values[a].kind == PValue::TensorList)
+        for (auto t : P.values[a].items) readers[t].push_back(i);
+    }
+  }
+  std::set<int64_t> outputs(P.output_ids.begin(), P.output_ids.end());
+  auto T = [&](int64_t v) -> const wgx_tensor * {
+    auto it = tensors.find(v);
+    return it == tensors.end() ? nullptr : it->second;
+  };
+  // the single reader of value v, or SIZE_MAX
+  auto only_reader = [&](int64_t v) -> size_t {
+    auto it = readers.find(v);
+    if (it == readers.end() || it->second.size() != 1 || outputs.count(v)) return SIZE_MAX;
+    return it->second[0];
+  };
+  for (size_t i = 0; i < P.chain.size(); ++i) {
+    const POp &b1 = P.chain[i];
+    if (b1.name != "aten.bmm.default" || b1.args.size() != 3 || fusion[i] == 2) continue;
+    const wgx_tensor *q = T(b1.args[0]), *kt = T(b1.args[1]), *s = T(b1.args[2]);
+    if (!q || !kt || !s || q->ndim != 3 || kt->ndim != 3 || q->dtype != WGX_FLOAT16) continue;
+    const int64_t n = q->shape[0], L = q->shape[1], dq = q->shape[2];
+    if (kt->shape[0] != n || kt->shape[1] != dq || kt->shape[2] != L) continue;
+    std::vector<size_t> chain_ops{i};
+    size_t r1 = only_reader(b1.args[2]);
+    if (r1 == SIZE_MAX || P.chain[r1].name != "aten.view_copy.default") continue;
+    size_t r2 = only_reader(P.chain[r1].args.back());
+    if (r2 == SIZE_MAX || P.chain[r2].name != "aten._softmax.default") continue;
+    {
+      const wgx_tensor *x = T(P.chain[r2].args[0]);
+      const PValue &d = P.values[P.chain[r2].args[1]];
+      if (!x || d.kind != PValue::Scalar || (int(d.num) != -1 && int(d.num) != x->ndim - 1))
+        continue;
+    }
+    size_t r3 = only_reader(P.chain[r2].args.back());
+    if (r3 == SIZE_MAX || P.chain[r3].name != "aten.permute_copy.default") continue;
+    {
+      const PValue &pv = P.values[P.chain[r3].args[1]];
+      const wgx_tensor *x = T(P.chain[r3].args[0]);
+      if (!x || pv.kind != PValue::List || int(pv.items.size()) != x->ndim) continue;
+      bool swap_last = true;
+      const int nd = x->ndim;
+      for (int d = 0; d < nd; ++d) {
+        const int64_t want = d == nd - 1 ? nd - 2 : d == nd - 2 ? nd - 1 : d;
+        const int64_t got = pv.items[d] < 0 ? pv.items[d] + nd : pv.items[d];
+        swap_last = swap_last && got == want;
+      }
+      if (!swap_last) continue;
+    }
+    size_t r4 = only_reader(P.chain[r3].args.back());
+    if (r4 == SIZE_MAX || (P.chain[r4].name != "aten.squeeze_copy.dims" &&
+                           P.chain[r4].name != "aten.view_copy.default"))
+      continue;
+    const int64_t pt = P.chain[r4].args.back();
+    size_t r5 = only_reader(pt);
+    if (r5 == SIZE_MAX || P.chain[r5].name != "aten.bmm.default" ||
+        P.chain[r5].args.size() != 3 || P.chain[r5].args[1] != pt)
+      continue;
+    const wgx_tensor *vt = T(P.chain[r5].args[0]), *ot = T(P.chain[r5].args[2]),
+                     *ptt = T(pt);
+    if (!vt || !ot || !ptt || vt->ndim != 3 || vt->dtype != WGX_FLOAT16) continue;
+    const int64_t dv = vt->shape[1];
+    if (vt->shape[0] != n || vt->shape[2] != L || ptt->numel != n * L * L) continue;
+    if (ot->shape[0] != n || ot->shape[1] != dv || ot->shape[2] != L) continue;
+    if (!attention_supported(n, L, dq, dv)) continue;
+    if (!(i < r1 && r1 < r2 && r2 < r3 && r3 < r4 && r4 < r5)) continue;
+    std::set<size_t> absorbed{i, r1, r2, r3, r4};
+    bool safe = true;
+    for (size_t k = i + 1; k < r5 && safe; ++k) {
+      if (absorbed.count(k) || fusion[k] == 2 || already_skipped.count(k)) continue;
+      const int64_t o = fusion[k] == 1 ? P.chain[k + 2].args[2] : P.chain[k].args.back();
+      std::vector<int64_t> outs{o};
+      if (P.values[o].kind == PValue::TensorList) outs = P.values[o].items;
+      for (auto t : outs) {
+        const wgx_tensor *w = T(t);
+        if (w && (w->buffer == q->buffer || w->buffer == kt->buffer)) safe = false;
+      }
+    }
+    AttnPlan::Site site{b1.args[0], b1.args[1], P.chain[r5].args[0], P.chain[r5].args[2]};
+    if (!safe) {
+      site.q_snap = ctx->alloc_device(q->byte_length());
+      site.kt_snap = ctx->alloc_device(kt->byte_length());
+      A.snap_at[i] = r5;
+    }
+    A.at[r5] = site;
+    A.skip.insert(absorbed.begin(), absorbed.end());
+  }
+  return A;
+}
+
 }  // namespace
 
 static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len,
@@ -462,8 +581,42 @@ static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len
   const auto &reg = op_registry();
   std::vector<int> fusion = plan_fusion(P, tensors);
   const LinkPlan links = plan_links(ctx, P, tensors, fusion);
+  const AttnPlan attn = plan_attention(ctx, P, tensors, fusion, links.skip);
   for (size_t oi = 0; oi < P.chain.size(); ++oi) {
-    if (fusion[oi] == 2 || links.skip.count(oi)) continue;
+    if (auto sn = attn.snap_at.find(oi); sn != attn.snap_at.end()) {
+      // snapshot Q and K^T where the first bmm read them
+      const AttnPlan::Site &site = attn.at.at(sn->second);
+      const wgx_tensor *q = tensors[site.q], *kt = tensors[site.kt];
+      const void *sq = q->data(), *sk = kt->data();
+      void *dq_ = site.q_snap, *dk = site.kt_snap;
+      const uint64_t nq = q->byte_length(), nk = kt->byte_length();
+      Command c;
+      c.name = "attention operand snapshot";
+      c.run = [=](const ExecEnv &env) {
+        check_cuda(cudaMemcpyAsync(dq_, sq, nq, cudaMemcpyDeviceToDevice, env.stream), "snapshot");
+        check_cuda(cudaMemcpyAsync(dk, sk, nk, cudaMemcpyDeviceToDevice, env.stream), "snapshot");
+      };
+      ctx->commands.push_back(std::move(c));
+      continue;
+    }
+    if (fusion[oi] == 2 || links.skip.count(oi) || attn.skip.count(oi)) continue;
+    if (auto at = attn.at.find(oi); at != attn.at.end()) {
+      const wgx_tensor *q = tensors[at->second.q], *kt = tensors[at->second.kt],
+                       *vt = tensors[at->second.vt], *ot = tensors[at->second.ot];
+      const int64_t n = q->shape[0], L = q->shape[1], dq = q->shape[2], dv = vt->shape[1];
+      const __half *pq = static_cast<const __half *>(at->second.q_snap ? at->second.q_snap
+                                                                       : q->data()),
+                   *pk = static_cast<const __half *>(at->second.kt_snap ? at->second.kt_snap
+                                                                        : kt->data()),
+                   *pv = static_cast<const __half *>(vt->data());
+      __half *po = static_cast<__half *>(ot->data());
+      Command c;
+      c.name = "attention (bmm -> softmax -> bmm)";
+      c.kernel_launches = 1;
+      c.run = [=](const ExecEnv &env) { launch_attention(pq, pk, pv, po, n, L, dq, dv, env.stream); };
+      ctx->commands.push_back(std::move(c));
+      continue;
+    }
     const POp &op = P.chain[oi];
     auto rit = reg.find(op.name);
     if (rit == reg.end()) fail("program: unknown operator '" + op.name + "'");

@@ -46,6 +46,7 @@
 // Every mbarrier wait is bounded (about 2 s of %globaltimer); on expiry the
 // waiting role sets a bit in the device error word and stops, so a broken
 // pipeline returns an error instead of hanging the GPU.
+#include "tcgen05.h"
 #include "umma_conv.h"
 
 namespace wgx {
@@ -57,7 +58,6 @@ constexpr int EPI_WARPS = 16;    // four per TMEM lane quadrant
 constexpr int THREADS = 32 * (EPI_WARP0 + EPI_WARPS);
 constexpr uint32_t TMEM_COLS = 512;  // two accumulators of UN fp32 columns
 constexpr int MAX_KW = 7;
-constexpr uint64_t WAIT_NS = 2000000000ull;
 constexpr int EPI_COLS = 16;     // positions per staged epilogue block
 constexpr int EPI_ROWB = 48;     // staged channel row: 16 fp16 + 16 B pad
 constexpr uint32_t EPI_BYTES = EPI_WARPS * 32 * EPI_ROWB;
@@ -692,103 +692,7 @@ __global__ void pack_weights(UmmaGeom g, const __half *__restrict__ w, uint4 *__
   if (i < n_slots) pack_weights_body(g, w, packed, i);
 }
 
-// ------------------------------------------------------------ PTX helpers
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-// Bounded wait: true when the phase with `parity` completed, false after
-// WAIT_NS (the caller then records the error and stops its role).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  uint64_t t0 = global_ns();
-  while (true) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    if (global_ns() - t0 > WAIT_NS) return false;
-  }
-}
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
-                                         uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(dst),
-      "l"(src), "r"(bytes), "r"(bar)
-      : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-// K-major, no swizzle: rows 16 B apart (SBO = 128 B between 8-row core
-// matrices), the two 8-element K chunks of one MMA `lbo` bytes apart.
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t addr, uint32_t lbo) {
-  uint64_t d = 0;
-  d |= uint64_t((addr & 0x3FFFF) >> 4);
-  d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
-  d |= uint64_t((128u >> 4) & 0x3FFF) << 32;
-  d |= uint64_t(1) << 46;  // descriptor version for sm_100
-  return d;                // base offset 0, layout SWIZZLE_NONE (0)
-}
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                        uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *r) {
-  uint32_t *u = reinterpret_cast<uint32_t *>(r);
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]),
-        "=r"(u[7]), "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]),
-        "=r"(u[14]), "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]),
-        "=r"(u[20]), "=r"(u[21]), "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]),
-        "=r"(u[26]), "=r"(u[27]), "=r"(u[28]), "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *r) {
-  uint32_t *u = reinterpret_cast<uint32_t *>(r);
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]),
-        "=r"(u[7]), "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]),
-        "=r"(u[14]), "=r"(u[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
+// PTX helpers: tcgen05.h
 
 __device__ __forceinline__ float tanh_approx(float x) {
   float y;
