@@ -323,6 +323,49 @@ def test_config2_full_batch_properties(ctx):
 
 
 # --------------------------------------------------- program fusion
+def test_program_depthwise_silu_fusion_in_place(ctx):
+    """A depthwise conv -> sigmoid -> mul whose output reuses the conv
+    input's pool fuses (the tiled depthwise kernel stages whole planes
+    before writing them): 3 commands, result equal to the oracle's."""
+    C, H, W = 24, 20, 20
+    (x,) = oracle.make_inputs([(2, C, H, W)], seed=110)
+    (w, b) = oracle.make_inputs([(C, 1, 3, 3), (C,)], seed=111, scale=[0.3, 0.05])
+    wbytes = w.tobytes() + b.tobytes()
+    shape = [2, C, H, W]
+    nb = 2 * C * H * W * 2
+    prog = {
+        "version": "1",
+        "chain": [
+            {"name": "aten.convolution.default", "args": [0, 1, 2, 3, 4, 5, 6, 7, 8, 9]},
+            {"name": "aten.sigmoid.default", "args": [9, 10]},
+            {"name": "aten.mul.Tensor", "args": [9, 10, 11]},
+        ],
+        "values": [
+            {"type": "tensor", "shape": shape, "dtype": "float16", "memObjId": 0},
+            {"type": "tensor", "shape": [C, 1, 3, 3], "dtype": "float16", "weightsOffset": 0,
+             "weightsLength": w.nbytes},
+            {"type": "tensor", "shape": [C], "dtype": "float16", "weightsOffset": w.nbytes,
+             "weightsLength": b.nbytes},
+            {"type": "list", "items": [1, 1]}, {"type": "list", "items": [1, 1]},
+            {"type": "list", "items": [1, 1]}, {"type": "scalar", "value": False},
+            {"type": "list", "items": [0, 0]}, {"type": "scalar", "value": C},
+            {"type": "tensor", "shape": shape, "dtype": "float16", "memObjId": 1},
+            {"type": "tensor", "shape": shape, "dtype": "float16", "memObjId": 2},
+            {"type": "tensor", "shape": shape, "dtype": "float16", "memObjId": 0},
+        ],
+        "inputIds": [0], "outputIds": [11],
+        "memoryPlan": {"pools": [{"id": i, "size": nb} for i in range(3)]},
+    }
+    tin = ctx.tensor("float16", shape).setData(x)
+    tout = ctx.tensor("float16", shape)
+    ctx.recordProgram(prog, wbytes, [tin, tout])
+    assert ctx.stats()["commands"] == 3
+    ctx.submit()
+    ctx.sync()
+    ex = oracle.conv2d(x, w, b, 1, 1, 1, C, act=oracle.ACT_SILU, mode="exact")
+    assert oracle.rel_err(tout.numpy(), ex) <= 5e-3
+
+
 @pytest.mark.parametrize("out_pool,ic,commands", [(3, 32, 3), (0, 32, 3), (0, 4, 5)])
 def test_program_conv_sigmoid_mul_fusion(ctx, out_pool, ic, commands):
     """conv -> sigmoid -> mul becomes one conv with a SiLU epilogue (input

@@ -736,6 +736,23 @@ wgx_conv2d_plan plan_conv2d(const wgx_conv2d_params &p) {
   return plan;
 }
 
+bool conv2d_in_place_safe(const wgx_conv2d_params &p) {
+  wgx_conv2d_plan plan;
+  try {
+    plan = plan_conv2d(p);
+  } catch (const Error &) {
+    return false;
+  }
+  // tensor cores: the first kernel stages the whole input before the second writes
+  if (plan.variant == WGX_CONV_UMMA) return true;
+  // tiled depthwise with whole planes per CTA: each CTA stages its planes in
+  // shared memory before writing them, and no other CTA reads those planes
+  DwTile d{};
+  const int esize = p.dtype == WGX_FLOAT16 ? 2 : 4;
+  return plan.variant == WGX_CONV_DEPTHWISE && dw_tiling(p, esize, d) && d.bands == 1 &&
+         p.OH == p.IH && p.OW == p.IW;
+}
+
 uint64_t conv2d_packed_weight_bytes(const wgx_conv2d_params &p) {
   if (plan_conv2d(p).variant != WGX_CONV_UMMA) return 0;
   return umma_conv_packed_weight_bytes(p);

@@ -151,6 +151,8 @@ void launch_attention(const __half *Q, const __half *KT, const __half *VT, __hal
                       int64_t L, int64_t dq, int64_t dv, cudaStream_t stream);
 
 wgx_conv2d_plan plan_conv2d(const wgx_conv2d_params &p);
+// true when the convolution may write its output over its own input
+bool conv2d_in_place_safe(const wgx_conv2d_params &p);
 // packed-weight layout size for the tcgen05 path (0 when the plan is not UMMA)
 uint64_t conv2d_packed_weight_bytes(const wgx_conv2d_params &p);
 uint64_t conv2d_input_scratch_bytes(const wgx_conv2d_params &p);

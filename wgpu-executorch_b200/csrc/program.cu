@@ -201,12 +201,12 @@ bool is_umma(const wgx_conv2d_params &p) {
   }
 }
 
-// True when the convolution `c` (aten.convolution positional args) takes
-// the tensor-core path, which stages its whole input in scratch first.
+// True when the convolution `c` (aten.convolution positional args) may
+// write over its own input (see conv2d_in_place_safe).
 bool conv_in_place_safe(const Program &P, const POp &c,
                         const std::map<int64_t, wgx_tensor *> &tensors) {
   wgx_conv2d_params p{};
-  return conv_params(P, c, tensors, c.args[9], WGX_ACT_SILU, &p) && is_umma(p);
+  return conv_params(P, c, tensors, c.args[9], WGX_ACT_SILU, &p) && conv2d_in_place_safe(p);
 }
 
 // SiLU fusion: conv(v) ; sigmoid(v)->s ; mul(v,s)->y  ==>  conv_silu -> y
@@ -241,10 +241,8 @@ std::vector<int> plan_fusion(const Program &P, const std::map<int64_t, wgx_tenso
     if (tv->second->numel != ty->second->numel || tv->second->dtype != ty->second->dtype)
       continue;
     // The fused conv writes y directly. When y shares the conv input's
-    // buffer, only the tensor-core path is safe (its first kernel copies the
-    // whole input into scratch before the second writes the output); the
-    // CUDA-core variants read the input while writing, so they never fuse
-    // in place.
+    // buffer, only variants that read all of a region before writing it
+    // may fuse (conv2d_in_place_safe).
     if (ty->second->buffer->dptr == tx->second->buffer->dptr &&
         !conv_in_place_safe(P, c, tensors))
       continue;
