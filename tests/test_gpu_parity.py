@@ -93,6 +93,10 @@ DENSE_F16 = [
     (1, 96, 40, 40, 96, 3, 3, 1, 1),
     (8, 64, 48, 48, 192, 3, 3, 1, 1),     # streamed weights, >1 tile per CTA
     (3, 16, 30, 30, 24, 5, 3, 2, 1),      # KH != KW with padding
+    # 1x1 / stride 1 / no padding: activations read from NCHW by TMA
+    (2, 40, 16, 24, 96, 1, 1, 0, 1),      # IC % 32 != 0: zero-filled channel rows
+    (3, 64, 20, 20, 200, 1, 1, 0, 1),     # two output-channel tiles
+    (2, 16, 32, 32, 24, 1, 1, 0, 1),      # positions on M, 16-channel stages
     # OC <= 64: positions on the MMA M side (N = 16 / 32 / 64)
     (2, 64, 40, 40, 64, 3, 3, 1, 1),
     (2, 48, 33, 35, 17, 1, 1, 0, 1),

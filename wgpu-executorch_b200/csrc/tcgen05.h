@@ -106,4 +106,27 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *r) {
 }
 
 
+// 3-D tiled TMA load (no multicast) completing on mbarrier `bar`.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, int x, int y, int z,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+// MN-major operand with 128-byte swizzle: atoms of 8 K-rows x 128 bytes (64
+// fp16 along M/N), `lbo` bytes between atoms along M/N, `sbo` bytes between
+// 8-row groups along K; `addr` 1024-byte aligned per atom.
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= uint64_t((addr & 0x3FFFF) >> 4);
+  d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
+  d |= uint64_t((sbo >> 4) & 0x3FFF) << 32;
+  d |= uint64_t(1) << 46;  // descriptor version for sm_100
+  d |= uint64_t(2) << 61;  // SWIZZLE_128B
+  return d;
+}
+
 }  // namespace wgx

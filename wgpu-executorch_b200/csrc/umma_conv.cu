@@ -46,7 +46,10 @@
 // Every mbarrier wait is bounded (about 2 s of %globaltimer); on expiry the
 // waiting role sets a bit in the device error word and stops, so a broken
 // pipeline returns an error instead of hanging the GPU.
+#include <cstring>
+
 #include "tcgen05.h"
+#include "tma.h"
 #include "umma_conv.h"
 
 namespace wgx {
@@ -100,11 +103,16 @@ struct UmmaGeom {
   int nsrc;
   int src_c0[kMaxSrc + 1];
   const __half *src[kMaxSrc];
+  // direct = 1 (1x1, stride 1, no padding): the producer loads activation
+  // tiles straight from the NCHW sources with TMA (boxes of 64 positions x
+  // dbox channels, 128-byte swizzle, zero fill past the image and past a
+  // source's channels) and the MMAs read them MN-major; no re-layout runs
+  int direct, dbox;
 };
 
 static uint32_t smem_need(const UmmaGeom &g) {
   return g.w_region_bytes + uint32_t(g.stages) * g.b_stage_bytes + EPI_BYTES +
-         (2 * g.stages + 5) * 8 + 16 + 128;
+         (2 * g.stages + 5) * 8 + 16 + 1024;
 }
 
 // Geometry for one staging choice: each pipeline stage carries `bk` input
@@ -783,15 +791,17 @@ template <int KW_T, int ACT_T, int TRANS>
 __global__ void __launch_bounds__(THREADS, 1)
     umma_conv_kernel(const UmmaGeom g, const uint8_t *__restrict__ xs,
                      const uint8_t *__restrict__ wpk, const __half *__restrict__ bias,
-                     __half *__restrict__ out) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
-                                              ~uintptr_t(127));
+                     __half *__restrict__ out, const __grid_constant__ TmapSet tm) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // activation stages first, on a 1024-byte boundary (128-byte swizzle atoms
+  // of the direct mode); stage sizes are multiples of 1024 bytes there
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int S = g.stages;
-  uint8_t *sW = smem;                                  // weights (resident or per stage)
-  uint8_t *sB = sW + g.w_region_bytes;                 // activation stages
-  uint8_t *sE = sB + size_t(S) * g.b_stage_bytes;      // epilogue staging
+  uint8_t *sB = smem;                                  // activation stages
+  uint8_t *sW = sB + size_t(S) * g.b_stage_bytes;      // weights (resident or per stage)
+  uint8_t *sE = sW + g.w_region_bytes;                 // epilogue staging
   uint64_t *bars = reinterpret_cast<uint64_t *>(sE + EPI_BYTES);
   uint64_t *full = bars, *empty = bars + S;
   uint64_t *accf = bars + 2 * S, *acce = accf + 2, *wbar = acce + 2;
@@ -851,6 +861,22 @@ __global__ void __launch_bounds__(THREADS, 1)
             bulk_g2s(smem_u32(sW + size_t(slot) * g.a_stage_bytes),
                      wpk + (size_t(oct) * g.n_kstages + s) * g.a_stage_bytes, g.a_stage_bytes,
                      fb);
+          if (g.direct) {
+            // TMA boxes of 64 positions x dbox channels: atom j (64 positions,
+            // bk rows of 128 bytes) at j * bk * 128, channel group rows inside
+            uint8_t *stage = sB + size_t(slot) * g.b_stage_bytes;
+            for (int c = cbk * g.bk; c < (cbk + 1) * g.bk; c += g.dbox) {
+              int src = 0;
+              for (int k = 1; k < g.nsrc; ++k)
+                if (c >= g.src_c0[k]) src = k;
+              const int y = c - g.src_c0[src];
+              const int row = c - cbk * g.bk;
+              for (int j = 0; j < g.tile_pos / 64; ++j)
+                tma_load_3d(smem_u32(stage + size_t(j) * g.bk * 128 + size_t(row) * 128),
+                            &tm.m[src], int(p0) + 64 * j, y, b, fb);
+            }
+            continue;
+          }
           const long long row0 = p0 + (long long)khg * g.khs * g.dH * g.Wp;
           for (int ch = 0; ch < g.chunks; ++ch) {
             const long long plane = (long long)b * (g.C8 / 8) + cbk * g.chunks + ch;
@@ -908,6 +934,27 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t a_base =
               smem_u32(sW + size_t(g.resident ? s : slot) * g.a_stage_bytes);
           const uint32_t b_base = smem_u32(sB + size_t(slot) * g.b_stage_bytes);
+          if (g.direct) {
+            // activations MN-major (128-byte swizzle): atoms of 64 positions
+            // bk*128 bytes apart, 8-channel groups 1024 bytes apart; one MMA
+            // takes two groups (K = 16); weights K-major as always
+            const uint32_t x_lbo = uint32_t(g.bk) * 128;
+            const uint32_t idesc_mn = idesc | (TRANS ? (1u << 15) : (1u << 16));
+            for (int ks = 0; ks < g.bk / 16; ++ks) {
+              const uint64_t wdesc = kmajor_desc(a_base + uint32_t(ks) * 2 * a_lbo, a_lbo);
+              const uint32_t xaddr = b_base + uint32_t(ks) * 2 * 1024;
+              if constexpr (TRANS) {
+                for (int mb = 0; mb < g.G; ++mb)
+                  mma_f16(d + uint32_t(mb * g.NT),
+                          sw128_mn_desc(xaddr + uint32_t(mb) * 2 * x_lbo, x_lbo, 1024), wdesc,
+                          idesc_mn, (s | ks) != 0);
+              } else {
+                mma_f16(d, wdesc, sw128_mn_desc(xaddr, x_lbo, 1024), idesc_mn, (s | ks) != 0);
+              }
+            }
+            mma_commit(smem_u32(&empty[slot]));
+            continue;
+          }
           if constexpr (KW_T > 0) {
             // descriptors differ from the stage's base descriptors only in
             // the start-address field: add precomputed (offset >> 4) values
@@ -1239,13 +1286,36 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   }
   const bool xs_ready = link && link->xs_ready;
   if (xs_ready && w_to_pack) fail("conv2d: weights must be packed before a linked launch");
+  // ---- direct mode: 1x1 / stride 1 / no padding reads NCHW through TMA
+  TmapSet tm;
+  std::memset(&tm, 0, sizeof tm);
+  {
+    const int64_t hw = int64_t(p.IH) * p.IW;
+    bool direct = !xs_ready && p.KH == 1 && p.KW == 1 && p.sH == 1 && p.sW == 1 && p.pH == 0 &&
+                  p.pW == 0 && hw % 8 == 0 && srcs_aligned && g.tile_pos % 64 == 0 &&
+                  hw < (1ll << 31) && g.b_stage_bytes % 1024 == 0;
+    const int dbox = g.nsrc == 1 ? g.bk : 8;
+    for (int k = 0; k < g.nsrc && direct; ++k)
+      direct = (g.src_c0[k + 1] - g.src_c0[k]) % dbox == 0 || g.nsrc == 1;
+    if (direct) {
+      g.direct = 1;
+      g.dbox = dbox;
+      for (int k = 0; k < g.nsrc; ++k)
+        encode_nchw_tmap(&tm.m[k], g.src[k], p.B, g.src_c0[k + 1] - g.src_c0[k], int(hw), dbox);
+    }
+  }
   const uint64_t n_w64 = w_to_pack ? umma_conv_packed_weight_bytes(p) / 16 : 0;
   if (n_w64 >= (1ull << 31)) fail("conv2d: weights too large for the tensor-core path");
   const int n_w = int(n_w64);
   const bool strided = g.sH != 1 || g.sW != 1;
-  const int th_pack = xs_ready ? -1 : timer_begin("umma_conv_pack", stream);
+  const int th_pack = (xs_ready || g.direct) ? -1 : timer_begin("umma_conv_pack", stream);
   if (xs_ready) {
     // re-laid by the producer
+  } else if (g.direct) {
+    // read from NCHW by the kernel's TMA loads; only the weights may need packing
+    if (w_to_pack)
+      pack_weights<<<unsigned((n_w + 255) / 256), 256, 0, stream>>>(
+          g, w_to_pack, static_cast<uint4 *>(packed), n_w);
   } else if (strided) {
     if (w_to_pack)
       pack_weights<<<unsigned((n_w + 255) / 256), 256, 0, stream>>>(
@@ -1310,7 +1380,7 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   timer_end(th_pack, stream);
   uint32_t smem = smem_bytes(g);
   using KernelFn = void (*)(const UmmaGeom, const uint8_t *, const uint8_t *, const __half *,
-                           __half *);
+                           __half *, const TmapSet);
   // specialisations: filter width (1/3/5/7, per-row 32-channel staging) x
   // epilogue activation
 #define WGX_UMMA_ROW(KW, T) \
@@ -1341,7 +1411,7 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   const int grid = g.total_tiles < n_sm ? g.total_tiles : n_sm;
   int th = timer_begin("umma_conv_kernel", stream);
   kern<<<grid, THREADS, smem, stream>>>(g, static_cast<const uint8_t *>(xs),
-                                        static_cast<const uint8_t *>(packed), bias, out);
+                                        static_cast<const uint8_t *>(packed), bias, out, tm);
   check_cuda(cudaGetLastError(), "umma_conv launch");
   timer_end(th, stream);
 }
