@@ -421,3 +421,73 @@ def test_program_conv_sigmoid_mul_fusion(ctx, out_pool, ic, commands):
     assert ctx.stats()["commands"] == commands
     ex = oracle.conv2d(x, w, b, 1, 1, 1, 1, act=oracle.ACT_SILU, mode="exact")
     assert oracle.rel_err(y, ex) <= 5e-3
+
+
+def test_program_split_and_residual_folded_into_convs(ctx):
+    """C2f-style block: conv1 (+SiLU) -> split [a, b]; conv2 (+SiLU) of b;
+    y = b + conv2(b) (residual); cat [a, b, y]. The split and the add are
+    done by the convolutions' epilogues; the result equals the program
+    oracle's."""
+    import program_oracle
+    B, C, H, W = 2, 32, 16, 20
+    rng = np.random.default_rng(120)
+    x = rng.standard_normal((B, C, H, W)).astype(np.float16)
+    w1 = kaiming((2 * C, C, 1, 1), 121)
+    w2 = kaiming((C, C, 3, 3), 122)
+    b1 = (rng.standard_normal(2 * C) * 0.01).astype(np.float16)
+    b2 = (rng.standard_normal(C) * 0.01).astype(np.float16)
+    wb = w1.tobytes() + b1.tobytes() + w2.tobytes() + b2.tobytes()
+    o = [0, w1.nbytes, w1.nbytes + b1.nbytes, w1.nbytes + b1.nbytes + w2.nbytes]
+    t = lambda shape, pool: {"type": "tensor", "shape": shape, "dtype": "float16",
+                             "memObjId": pool}
+    vals = [
+        t([B, C, H, W], 0),                                                        # 0 x
+        {"type": "tensor", "shape": [2 * C, C, 1, 1], "dtype": "float16",
+         "weightsOffset": o[0], "weightsLength": w1.nbytes},                      # 1
+        {"type": "tensor", "shape": [2 * C], "dtype": "float16",
+         "weightsOffset": o[1], "weightsLength": b1.nbytes},                      # 2
+        {"type": "list", "items": [1, 1]}, {"type": "list", "items": [0, 0]},    # 3 4
+        {"type": "list", "items": [1, 1]}, {"type": "scalar", "value": False},   # 5 6
+        {"type": "list", "items": [0, 0]}, {"type": "scalar", "value": 1},       # 7 8
+        t([B, 2 * C, H, W], 1),                                                    # 9 v1
+        t([B, 2 * C, H, W], 2),                                                    # 10 s1
+        t([B, 2 * C, H, W], 3),                                                    # 11 y1
+        {"type": "list", "items": [C, C]}, {"type": "scalar", "value": 1},       # 12 13
+        t([B, C, H, W], 4), t([B, C, H, W], 5),                                    # 14 a, 15 b
+        {"type": "tensorlist", "items": [14, 15]},                                 # 16
+        {"type": "tensor", "shape": [C, C, 3, 3], "dtype": "float16",
+         "weightsOffset": o[2], "weightsLength": w2.nbytes},                      # 17
+        {"type": "tensor", "shape": [C], "dtype": "float16",
+         "weightsOffset": o[3], "weightsLength": b2.nbytes},                      # 18
+        {"type": "list", "items": [1, 1]},                                         # 19 pad 1
+        t([B, C, H, W], 1), t([B, C, H, W], 2), t([B, C, H, W], 3),               # 20 v2 21 s2 22 m
+        t([B, C, H, W], 6),                                                        # 23 y = b + m
+        {"type": "tensorlist", "items": [14, 15, 23]},                             # 24
+        t([B, 3 * C, H, W], 7),                                                    # 25 out
+    ]
+    chain = [
+        {"name": "aten.convolution.default", "args": [0, 1, 2, 3, 4, 5, 6, 7, 8, 9]},
+        {"name": "aten.sigmoid.default", "args": [9, 10]},
+        {"name": "aten.mul.Tensor", "args": [9, 10, 11]},
+        {"name": "aten.split_with_sizes_copy.default", "args": [11, 12, 13, 16]},
+        {"name": "aten.convolution.default", "args": [15, 17, 18, 3, 19, 5, 6, 7, 8, 20]},
+        {"name": "aten.sigmoid.default", "args": [20, 21]},
+        {"name": "aten.mul.Tensor", "args": [20, 21, 22]},
+        {"name": "aten.add.Tensor", "args": [15, 22, 8, 23]},
+        {"name": "aten.cat.default", "args": [24, 13, 25]},
+    ]
+    nb = lambda c: B * c * H * W * 2
+    prog = {"version": "1", "chain": chain, "values": vals, "inputIds": [0], "outputIds": [25],
+            "memoryPlan": {"pools": [{"id": 0, "size": nb(C)}, {"id": 1, "size": nb(2 * C)},
+                                     {"id": 2, "size": nb(2 * C)}, {"id": 3, "size": nb(2 * C)},
+                                     {"id": 4, "size": nb(C)}, {"id": 5, "size": nb(C)},
+                                     {"id": 6, "size": nb(C)}, {"id": 7, "size": nb(3 * C)}]}}
+    tin = ctx.tensor("float16", x.shape).setData(x)
+    tout = ctx.tensor("float16", [B, 3 * C, H, W])
+    ctx.recordProgram(prog, wb, [tin, tout])
+    # input copy, conv1 (split), conv2 (residual), cat, output copy
+    assert ctx.stats()["commands"] == 5
+    ctx.submit()
+    ctx.sync()
+    (ref,) = program_oracle.run_program(prog, wb, [x])
+    assert oracle.rel_err(tout.numpy(), ref) <= 5e-3

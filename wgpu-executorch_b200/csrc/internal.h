@@ -103,6 +103,13 @@ struct ConvRecordLink {
   void *in_xs = nullptr;
   // the input is the channel concatenation of these tensors
   std::vector<wgx_tensor *> cat;
+  // NCHW output: add this tensor (same shape) after the activation
+  const wgx_tensor *resid = nullptr;
+  // NCHW output split along channels into these tensors (replaces `out`)
+  std::vector<wgx_tensor *> split;
+  // write the output into this tensor instead of the op's own output (the
+  // result of a residual add folded into the convolution)
+  wgx_tensor *out_override = nullptr;
 };
 
 }  // namespace wgx

@@ -153,6 +153,19 @@ static void append_conv(wgx_context *ctx, const char *name, const wgx_conv2d_par
         in_xs = lk->in_xs;
         link.xs_ready = linked = true;
       }
+      if (lk->resid) {
+        link.resid = static_cast<const __half *>(lk->resid->data());
+        linked = true;
+      }
+      if (!lk->split.empty()) {
+        if (lk->split.size() > 4) fail(std::string(name) + ": too many output pieces");
+        link.nout = int(lk->split.size());
+        for (size_t k = 0; k < lk->split.size(); ++k) {
+          link.outp[k] = static_cast<__half *>(lk->split[k]->data());
+          link.out_ch[k] = int(lk->split[k]->shape[1]);
+        }
+        linked = true;
+      }
       if (!lk->cat.empty()) {
         if (lk->cat.size() > 8) fail(std::string(name) + ": too many concatenated inputs");
         link.nsrc = int(lk->cat.size());
@@ -162,6 +175,30 @@ static void append_conv(wgx_context *ctx, const char *name, const wgx_conv2d_par
         }
         linked = true;
       }
+    }
+    // outputs written over an input: stage the input first (no direct mode)
+    {
+      // (an output written into a consumer's dedicated re-layout buffer
+      // overlaps nothing; a split output replaces `out`)
+      // A 1x1 tile reads and writes only its own positions and writes after
+      // all of its loads completed, so an output over an input of the same
+      // shape is safe for the direct mode; other overlaps are not.
+      auto same_shape = [](const wgx_tensor *a, const wgx_tensor *b) {
+        if (a->ndim != b->ndim) return false;
+        for (int d = 0; d < a->ndim; ++d)
+          if (a->shape[d] != b->shape[d]) return false;
+        return true;
+      };
+      std::vector<const wgx_tensor *> in_t{in}, out_t;
+      if (lk)
+        for (auto *t : lk->cat) in_t.push_back(t);
+      if (!(lk && (lk->out_xs || !lk->split.empty()))) out_t.push_back(out);
+      if (lk)
+        for (auto *t : lk->split) out_t.push_back(t);
+      for (auto *o : out_t)
+        for (auto *i : in_t)
+          if (o->buffer == i->buffer && !same_shape(o, i)) link.allow_direct = false;
+      if (!link.allow_direct) linked = true;
     }
     c.workspace_bytes = in_xs ? 0 : umma_conv_input_bytes(p);
     c.kernel_launches = in_xs ? 1 : 2;

@@ -341,6 +341,82 @@ LinkPlan plan_links(wgx_context *ctx, const Program &P,
       L.skip.insert(k);
     }
   }
+  // * split: a channel split immediately after a convolution whose output
+  //   it alone reads is done by the convolution's epilogue (each channel
+  //   range written straight into its piece);
+  // * residual: add(x, conv) immediately after a convolution whose output it
+  //   alone reads is done by the convolution's epilogue (x added after the
+  //   activation, the sum written to the add's output).
+  auto last_of = [&](size_t i) { return fusion[i] == 1 ? i + 2 : i; };
+  auto free_output = [&](size_t k) {
+    auto it = L.conv.find(k);
+    return it == L.conv.end() || (!it->second.out_xs && it->second.split.empty() &&
+                                  !it->second.resid && !it->second.out_override);
+  };
+  auto same4 = [](const wgx_tensor *a, const wgx_tensor *b) {
+    if (!a || !b || a->ndim != 4 || b->ndim != 4 || a->dtype != b->dtype) return false;
+    for (int d = 0; d < 4; ++d)
+      if (a->shape[d] != b->shape[d]) return false;
+    return true;
+  };
+  for (size_t j = 0; j < P.chain.size(); ++j) {
+    if (fusion[j] == 2 || L.skip.count(j)) continue;
+    const POp &op = P.chain[j];
+    if (op.name == "aten.split_with_sizes_copy.default" && op.args.size() == 4) {
+      const int64_t x = op.args[0];
+      if (!producer.count(x) || readers[x] != 1 || boundary.count(x)) continue;
+      const size_t k = producer[x];
+      wgx_conv2d_params pp{};
+      if (!conv_of(k, &pp) || last_of(k) + 1 != j || !free_output(k)) continue;
+      const PValue &dimv = P.values[op.args[2]];
+      const int dim = dimv.kind == PValue::Scalar ? int(dimv.num) : -99;
+      const PValue &outs = P.values[op.args[3]];
+      if ((dim != 1 && dim != -3) || outs.kind != PValue::TensorList || outs.items.empty() ||
+          outs.items.size() > 4)
+        continue;
+      std::vector<wgx_tensor *> pieces;
+      int64_t csum = 0;
+      bool ok = true;
+      for (auto t : outs.items) {
+        auto it = tensors.find(t);
+        if (it == tensors.end()) {
+          ok = false;
+          break;
+        }
+        const wgx_tensor *pt = it->second;
+        ok = ok && pt->ndim == 4 && pt->dtype == WGX_FLOAT16 && pt->shape[0] == pp.B &&
+             pt->shape[2] == pp.OH && pt->shape[3] == pp.OW;
+        csum += pt->shape[1];
+        pieces.push_back(it->second);
+      }
+      if (!ok || csum != pp.OC) continue;
+      L.conv[k].split = pieces;
+      L.skip.insert(j);
+    } else if (op.name == "aten.add.Tensor" && (op.args.size() == 3 || op.args.size() == 4)) {
+      if (op.args.size() == 4) {
+        const PValue &al = P.values[op.args[2]];
+        if (!(al.kind == PValue::Null || (al.kind == PValue::Scalar && al.num == 1.0))) continue;
+      }
+      auto yt = tensors.find(op.args.back());
+      if (yt == tensors.end()) continue;
+      for (int side = 1; side >= 0; --side) {
+        const int64_t m = op.args[side], r = op.args[1 - side];
+        if (!producer.count(m) || readers[m] != 1 || boundary.count(m)) continue;
+        const size_t k = producer[m];
+        wgx_conv2d_params pp{};
+        if (!conv_of(k, &pp) || last_of(k) + 1 != j || !free_output(k)) continue;
+        auto mt = tensors.find(m), rt = tensors.find(r);
+        if (mt == tensors.end() || rt == tensors.end()) continue;
+        if (!same4(mt->second, rt->second) || !same4(mt->second, yt->second) ||
+            mt->second->dtype != WGX_FLOAT16)
+          continue;
+        L.conv[k].resid = rt->second;
+        L.conv[k].out_override = yt->second;
+        L.skip.insert(j);
+        break;
+      }
+    }
+  }
   if (!L.conv.empty()) check_cuda(cudaStreamSynchronize(ctx->stream), "link buffers");
   return L;
 }
@@ -684,8 +760,12 @@ static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len
       if (fusion[oi] == 1) {
         // fused conv + SiLU writes straight into the mul's output
         a[9].v.tensor = tensors[P.chain[oi + 2].args[2]];
+        if (ctx->conv_link && ctx->conv_link->out_override)
+          a[9].v.tensor = ctx->conv_link->out_override;
         record_convolution_act(ctx, a, WGX_ACT_SILU);
       } else {
+        if (ctx->conv_link && ctx->conv_link->out_override && a.size() == 10)
+          a[9].v.tensor = ctx->conv_link->out_override;
         rit->second(ctx, a);
       }
     } catch (...) {

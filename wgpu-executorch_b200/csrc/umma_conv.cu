@@ -67,6 +67,7 @@ constexpr uint32_t EPI_BYTES = EPI_WARPS * 32 * EPI_ROWB;
 constexpr uint32_t SMEM_MAX = 227u * 1024u;
 
 constexpr int kMaxSrc = 8;
+constexpr int kMaxOut = 4;
 
 struct UmmaGeom {
   // IC, KH, KW, dH, dW, pH, pW describe the stride-1 convolution the MMA
@@ -108,6 +109,13 @@ struct UmmaGeom {
   // dbox channels, 128-byte swizzle, zero fill past the image and past a
   // source's channels) and the MMAs read them MN-major; no re-layout runs
   int direct, dbox;
+  // NCHW output options (omode 0): `resid` (same shape as the output) is
+  // added after the activation; nout > 0 splits the output channels into
+  // tensors outp[k] holding channels [out_c0[k], out_c0[k+1])
+  const __half *resid;
+  int nout;
+  int out_c0[kMaxOut + 1];
+  __half *outp[kMaxOut];
 };
 
 static uint32_t smem_need(const UmmaGeom &g) {
@@ -770,6 +778,31 @@ __device__ __forceinline__ uint4 *xs_slot(const UmmaGeom &g, int b, int c, int o
   return g.oxs + ((size_t(b) * g.oplanes + (vc >> 3)) * g.oHp + hp) * g.oWp + wp;
 }
 
+// v (two fp16 outputs) + the residual pair r, added in fp32 and rounded once
+// (what the separate add operator computes on the stored conv output).
+__device__ __forceinline__ uint32_t add_resid2(uint32_t v, uint32_t r) {
+  const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&v));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&r));
+  const __half2 y = __floats2half2_rn(a.x + b.x, a.y + b.y);
+  return *reinterpret_cast<const uint32_t *>(&y);
+}
+__device__ __forceinline__ __half add_resid1(__half v, __half r) {
+  return __float2half_rn(__half2float(v) + __half2float(r));
+}
+
+// Start of output plane (b, c): `out` itself, or the split piece holding
+// channel c.
+__device__ __forceinline__ __half *out_plane(const UmmaGeom &g, __half *out, int b, int c,
+                                             size_t plane) {
+  if (g.nout == 0) return out + (size_t(b) * g.OC + c) * plane;
+  int k = 0;
+#pragma unroll
+  for (int j = 1; j < kMaxOut; ++j)
+    if (j < g.nout && c >= g.out_c0[j]) k = j;
+  const int ck = g.out_c0[k + 1] - g.out_c0[k];
+  return g.outp[k] + (size_t(b) * ck + (c - g.out_c0[k])) * plane;
+}
+
 // tile index -> (image, first position, output-channel tile); oc tile
 // fastest so that CTAs working on the same positions run together.
 __device__ __forceinline__ void tile_coords(const UmmaGeom &g, int t, int &b, long long &p0,
@@ -787,7 +820,9 @@ __device__ __forceinline__ void tile_coords(const UmmaGeom &g, int t, int &b, lo
 // TRANS (geometry trans = 1): positions are the MMA's M rows and output
 // channels its N columns; the staged activation rows become the A operand
 // and the packed weights the B operand, with no change to either layout.
-template <int KW_T, int ACT_T, int TRANS>
+// EXT: NCHW output with a residual add and/or a channel split (separate
+// instantiations keep the common epilogue free of those branches).
+template <int KW_T, int ACT_T, int TRANS, int EXT>
 __global__ void __launch_bounds__(THREADS, 1)
     umma_conv_kernel(const UmmaGeom g, const uint8_t *__restrict__ xs,
                      const uint8_t *__restrict__ wpk, const __half *__restrict__ bias,
@@ -1019,7 +1054,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int i = threadIdx.x - EPI_WARP0 * 32; i < g.NT; i += EPI_WARPS * 32)
       sbias[i] = (g.has_bias && i < g.OC) ? __half2float(bias[i]) : 0.f;
     asm volatile("bar.sync 1, %0;" ::"r"(EPI_WARPS * 32) : "memory");
-    float r[32];
+    float r[EXT ? 16 : 32];
     int it = 0;
     for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1, use_acc = it >> 1;
@@ -1031,6 +1066,78 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
+      if constexpr (EXT) {
+      // the warp's acc_cols / 4 columns, 16 at a time (16 columns always lie
+      // in one M block, NT >= 16)
+      const int n16 = g.acc_cols / 64;
+      __half *base = out + size_t(b) * g.OC * plane;
+      for (int h = 0; h < n16; ++h) {
+        const int c0 = cq * (g.acc_cols / 4) + h * 16;
+        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * g.acc_cols + c0), r);
+        if (h == n16 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
+        }
+        const int mb = c0 >> g.lgNT;
+        const int pos = int(p0) + mb * 128 + q * 32 + lane;
+        const int oh = pos / g.Wp, ow = pos - oh * g.Wp;
+        const bool okp = oh < g.OH && ow < g.OW;
+        const int oc0 = c0 & (g.NT - 1);  // first of this lane's 16 channels
+        // columns 2j, 2j+1: channels oc0+2j, oc0+2j+1 of one position
+        uint32_t pr[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int oc = oc0 + 2 * j;
+          pr[j] = epi_act2<ACT_T>(r[2 * j], r[2 * j + 1], sbias[oc], sbias[oc + 1], g.lo, g.hi);
+        }
+        if (!okp) continue;
+        if (g.omode) {
+          // 8 consecutive columns = 8 channels of one position: one 16-byte slot
+#pragma unroll
+          for (int q8 = 0; q8 < 2; ++q8) {
+            const int oc = oc0 + 8 * q8;
+            if (oc >= g.OC) continue;
+            uint4 *slot = xs_slot(g, b, oc, oh, ow);
+            if (slot) *slot = make_uint4(pr[4 * q8], pr[4 * q8 + 1], pr[4 * q8 + 2], pr[4 * q8 + 3]);
+          }
+          continue;
+        }
+        const size_t posoff = size_t(oh) * g.OW + ow;
+        if (g.nout == 0 && !g.resid) {
+          __half *d = base + posoff;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int oc = oc0 + 2 * j;
+            const __half2 h2 = *reinterpret_cast<const __half2 *>(&pr[j]);
+            if (oc < g.OC) d[size_t(oc) * plane] = __low2half(h2);
+            if (oc + 1 < g.OC) d[size_t(oc + 1) * plane] = __high2half(h2);
+          }
+          continue;
+        }
+        // residual pairs of the 16 channels, all loads issued before use
+        uint32_t rres[8];
+        if (g.resid) {
+          const __half *rp = g.resid + size_t(b) * g.OC * plane + posoff;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int oc = oc0 + 2 * j;
+            const uint32_t lo = oc < g.OC ? uint32_t(__half_as_ushort(rp[size_t(oc) * plane])) : 0u;
+            const uint32_t hi =
+                oc + 1 < g.OC ? uint32_t(__half_as_ushort(rp[size_t(oc + 1) * plane])) : 0u;
+            rres[j] = lo | (hi << 16);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int oc = oc0 + 2 * j;
+          const uint32_t v = g.resid ? add_resid2(pr[j], rres[j]) : pr[j];
+          const __half2 h2 = *reinterpret_cast<const __half2 *>(&v);
+          if (oc < g.OC) out_plane(g, out, b, oc, plane)[posoff] = __low2half(h2);
+          if (oc + 1 < g.OC) out_plane(g, out, b, oc + 1, plane)[posoff] = __high2half(h2);
+        }
+      }
+      } else {
       // the warp's acc_cols / 4 columns, in chunks of 32
       const int nchunk = g.acc_cols / 128;
       __half *base = out + size_t(b) * g.OC * plane;
@@ -1084,6 +1191,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
         }
+      }
       }
     }
   } else if (warp >= EPI_WARP0) {
@@ -1180,6 +1288,45 @@ __global__ void __launch_bounds__(THREADS, 1)
         const bool wrap = ow + 1 >= g.Wp;
         const bool v1 = wrap ? (oh + 1 < g.OH) : (oh < g.OH && ow + 1 < g.OW);
         const int off1 = wrap ? (oh + 1) * g.OW : off0 + 1;
+        if constexpr (EXT) {
+        const uint8_t *src = stage + rsel * EPI_ROWB + 4 * sub;
+        // residual pairs of this lane's 8 rows, all loads issued before use
+        uint32_t rv[8];
+        if (g.resid) {
+#pragma unroll
+          for (int r4 = 0; r4 < 8; ++r4) {
+            rv[r4] = 0;
+            if (4 * r4 + rsel < nrows) {
+              const __half *rrow = g.resid + (size_t(b) * g.OC + oc0 + rsel + 4 * r4) * plane;
+              if (pairs) {
+                if (v0) rv[r4] = *reinterpret_cast<const uint32_t *>(rrow + off0);
+              } else {
+                const uint32_t lo =
+                    v0 ? uint32_t(*reinterpret_cast<const uint16_t *>(rrow + off0)) : 0u;
+                const uint32_t hi =
+                    v1 ? uint32_t(*reinterpret_cast<const uint16_t *>(rrow + off1)) : 0u;
+                rv[r4] = lo | (hi << 16);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int r4 = 0; r4 < 8; ++r4) {
+          uint32_t val = *reinterpret_cast<const uint32_t *>(src + r4 * 4 * EPI_ROWB);
+          if (4 * r4 + rsel < nrows) {
+            const int c = oc0 + rsel + 4 * r4;
+            __half *orow = g.nout ? out_plane(g, out, b, c, plane) : rowp + size_t(r4) * 4 * plane;
+            if (g.resid) val = add_resid2(val, rv[r4]);
+            if (pairs) {
+              if (v0) *reinterpret_cast<uint32_t *>(orow + off0) = val;
+            } else {
+              const __half2 h2 = *reinterpret_cast<const __half2 *>(&val);
+              if (v0) orow[off0] = __low2half(h2);
+              if (v1) orow[off1] = __high2half(h2);
+            }
+          }
+        }
+        } else {
         const uint8_t *src = stage + rsel * EPI_ROWB + 4 * sub;
 #pragma unroll
         for (int r4 = 0; r4 < 8; ++r4) {
@@ -1194,6 +1341,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               if (v1) orow[off1] = __high2half(h2);
             }
           }
+        }
         }
         __syncwarp();
         ow += EPI_COLS;
@@ -1286,12 +1434,28 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   }
   const bool xs_ready = link && link->xs_ready;
   if (xs_ready && w_to_pack) fail("conv2d: weights must be packed before a linked launch");
+  // ---- NCHW output options
+  if (link && (link->resid || link->nout > 0)) {
+    if (g.omode) fail("conv2d: a linked output cannot also be split or take a residual");
+    g.resid = link->resid;
+    if (link->nout > 0) {
+      if (link->nout > kMaxOut) fail("conv2d: too many output pieces");
+      g.nout = link->nout;
+      g.out_c0[0] = 0;
+      for (int k = 0; k < link->nout; ++k) {
+        g.outp[k] = link->outp[k];
+        g.out_c0[k + 1] = g.out_c0[k] + link->out_ch[k];
+      }
+      if (g.out_c0[g.nout] != p.OC) fail("conv2d: output pieces do not add up to OC");
+    }
+  }
   // ---- direct mode: 1x1 / stride 1 / no padding reads NCHW through TMA
   TmapSet tm;
   std::memset(&tm, 0, sizeof tm);
   {
     const int64_t hw = int64_t(p.IH) * p.IW;
-    bool direct = !xs_ready && p.KH == 1 && p.KW == 1 && p.sH == 1 && p.sW == 1 && p.pH == 0 &&
+    bool direct = !xs_ready && (!link || link->allow_direct) && p.KH == 1 && p.KW == 1 &&
+                  p.sH == 1 && p.sW == 1 && p.pH == 0 &&
                   p.pW == 0 && hw % 8 == 0 && srcs_aligned && g.tile_pos % 64 == 0 &&
                   hw < (1ll << 31) && g.b_stage_bytes % 1024 == 0;
     const int dbox = g.nsrc == 1 ? g.bk : 8;
@@ -1384,7 +1548,7 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   // specialisations: filter width (1/3/5/7, per-row 32-channel staging) x
   // epilogue activation
 #define WGX_UMMA_ROW(KW, T) \
-  { umma_conv_kernel<KW, 0, T>, umma_conv_kernel<KW, 1, T>, umma_conv_kernel<KW, 2, T> }
+  { umma_conv_kernel<KW, 0, T, 0>, umma_conv_kernel<KW, 1, T, 0>, umma_conv_kernel<KW, 2, T, 0> }
   static const KernelFn table[2][7][3] = {
       {WGX_UMMA_ROW(0, 0), WGX_UMMA_ROW(1, 0), WGX_UMMA_ROW(2, 0), WGX_UMMA_ROW(3, 0),
        WGX_UMMA_ROW(4, 0), WGX_UMMA_ROW(5, 0), WGX_UMMA_ROW(7, 0)},
@@ -1396,9 +1560,14 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
     kw_idx = g.KW == 7 ? 6 : (g.KW >= 1 && g.KW <= 5) ? g.KW : 0;
   if (g.trans && kw_idx > 3) kw_idx = 0;  // transposed: specialised for KW <= 3 only
   const int act_idx = (g.act >= 0 && g.act <= 2) ? g.act : 0;
-  KernelFn kern = table[g.trans][kw_idx][act_idx];
-  const int kidx = (g.trans * 7 + kw_idx) * 3 + act_idx;
-  static bool attr_set[64][42] = {};
+  // residual / split outputs: generic MMA loop, EXT epilogue
+  static const KernelFn table_ext[2][3] = {
+      {umma_conv_kernel<0, 0, 0, 1>, umma_conv_kernel<0, 1, 0, 1>, umma_conv_kernel<0, 2, 0, 1>},
+      {umma_conv_kernel<0, 0, 1, 1>, umma_conv_kernel<0, 1, 1, 1>, umma_conv_kernel<0, 2, 1, 1>}};
+  const bool ext = g.resid != nullptr || g.nout > 0;
+  KernelFn kern = ext ? table_ext[g.trans][act_idx] : table[g.trans][kw_idx][act_idx];
+  const int kidx = ext ? 42 + g.trans * 3 + act_idx : (g.trans * 7 + kw_idx) * 3 + act_idx;
+  static bool attr_set[64][48] = {};
   if (dev < 64 && !attr_set[dev][kidx]) {
     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(SMEM_MAX)),

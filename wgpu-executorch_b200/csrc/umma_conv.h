@@ -25,6 +25,17 @@ struct UmmaLink {
   int nsrc = 0;
   const __half *src[8] = {};
   int src_ch[8] = {};
+  // NCHW output: add `resid` (same shape as the output) after the
+  // activation; or split the output channels into nout tensors (channel
+  // counts out_ch)
+  const __half *resid = nullptr;
+  // false when an output buffer is also an input buffer: the input must then
+  // be staged (re-layout kernel) before the main kernel writes, so the TMA
+  // direct mode, which reads the input while writing, is not used
+  bool allow_direct = true;
+  int nout = 0;
+  __half *outp[4] = {};
+  int out_ch[4] = {};
 };
 
 // True when `prod` can write its output straight into the re-laid input of
