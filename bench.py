@@ -576,7 +576,10 @@ def run_only(args):
                           "kernel_launches_per_step": ctx.stats()["kernel_launches"]}))
     else:
         rng = np.random.default_rng(0)
-        launch, *_ = make_conv(ctx, "cuda:0", rng, *ONLY_CONV[args.only])
+        cfg = ONLY_CONV[args.only]
+        if args.batch:
+            cfg = (args.batch,) + cfg[1:]
+        launch, *_ = make_conv(ctx, "cuda:0", rng, *cfg)
         for _ in range(args.warmup + args.steps):
             launch()
         ctx.sync()
@@ -595,7 +598,7 @@ def main():
     ap.add_argument("--only", default=None, choices=["yolo"] + sorted(ONLY_CONV),
                     help="run one workload's launches only (for profilers)")
     ap.add_argument("--batch", type=int, default=0,
-                    help="images per GPU for --only yolo (default 64)")
+                    help="images per GPU for --only (default: 64 for yolo, the listed batch otherwise)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -104,9 +104,10 @@ def test_plan_strided_convs_use_tensor_cores():
     stem = plan(B=64, IC=3, IH=640, IW=640, OC=16, OH=320, OW=320, KH=3, KW=3, sH=2, sW=2,
                 pH=1, pW=1)
     assert stem.variant == _lib.CONV_UMMA
-    # 321 x 321 virtual positions per image (OW + 1 columns); OC = 16 puts
-    # positions on the MMA M side, 8 M blocks of 128 = 1024 positions per tile
-    assert stem.grid_ctas == 64 * ((319 * 321 + 320 + 1023) // 1024)
+    # 321 virtual rows of OW + 1 columns per image, the row pitch rounded up
+    # to 328 (a multiple of 8); OC = 16 puts positions on the MMA M side,
+    # 8 M blocks of 128 = 1024 positions per tile
+    assert stem.grid_ctas == 64 * ((319 * 328 + 320 + 1023) // 1024)
     down = plan(B=64, IC=128, IH=80, IW=80, OC=128, OH=40, OW=40, KH=3, KW=3, sH=2, sW=2,
                 pH=1, pW=1)
     assert down.variant == _lib.CONV_UMMA

@@ -189,9 +189,12 @@ static void append_conv(wgx_context *ctx, const char *name, const wgx_conv2d_par
           if (a->shape[d] != b->shape[d]) return false;
         return true;
       };
-      std::vector<const wgx_tensor *> in_t{in}, out_t;
-      if (lk)
-        for (auto *t : lk->cat) in_t.push_back(t);
+      // (a linked concatenation is read from its sources, never from `in`)
+      std::vector<const wgx_tensor *> in_t, out_t;
+      if (lk && !lk->cat.empty())
+        in_t.assign(lk->cat.begin(), lk->cat.end());
+      else
+        in_t.push_back(in);
       if (!(lk && (lk->out_xs || !lk->split.empty()))) out_t.push_back(out);
       if (lk)
         for (auto *t : lk->split) out_t.push_back(t);
@@ -200,6 +203,16 @@ static void append_conv(wgx_context *ctx, const char *name, const wgx_conv2d_par
           if (o->buffer == i->buffer && !same_shape(o, i)) link.allow_direct = false;
       if (!link.allow_direct) linked = true;
     }
+    // program links in the label: "[xs<]" input written by its producer,
+    // "[->xs]" output written into the consumer's input, "[catN]" N
+    // concatenated sources, "[+res]" residual add, "[splitN]" N output pieces,
+    // "[staged]" no direct mode
+    if (has_consumer) c.name += " [->xs]";
+    if (in_xs) c.name += " [xs<]";
+    if (link.nsrc) c.name += " [cat" + std::to_string(link.nsrc) + "]";
+    if (link.resid) c.name += " [+res]";
+    if (link.nout) c.name += " [split" + std::to_string(link.nout) + "]";
+    if (!link.allow_direct) c.name += " [staged]";
     c.workspace_bytes = in_xs ? 0 : umma_conv_input_bytes(p);
     c.kernel_launches = in_xs ? 1 : 2;
     c.run = [=](const ExecEnv &env) {

@@ -417,6 +417,48 @@ LinkPlan plan_links(wgx_context *ctx, const Program &P,
       }
     }
   }
+  // * private outputs: a 1x1 convolution reads its input with TMA while its
+  //   epilogue writes, which is safe only when no output overlays an input
+  //   of another shape. The memory plan may place the output in the buffer
+  //   of a concatenation source (free once the concatenation ran, which the
+  //   link above absorbs) or of an input that dies at the convolution; such
+  //   an output gets a buffer of its own, so that the input need not be
+  //   staged through the re-layout kernel first. Every reader of the value
+  //   goes through its tensor, which now points at the new buffer.
+  for (size_t j = 0; j < P.chain.size(); ++j) {
+    wgx_conv2d_params pc{};
+    if (!conv_of(j, &pc)) continue;
+    if (pc.KH != 1 || pc.KW != 1 || pc.sH != 1 || pc.sW != 1 || pc.pH != 0 || pc.pW != 0) continue;
+    auto lk = L.conv.find(j);
+    const ConvRecordLink *cl = lk == L.conv.end() ? nullptr : &lk->second;
+    if (cl && (cl->in_xs || cl->out_xs)) continue;  // re-laid input / output into a consumer
+    auto xt = tensors.find(P.chain[j].args[0]);
+    auto ot = tensors.find(out_of(j));
+    if (xt == tensors.end() || ot == tensors.end()) continue;
+    std::vector<const wgx_tensor *> reads;
+    if (cl && !cl->cat.empty())
+      reads.assign(cl->cat.begin(), cl->cat.end());
+    else
+      reads.push_back(xt->second);
+    std::vector<wgx_tensor *> outs;
+    if (cl && !cl->split.empty())
+      outs = cl->split;
+    else
+      outs.push_back(cl && cl->out_override ? cl->out_override : ot->second);
+    for (wgx_tensor *o : outs) {
+      bool clash = false;
+      for (const wgx_tensor *r : reads) clash = clash || (o->buffer == r->buffer && !same4(o, r));
+      if (!clash) continue;
+      auto *b = new wgx_buffer();
+      b->ctx = ctx;
+      b->size = (o->byte_length() + 3) / 4 * 4;
+      b->dptr = ctx->alloc_device(b->size);
+      b->usage = o->buffer->usage;
+      b->device = ctx->device;
+      ctx->owned.push_back(b);
+      o->buffer = b;
+    }
+  }
   if (!L.conv.empty()) check_cuda(cudaStreamSynchronize(ctx->stream), "link buffers");
   return L;
 }

@@ -106,6 +106,29 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *r) {
 }
 
 
+// tcgen05.ld of 16 columns without waiting; tmem_wait16 completes it. The
+// wait names the 16 destination registers as operands, so no use of them
+// can be scheduled before it.
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, float *r) {
+  uint32_t *u = reinterpret_cast<uint32_t *>(r);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]),
+        "=r"(u[7]), "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]),
+        "=r"(u[14]), "=r"(u[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait16(float *r) {
+  uint32_t *u = reinterpret_cast<uint32_t *>(r);
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(u[0]), "+r"(u[1]), "+r"(u[2]), "+r"(u[3]), "+r"(u[4]), "+r"(u[5]),
+                 "+r"(u[6]), "+r"(u[7]), "+r"(u[8]), "+r"(u[9]), "+r"(u[10]), "+r"(u[11]),
+                 "+r"(u[12]), "+r"(u[13]), "+r"(u[14]), "+r"(u[15])
+               :
+               : "memory");
+}
+
 // 3-D tiled TMA load (no multicast) completing on mbarrier `bar`.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, int x, int y, int z,
                                             uint32_t bar) {

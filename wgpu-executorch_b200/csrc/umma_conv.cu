@@ -11,8 +11,9 @@
 //
 // Data layout (B200 design, no materialised im2col):
 //  * input re-laid by pack_input into a zero-padded, channel-blocked
-//    layout xs[b][c/8][Hp][Wp][8] (Hp = IH+2pH, Wp = IW+2pW, channels padded
-//    to a multiple of 32). One "row" = one padded position = 16 bytes.
+//    layout xs[b][c/8][Hp][Wp][8] (Hp = IH+2pH, Wp = IW+2pW, for the
+//    transposed variant rounded up to a multiple of 8 where that costs at
+//    most 5 %; channels padded to a multiple of 32). One "row" = one padded position = 16 bytes.
 //    Flattening (hp, wp) to p = hp*Wp + wp turns a stride-1 convolution into
 //    out[p] = sum_taps W_tap . xs[p + kh*dH*Wp + kw*dW]: every tap is a pure
 //    row shift.
@@ -64,6 +65,9 @@ constexpr int MAX_KW = 7;
 constexpr int EPI_COLS = 16;     // positions per staged epilogue block
 constexpr int EPI_ROWB = 48;     // staged channel row: 16 fp16 + 16 B pad
 constexpr uint32_t EPI_BYTES = EPI_WARPS * 32 * EPI_ROWB;
+// transposed epilogue: bias (<= 64 floats) in the first 1 KB, then 1 KB of
+// transpose rows per warp
+static_assert(1024 + EPI_WARPS * 1024 <= EPI_BYTES, "epilogue staging");
 constexpr uint32_t SMEM_MAX = 227u * 1024u;
 
 constexpr int kMaxSrc = 8;
@@ -196,6 +200,16 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans)
     g.Hp = p.OH + g.KH - 1;
     g.Wp = p.OW + g.KW - 1;
   }
+  // transposed variant: the padded row pitch is rounded up to a multiple of
+  // 8 (extra zero columns, whose outputs are discarded), so that 8-position
+  // groups never straddle an output row (vector epilogue stores), when that
+  // adds at most 5 % positions (the extra MMA work outweighs the cheaper
+  // stores above that). 1x1 stride-1 unpadded convolutions keep Wp = IW:
+  // the direct mode reads NCHW rows as they are.
+  const bool plain_1x1 =
+      p.KH == 1 && p.KW == 1 && p.sH == 1 && p.sW == 1 && p.pH == 0 && p.pW == 0;
+  const int wp8 = (g.Wp + 7) / 8 * 8;
+  if (trans && !plain_1x1 && (wp8 - g.Wp) * 20 <= g.Wp) g.Wp = wp8;
   if (khs <= 0) khs = g.KH;
   g.bk = bk;
   g.chunks = bk / 8;
@@ -817,8 +831,8 @@ __device__ __forceinline__ void tile_coords(const UmmaGeom &g, int t, int &b, lo
 // KW_T > 0: compile-time filter width with one filter row and 32 channels
 // per stage (the common staging); the MMA issue loop is then fully unrolled
 // over precomputed descriptor offsets. KW_T == 0: any staging, runtime loops.
-// TRANS (geometry trans = 1): positions are the MMA's M rows and output
-// channels its N columns; the staged activation rows become the A operand
+// TRANS > 0 (geometry trans = 1, NT = TRANS): positions are the MMA's M
+// rows and output channels its N columns; the staged activation rows become the A operand
 // and the packed weights the B operand, with no change to either layout.
 // EXT: NCHW output with a residual add and/or a channel split (separate
 // instantiations keep the common epilogue free of those branches).
@@ -828,6 +842,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                      const uint8_t *__restrict__ wpk, const __half *__restrict__ bias,
                      __half *__restrict__ out, const __grid_constant__ TmapSet tm) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // transposed variant: output channels per M block (N), M blocks per tile
+  constexpr int NT_C = TRANS > 0 ? TRANS : UN;
+  constexpr int G_C = TRANS == 64 ? 4 : TRANS > 0 ? 8 : 1;
+  constexpr int LG_NT = TRANS == 16 ? 4 : TRANS == 32 ? 5 : 6;
   // activation stages first, on a 1024-byte boundary (128-byte swizzle atoms
   // of the direct mode); stage sizes are multiples of 1024 bytes there
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -927,7 +945,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // (a = packed weights, b = staged activation rows, whichever MMA
       // operand slot they take)
       const uint32_t idesc = (1u << 4)                                  // D = f32
-                             | (uint32_t((TRANS ? g.NT : UN) >> 3) << 17)  // N
+                             | (uint32_t((TRANS ? TRANS : UN) >> 3) << 17)  // N
                              | (uint32_t(128 >> 4) << 24);              // M; f16 K-major
       const uint32_t a_lbo = uint32_t(g.wrows) * 16;        // chunk plane of the weights
       const uint32_t b_lbo = uint32_t(g.R_alloc) * 16;      // chunk plane of the activations
@@ -979,8 +997,9 @@ __global__ void __launch_bounds__(THREADS, 1)
               const uint64_t wdesc = kmajor_desc(a_base + uint32_t(ks) * 2 * a_lbo, a_lbo);
               const uint32_t xaddr = b_base + uint32_t(ks) * 2 * 1024;
               if constexpr (TRANS) {
-                for (int mb = 0; mb < g.G; ++mb)
-                  mma_f16(d + uint32_t(mb * g.NT),
+#pragma unroll
+                for (int mb = 0; mb < G_C; ++mb)
+                  mma_f16(d + uint32_t(mb * NT_C),
                           sw128_mn_desc(xaddr + uint32_t(mb) * 2 * x_lbo, x_lbo, 1024), wdesc,
                           idesc_mn, (s | ks) != 0);
               } else {
@@ -1001,8 +1020,9 @@ __global__ void __launch_bounds__(THREADS, 1)
               // the previous one's accumulation)
 #pragma unroll
               for (int i = 0; i < 2 * KW_T; ++i)
-                for (int mb = 0; mb < g.G; ++mb)
-                  mma_f16(d + uint32_t(mb * g.NT), b0 + uint64_t(mb * 128) + b_off[i],
+#pragma unroll
+                for (int mb = 0; mb < G_C; ++mb)
+                  mma_f16(d + uint32_t(mb * NT_C), b0 + uint64_t(mb * 128) + b_off[i],
                           a0 + a_off[i], idesc, (s | i) != 0);
             } else {
 #pragma unroll
@@ -1025,8 +1045,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t acc_flag = (s | khl | kw | ks) != 0;
                 if constexpr (TRANS) {
                   // M blocks innermost (see the specialised path)
-                  for (int mb = 0; mb < g.G; ++mb)
-                    mma_f16(d + uint32_t(mb * g.NT), xdesc + uint64_t(mb * 128), wdesc, idesc,
+#pragma unroll
+                  for (int mb = 0; mb < G_C; ++mb)
+                    mma_f16(d + uint32_t(mb * NT_C), xdesc + uint64_t(mb * 128), wdesc, idesc,
                             acc_flag);
                 } else {
                   mma_f16(d, wdesc, xdesc, idesc, acc_flag);
@@ -1051,9 +1072,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     // bias (and its half, for SiLU) of the NT channels, staged once in the
     // otherwise unused epilogue staging area
     float *sbias = reinterpret_cast<float *>(sE);
-    for (int i = threadIdx.x - EPI_WARP0 * 32; i < g.NT; i += EPI_WARPS * 32)
+    for (int i = threadIdx.x - EPI_WARP0 * 32; i < NT_C; i += EPI_WARPS * 32)
       sbias[i] = (g.has_bias && i < g.OC) ? __half2float(bias[i]) : 0.f;
     asm volatile("bar.sync 1, %0;" ::"r"(EPI_WARPS * 32) : "memory");
+    // per-warp transpose rows of the vector-store path: 16 rows x 64 bytes
+    // after the bias (1 KB reserved), 16 KB in all
+    uint32_t *tstage = reinterpret_cast<uint32_t *>(sE + 1024 + ew * 1024);
+    const bool tvec = !g.omode && ((g.Wp | g.OW) & 7) == 0 &&
+                      (reinterpret_cast<uintptr_t>(out) & 15) == 0;
     float r[EXT ? 16 : 32];
     int it = 0;
     for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++it) {
@@ -1079,11 +1105,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
         }
-        const int mb = c0 >> g.lgNT;
+        const int mb = c0 >> LG_NT;
         const int pos = int(p0) + mb * 128 + q * 32 + lane;
         const int oh = pos / g.Wp, ow = pos - oh * g.Wp;
         const bool okp = oh < g.OH && ow < g.OW;
-        const int oc0 = c0 & (g.NT - 1);  // first of this lane's 16 channels
+        const int oc0 = c0 & (NT_C - 1);  // first of this lane's 16 channels
         // columns 2j, 2j+1: channels oc0+2j, oc0+2j+1 of one position
         uint32_t pr[8];
 #pragma unroll
@@ -1138,19 +1164,21 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       } else {
-      // the warp's acc_cols / 4 columns, in chunks of 32
-      const int nchunk = g.acc_cols / 128;
+      // the warp's ACC_COLS / 4 columns, in chunks of 32
+      constexpr int ACC_COLS = G_C * NT_C;
+      constexpr int NCHUNK = ACC_COLS / 128;
       __half *base = out + size_t(b) * g.OC * plane;
-      for (int h = 0; h < nchunk; ++h) {
-        const int c0 = cq * (g.acc_cols / 4) + h * 32;
-        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * g.acc_cols + c0), r);
-        if (h == nchunk - 1) {
+#pragma unroll
+      for (int h = 0; h < NCHUNK; ++h) {
+        const int c0 = cq * (ACC_COLS / 4) + h * 32;
+        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * ACC_COLS + c0), r);
+        if (h == NCHUNK - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
         }
         // 32 columns cover one M block (NT >= 32) or two (NT = 16)
-        const int mb0 = c0 >> g.lgNT, mb1 = (c0 + 31) >> g.lgNT;
+        const int mb0 = c0 >> LG_NT, mb1 = (c0 + 31) >> LG_NT;
         const int pos_a = int(p0) + mb0 * 128 + q * 32 + lane;
         const int pos_b = int(p0) + mb1 * 128 + q * 32 + lane;
         const int oh_a = pos_a / g.Wp, ow_a = pos_a - oh_a * g.Wp;
@@ -1162,27 +1190,66 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t pr[16];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
-          const int oc = (c0 + j) & (g.NT - 1);
-          pr[j / 2] = epi_act2<ACT_T>(r[j], r[j + 1], sbias[oc], sbias[oc + 1], g.lo, g.hi);
+          const int oc = (c0 + j) & (NT_C - 1);
+          const float2 bb = reinterpret_cast<const float2 *>(sbias)[oc >> 1];
+          pr[j / 2] = epi_act2<ACT_T>(r[j], r[j + 1], bb.x, bb.y, g.lo, g.hi);
+        }
+        if (tvec) {
+          // transpose through the warp's staging rows, 16 columns a round:
+          // lanes l, l^1 swap halves so that even lanes hold positions
+          // (l, l+1) of column 2k and odd lanes positions (l-1, l) of column
+          // 2k+1; row = column (64 bytes: 32 positions). Then lane -> row
+          // lane/4 (+8), 8 positions from (lane%4)*8: one 16-byte store of 8
+          // consecutive outputs (Wp % 8 == 0: an 8-group never leaves its
+          // output row; OW % 8 == 0: it is entirely valid or entirely padding)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint32_t v = pr[hf * 8 + k];
+              const uint32_t o = __shfl_xor_sync(0xffffffffu, v, 1);
+              const bool odd = lane & 1;
+              tstage[(2 * k + (odd ? 1 : 0)) * 16 + (lane >> 1)] =
+                  odd ? __byte_perm(o, v, 0x7632) : __byte_perm(v, o, 0x5410);
+            }
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const int row = (lane >> 2) + 8 * k, part = lane & 3;
+              const uint4 val = reinterpret_cast<const uint4 *>(tstage)[row * 4 + part];
+              const int c = c0 + hf * 16 + row;
+              const int oc = c & (NT_C - 1);
+              const int pos = int(p0) + (c >> LG_NT) * 128 + q * 32 + part * 8;
+              const int oh = pos / g.Wp, ow = pos - oh * g.Wp;
+              if (oc < g.OC && oh < g.OH && ow < g.OW)
+                *reinterpret_cast<uint4 *>(base + size_t(oc) * plane + size_t(oh) * g.OW + ow) = val;
+            }
+            __syncwarp();
+          }
+          continue;
         }
         if (g.omode) {
-          // 8 consecutive columns = 8 channels of one position: one 16-byte slot
+          // 8 consecutive columns = 8 channels of one position: one 16-byte
+          // slot; the slot of channel c is that of channel 0 plus c / 8
+          // planes (the consumer's channel count is a multiple of 8)
+          const size_t pstride = size_t(g.oHp) * g.oWp;
+          uint4 *slot_a = ok_a ? xs_slot(g, b, 0, oh_a, ow_a) : nullptr;
+          uint4 *slot_b = mb1 == mb0 ? slot_a : ok_b ? xs_slot(g, b, 0, oh_b, ow_b) : nullptr;
 #pragma unroll
           for (int q8 = 0; q8 < 4; ++q8) {
             const int c = c0 + 8 * q8;
-            const int oc = c & (g.NT - 1);
-            const bool second = (c >> g.lgNT) != mb0;
-            if (!(second ? ok_b : ok_a) || oc >= g.OC) continue;
-            uint4 *slot = xs_slot(g, b, oc, second ? oh_b : oh_a, second ? ow_b : ow_a);
-            if (slot)
-              *slot = make_uint4(pr[4 * q8], pr[4 * q8 + 1], pr[4 * q8 + 2], pr[4 * q8 + 3]);
+            const int oc = c & (NT_C - 1);
+            uint4 *slot = (c >> LG_NT) != mb0 ? slot_b : slot_a;
+            if (slot && oc < g.OC)
+              slot[size_t(oc >> 3) * pstride] =
+                  make_uint4(pr[4 * q8], pr[4 * q8 + 1], pr[4 * q8 + 2], pr[4 * q8 + 3]);
           }
         } else {
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
             const int c = c0 + j;
-            const int oc = c & (g.NT - 1);
-            const bool second = (c >> g.lgNT) != mb0;
+            const int oc = c & (NT_C - 1);
+            const bool second = (c >> LG_NT) != mb0;
             const __half2 h2 = *reinterpret_cast<const __half2 *>(&pr[j / 2]);
             if (second ? ok_b : ok_a) {
               __half *d = (second ? dst_b : dst_a) + size_t(oc) * plane;
@@ -1210,7 +1277,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const bool pairs = ((g.OW | g.Wp) & 1) == 0;
     const size_t plane = size_t(g.OH) * g.OW;
     const int sub = lane & 7, rsel = lane >> 3;  // position pair, row within 4
-    float r[EPI_COLS];
+    float rb[2][EPI_COLS];
     int it = 0;
     for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1, use_acc = it >> 1;
@@ -1233,9 +1300,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int pos0 = int(p0) + colh * WCOLS + 2 * sub;
       int oh = pos0 / g.Wp, ow = pos0 - oh * g.Wp;
       constexpr int NBLK = WCOLS / EPI_COLS;
+      // TMEM reads are software-pipelined: block blk + 1 is requested right
+      // after block blk has arrived, so its latency hides behind blk's stores
+      const uint32_t tq = tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * g.acc_cols + colh * WCOLS);
+      tmem_ld16_async(tq, rb[0]);
+#pragma unroll
       for (int blk = 0; blk < NBLK; ++blk) {
         const int col0 = colh * WCOLS + blk * EPI_COLS;
-        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * g.acc_cols + col0), r);
+        float *r = rb[blk & 1];
+        tmem_wait16(r);
+        if (blk + 1 < NBLK) tmem_ld16_async(tq + uint32_t((blk + 1) * EPI_COLS), rb[(blk + 1) & 1]);
         if (blk == NBLK - 1) {
           // all TMEM reads of this accumulator are done: hand it back
           tc_fence_before();
@@ -1458,7 +1532,16 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
                   p.sH == 1 && p.sW == 1 && p.pH == 0 &&
                   p.pW == 0 && hw % 8 == 0 && srcs_aligned && g.tile_pos % 64 == 0 &&
                   hw < (1ll << 31) && g.b_stage_bytes % 1024 == 0;
-    const int dbox = g.nsrc == 1 ? g.bk : 8;
+    // channel box: a whole stage (bk channels) for one source; for a
+    // concatenation the largest of bk, 16, 8 dividing every source's channel
+    // count, so that no box straddles two sources
+    int dbox = g.bk;
+    while (g.nsrc > 1 && dbox > 8) {
+      bool fits = true;
+      for (int k = 0; k < g.nsrc; ++k) fits = fits && (g.src_c0[k + 1] - g.src_c0[k]) % dbox == 0;
+      if (fits) break;
+      dbox /= 2;
+    }
     for (int k = 0; k < g.nsrc && direct; ++k)
       direct = (g.src_c0[k + 1] - g.src_c0[k]) % dbox == 0 || g.nsrc == 1;
     if (direct) {
@@ -1549,11 +1632,15 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   // epilogue activation
 #define WGX_UMMA_ROW(KW, T) \
   { umma_conv_kernel<KW, 0, T, 0>, umma_conv_kernel<KW, 1, T, 0>, umma_conv_kernel<KW, 2, T, 0> }
-  static const KernelFn table[2][7][3] = {
+#define WGX_UMMA_TRANS(T)                                                                  \
+  {WGX_UMMA_ROW(0, T), WGX_UMMA_ROW(1, T), WGX_UMMA_ROW(2, T), WGX_UMMA_ROW(3, T),          \
+   WGX_UMMA_ROW(0, T), WGX_UMMA_ROW(0, T), WGX_UMMA_ROW(0, T)}
+  // [standard, transposed N = 16 / 32 / 64][filter width][activation]
+  static const KernelFn table[4][7][3] = {
       {WGX_UMMA_ROW(0, 0), WGX_UMMA_ROW(1, 0), WGX_UMMA_ROW(2, 0), WGX_UMMA_ROW(3, 0),
        WGX_UMMA_ROW(4, 0), WGX_UMMA_ROW(5, 0), WGX_UMMA_ROW(7, 0)},
-      {WGX_UMMA_ROW(0, 1), WGX_UMMA_ROW(1, 1), WGX_UMMA_ROW(2, 1), WGX_UMMA_ROW(3, 1),
-       WGX_UMMA_ROW(0, 1), WGX_UMMA_ROW(0, 1), WGX_UMMA_ROW(0, 1)}};
+      WGX_UMMA_TRANS(16), WGX_UMMA_TRANS(32), WGX_UMMA_TRANS(64)};
+#undef WGX_UMMA_TRANS
 #undef WGX_UMMA_ROW
   int kw_idx = 0;
   if (g.khs == 1 && g.bk == 32)
@@ -1561,13 +1648,17 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   if (g.trans && kw_idx > 3) kw_idx = 0;  // transposed: specialised for KW <= 3 only
   const int act_idx = (g.act >= 0 && g.act <= 2) ? g.act : 0;
   // residual / split outputs: generic MMA loop, EXT epilogue
-  static const KernelFn table_ext[2][3] = {
-      {umma_conv_kernel<0, 0, 0, 1>, umma_conv_kernel<0, 1, 0, 1>, umma_conv_kernel<0, 2, 0, 1>},
-      {umma_conv_kernel<0, 0, 1, 1>, umma_conv_kernel<0, 1, 1, 1>, umma_conv_kernel<0, 2, 1, 1>}};
+#define WGX_UMMA_EXT(T) \
+  { umma_conv_kernel<0, 0, T, 1>, umma_conv_kernel<0, 1, T, 1>, umma_conv_kernel<0, 2, T, 1> }
+  static const KernelFn table_ext[4][3] = {WGX_UMMA_EXT(0), WGX_UMMA_EXT(16), WGX_UMMA_EXT(32),
+                                           WGX_UMMA_EXT(64)};
+#undef WGX_UMMA_EXT
+  const int nt_idx = !g.trans ? 0 : g.NT == 16 ? 1 : g.NT == 32 ? 2 : 3;
+  if (g.trans && g.NT != 16 && g.NT != 32 && g.NT != 64) fail("conv2d: bad transposed tile");
   const bool ext = g.resid != nullptr || g.nout > 0;
-  KernelFn kern = ext ? table_ext[g.trans][act_idx] : table[g.trans][kw_idx][act_idx];
-  const int kidx = ext ? 42 + g.trans * 3 + act_idx : (g.trans * 7 + kw_idx) * 3 + act_idx;
-  static bool attr_set[64][48] = {};
+  KernelFn kern = ext ? table_ext[nt_idx][act_idx] : table[nt_idx][kw_idx][act_idx];
+  const int kidx = ext ? 84 + nt_idx * 3 + act_idx : (nt_idx * 7 + kw_idx) * 3 + act_idx;
+  static bool attr_set[64][96] = {};
   if (dev < 64 && !attr_set[dev][kidx]) {
     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(SMEM_MAX)),
