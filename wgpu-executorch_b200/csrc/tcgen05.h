@@ -23,20 +23,26 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
 }
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait: true when the phase with `parity` completed, false after
-// kWaitNs (the caller then records the error and stops its role).
+// kWaitNs (the caller then records the error and stops its role). A phase
+// that already completed costs one try_wait (the clock is read only when
+// the first try fails).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  uint64_t t0 = global_ns();
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
   while (true) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (ok) return true;
+    if (mbar_try(bar, parity)) return true;
     if (global_ns() - t0 > kWaitNs) return false;
   }
 }

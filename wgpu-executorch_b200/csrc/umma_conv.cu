@@ -122,9 +122,13 @@ struct UmmaGeom {
   __half *outp[kMaxOut];
 };
 
+// MMA groups (filter tap x 16-channel step) of one stage whose descriptor
+// offsets the generic staging keeps in shared memory
+constexpr int kMaxGroups = 128;
+
 static uint32_t smem_need(const UmmaGeom &g) {
   return g.w_region_bytes + uint32_t(g.stages) * g.b_stage_bytes + EPI_BYTES +
-         (2 * g.stages + 5) * 8 + 16 + 1024;
+         (2 * g.stages + 5) * 8 + 16 + kMaxGroups * 8 + 1024;
 }
 
 // Geometry for one staging choice: each pipeline stage carries `bk` input
@@ -323,6 +327,7 @@ bool umma_conv_supported(const wgx_conv2d_params &p) {
   }
   UmmaGeom g = make_geom(p);
   if (g.KW > MAX_KW || g.IC < 8) return false;
+  if (g.khs * g.KW * (g.bk / 16) > kMaxGroups) return false;
   if (g.stages < 2) return false;
   if (smem_need(g) > SMEM_MAX) return false;
   if (g.R_alloc * 16 >= (1 << 18)) return false;  // LBO field range
@@ -859,6 +864,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t *full = bars, *empty = bars + S;
   uint64_t *accf = bars + 2 * S, *acce = accf + 2, *wbar = acce + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(wbar + 1);
+  // generic staging: (activation, weight) descriptor offsets of every MMA
+  // group of a stage, in 16-byte units (written and read by the MMA thread)
+  uint2 *grp_off = reinterpret_cast<uint2 *>(tmem_slot + 4);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -894,14 +902,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_expect_tx(wb, g.w_region_bytes);
         bulk_g2s(smem_u32(sW), wpk, g.w_region_bytes, wb);
       }
-      int gs = 0;
+      int slot = 0, use = 0;  // pipeline stage slot and its use count
       bool ok = true;
       for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x) {
         int b, oct;
         long long p0;
         tile_coords(g, t, b, p0, oct);
-        for (int s = 0; s < g.n_kstages; ++s, ++gs) {
-          const int slot = gs % S, use = gs / S;
+        // (slot, use) advance without a division
+        for (int s = 0; s < g.n_kstages; ++s, slot = slot + 1 == S ? (++use, 0) : slot + 1) {
           if (use > 0 && !mbar_wait(smem_u32(&empty[slot]), (use - 1) & 1)) {
             atomicOr(g.err, kErrLoadTimeout);
             ok = false;
@@ -966,7 +974,19 @@ __global__ void __launch_bounds__(THREADS, 1)
             b_off[2 * kw + ks] = (uint32_t(kw * g.dW) * 16 + uint32_t(ks) * 2 * b_lbo) >> 4;
           }
       }
-      int gs = 0, it = 0;
+      const int ngroups = g.khs * g.KW * (g.bk / 16);
+      if constexpr (KW_T == 0) {
+        int j = 0;
+        for (int khl = 0; khl < g.khs; ++khl)
+          for (int kw = 0; kw < g.KW; ++kw)
+            for (int ks = 0; ks < g.bk / 16; ++ks, ++j) {
+              const uint32_t tap = uint32_t(khl * g.KW + kw);
+              const uint32_t shift = uint32_t(khl * g.dH * g.Wp + kw * g.dW);
+              grp_off[j] = make_uint2((shift * 16 + uint32_t(ks) * 2 * b_lbo) >> 4,
+                                      (tap * uint32_t(g.chunks) * a_lbo + uint32_t(ks) * 2 * a_lbo) >> 4);
+            }
+      }
+      int it = 0, slot = 0, use = 0;
       for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x, ++it) {
         const int acc = it & 1, use_acc = it >> 1;
         if (use_acc > 0 && !mbar_wait(smem_u32(&acce[acc]), (use_acc - 1) & 1)) {
@@ -976,8 +996,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem + uint32_t(acc * g.acc_cols);
-        for (int s = 0; s < g.n_kstages; ++s, ++gs) {
-          const int slot = gs % S, use = gs / S;
+        for (int s = 0; s < g.n_kstages; ++s, slot = slot + 1 == S ? (++use, 0) : slot + 1) {
           if (!mbar_wait(smem_u32(&full[slot]), use & 1)) {
             atomicOr(g.err, kErrMmaTimeout);
             ok = false;
@@ -1032,26 +1051,22 @@ __global__ void __launch_bounds__(THREADS, 1)
             mma_commit(smem_u32(&empty[slot]));
             continue;
           }
-          const int ksteps = g.bk / 16;
-          for (int khl = 0; khl < g.khs; ++khl) {
-            for (int kw = 0; kw < g.KW; ++kw) {
-              const uint32_t tap = uint32_t(khl * g.KW + kw);
-              // activation row shift of this tap
-              const uint32_t shift = uint32_t(khl * g.dH * g.Wp + kw * g.dW);
-              for (int ks = 0; ks < ksteps; ++ks) {
-                const uint64_t wdesc = kmajor_desc(
-                    a_base + tap * uint32_t(g.chunks) * a_lbo + ks * 2 * a_lbo, a_lbo);
-                const uint64_t xdesc = kmajor_desc(b_base + shift * 16 + ks * 2 * b_lbo, b_lbo);
-                const uint32_t acc_flag = (s | khl | kw | ks) != 0;
-                if constexpr (TRANS) {
-                  // M blocks innermost (see the specialised path)
+          {
+            // generic staging: one MMA group per (filter tap, 16-channel
+            // step), offsets from the table
+            const uint64_t x0 = kmajor_desc(b_base, b_lbo), w0 = kmajor_desc(a_base, a_lbo);
+#pragma unroll 2
+            for (int j = 0; j < ngroups; ++j) {
+              const uint2 o = grp_off[j];
+              const uint64_t xd = x0 + o.x, wd = w0 + o.y;
+              const uint32_t acc_flag = (s | j) != 0;
+              if constexpr (TRANS) {
+                // M blocks innermost (see the specialised path)
 #pragma unroll
-                  for (int mb = 0; mb < G_C; ++mb)
-                    mma_f16(d + uint32_t(mb * NT_C), xdesc + uint64_t(mb * 128), wdesc, idesc,
-                            acc_flag);
-                } else {
-                  mma_f16(d, wdesc, xdesc, idesc, acc_flag);
-                }
+                for (int mb = 0; mb < G_C; ++mb)
+                  mma_f16(d + uint32_t(mb * NT_C), xd + uint64_t(mb * 128), wd, idesc, acc_flag);
+              } else {
+                mma_f16(d, wd, xd, idesc, acc_flag);
               }
             }
           }
