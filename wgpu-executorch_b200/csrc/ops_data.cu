@@ -760,6 +760,22 @@ __global__ void nearest_v8_kernel(Resample r, const __half *__restrict__ x, uint
   }
 }
 
+// Integer scale: OW = 2*IW, OH = sH*IH (the 2x upsample of detection necks).
+// One thread reads 4 input values (8 bytes) of input row `row` and writes
+// the 8 duplicated values (16 bytes) into each of the sH output rows
+// row*sH .. row*sH + sH - 1 (output row of (plane, ih*sH + k) =
+// (plane*IH + ih)*sH + k); 32-bit indices (checked by the host).
+__global__ void nearest_x2_kernel(const uint2 *__restrict__ x, uint4 *__restrict__ y, int ow8,
+                                  int sH, int n_items) {
+  const int item = blockIdx.x * blockDim.x + threadIdx.x;
+  if (item >= n_items) return;
+  const int row = item / ow8, g = item - row * ow8;
+  const uint2 v = x[item];  // input row `row`, columns 4g .. 4g + 3
+  const uint4 o = make_uint4(__byte_perm(v.x, 0, 0x1010), __byte_perm(v.x, 0, 0x3232),
+                             __byte_perm(v.y, 0, 0x1010), __byte_perm(v.y, 0, 0x3232));
+  for (int k = 0; k < sH; ++k) y[(size_t(row) * sH + k) * ow8 + g] = o;
+}
+
 void record_nearest(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   const char *name = "aten.upsample_nearest2d.vec";
   wgx_tensor *in = tensor_at(a, 0, name), *out = tensor_at(a, 3, name);
@@ -775,6 +791,19 @@ void record_nearest(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   void *py = out->data();
   const long long n = out->numel;
   const int dt = in->dtype;
+  const long long in_rows = (long long)r.N * r.C * r.IH;
+  if (dt == WGX_FLOAT16 && r.OW == 2 * r.IW && r.OH % r.IH == 0 && r.IW % 4 == 0 &&
+      (reinterpret_cast<uintptr_t>(py) & 15) == 0 && (reinterpret_cast<uintptr_t>(px) & 7) == 0 &&
+      in_rows * (r.OW / 8) < (1ll << 31)) {
+    const int ow8 = r.OW / 8, sH = r.OH / r.IH;
+    const int n_items = int(in_rows * ow8);
+    push(ctx, name, 1, [=](const ExecEnv &env) {
+      nearest_x2_kernel<<<unsigned((n_items + 255) / 256), 256, 0, env.stream>>>(
+          (const uint2 *)px, (uint4 *)py, ow8, sH, n_items);
+      check_cuda(cudaGetLastError(), "upsample launch");
+    });
+    return;
+  }
   if (dt == WGX_FLOAT16 && r.OW % 8 == 0 && (reinterpret_cast<uintptr_t>(py) & 15) == 0) {
     const long long n8 = n / 8;
     push(ctx, name, 1, [=](const ExecEnv &env) {

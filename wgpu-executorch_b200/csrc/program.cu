@@ -16,6 +16,8 @@
 //     arena; every slice starts on a 256-byte boundary.
 //   * constants alias their bytes inside a device copy of weights.bin that
 //     is uploaded with a single pinned, asynchronous host-to-device copy.
+//   * inputs that no operator writes are read from the caller's tensors and
+//     outputs written into them (no copies; see the binding step).
 //   * a fusion pass rewrites convolution -> sigmoid -> mul (SiLU) into one
 //     convolution with a SiLU epilogue when the intermediate values have no
 //     other reader.
@@ -288,10 +290,11 @@ LinkPlan plan_links(wgx_context *ctx, const Program &P,
   // value -> producing chain index; fused heads own the mul's output
   std::map<int64_t, size_t> producer;
   auto out_of = [&](size_t i) -> int64_t {
-    return fusion[i] == 1 ? P.chain[i + 2].args[2] : P.chain[i].args.back();
+    if (fusion[i] == 1) return P.chain[i + 2].args[2];
+    return P.chain[i].args.empty() ? int64_t(-1) : P.chain[i].args.back();
   };
   for (size_t i = 0; i < P.chain.size(); ++i)
-    if (fusion[i] != 2) producer[out_of(i)] = i;
+    if (fusion[i] != 2 && out_of(i) >= 0) producer[out_of(i)] = i;
   auto conv_of = [&](size_t i, wgx_conv2d_params *pp) {
     const POp &op = P.chain[i];
     if (op.name != "aten.convolution.default" || fusion[i] == 2) return false;
@@ -684,12 +687,68 @@ static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len
     tensors[int64_t(i)] = t;
   }
 
+  // ---- zero-copy binding (B200 design): an input value that no operator
+  // writes reads the caller's tensor directly, and an output value is
+  // written straight into the caller's tensor, instead of the copies of
+  // steps 5 and 7 (same bytes at every submit: the copies would run at
+  // submit time too). Only the bound value's tensor moves: the other values
+  // of its pool keep the pool. Written values are taken conservatively as
+  // the last two arguments of every operator (and the items of tensor lists
+  // there); a caller tensor that is both an input and an output, or whose
+  // dtype or shape differs from the value's, keeps the copy.
+  std::set<int64_t> written;
+  for (const POp &op : P.chain) {
+    const size_t na = op.args.size();
+    for (size_t k = na >= 2 ? na - 2 : 0; k < na; ++k) {
+      const int64_t v = op.args[k];
+      if (v < 0 || size_t(v) >= P.values.size()) continue;
+      written.insert(v);
+      if (P.values[v].kind == PValue::TensorList)
+        for (auto t : P.values[v].items) written.insert(t);
+    }
+  }
+  std::set<const wgx_buffer *> in_bufs, out_bufs;
+  for (size_t i = 0; i < n_in; ++i)
+    if (args[i].kind == WGX_ARG_TENSOR) in_bufs.insert(args[i].v.tensor->buffer);
+  for (size_t i = 0; i < n_out; ++i)
+    if (args[n_in + i].kind == WGX_ARG_TENSOR) out_bufs.insert(args[n_in + i].v.tensor->buffer);
+  auto same_layout = [](const wgx_tensor *a, const wgx_tensor *b) {
+    if (a->dtype != b->dtype || a->ndim != b->ndim) return false;
+    for (int d = 0; d < a->ndim; ++d)
+      if (a->shape[d] != b->shape[d]) return false;
+    return true;
+  };
+  const std::set<int64_t> prog_inputs(P.input_ids.begin(), P.input_ids.end());
+  std::set<int64_t> bound_out;
+  for (size_t i = 0; i < n_out; ++i) {
+    const wgx_arg &dst = args[n_in + i];
+    auto it = tensors.find(P.output_ids[i]);
+    if (dst.kind != WGX_ARG_TENSOR || it == tensors.end()) continue;
+    const int64_t v = P.output_ids[i];
+    if (prog_inputs.count(v) || bound_out.count(v) || in_bufs.count(dst.v.tensor->buffer) ||
+        !same_layout(it->second, dst.v.tensor))
+      continue;
+    bool dup = false;  // one caller tensor for two outputs: keep the copies
+    for (size_t k = 0; k < n_out; ++k)
+      dup = dup || (k != i && args[n_in + k].kind == WGX_ARG_TENSOR &&
+                    args[n_in + k].v.tensor->buffer == dst.v.tensor->buffer);
+    if (dup) continue;
+    it->second->buffer = dst.v.tensor->buffer;
+    bound_out.insert(v);
+  }
+
   // ---- input copies
   for (size_t i = 0; i < n_in; ++i) {
     if (args[i].kind != WGX_ARG_TENSOR) continue;  // non-Tensor inputs are skipped
     auto it = tensors.find(P.input_ids[i]);
     if (it == tensors.end())
       fail("program: no tensor for input value " + std::to_string(P.input_ids[i]));
+    const int64_t v = P.input_ids[i];
+    if (!written.count(v) && !out_bufs.count(args[i].v.tensor->buffer) &&
+        same_layout(it->second, args[i].v.tensor)) {
+      it->second->buffer = args[i].v.tensor->buffer;
+      continue;
+    }
     if (wgx_copy(ctx, args[i].v.tensor, it->second) != WGX_OK) fail(wgx_last_error());
   }
 
@@ -825,6 +884,7 @@ static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len
     if (dst.kind != WGX_ARG_TENSOR) fail("program: output " + std::to_string(i) + " must be a Tensor");
     if (it == tensors.end())
       fail("program: no tensor for output value " + std::to_string(P.output_ids[i]));
+    if (bound_out.count(P.output_ids[i])) continue;  // written in place
     if (wgx_copy(ctx, it->second, dst.v.tensor) != WGX_OK) fail(wgx_last_error());
   }
 }

@@ -384,6 +384,13 @@ class WgpuExecutionContext:
         check(lib.wgx_context_stats(self._h, byref(n), byref(k)))
         return {"commands": n.value, "kernel_launches": k.value}
 
+    def command_names(self) -> list:
+        """Labels of the recorded commands in recording order (the names
+        ``profile`` reports), without running them."""
+        self._assert_alive()
+        n = self.stats()["commands"]
+        return [lib.wgx_context_command_name(self._h, i).decode() for i in range(n)]
+
     def profile(self, repeats: int = 1) -> list:
         """Per-command device time: the recorded commands replayed eagerly
         ``repeats`` times with CUDA events around each one. Returns
