@@ -274,6 +274,7 @@ LinkPlan plan_links(wgx_context *ctx, const Program &P,
                     const std::map<int64_t, wgx_tensor *> &tensors, const std::vector<int> &fusion) {
   LinkPlan L;
   std::map<int64_t, int> readers;
+  std::map<int64_t, std::vector<size_t>> reader_ops;  // direct (non-list) readers
   for (size_t i = 0; i < P.chain.size(); ++i) {
     if (fusion[i] == 2) continue;
     const POp &op = P.chain[i];
@@ -281,6 +282,7 @@ LinkPlan plan_links(wgx_context *ctx, const Program &P,
       const int64_t a = op.args[k];
       if (a < 0 || size_t(a) >= P.values.size()) continue;
       readers[a]++;
+      reader_ops[a].push_back(i);
       if (P.values[a].kind == PValue::TensorList)
         for (auto t : P.values[a].items) readers[t]++;
     }
@@ -367,16 +369,42 @@ LinkPlan plan_links(wgx_context *ctx, const Program &P,
     const POp &op = P.chain[j];
     if (op.name == "aten.split_with_sizes_copy.default" && op.args.size() == 4) {
       const int64_t x = op.args[0];
-      if (!producer.count(x) || readers[x] != 1 || boundary.count(x)) continue;
+      if (!producer.count(x) || boundary.count(x)) continue;
       const size_t k = producer[x];
       wgx_conv2d_params pp{};
-      if (!conv_of(k, &pp) || last_of(k) + 1 != j || !free_output(k)) continue;
+      if (!conv_of(k, &pp) || !free_output(k)) continue;
       const PValue &dimv = P.values[op.args[2]];
       const int dim = dimv.kind == PValue::Scalar ? int(dimv.num) : -99;
       const PValue &outs = P.values[op.args[3]];
       if ((dim != 1 && dim != -3) || outs.kind != PValue::TensorList || outs.items.empty() ||
           outs.items.size() > 4)
         continue;
+      // every reader of x must be a split into the same channel ranges (the
+      // exported graph may split one value twice); this one comes first
+      std::vector<size_t> splits;
+      bool all_split = readers[x] == int(reader_ops[x].size());
+      for (size_t r : reader_ops[x]) {
+        const POp &o = P.chain[r];
+        const bool same =
+            o.name == op.name && o.args.size() == 4 && o.args[0] == x &&
+            P.values[o.args[1]].items == P.values[op.args[1]].items &&
+            P.values[o.args[2]].kind == PValue::Scalar && int(P.values[o.args[2]].num) == dim &&
+            P.values[o.args[3]].kind == PValue::TensorList &&
+            P.values[o.args[3]].items.size() == outs.items.size();
+        all_split = all_split && same;
+        splits.push_back(r);
+      }
+      if (!all_split || splits.empty() || splits.front() != j) continue;
+      // a single split right after the convolution writes the pieces where
+      // the memory plan put them; otherwise the pieces get buffers of their
+      // own (the planned ones may still hold live values when the
+      // convolution runs), shared by the splits' equal pieces
+      const bool adjacent = splits.size() == 1 && last_of(k) + 1 == j;
+      bool pieces_ok = true;
+      for (size_t r : splits)
+        for (auto t : P.values[P.chain[r].args[3]].items)
+          pieces_ok = pieces_ok && !boundary.count(t) && tensors.count(t);
+      if (!pieces_ok) continue;
       std::vector<wgx_tensor *> pieces;
       int64_t csum = 0;
       bool ok = true;
@@ -393,8 +421,21 @@ LinkPlan plan_links(wgx_context *ctx, const Program &P,
         pieces.push_back(it->second);
       }
       if (!ok || csum != pp.OC) continue;
+      if (!adjacent) {
+        for (size_t i = 0; i < outs.items.size(); ++i) {
+          const wgx_tensor *pt = pieces[i];
+          auto *b = new wgx_buffer();
+          b->ctx = ctx;
+          b->size = (pt->byte_length() + 3) / 4 * 4;
+          b->dptr = ctx->alloc_device(b->size);
+          b->usage = pt->buffer->usage;
+          b->device = ctx->device;
+          ctx->owned.push_back(b);
+          for (size_t r : splits) tensors.at(P.values[P.chain[r].args[3]].items[i])->buffer = b;
+        }
+      }
       L.conv[k].split = pieces;
-      L.skip.insert(j);
+      for (size_t r : splits) L.skip.insert(r);
     } else if (op.name == "aten.add.Tensor" && (op.args.size() == 3 || op.args.size() == 4)) {
       if (op.args.size() == 4) {
         const PValue &al = P.values[op.args[2]];

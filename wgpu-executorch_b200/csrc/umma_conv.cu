@@ -113,6 +113,9 @@ struct UmmaGeom {
   // dbox channels, 128-byte swizzle, zero fill past the image and past a
   // source's channels) and the MMAs read them MN-major; no re-layout runs
   int direct, dbox;
+  // transposed variant, NCHW output (or split pieces) with Wp % 8 == 0,
+  // OW % 8 == 0 and 16-byte aligned outputs: 16-byte epilogue stores
+  int tvec;
   // NCHW output options (omode 0): `resid` (same shape as the output) is
   // added after the activation; nout > 0 splits the output channels into
   // tensors outp[k] holding channels [out_c0[k], out_c0[k+1])
@@ -1093,8 +1096,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // per-warp transpose rows of the vector-store path: 16 rows x 64 bytes
     // after the bias (1 KB reserved), 16 KB in all
     uint32_t *tstage = reinterpret_cast<uint32_t *>(sE + 1024 + ew * 1024);
-    const bool tvec = !g.omode && ((g.Wp | g.OW) & 7) == 0 &&
-                      (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+    const bool tvec = g.tvec != 0;
     float r[EXT ? 16 : 32];
     int it = 0;
     for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++it) {
@@ -1237,7 +1239,8 @@ __global__ void __launch_bounds__(THREADS, 1)
               const int pos = int(p0) + (c >> LG_NT) * 128 + q * 32 + part * 8;
               const int oh = pos / g.Wp, ow = pos - oh * g.Wp;
               if (oc < g.OC && oh < g.OH && ow < g.OW)
-                *reinterpret_cast<uint4 *>(base + size_t(oc) * plane + size_t(oh) * g.OW + ow) = val;
+                *reinterpret_cast<uint4 *>(out_plane(g, out, b, oc, plane) + size_t(oh) * g.OW + ow) =
+                    val;
             }
             __syncwarp();
           }
@@ -1670,7 +1673,16 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
 #undef WGX_UMMA_EXT
   const int nt_idx = !g.trans ? 0 : g.NT == 16 ? 1 : g.NT == 32 ? 2 : 3;
   if (g.trans && g.NT != 16 && g.NT != 32 && g.NT != 64) fail("conv2d: bad transposed tile");
-  const bool ext = g.resid != nullptr || g.nout > 0;
+  // 16-byte stores of the transposed epilogue (split pieces included)
+  {
+    bool aligned = g.nout > 0 || (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+    for (int k = 0; k < g.nout; ++k)
+      aligned = aligned && (reinterpret_cast<uintptr_t>(g.outp[k]) & 15) == 0;
+    g.tvec = g.trans && !g.omode && ((g.Wp | g.OW) & 7) == 0 && aligned;
+  }
+  // residual adds, and split outputs the vector path cannot store: the EXT
+  // epilogue
+  const bool ext = g.resid != nullptr || (g.nout > 0 && !g.tvec);
   KernelFn kern = ext ? table_ext[nt_idx][act_idx] : table[nt_idx][kw_idx][act_idx];
   const int kidx = ext ? 84 + nt_idx * 3 + act_idx : (nt_idx * 7 + kw_idx) * 3 + act_idx;
   static bool attr_set[64][96] = {};
