@@ -507,6 +507,46 @@ LinkPlan plan_links(wgx_context *ctx, const Program &P,
   return L;
 }
 
+// View-like copies (reshape, squeeze, unsqueeze, contiguous clone) of a
+// dense tensor move no bytes: the output value aliases the input's storage
+// and the operator records nothing. The input's storage must then outlive
+// the output, so an input held in a memory-plan pool (reused once the input
+// dies) first gets a buffer of its own. Program inputs and outputs keep
+// their operators.
+std::set<size_t> plan_aliases(wgx_context *ctx, const Program &P,
+                              const std::map<int64_t, wgx_tensor *> &tensors,
+                              const std::set<const wgx_buffer *> &pools) {
+  static const std::set<std::string> kViews = {
+      "aten.view_copy.default",      "aten.clone.default",        "aten.squeeze_copy.dims",
+      "aten.squeeze_copy.dim",       "aten.squeeze_copy.default", "aten.unsqueeze_copy.default",
+      "aten._unsafe_view.default",   "aten.alias_copy.default"};
+  std::set<int64_t> boundary(P.output_ids.begin(), P.output_ids.end());
+  boundary.insert(P.input_ids.begin(), P.input_ids.end());
+  std::set<size_t> skip;
+  for (size_t i = 0; i < P.chain.size(); ++i) {
+    const POp &op = P.chain[i];
+    if (!kViews.count(op.name) || op.args.size() < 2) continue;
+    const int64_t x = op.args.front(), o = op.args.back();
+    auto xt = tensors.find(x), ot = tensors.find(o);
+    if (x == o || xt == tensors.end() || ot == tensors.end() || boundary.count(o)) continue;
+    wgx_tensor *tx = xt->second, *to = ot->second;
+    if (tx->dtype != to->dtype || tx->numel != to->numel) continue;
+    if (pools.count(tx->buffer)) {
+      auto *b = new wgx_buffer();
+      b->ctx = ctx;
+      b->size = (tx->byte_length() + 3) / 4 * 4;
+      b->dptr = ctx->alloc_device(b->size);
+      b->usage = tx->buffer->usage;
+      b->device = ctx->device;
+      ctx->owned.push_back(b);
+      tx->buffer = b;
+    }
+    to->buffer = tx->buffer;
+    skip.insert(i);
+  }
+  return skip;
+}
+
 // Attention fusion: bmm(Q, K^T) -> view -> softmax(-1) -> permute(last two)
 // -> squeeze/view -> bmm(V^T, .) (the PSA block of YOLO26-N) becomes one
 // fused tcgen05 kernel recorded where the second bmm stood. Every
@@ -778,6 +818,12 @@ static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len
     bound_out.insert(v);
   }
 
+  // ---- views alias their inputs (before the input copies: an aliased input
+  // value may move to a buffer of its own)
+  std::set<const wgx_buffer *> pool_set;
+  for (auto &kv : pool_buf) pool_set.insert(kv.second);
+  const std::set<size_t> alias_skip = plan_aliases(ctx, P, tensors, pool_set);
+
   // ---- input copies
   for (size_t i = 0; i < n_in; ++i) {
     if (args[i].kind != WGX_ARG_TENSOR) continue;  // non-Tensor inputs are skipped
@@ -815,7 +861,8 @@ static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len
       ctx->commands.push_back(std::move(c));
       continue;
     }
-    if (fusion[oi] == 2 || links.skip.count(oi) || attn.skip.count(oi)) continue;
+    if (fusion[oi] == 2 || links.skip.count(oi) || attn.skip.count(oi) || alias_skip.count(oi))
+      continue;
     if (auto at = attn.at.find(oi); at != attn.at.end()) {
       const wgx_tensor *q = tensors[at->second.q], *kt = tensors[at->second.kt],
                        *vt = tensors[at->second.vt], *ot = tensors[at->second.ot];
