@@ -508,54 +508,61 @@ __global__ void maxpool_kernel(PoolGeom g, const T *__restrict__ x, T *__restric
 // over those row maxima with strict '>', so the winner is the first
 // maximum in the reference's row-major window order, with the same start
 // value and flat index ih*IW + iw as maxpool_kernel.
+// Small planes: each block takes `ppb` consecutive planes (ppb * (hw + rw)
+// floats + ppb * rw indices of shared memory), so that a block has work for
+// all of its threads; the planes are independent.
 template <class T>
 __global__ void __launch_bounds__(256) maxpool_plane_kernel(PoolGeom g, const T *__restrict__ x,
                                                             T *__restrict__ y,
-                                                            int32_t *__restrict__ idx) {
+                                                            int32_t *__restrict__ idx, int ppb,
+                                                            long long planes) {
   extern __shared__ __align__(16) unsigned char mp_smem[];
   const int hw = g.IH * g.IW;
+  const int rw = g.IH * g.OW;
+  const long long plane0 = (long long)blockIdx.x * ppb;
+  const int np = int(min((long long)ppb, planes - plane0));
   float *tile = reinterpret_cast<float *>(mp_smem);
-  float *rmax = tile + hw;
-  int16_t *rarg = reinterpret_cast<int16_t *>(rmax + g.IH * g.OW);
-  const long long plane = blockIdx.x;
-  const T *xp = x + plane * hw;
-  for (int i = threadIdx.x; i < hw; i += 256) tile[i] = lf(xp[i]);
+  float *rmax = tile + size_t(ppb) * hw;
+  int16_t *rarg = reinterpret_cast<int16_t *>(rmax + size_t(ppb) * rw);
+  const T *xp = x + plane0 * hw;
+  for (int i = threadIdx.x; i < np * hw; i += 256) tile[i] = lf(xp[i]);
   __syncthreads();
   const float start = sizeof(T) == 2 ? -65504.0f : -3.402823466e38f;
-  const int rw = g.IH * g.OW;
-  for (int i = threadIdx.x; i < rw; i += 256) {
+  for (int pi = threadIdx.x; pi < np * rw; pi += 256) {
+    const int pl = pi / rw, i = pi - pl * rw;
     const int ih = i / g.OW, ow = i - ih * g.OW;
     float best = start;
     int arg = -1;
     for (int kw = 0; kw < g.kW; ++kw) {
       const int iw = ow * g.sW - g.pW + kw * g.dW;
       if (iw < 0 || iw >= g.IW) continue;
-      const float v = tile[ih * g.IW + iw];
+      const float v = tile[pl * hw + ih * g.IW + iw];
       if (v > best) {
         best = v;
         arg = iw;
       }
     }
-    rmax[i] = best;
-    rarg[i] = int16_t(arg);
+    rmax[pi] = best;
+    rarg[pi] = int16_t(arg);
   }
   __syncthreads();
   const int ohw = g.OH * g.OW;
-  for (int o = threadIdx.x; o < ohw; o += 256) {
+  for (int po = threadIdx.x; po < np * ohw; po += 256) {
+    const int pl = po / ohw, o = po - pl * ohw;
     const int oh = o / g.OW, ow = o - oh * g.OW;
     float best = start;
     int best_idx = 0;
     for (int kh = 0; kh < g.kH; ++kh) {
       const int ih = oh * g.sH - g.pH + kh * g.dH;
       if (ih < 0 || ih >= g.IH) continue;
-      const float v = rmax[ih * g.OW + ow];
+      const float v = rmax[pl * rw + ih * g.OW + ow];
       if (v > best) {
         best = v;
-        best_idx = ih * g.IW + rarg[ih * g.OW + ow];
+        best_idx = ih * g.IW + rarg[pl * rw + ih * g.OW + ow];
       }
     }
-    y[plane * ohw + o] = sf<T>(best);
-    if (idx) idx[plane * ohw + o] = best_idx;
+    y[plane0 * ohw + po] = sf<T>(best);
+    if (idx) idx[plane0 * ohw + po] = best_idx;
   }
 }
 
@@ -617,15 +624,20 @@ void record_maxpool(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   const long long planes = (long long)g.N * g.C;
   if ((long long)g.IH * g.IW <= 4096 && (long long)g.IH * g.OW <= 4096 && g.IW <= 32767 &&
       planes > 0 && planes < (1ll << 31)) {
+    // planes per block: about 1024 input elements per block, within 40 KB
+    const size_t per_plane = (size_t(g.IH) * g.IW + size_t(g.IH) * g.OW) * 4 +
+                             size_t(g.IH) * g.OW * 2;
+    int ppb = int(std::max<long long>(1, 1024 / ((long long)g.IH * g.IW)));
+    ppb = int(std::min<size_t>(size_t(ppb), std::max<size_t>(1, 40 * 1024 / per_plane)));
+    const size_t smem = per_plane * ppb + 16;
+    const long long blocks = (planes + ppb - 1) / ppb;
     push(ctx, name, 1, [=](const ExecEnv &env) {
-      const size_t smem = (size_t(g.IH) * g.IW + size_t(g.IH) * g.OW) * 4 +
-                          size_t(g.IH) * g.OW * 2;
       if (dt == WGX_FLOAT16)
-        maxpool_plane_kernel<__half><<<unsigned(planes), 256, smem, env.stream>>>(
-            g, (const __half *)px, (__half *)py, pi);
+        maxpool_plane_kernel<__half><<<unsigned(blocks), 256, smem, env.stream>>>(
+            g, (const __half *)px, (__half *)py, pi, ppb, planes);
       else
-        maxpool_plane_kernel<float><<<unsigned(planes), 256, smem, env.stream>>>(
-            g, (const float *)px, (float *)py, pi);
+        maxpool_plane_kernel<float><<<unsigned(blocks), 256, smem, env.stream>>>(
+            g, (const float *)px, (float *)py, pi, ppb, planes);
       check_cuda(cudaGetLastError(), "maxpool launch");
     });
     return;

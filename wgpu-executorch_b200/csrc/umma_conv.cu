@@ -128,6 +128,9 @@ struct UmmaGeom {
 // MMA groups (filter tap x 16-channel step) of one stage whose descriptor
 // offsets the generic staging keeps in shared memory
 constexpr int kMaxGroups = 128;
+// generic staging: stages of at most this many MMA groups issue as one
+// straight-line sequence
+constexpr int kSeqGroups = 8;
 
 static uint32_t smem_need(const UmmaGeom &g) {
   return g.w_region_bytes + uint32_t(g.stages) * g.b_stage_bytes + EPI_BYTES +
@@ -1056,20 +1059,56 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           {
             // generic staging: one MMA group per (filter tap, 16-channel
-            // step), offsets from the table
+            // step), offsets from the table. Up to kSeqGroups groups are
+            // issued as straight-line code entered once per stage (a branch
+            // between MMAs stalls the issuing thread far longer than an MMA
+            // takes to issue): the stage's offsets are loaded first, last
+            // group in the last slot, and the switch falls through the
+            // groups in table order.
             const uint64_t x0 = kmajor_desc(b_base, b_lbo), w0 = kmajor_desc(a_base, a_lbo);
-#pragma unroll 2
-            for (int j = 0; j < ngroups; ++j) {
-              const uint2 o = grp_off[j];
-              const uint64_t xd = x0 + o.x, wd = w0 + o.y;
-              const uint32_t acc_flag = (s | j) != 0;
-              if constexpr (TRANS) {
-                // M blocks innermost (see the specialised path)
+            uint32_t acc_flag = s != 0;
+            if (ngroups <= kSeqGroups) {
+              uint2 e[kSeqGroups];
 #pragma unroll
-                for (int mb = 0; mb < G_C; ++mb)
-                  mma_f16(d + uint32_t(mb * NT_C), xd + uint64_t(mb * 128), wd, idesc, acc_flag);
-              } else {
-                mma_f16(d, wd, xd, idesc, acc_flag);
+              for (int k = 0; k < kSeqGroups; ++k) {
+                const int j = k - (kSeqGroups - ngroups);
+                e[k] = grp_off[j < 0 ? 0 : j];
+              }
+#define WGX_GROUP(K)                                                                      \
+  {                                                                                       \
+    const uint64_t xd = x0 + e[K].x, wd = w0 + e[K].y;                                    \
+    if constexpr (TRANS) {                                                                \
+      _Pragma("unroll") for (int mb = 0; mb < G_C; ++mb)                                  \
+          mma_f16(d + uint32_t(mb * NT_C), xd + uint64_t(mb * 128), wd, idesc, acc_flag); \
+    } else {                                                                              \
+      mma_f16(d, wd, xd, idesc, acc_flag);                                                \
+    }                                                                                     \
+    acc_flag = 1;                                                                         \
+  }
+              switch (ngroups) {
+                case 8: WGX_GROUP(0) [[fallthrough]];
+                case 7: WGX_GROUP(1) [[fallthrough]];
+                case 6: WGX_GROUP(2) [[fallthrough]];
+                case 5: WGX_GROUP(3) [[fallthrough]];
+                case 4: WGX_GROUP(4) [[fallthrough]];
+                case 3: WGX_GROUP(5) [[fallthrough]];
+                case 2: WGX_GROUP(6) [[fallthrough]];
+                default: WGX_GROUP(7)
+              }
+#undef WGX_GROUP
+            } else {
+#pragma unroll 2
+              for (int j = 0; j < ngroups; ++j) {
+                const uint2 o = grp_off[j];
+                const uint64_t xd = x0 + o.x, wd = w0 + o.y;
+                if constexpr (TRANS) {
+#pragma unroll
+                  for (int mb = 0; mb < G_C; ++mb)
+                    mma_f16(d + uint32_t(mb * NT_C), xd + uint64_t(mb * 128), wd, idesc, acc_flag);
+                } else {
+                  mma_f16(d, wd, xd, idesc, acc_flag);
+                }
+                acc_flag = 1;
               }
             }
           }
