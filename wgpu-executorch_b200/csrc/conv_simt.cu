@@ -402,6 +402,42 @@ __device__ __forceinline__ void dw_stage_vec(const ConvGeom &g, const DwTile &d,
   }
 }
 
+// Rows whose width is a whole number of 8-byte units (IW * sizeof(T) % 8 ==
+// 0, e.g. 20-wide fp16 planes): every 8-byte unit of every staged row is
+// written once, the interior from global memory (8-byte aligned loads),
+// the halo columns and the rows outside the image as zeros (DW_PADL is a
+// whole number of units, so a unit is entirely inside or outside).
+template <class T>
+__device__ __forceinline__ void dw_stage_vec8b(const ConvGeom &g, const DwTile &d,
+                                               const T *__restrict__ x, T *tile, long long plane0,
+                                               int np, int ih0, size_t plane_tile) {
+  constexpr int U = 8 / sizeof(T);  // elements per unit
+  const int urow = d.TWs / U;
+  const int total = np * d.rows * urow;
+  for (int base = threadIdx.x; base < total; base += blockDim.x * DW_STAGE_U) {
+    uint2 val[DW_STAGE_U];
+    int dst[DW_STAGE_U];
+#pragma unroll
+    for (int u = 0; u < DW_STAGE_U; ++u) {
+      const int i = base + u * blockDim.x;
+      val[u] = make_uint2(0u, 0u);
+      dst[u] = -1;
+      if (i < total) {
+        const int v = i % urow;
+        const int rr = i / urow;
+        const int r = rr % d.rows, p = rr / d.rows;
+        const int ih = ih0 + r, iw = v * U - DW_PADL;
+        dst[u] = int(p * plane_tile + size_t(r) * d.TWs + v * U);
+        if (ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW)
+          val[u] = *reinterpret_cast<const uint2 *>(x + ((plane0 + p) * g.IH + ih) * (long long)g.IW + iw);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < DW_STAGE_U; ++u)
+      if (dst[u] >= 0) *reinterpret_cast<uint2 *>(tile + dst[u]) = val[u];
+  }
+}
+
 // Staging for rows that are not whole 16-byte vectors: a plane's row band
 // is one contiguous run of memory, so it is read as aligned 16-byte vectors
 // (the plane size is a multiple of the vector width) and each element is
@@ -465,6 +501,8 @@ __global__ void __launch_bounds__(256)
   constexpr int V = 16 / sizeof(T);
   if (vec_in == 1) {
     dw_stage_vec<T>(g, d, x, tile, plane0, np, ih0, plane_tile);
+  } else if (vec_in == 3) {
+    dw_stage_vec8b<T>(g, d, x, tile, plane0, np, ih0, plane_tile);
   } else if (vec_in == 2) {
     dw_stage_flat<T>(g, d, x, tile, plane0, np, ih0, plane_tile);
   } else {
@@ -571,6 +609,8 @@ __global__ void __launch_bounds__(256)
   }
   if (vec_in == 1) {
     dw_stage_vec<__half>(g, d, x, tile, plane0, np, ih0, plane_tile);
+  } else if (vec_in == 3) {
+    dw_stage_vec8b<__half>(g, d, x, tile, plane0, np, ih0, plane_tile);
   } else if (vec_in == 2) {
     dw_stage_flat<__half>(g, d, x, tile, plane0, np, ih0, plane_tile);
   } else {
@@ -795,11 +835,12 @@ static void launch_simt(const wgx_conv2d_params &p, int variant, const T *in, co
     pointwise_single<T><<<grid, 256, 0, s>>>(g, in, w, bias, out);
   } else if (variant == WGX_CONV_DEPTHWISE && dw_tiling(p, int(sizeof(T)), dt)) {
     constexpr int V = 16 / sizeof(T);
-    // staging: 1 = whole-vector rows, 2 = vector reads of contiguous row
-    // bands scattered into the tile, 0 = per element
+    // staging: 1 = whole-vector rows, 3 = whole 8-byte-unit rows, 2 = vector
+    // reads of contiguous row bands scattered into the tile, 0 = per element
     const bool aligned = (reinterpret_cast<uintptr_t>(in) & 15) == 0;
     const int vec_in = !aligned ? 0
                        : p.IW % V == 0 ? 1
+                       : (p.IW * int(sizeof(T))) % 8 == 0 && dt.TWs % (8 / int(sizeof(T))) == 0 ? 3
                        : (int64_t(p.IH) * p.IW) % V == 0 ? 2 : 0;
     const int vec_out = (p.OW % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
     const size_t smem = size_t(dt.P) * dt.rows * dt.TWs * sizeof(T);

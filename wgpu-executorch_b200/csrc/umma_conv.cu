@@ -73,6 +73,9 @@ constexpr uint32_t SMEM_MAX = 227u * 1024u;
 constexpr int kMaxSrc = 8;
 constexpr int kMaxOut = 4;
 
+// space-to-depth tap masks: filter-row groups x phases
+constexpr int kMaxKhg = 4, kMaxPhases = 16;
+
 struct UmmaGeom {
   // IC, KH, KW, dH, dW, pH, pW describe the stride-1 convolution the MMA
   // pipeline runs (for a strided convolution: the space-to-depth view);
@@ -116,6 +119,15 @@ struct UmmaGeom {
   // transposed variant, NCHW output (or split pieces) with Wp % 8 == 0,
   // OW % 8 == 0 and 16-byte aligned outputs: 16-byte epilogue stores
   int tvec;
+  // channels-on-M space-to-depth stages whose channel block lies within one
+  // phase (xIC % bk == 0): taps (bit khl*KW + kw) of filter-row group khg and
+  // phase whose packed weights are not all zero. The MMAs of the other taps
+  // add zeros and are skipped; a stage with none is neither loaded nor
+  // issued (3x3 / stride 2: 9 of the 16 phase x tap pairs, and a quarter of
+  // the stages). tapskip = 0: every stage uses every tap. cbpp = channel
+  // blocks per phase.
+  int tapskip, cbpp;
+  uint16_t tapmask[kMaxKhg][kMaxPhases];
   // NCHW output options (omode 0): `resid` (same shape as the output) is
   // added after the activation; nout > 0 splits the output channels into
   // tensors outp[k] holding channels [out_c0[k], out_c0[k+1])
@@ -270,6 +282,30 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans)
         break;
       }
     }
+  }
+  // tap masks of channels-on-M space-to-depth stages (the rule of the weight
+  // packing); the positions-on-M variant issues short MMAs whose rate
+  // depends on full stages, so it keeps every tap
+  g.tapskip = 0;
+  g.cbpp = 1;
+  const int nph = g.nphH * g.nphW;
+  if (!trans && nph > 1 && g.xIC % g.bk == 0 && g.n_khg <= kMaxKhg && nph <= kMaxPhases &&
+      g.khs * g.KW <= 16) {
+    g.cbpp = g.xIC / g.bk;
+    for (int khg = 0; khg < g.n_khg; ++khg)
+      for (int ph = 0; ph < nph; ++ph) {
+        uint16_t m = 0;
+        for (int khl = 0; khl < g.khs; ++khl) {
+          const int rkh = g.sH * (khg * g.khs + khl - g.pH) + g.phH[ph / g.nphW] + g.xpH;
+          if (rkh < 0 || rkh >= g.xKH) continue;
+          for (int kw = 0; kw < g.KW; ++kw) {
+            const int rkw = g.sW * (kw - g.pW) + g.phW[ph % g.nphW] + g.xpW;
+            if (rkw >= 0 && rkw < g.xKW) m |= uint16_t(1u << (khl * g.KW + kw));
+          }
+        }
+        g.tapmask[khg][ph] = m;
+        if (m != uint16_t((1u << (g.khs * g.KW)) - 1)) g.tapskip = 1;
+      }
   }
   g.has_bias = p.has_bias;
   g.act = p.act;
@@ -830,6 +866,24 @@ __device__ __forceinline__ __half *out_plane(const UmmaGeom &g, __half *out, int
 
 // tile index -> (image, first position, output-channel tile); oc tile
 // fastest so that CTAs working on the same positions run together.
+// Pipeline stage walk: (filter-row group khg, channel block cbk) and the
+// space-to-depth phase of cbk, advanced without divisions.
+struct StageWalk {
+  int khg = 0, cbk = 0, pc = 0, phase = 0;
+  __device__ __forceinline__ void next(const UmmaGeom &g) {
+    if (++cbk == g.ncb) {
+      cbk = pc = phase = 0;
+      ++khg;
+    } else if (++pc == g.cbpp) {
+      pc = 0;
+      ++phase;
+    }
+  }
+  __device__ __forceinline__ uint32_t taps(const UmmaGeom &g) const {
+    return g.tapskip ? g.tapmask[khg][phase] : 0xFFFFu;
+  }
+};
+
 __device__ __forceinline__ void tile_coords(const UmmaGeom &g, int t, int &b, long long &p0,
                                             int &oct) {
   oct = t % g.n_oct;
@@ -908,20 +962,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_expect_tx(wb, g.w_region_bytes);
         bulk_g2s(smem_u32(sW), wpk, g.w_region_bytes, wb);
       }
-      int slot = 0, use = 0;  // pipeline stage slot and its use count
+      int slot = S - 1, use = -1;  // pipeline slot and its use count, advanced per loaded stage
       bool ok = true;
       for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x) {
         int b, oct;
         long long p0;
         tile_coords(g, t, b, p0, oct);
-        // (slot, use) advance without a division
-        for (int s = 0; s < g.n_kstages; ++s, slot = slot + 1 == S ? (++use, 0) : slot + 1) {
+        StageWalk sw;
+        for (int s = 0; s < g.n_kstages; ++s, sw.next(g)) {
+          if (!sw.taps(g)) continue;  // all-zero weights: not loaded
+          if (++slot == S) {
+            slot = 0;
+            ++use;
+          }
           if (use > 0 && !mbar_wait(smem_u32(&empty[slot]), (use - 1) & 1)) {
             atomicOr(g.err, kErrLoadTimeout);
             ok = false;
             break;
           }
-          const int khg = s / g.ncb, cbk = s % g.ncb;
+          const int khg = sw.khg, cbk = sw.cbk;
           const uint32_t fb = smem_u32(&full[slot]);
           mbar_expect_tx(fb, (g.resident ? 0u : g.a_stage_bytes) + g.chunks * b_copy);
           if (!g.resident)
@@ -992,7 +1051,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                                       (tap * uint32_t(g.chunks) * a_lbo + uint32_t(ks) * 2 * a_lbo) >> 4);
             }
       }
-      int it = 0, slot = 0, use = 0;
+      int it = 0, slot = S - 1, use = -1;
       for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x, ++it) {
         const int acc = it & 1, use_acc = it >> 1;
         if (use_acc > 0 && !mbar_wait(smem_u32(&acce[acc]), (use_acc - 1) & 1)) {
@@ -1002,7 +1061,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem + uint32_t(acc * g.acc_cols);
-        for (int s = 0; s < g.n_kstages; ++s, slot = slot + 1 == S ? (++use, 0) : slot + 1) {
+        uint32_t acc_on = 0;  // the tile's accumulator already holds a product
+        StageWalk sw;
+        for (int s = 0; s < g.n_kstages; ++s, sw.next(g)) {
+          const uint32_t tmask = sw.taps(g);
+          if (!tmask) continue;  // all-zero weights: not loaded, no MMA
+          if (++slot == S) {
+            slot = 0;
+            ++use;
+          }
           if (!mbar_wait(smem_u32(&full[slot]), use & 1)) {
             atomicOr(g.err, kErrMmaTimeout);
             ok = false;
@@ -1026,11 +1093,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int mb = 0; mb < G_C; ++mb)
                   mma_f16(d + uint32_t(mb * NT_C),
                           sw128_mn_desc(xaddr + uint32_t(mb) * 2 * x_lbo, x_lbo, 1024), wdesc,
-                          idesc_mn, (s | ks) != 0);
+                          idesc_mn, (acc_on | ks) != 0);
               } else {
-                mma_f16(d, wdesc, sw128_mn_desc(xaddr, x_lbo, 1024), idesc_mn, (s | ks) != 0);
+                mma_f16(d, wdesc, sw128_mn_desc(xaddr, x_lbo, 1024), idesc_mn, (acc_on | ks) != 0);
               }
             }
+            acc_on = 1;
             mma_commit(smem_u32(&empty[slot]));
             continue;
           }
@@ -1048,11 +1116,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int mb = 0; mb < G_C; ++mb)
                   mma_f16(d + uint32_t(mb * NT_C), b0 + uint64_t(mb * 128) + b_off[i],
-                          a0 + a_off[i], idesc, (s | i) != 0);
+                          a0 + a_off[i], idesc, (acc_on | i) != 0);
+              acc_on = 1;
             } else {
+              // (taps whose weights are all zero are skipped: tapskip)
 #pragma unroll
-              for (int i = 0; i < 2 * KW_T; ++i)
-                mma_f16(d, a0 + a_off[i], b0 + b_off[i], idesc, (s | i) != 0);
+              for (int i = 0; i < 2 * KW_T; ++i) {
+                if (!((tmask >> (i >> 1)) & 1)) continue;
+                mma_f16(d, a0 + a_off[i], b0 + b_off[i], idesc, acc_on);
+                acc_on = 1;
+              }
             }
             mma_commit(smem_u32(&empty[slot]));
             continue;
@@ -1066,7 +1139,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             // group in the last slot, and the switch falls through the
             // groups in table order.
             const uint64_t x0 = kmajor_desc(b_base, b_lbo), w0 = kmajor_desc(a_base, a_lbo);
-            uint32_t acc_flag = s != 0;
+            uint32_t acc_flag = acc_on;
             if (ngroups <= kSeqGroups) {
               uint2 e[kSeqGroups];
 #pragma unroll
@@ -1112,6 +1185,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
             }
           }
+          acc_on = 1;
           mma_commit(smem_u32(&empty[slot]));
         }
         if (ok) mma_commit(smem_u32(&accf[acc]));
