@@ -554,6 +554,7 @@ ONLY_CONV = {
     "yolo_stem": (8, 3, 640, 640, 16, 3, 2, 1, 1, 2),   # YOLO26-N shapes, batch 8
     "yolo_down": (8, 64, 160, 160, 64, 3, 2, 1, 1, 2),
     "yolo_1x1": (8, 48, 160, 160, 64, 1, 1, 0, 1, 2),
+    "yolo_dw20": (64, 256, 20, 20, 256, 3, 1, 1, 256, 2),   # 20x20 depthwise of the neck
 }
 
 

@@ -600,6 +600,10 @@ __global__ void __launch_bounds__(256)
   const int ih0 = oh0 - g.pH;
   const size_t plane_tile = size_t(d.rows) * d.TWs;
   __half2 *wsm = reinterpret_cast<__half2 *>(tile + size_t(d.P) * plane_tile);
+  // vec_out == 2: the CTA's outputs are staged after the weights (16-byte
+  // aligned) and stored contiguously at the end
+  __half *ostg = reinterpret_cast<__half *>(
+      (reinterpret_cast<uintptr_t>(wsm + size_t(d.P) * (K * K + 1)) + 15) & ~uintptr_t(15));
   for (int i = threadIdx.x; i < np * (K * K + 1); i += blockDim.x) {
     const int p = i / (K * K + 1), t = i % (K * K + 1);
     const int c = int((plane0 + p) % g.OC);
@@ -689,8 +693,15 @@ __global__ void __launch_bounds__(256)
         }
         res[j] = *reinterpret_cast<const uint32_t *>(&v);
       }
-      if (vec_out && ow0 + 8 <= g.OW) {
+      if (vec_out == 1 && ow0 + 8 <= g.OW) {
         *reinterpret_cast<uint4 *>(orow + ow0) = make_uint4(res[0], res[1], res[2], res[3]);
+      } else if (vec_out == 2) {
+        // into the CTA's output image (stored below, coalesced)
+        __half *srow = ostg + (size_t(p) * g.OH + oh) * g.OW;
+        const __half *hv = reinterpret_cast<const __half *>(res);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (ow0 + e < g.OW) srow[ow0 + e] = hv[e];
       } else {
         const __half *hv = reinterpret_cast<const __half *>(res);
 #pragma unroll
@@ -698,6 +709,15 @@ __global__ void __launch_bounds__(256)
           if (ow0 + e < g.OW) orow[ow0 + e] = hv[e];
       }
     }
+  }
+  if (vec_out == 2) {
+    // whole planes (one band): the CTA's np planes are one contiguous run of
+    // the output; copy the staged image with 16-byte stores
+    __syncthreads();
+    const int n16 = int(size_t(np) * g.OH * g.OW / 8);
+    uint4 *dst = reinterpret_cast<uint4 *>(out + plane0 * g.OH * (long long)g.OW);
+    const uint4 *src = reinterpret_cast<const uint4 *>(ostg);
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src[i];
   }
 }
 
@@ -847,17 +867,34 @@ static void launch_simt(const wgx_conv2d_params &p, int variant, const T *in, co
     const unsigned grid = unsigned((dt.planes + dt.P - 1) / dt.P * dt.bands);
     if constexpr (sizeof(T) == 2) {
       if (p.pW == (p.KW - 1) / 2) {
-        const size_t smem_h2 = smem + size_t(dt.P) * (p.KH * p.KW + 1) * 4;
+        // rows that are not whole 16-byte vectors: whole planes are staged in
+        // shared memory and stored contiguously (a thread's 8 outputs of one
+        // row would otherwise be 2-byte stores to addresses far from its
+        // neighbours'), with fewer planes per CTA if needed
+        int vo = vec_out;
+        DwTile dh = dt;
+        const bool out16 = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+        if (!vo && dh.bands == 1 && (int64_t(p.OH) * p.OW) % 8 == 0 && out16) {
+          const size_t per_plane = size_t(dh.rows) * dh.TWs * 2 + size_t(p.KH * p.KW + 1) * 4 +
+                                   size_t(p.OH) * p.OW * 2;
+          dh.P = std::max(1, std::min(dh.P, int(size_t(DW_SMEM) / per_plane)));
+          vo = 2;
+        }
+        const size_t smem_h2 = size_t(dh.P) * dh.rows * dh.TWs * 2 +
+                               size_t(dh.P) * (p.KH * p.KW + 1) * 4 +
+                               (vo == 2 ? size_t(dh.P) * p.OH * p.OW * 2 + 16 : 0);
+        const unsigned grid_h2 = unsigned((dh.planes + dh.P - 1) / dh.P * dh.bands);
         const __half *hin = reinterpret_cast<const __half *>(in);
         const __half *hw = reinterpret_cast<const __half *>(w);
         const __half *hb = reinterpret_cast<const __half *>(bias);
         __half *hout = reinterpret_cast<__half *>(out);
+        if (smem_h2 > 48 * 1024) fail("conv2d: depthwise tile exceeds 48 KB");
         if (p.KH == 3)
-          depthwise_tiled_h2<3><<<grid, 256, smem_h2, s>>>(g, dt, hin, hw, hb, hout, vec_in, vec_out);
+          depthwise_tiled_h2<3><<<grid_h2, 256, smem_h2, s>>>(g, dh, hin, hw, hb, hout, vec_in, vo);
         else if (p.KH == 5)
-          depthwise_tiled_h2<5><<<grid, 256, smem_h2, s>>>(g, dt, hin, hw, hb, hout, vec_in, vec_out);
+          depthwise_tiled_h2<5><<<grid_h2, 256, smem_h2, s>>>(g, dh, hin, hw, hb, hout, vec_in, vo);
         else
-          depthwise_tiled_h2<7><<<grid, 256, smem_h2, s>>>(g, dt, hin, hw, hb, hout, vec_in, vec_out);
+          depthwise_tiled_h2<7><<<grid_h2, 256, smem_h2, s>>>(g, dh, hin, hw, hb, hout, vec_in, vo);
         check_cuda(cudaGetLastError(), "conv2d launch");
         return;
       }
