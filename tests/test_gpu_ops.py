@@ -128,10 +128,16 @@ def maxpool_ref(x, k, s, p, d, ceil_mode, f16):
     ((2, 4, 9, 11), (3, 3), (2, 2), (1, 1), (1, 1), True),      # ceil mode
     ((1, 2, 70, 70), (2, 2), (2, 2), (0, 0), (1, 1), False),    # plane > 4096: generic
     ((1, 3, 12, 12), (3, 3), (1, 1), (0, 0), (2, 2), False),    # dilation
+    ((2, 9, 13, 17), (3, 3), (1, 1), (1, 1), (1, 1), False),    # row kernel, K = 3
+    ((1, 5, 11, 9), (7, 7), (1, 1), (3, 3), (1, 1), False),     # row kernel, K = 7
+    ((2, 40, 20, 20), (5, 5), (1, 1), (0, 0), (1, 1), False),   # row kernel, no padding
 ])
-def test_maxpool(ctx, geom):
+@pytest.mark.parametrize("ties", [False, True])
+def test_maxpool(ctx, geom, ties):
     shape, k, s, p, d, ceil_mode = geom
     x = rnd(shape)
+    if ties:  # coarse values: many equal maxima, the first one in window order wins
+        x = (np.round(x.astype(np.float32) * 2) / 2).astype(x.dtype)
     y, idx = maxpool_ref(x, k, s, p, d, ceil_mode, True)
     vals = empty(ctx, y.shape, "float16")
     ind = empty(ctx, y.shape, "int32")

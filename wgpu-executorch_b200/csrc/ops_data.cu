@@ -566,6 +566,80 @@ __global__ void __launch_bounds__(256) maxpool_plane_kernel(PoolGeom g, const T 
   }
 }
 
+// Stride-1, dilation-1, K x K pooling of small planes (compile-time K): the
+// same two passes as maxpool_plane_kernel (row maxima with the first
+// maximising column, then a top-to-bottom scan of those with strict '>'),
+// but a thread takes a whole row (pass 1) or a whole column (pass 2) of a
+// plane, so the index arithmetic is paid once per row or column and every
+// window is K unrolled shared-memory reads. Values are compared in their
+// storage type (the order of fp16 values is that of their fp32 images).
+// `ppb` consecutive planes per CTA.
+template <class T, int K>
+__global__ void __launch_bounds__(256) maxpool_rows_kernel(PoolGeom g, const T *__restrict__ x,
+                                                           T *__restrict__ y,
+                                                           int32_t *__restrict__ idx, int ppb,
+                                                           long long planes) {
+  extern __shared__ __align__(16) unsigned char mp_smem[];
+  const int hw = g.IH * g.IW, rw = g.IH * g.OW, ohw = g.OH * g.OW;
+  const long long plane0 = (long long)blockIdx.x * ppb;
+  const int np = int(min((long long)ppb, planes - plane0));
+  T *tile = reinterpret_cast<T *>(mp_smem);
+  T *rmax = tile + size_t(ppb) * hw;
+  int16_t *rarg = reinterpret_cast<int16_t *>(rmax + size_t(ppb) * rw);
+  const T *xp = x + plane0 * hw;
+  for (int i = threadIdx.x; i < np * hw; i += 256) tile[i] = xp[i];
+  __syncthreads();
+  const float start = sizeof(T) == 2 ? -65504.0f : -3.402823466e38f;
+  // pass 1: one (plane, input row) per thread
+  for (int it = threadIdx.x; it < np * g.IH; it += 256) {
+    const T *trow = tile + size_t(it) * g.IW;  // plane-major rows: it = p * IH + ih
+    T *mrow = rmax + size_t(it) * g.OW;
+    int16_t *arow = rarg + size_t(it) * g.OW;
+    for (int ow = 0; ow < g.OW; ++ow) {
+      float best = start;
+      int arg = -1;
+#pragma unroll
+      for (int kw = 0; kw < K; ++kw) {
+        const int iw = ow - g.pW + kw;
+        if (iw < 0 || iw >= g.IW) continue;
+        const float v = lf(trow[iw]);
+        if (v > best) {
+          best = v;
+          arg = iw;
+        }
+      }
+      mrow[ow] = sf<T>(best);
+      arow[ow] = int16_t(arg);
+    }
+  }
+  __syncthreads();
+  // pass 2: one (plane, output column) per thread; consecutive threads store
+  // consecutive columns of a row
+  for (int it = threadIdx.x; it < np * g.OW; it += 256) {
+    const int pl = it / g.OW, ow = it - pl * g.OW;
+    const T *mcol = rmax + size_t(pl) * rw + ow;
+    const int16_t *acol = rarg + size_t(pl) * rw + ow;
+    T *ycol = y + (plane0 + pl) * ohw + ow;
+    int32_t *icol = idx ? idx + (plane0 + pl) * ohw + ow : nullptr;
+    for (int oh = 0; oh < g.OH; ++oh) {
+      float best = start;
+      int best_idx = 0;
+#pragma unroll
+      for (int kh = 0; kh < K; ++kh) {
+        const int ih = oh - g.pH + kh;
+        if (ih < 0 || ih >= g.IH) continue;
+        const float v = lf(mcol[size_t(ih) * g.OW]);
+        if (v > best) {
+          best = v;
+          best_idx = ih * g.IW + acol[size_t(ih) * g.OW];
+        }
+      }
+      ycol[size_t(oh) * g.OW] = sf<T>(best);
+      if (icol) icol[size_t(oh) * g.OW] = best_idx;
+    }
+  }
+}
+
 void parse_hw(const std::vector<int64_t> &v, const char *name, const char *what, int *h, int *w) {
   if (v.size() == 1) {
     *h = *w = int(v[0]);
@@ -622,6 +696,35 @@ void record_maxpool(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   const long long n = vals->numel;
   const int dt = in->dtype;
   const long long planes = (long long)g.N * g.C;
+  const int Kp = g.kH;
+  if (g.sH == 1 && g.sW == 1 && g.dH == 1 && g.dW == 1 && g.kW == Kp &&
+      (Kp == 3 || Kp == 5 || Kp == 7) && (long long)g.IH * g.IW <= 4096 &&
+      (long long)g.IH * g.OW <= 4096 && g.IW <= 32767 && planes > 0 && planes < (1ll << 31)) {
+    // about 40 KB of planes per block
+    const size_t esz = dt == WGX_FLOAT16 ? 2 : 4;
+    const size_t per_plane = (size_t(g.IH) * g.IW + size_t(g.IH) * g.OW) * esz +
+                             size_t(g.IH) * g.OW * 2;
+    const int ppb = int(std::max<size_t>(1, std::min<size_t>(64, 40 * 1024 / per_plane)));
+    const size_t smem = per_plane * ppb + 16;
+    const long long blocks = (planes + ppb - 1) / ppb;
+    push(ctx, name, 1, [=](const ExecEnv &env) {
+#define WGX_MP_ROWS(TT, KK)                                                                  \
+  maxpool_rows_kernel<TT, KK><<<unsigned(blocks), 256, smem, env.stream>>>(g, (const TT *)px, \
+                                                                         (TT *)py, pi, ppb, planes)
+      if (dt == WGX_FLOAT16) {
+        if (Kp == 3) WGX_MP_ROWS(__half, 3);
+        else if (Kp == 5) WGX_MP_ROWS(__half, 5);
+        else WGX_MP_ROWS(__half, 7);
+      } else {
+        if (Kp == 3) WGX_MP_ROWS(float, 3);
+        else if (Kp == 5) WGX_MP_ROWS(float, 5);
+        else WGX_MP_ROWS(float, 7);
+      }
+#undef WGX_MP_ROWS
+      check_cuda(cudaGetLastError(), "maxpool launch");
+    });
+    return;
+  }
   if ((long long)g.IH * g.IW <= 4096 && (long long)g.IH * g.OW <= 4096 && g.IW <= 32767 &&
       planes > 0 && planes < (1ll << 31)) {
     // planes per block: about 1024 input elements per block, within 40 KB
