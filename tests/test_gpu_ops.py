@@ -275,3 +275,47 @@ def test_fused_attention_program(ctx, n, L, dq, dv):
     ref = np.matmul(vt.astype(np.float64), np.swapaxes(p, 1, 2))
     err = np.abs(out.numpy().astype(np.float64) - ref).max() / np.abs(ref).max()
     assert err <= 5e-3, err
+
+
+# Elementwise operators (src/shaders/add, sub, mul, sigmoid): same shapes
+# (16-byte path), leading-dimension broadcasts (the repeating-operand path),
+# other broadcasts and odd sizes (element paths). alpha = 1 keeps the fp32
+# arithmetic exactly that of numpy (one rounding), so those cases are
+# compared bit for bit; alpha = 2.5 within one fp16 ulp of the result.
+@pytest.mark.gpu
+@pytest.mark.parametrize("dt", [np.float16, np.float32])
+@pytest.mark.parametrize("op", ["add", "sub", "mul"])
+@pytest.mark.parametrize("sa,sb", [
+    ((4, 3, 40), (4, 3, 40)),       # same shape
+    ((6, 4, 8400), (1, 8400)),      # the detection head's anchor scaling
+    ((1, 2, 24), (5, 2, 24)),       # broadcast first operand
+    ((3, 5, 7), (7,)),              # odd sizes
+    ((2, 3, 4, 8), (3, 1, 8)),      # broadcast in the middle
+])
+def test_elementwise_binary(ctx, dt, op, sa, sb):
+    a, b = rnd(sa, dt), rnd(sb, dt)
+    out_shape = np.broadcast_shapes(sa, sb)
+    out = empty(ctx, out_shape, "float16" if dt == np.float16 else "float32")
+    shader = getattr(wgx.shaders, op)
+    for alpha in ([1.0, 2.5] if op != "mul" else [None]):
+        args = [T(ctx, a), T(ctx, b)] + ([alpha] if alpha is not None else []) + [out]
+        run(ctx, shader, args)
+        af, bf = a.astype(np.float32), b.astype(np.float32)
+        ref = (af + np.float32(alpha) * bf if op == "add" else
+               af - np.float32(alpha) * bf if op == "sub" else af * bf).astype(dt)
+        got = out.numpy().reshape(out_shape)
+        if alpha in (1.0, None):
+            np.testing.assert_array_equal(got, ref)
+        else:
+            err = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+            assert np.all(err <= np.abs(ref.astype(np.float64)) * (1e-3 if dt == np.float16 else 1e-6) + 1e-6)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", [(4, 80, 400), (3, 5, 7)])
+def test_sigmoid(ctx, shape):
+    x = rnd(shape)
+    out = empty(ctx, shape, "float16")
+    run(ctx, wgx.shaders.sigmoid, [T(ctx, x), out])
+    ref = 1.0 / (1.0 + np.exp(-x.astype(np.float64)))
+    assert np.max(np.abs(out.numpy().reshape(shape).astype(np.float64) - ref)) <= 1e-3

@@ -75,6 +75,17 @@ __global__ void ew_binary_same_h8(int op, float alpha, const uint4 *__restrict__
   for (; i < n8; i += stride) out[i] = map8(a[i], b[i], op, alpha);
 }
 
+// fp16 operands that are contiguous over the output's trailing dimensions
+// and repeated over its leading ones (index = i mod period, the period a
+// multiple of 8): eight elements per 16-byte access.
+__global__ void ew_binary_period_h8(int op, float alpha, const uint4 *__restrict__ a,
+                                    const uint4 *__restrict__ b, uint4 *__restrict__ out,
+                                    long long n8, long long pa8, long long pb8) {
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (; i < n8; i += stride) out[i] = map8(a[i % pa8], b[i % pb8], op, alpha);
+}
+
 template <class T>
 __global__ void ew_binary_bcast(int op, float alpha, BcastIdx ix, const T *__restrict__ a,
                                 const T *__restrict__ b, T *__restrict__ out, long long n) {
@@ -151,6 +162,30 @@ static void bcast_strides(const wgx_tensor *t, const wgx_tensor *out, int64_t *s
   }
 }
 
+// Number of output elements after which operand t repeats when t equals the
+// output's trailing dimensions from some dimension on and is 1 (or absent)
+// before it; 0 when t broadcasts in another pattern.
+static int64_t repeat_period(const wgx_tensor *t, const wgx_tensor *out) {
+  const int off = out->ndim - t->ndim;
+  int k = out->ndim;  // first dimension of the contiguous trailing block
+  for (int d = out->ndim - 1; d >= 0; --d) {
+    const int td = d - off;
+    const int64_t ts = td >= 0 ? t->shape[td] : 1;
+    if (ts == out->shape[d]) {
+      k = d;
+      continue;
+    }
+    break;
+  }
+  for (int d = 0; d < k; ++d) {
+    const int td = d - off;
+    if (td >= 0 && t->shape[td] != 1) return 0;
+  }
+  int64_t period = 1;
+  for (int d = k; d < out->ndim; ++d) period *= out->shape[d];
+  return period;
+}
+
 static bool same_shape(const wgx_tensor *a, const wgx_tensor *b) {
   if (a->ndim != b->ndim) return false;
   for (int i = 0; i < a->ndim; ++i)
@@ -196,6 +231,15 @@ static void record_binary(wgx_context *ctx, const std::vector<wgx_arg> &args, co
       else
         ew_binary_same<float><<<ew_blocks(n), 256, 0, env.stream>>>(
             op, alpha, (const float *)pa, (const float *)pb, (float *)po, n);
+      check_cuda(cudaGetLastError(), "elementwise launch");
+    };
+  } else if (dtype == WGX_FLOAT16 && vec8(n, pa, pb, po) && repeat_period(a, out) % 8 == 0 &&
+             repeat_period(b, out) % 8 == 0 && repeat_period(a, out) > 0 &&
+             repeat_period(b, out) > 0) {
+    const long long pa8 = repeat_period(a, out) / 8, pb8 = repeat_period(b, out) / 8;
+    c.run = [=](const ExecEnv &env) {
+      ew_binary_period_h8<<<ew_blocks(n / 8), 256, 0, env.stream>>>(
+          op, alpha, (const uint4 *)pa, (const uint4 *)pb, (uint4 *)po, n / 8, pa8, pb8);
       check_cuda(cudaGetLastError(), "elementwise launch");
     };
   } else {

@@ -507,8 +507,8 @@ LinkPlan plan_links(wgx_context *ctx, const Program &P,
   return L;
 }
 
-// View-like copies (reshape, squeeze, unsqueeze, contiguous clone) of a
-// dense tensor move no bytes: the output value aliases the input's storage
+// View-like copies (reshape, squeeze, unsqueeze, contiguous clone, and
+// et_vk.prepack, a copy of a constant) of a dense tensor move no bytes: the output value aliases the input's storage
 // and the operator records nothing. The input's storage must then outlive
 // the output, so an input held in a memory-plan pool (reused once the input
 // dies) first gets a buffer of its own. Program inputs and outputs keep
@@ -519,7 +519,7 @@ std::set<size_t> plan_aliases(wgx_context *ctx, const Program &P,
   static const std::set<std::string> kViews = {
       "aten.view_copy.default",      "aten.clone.default",        "aten.squeeze_copy.dims",
       "aten.squeeze_copy.dim",       "aten.squeeze_copy.default", "aten.unsqueeze_copy.default",
-      "aten._unsafe_view.default",   "aten.alias_copy.default"};
+      "aten._unsafe_view.default",   "aten.alias_copy.default",   "et_vk.prepack.default"};
   std::set<int64_t> boundary(P.output_ids.begin(), P.output_ids.end());
   boundary.insert(P.input_ids.begin(), P.input_ids.end());
   std::set<size_t> skip;

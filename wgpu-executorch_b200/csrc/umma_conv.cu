@@ -1351,9 +1351,19 @@ __global__ void __launch_bounds__(THREADS, 1)
               const int oc = c & (NT_C - 1);
               const int pos = int(p0) + (c >> LG_NT) * 128 + q * 32 + part * 8;
               const int oh = pos / g.Wp, ow = pos - oh * g.Wp;
-              if (oc < g.OC && oh < g.OH && ow < g.OW)
-                *reinterpret_cast<uint4 *>(out_plane(g, out, b, oc, plane) + size_t(oh) * g.OW + ow) =
-                    val;
+              if (oc < g.OC && oh < g.OH && ow < g.OW) {
+                const size_t off = size_t(oh) * g.OW + ow;
+                uint4 v = val;
+                if (g.resid) {
+                  // residual add after the activation, one rounding (as the
+                  // separate add would compute it)
+                  const uint4 rr = *reinterpret_cast<const uint4 *>(
+                      g.resid + (size_t(b) * g.OC + oc) * plane + off);
+                  v = make_uint4(add_resid2(val.x, rr.x), add_resid2(val.y, rr.y),
+                                 add_resid2(val.z, rr.z), add_resid2(val.w, rr.w));
+                }
+                *reinterpret_cast<uint4 *>(out_plane(g, out, b, oc, plane) + off) = v;
+              }
             }
             __syncwarp();
           }
@@ -1786,16 +1796,18 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
 #undef WGX_UMMA_EXT
   const int nt_idx = !g.trans ? 0 : g.NT == 16 ? 1 : g.NT == 32 ? 2 : 3;
   if (g.trans && g.NT != 16 && g.NT != 32 && g.NT != 64) fail("conv2d: bad transposed tile");
-  // 16-byte stores of the transposed epilogue (split pieces included)
+  // 16-byte stores of the transposed epilogue (split pieces and residual
+  // loads included)
   {
     bool aligned = g.nout > 0 || (reinterpret_cast<uintptr_t>(out) & 15) == 0;
     for (int k = 0; k < g.nout; ++k)
       aligned = aligned && (reinterpret_cast<uintptr_t>(g.outp[k]) & 15) == 0;
+    aligned = aligned && (reinterpret_cast<uintptr_t>(g.resid) & 15) == 0;
     g.tvec = g.trans && !g.omode && ((g.Wp | g.OW) & 7) == 0 && aligned;
   }
-  // residual adds, and split outputs the vector path cannot store: the EXT
+  // residual adds and split outputs the vector path cannot store: the EXT
   // epilogue
-  const bool ext = g.resid != nullptr || (g.nout > 0 && !g.tvec);
+  const bool ext = (g.resid != nullptr || g.nout > 0) && !g.tvec;
   KernelFn kern = ext ? table_ext[nt_idx][act_idx] : table[nt_idx][kw_idx][act_idx];
   const int kidx = ext ? 84 + nt_idx * 3 + act_idx : (nt_idx * 7 + kw_idx) * 3 + act_idx;
   static bool attr_set[64][96] = {};
