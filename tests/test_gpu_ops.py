@@ -319,3 +319,46 @@ def test_sigmoid(ctx, shape):
     run(ctx, wgx.shaders.sigmoid, [T(ctx, x), out])
     ref = 1.0 / (1.0 + np.exp(-x.astype(np.float64)))
     assert np.max(np.abs(out.numpy().reshape(shape).astype(np.float64) - ref)) <= 1e-3
+
+
+def pool_chain_program(shape, K, n):
+    """n chained max_pool2d_with_indices (K x K, stride 1, same padding), the
+    SPPF spelling; outputs every stage's values and the last indices."""
+    vals = [{"type": "tensor", "shape": list(shape), "dtype": "float16", "memObjId": 0},
+            {"type": "list", "items": [K, K]}, {"type": "list", "items": [1, 1]},
+            {"type": "list", "items": [(K - 1) // 2] * 2}, {"type": "list", "items": [1, 1]},
+            {"type": "scalar", "value": False}]
+    chain, outs = [], []
+    src = 0
+    for s in range(n):
+        v = len(vals)
+        vals += [{"type": "tensor", "shape": list(shape), "dtype": "float16", "memObjId": 1 + 2 * s},
+                 {"type": "tensor", "shape": list(shape), "dtype": "int32", "memObjId": 2 + 2 * s},
+                 {"type": "tensorlist", "items": [v, v + 1]}]
+        chain.append({"name": "aten.max_pool2d_with_indices.default",
+                      "args": [src, 1, 2, 3, 4, 5, v + 2]})
+        outs.append(v)
+        src = v
+    nb = int(np.prod(shape)) * 4
+    return {"version": "1", "chain": chain, "values": vals, "inputIds": [0],
+            "outputIds": outs + [outs[-1] + 1],
+            "memoryPlan": {"pools": [{"id": i, "size": nb} for i in range(1 + 2 * n)]}}
+
+
+@pytest.mark.parametrize("shape,K,n", [((2, 8, 20, 20), 5, 3), ((1, 6, 9, 13), 3, 2)])
+def test_maxpool_cascade_program(ctx, shape, K, n):
+    x = rnd(shape)
+    ys = [empty(ctx, shape, "float16") for _ in range(n)]
+    last_idx = empty(ctx, shape, "int32")
+    ctx.recordProgram(pool_chain_program(shape, K, n), b"", [T(ctx, x)] + ys + [last_idx])
+    names = ctx.command_names()
+    assert sum(nm.endswith("(cascade)") for nm in names) == 1, names
+    ctx.submit()
+    ctx.sync()
+    p = (K - 1) // 2
+    cur = x
+    for s in range(n):
+        y, idx = maxpool_ref(cur, (K, K), (1, 1), (p, p), (1, 1), False, True)
+        np.testing.assert_array_equal(ys[s].numpy().reshape(shape).astype(np.float32), y)
+        cur = y.astype(np.float16)
+    np.testing.assert_array_equal(last_idx.numpy().reshape(shape), idx)

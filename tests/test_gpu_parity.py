@@ -103,6 +103,10 @@ DENSE_F16 = [
     (1, 32, 24, 40, 1, 1, 1, 0, 1),       # one output channel
     (2, 16, 26, 26, 8, 3, 3, 1, 1),       # 16-channel stages, 8 M blocks per tile
     (1, 96, 20, 20, 40, 5, 5, 2, 1),
+    # planes of at most 512 positions: N = 16 / 32 tiles of 4 M blocks
+    (2, 64, 20, 20, 16, 3, 3, 1, 1),
+    (3, 32, 16, 16, 32, 3, 3, 1, 1),
+    (2, 24, 12, 12, 8, 3, 3, 1, 1),
 ]
 
 

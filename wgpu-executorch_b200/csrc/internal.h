@@ -11,6 +11,7 @@
 #include <memory>
 #include <string>
 #include <unordered_map>
+#include <utility>
 #include <vector>
 
 #include "wgx.h"
@@ -182,5 +183,10 @@ void launch_conv_transpose2d(const wgx_conv2d_params &p, int opH, int opW, const
 // conv recorder with a fused epilogue activation (program fusion pass):
 // args are aten.convolution's positional args.
 void record_convolution_act(wgx_context *ctx, const std::vector<wgx_arg> &args, int act);
+
+// SPPF-style cascade of 2-3 same-size max-pools in one launch (program
+// pass); false when the shapes do not qualify (nothing recorded).
+bool record_maxpool_cascade(wgx_context *ctx, wgx_tensor *in,
+                            const std::vector<std::pair<wgx_tensor *, wgx_tensor *>> &outs, int K);
 
 }  // namespace wgx

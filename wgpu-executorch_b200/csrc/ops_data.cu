@@ -573,12 +573,20 @@ __global__ void __launch_bounds__(256) maxpool_plane_kernel(PoolGeom g, const T 
 // plane, so the index arithmetic is paid once per row or column and every
 // window is K unrolled shared-memory reads. Values are compared in their
 // storage type (the order of fp16 values is that of their fp32 images).
-// `ppb` consecutive planes per CTA.
+// `ppb` consecutive planes per CTA. A cascade of o.n same-size poolings
+// (the SPPF block: pool(x), pool(pool(x)), ...) runs in one launch: each
+// stage's output also replaces the staged tile as the next stage's input,
+// and every stage writes its own values and indices.
+template <class T>
+struct MpOut {
+  T *y[3];
+  int32_t *idx[3];
+  int n;
+};
+
 template <class T, int K>
 __global__ void __launch_bounds__(256) maxpool_rows_kernel(PoolGeom g, const T *__restrict__ x,
-                                                           T *__restrict__ y,
-                                                           int32_t *__restrict__ idx, int ppb,
-                                                           long long planes) {
+                                                           MpOut<T> o, int ppb, long long planes) {
   extern __shared__ __align__(16) unsigned char mp_smem[];
   const int hw = g.IH * g.IW, rw = g.IH * g.OW, ohw = g.OH * g.OW;
   const long long plane0 = (long long)blockIdx.x * ppb;
@@ -590,53 +598,62 @@ __global__ void __launch_bounds__(256) maxpool_rows_kernel(PoolGeom g, const T *
   for (int i = threadIdx.x; i < np * hw; i += 256) tile[i] = xp[i];
   __syncthreads();
   const float start = sizeof(T) == 2 ? -65504.0f : -3.402823466e38f;
-  // pass 1: one (plane, input row) per thread
-  for (int it = threadIdx.x; it < np * g.IH; it += 256) {
-    const T *trow = tile + size_t(it) * g.IW;  // plane-major rows: it = p * IH + ih
-    T *mrow = rmax + size_t(it) * g.OW;
-    int16_t *arow = rarg + size_t(it) * g.OW;
-    for (int ow = 0; ow < g.OW; ++ow) {
-      float best = start;
-      int arg = -1;
+  for (int st = 0; st < o.n; ++st) {
+    // pass 1: one (plane, input row) per thread
+    for (int it = threadIdx.x; it < np * g.IH; it += 256) {
+      const T *trow = tile + size_t(it) * g.IW;  // plane-major rows: it = p * IH + ih
+      T *mrow = rmax + size_t(it) * g.OW;
+      int16_t *arow = rarg + size_t(it) * g.OW;
+      for (int ow = 0; ow < g.OW; ++ow) {
+        float best = start;
+        int arg = -1;
 #pragma unroll
-      for (int kw = 0; kw < K; ++kw) {
-        const int iw = ow - g.pW + kw;
-        if (iw < 0 || iw >= g.IW) continue;
-        const float v = lf(trow[iw]);
-        if (v > best) {
-          best = v;
-          arg = iw;
+        for (int kw = 0; kw < K; ++kw) {
+          const int iw = ow - g.pW + kw;
+          if (iw < 0 || iw >= g.IW) continue;
+          const float v = lf(trow[iw]);
+          if (v > best) {
+            best = v;
+            arg = iw;
+          }
         }
+        mrow[ow] = sf<T>(best);
+        arow[ow] = int16_t(arg);
       }
-      mrow[ow] = sf<T>(best);
-      arow[ow] = int16_t(arg);
     }
-  }
-  __syncthreads();
-  // pass 2: one (plane, output column) per thread; consecutive threads store
-  // consecutive columns of a row
-  for (int it = threadIdx.x; it < np * g.OW; it += 256) {
-    const int pl = it / g.OW, ow = it - pl * g.OW;
-    const T *mcol = rmax + size_t(pl) * rw + ow;
-    const int16_t *acol = rarg + size_t(pl) * rw + ow;
-    T *ycol = y + (plane0 + pl) * ohw + ow;
-    int32_t *icol = idx ? idx + (plane0 + pl) * ohw + ow : nullptr;
-    for (int oh = 0; oh < g.OH; ++oh) {
-      float best = start;
-      int best_idx = 0;
+    __syncthreads();
+    // pass 2: one (plane, output column) per thread; consecutive threads
+    // store consecutive columns of a row
+    T *y = o.y[st];
+    int32_t *idx = o.idx[st];
+    const bool next = st + 1 < o.n;  // (same-size poolings: OH = IH, OW = IW)
+    for (int it = threadIdx.x; it < np * g.OW; it += 256) {
+      const int pl = it / g.OW, ow = it - pl * g.OW;
+      const T *mcol = rmax + size_t(pl) * rw + ow;
+      const int16_t *acol = rarg + size_t(pl) * rw + ow;
+      T *ycol = y + (plane0 + pl) * ohw + ow;
+      T *tcol = tile + size_t(pl) * hw + ow;
+      int32_t *icol = idx ? idx + (plane0 + pl) * ohw + ow : nullptr;
+      for (int oh = 0; oh < g.OH; ++oh) {
+        float best = start;
+        int best_idx = 0;
 #pragma unroll
-      for (int kh = 0; kh < K; ++kh) {
-        const int ih = oh - g.pH + kh;
-        if (ih < 0 || ih >= g.IH) continue;
-        const float v = lf(mcol[size_t(ih) * g.OW]);
-        if (v > best) {
-          best = v;
-          best_idx = ih * g.IW + acol[size_t(ih) * g.OW];
+        for (int kh = 0; kh < K; ++kh) {
+          const int ih = oh - g.pH + kh;
+          if (ih < 0 || ih >= g.IH) continue;
+          const float v = lf(mcol[size_t(ih) * g.OW]);
+          if (v > best) {
+            best = v;
+            best_idx = ih * g.IW + acol[size_t(ih) * g.OW];
+          }
         }
+        const T bv = sf<T>(best);
+        ycol[size_t(oh) * g.OW] = bv;
+        if (next) tcol[size_t(oh) * g.OW] = bv;
+        if (icol) icol[size_t(oh) * g.OW] = best_idx;
       }
-      ycol[size_t(oh) * g.OW] = sf<T>(best);
-      if (icol) icol[size_t(oh) * g.OW] = best_idx;
     }
+    __syncthreads();
   }
 }
 
@@ -708,9 +725,10 @@ void record_maxpool(wgx_context *ctx, const std::vector<wgx_arg> &a) {
     const size_t smem = per_plane * ppb + 16;
     const long long blocks = (planes + ppb - 1) / ppb;
     push(ctx, name, 1, [=](const ExecEnv &env) {
-#define WGX_MP_ROWS(TT, KK)                                                                  \
-  maxpool_rows_kernel<TT, KK><<<unsigned(blocks), 256, smem, env.stream>>>(g, (const TT *)px, \
-                                                                         (TT *)py, pi, ppb, planes)
+#define WGX_MP_ROWS(TT, KK)                                                             \
+  maxpool_rows_kernel<TT, KK><<<unsigned(blocks), 256, smem, env.stream>>>(              \
+      g, (const TT *)px, MpOut<TT>{{(TT *)py, nullptr, nullptr}, {pi, nullptr, nullptr}, 1}, \
+      ppb, planes)
       if (dt == WGX_FLOAT16) {
         if (Kp == 3) WGX_MP_ROWS(__half, 3);
         else if (Kp == 5) WGX_MP_ROWS(__half, 5);
@@ -1097,6 +1115,71 @@ void record_pad(wgx_context *ctx, const std::vector<wgx_arg> &a) {
 }
 
 }  // namespace
+
+// A cascade of 2 or 3 same-size max-pools (stride 1, dilation 1, K x K with
+// K in {3, 5, 7}, padding (K-1)/2), each reading the previous one's values
+// (the SPPF block): one launch of maxpool_rows_kernel that writes every
+// stage's values and indices. False (nothing recorded) when the shapes do
+// not qualify; the caller then records the operators one by one.
+bool record_maxpool_cascade(wgx_context *ctx, wgx_tensor *in,
+                            const std::vector<std::pair<wgx_tensor *, wgx_tensor *>> &outs, int K) {
+  const int n = int(outs.size());
+  if (n < 2 || n > 3 || (K != 3 && K != 5 && K != 7)) return false;
+  if (in->ndim != 4 || (in->dtype != WGX_FLOAT16 && in->dtype != WGX_FLOAT32)) return false;
+  for (auto &o : outs) {
+    const wgx_tensor *v = o.first, *ix = o.second;
+    if (v->dtype != in->dtype || ix->dtype != WGX_INT32 || v->ndim != 4 || ix->ndim != 4) return false;
+    for (int d = 0; d < 4; ++d)
+      if (v->shape[d] != in->shape[d] || ix->shape[d] != in->shape[d]) return false;
+  }
+  PoolGeom g{};
+  g.N = int(in->shape[0]);
+  g.C = int(in->shape[1]);
+  g.IH = g.OH = int(in->shape[2]);
+  g.IW = g.OW = int(in->shape[3]);
+  g.kH = g.kW = K;
+  g.sH = g.sW = g.dH = g.dW = 1;
+  g.pH = g.pW = (K - 1) / 2;
+  const long long planes = (long long)g.N * g.C;
+  if ((long long)g.IH * g.IW > 4096 || planes <= 0 || planes >= (1ll << 31)) return false;
+  const size_t esz = in->dtype == WGX_FLOAT16 ? 2 : 4;
+  const size_t per_plane = size_t(g.IH) * g.IW * (2 * esz + 2);
+  const int ppb = int(std::max<size_t>(1, std::min<size_t>(64, 40 * 1024 / per_plane)));
+  const size_t smem = per_plane * ppb + 16;
+  const long long blocks = (planes + ppb - 1) / ppb;
+  const void *px = in->data();
+  void *py[3] = {}, *pi[3] = {};
+  for (int k = 0; k < n; ++k) {
+    py[k] = outs[k].first->data();
+    pi[k] = outs[k].second->data();
+  }
+  const int dt = in->dtype;
+  std::string name = "aten.max_pool2d_with_indices.default x" + std::to_string(n) + " (cascade)";
+  Command c;
+  c.name = name;
+  c.kernel_launches = 1;
+  c.run = [=](const ExecEnv &env) {
+#define WGX_MP_CASCADE(TT, KK)                                                              \
+  maxpool_rows_kernel<TT, KK><<<unsigned(blocks), 256, smem, env.stream>>>(                 \
+      g, (const TT *)px,                                                                    \
+      MpOut<TT>{{(TT *)py[0], (TT *)py[1], (TT *)py[2]},                                   \
+                {(int32_t *)pi[0], (int32_t *)pi[1], (int32_t *)pi[2]}, n},                 \
+      ppb, planes)
+    if (dt == WGX_FLOAT16) {
+      if (K == 3) WGX_MP_CASCADE(__half, 3);
+      else if (K == 5) WGX_MP_CASCADE(__half, 5);
+      else WGX_MP_CASCADE(__half, 7);
+    } else {
+      if (K == 3) WGX_MP_CASCADE(float, 3);
+      else if (K == 5) WGX_MP_CASCADE(float, 5);
+      else WGX_MP_CASCADE(float, 7);
+    }
+#undef WGX_MP_CASCADE
+    check_cuda(cudaGetLastError(), "maxpool launch");
+  };
+  ctx->commands.push_back(std::move(c));
+  return true;
+}
 
 void register_data_ops(std::unordered_map<std::string, OpRecorder> &r) {
   auto flat = [](const char *name) {

@@ -547,6 +547,58 @@ std::set<size_t> plan_aliases(wgx_context *ctx, const Program &P,
   return skip;
 }
 
+// Max-pool cascades (the SPPF block): 2-3 consecutive
+// max_pool2d_with_indices of one same-size geometry (K x K, K in {3, 5, 7},
+// stride 1, padding (K-1)/2, dilation 1, floor mode), each reading the
+// previous one's values, run as one launch (record_maxpool_cascade).
+struct PoolCascades {
+  std::map<size_t, std::vector<size_t>> at;  // first op -> the ops of its cascade
+};
+
+PoolCascades plan_pool_cascades(const Program &P) {
+  PoolCascades C;
+  auto items_of = [&](int64_t v) -> const std::vector<int64_t> * {
+    if (v < 0 || size_t(v) >= P.values.size()) return nullptr;
+    const PValue &pv = P.values[v];
+    return pv.kind == PValue::List ? &pv.items : nullptr;
+  };
+  auto pool_k = [&](const POp &op) -> int {  // K of a qualifying pool, or 0
+    if (op.name != "aten.max_pool2d_with_indices.default" || op.args.size() != 7) return 0;
+    const auto *k = items_of(op.args[1]), *s = items_of(op.args[2]), *p = items_of(op.args[3]),
+               *d = items_of(op.args[4]);
+    if (!k || !s || !p || !d || k->empty()) return 0;
+    const int64_t K = (*k)[0];
+    if (K != 3 && K != 5 && K != 7) return 0;
+    auto all = [](const std::vector<int64_t> *v, int64_t x) {
+      for (auto e : *v)
+        if (e != x) return false;
+      return !v->empty() && v->size() <= 2;
+    };
+    if (!all(k, K) || !all(s, 1) || !all(p, (K - 1) / 2) || !all(d, 1)) return 0;
+    const PValue &cm = P.values[op.args[5]];
+    if (!(cm.kind == PValue::Scalar && cm.num == 0 && !cm.b)) return 0;
+    const PValue &outs = P.values[op.args[6]];
+    if (outs.kind != PValue::TensorList || outs.items.size() != 2) return 0;
+    return int(K);
+  };
+  for (size_t i = 0; i < P.chain.size();) {
+    const int K = pool_k(P.chain[i]);
+    if (!K) {
+      ++i;
+      continue;
+    }
+    std::vector<size_t> ops{i};
+    while (ops.size() < 3 && ops.back() + 1 < P.chain.size()) {
+      const POp &prev = P.chain[ops.back()], &nx = P.chain[ops.back() + 1];
+      if (pool_k(nx) != K || nx.args[0] != P.values[prev.args[6]].items[0]) break;
+      ops.push_back(ops.back() + 1);
+    }
+    if (ops.size() >= 2) C.at[i] = ops;
+    i = ops.back() + 1;
+  }
+  return C;
+}
+
 // Attention fusion: bmm(Q, K^T) -> view -> softmax(-1) -> permute(last two)
 // -> squeeze/view -> bmm(V^T, .) (the PSA block of YOLO26-N) becomes one
 // fused tcgen05 kernel recorded where the second bmm stood. Every
@@ -844,6 +896,8 @@ static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len
   std::vector<int> fusion = plan_fusion(P, tensors);
   const LinkPlan links = plan_links(ctx, P, tensors, fusion);
   const AttnPlan attn = plan_attention(ctx, P, tensors, fusion, links.skip);
+  const PoolCascades pools = plan_pool_cascades(P);
+  std::set<size_t> pool_skip;
   for (size_t oi = 0; oi < P.chain.size(); ++oi) {
     if (auto sn = attn.snap_at.find(oi); sn != attn.snap_at.end()) {
       // snapshot Q and K^T where the first bmm read them
@@ -861,8 +915,28 @@ static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len
       ctx->commands.push_back(std::move(c));
       continue;
     }
-    if (fusion[oi] == 2 || links.skip.count(oi) || attn.skip.count(oi) || alias_skip.count(oi))
+    if (fusion[oi] == 2 || links.skip.count(oi) || attn.skip.count(oi) || alias_skip.count(oi) ||
+        pool_skip.count(oi))
       continue;
+    if (auto pc = pools.at.find(oi); pc != pools.at.end()) {
+      std::vector<std::pair<wgx_tensor *, wgx_tensor *>> outs;
+      bool ok = true;
+      for (size_t k : pc->second) {
+        const auto &items = P.values[P.chain[k].args[6]].items;
+        auto v = tensors.find(items[0]), ix = tensors.find(items[1]);
+        if (v == tensors.end() || ix == tensors.end()) {
+          ok = false;
+          break;
+        }
+        outs.emplace_back(v->second, ix->second);
+      }
+      auto in = tensors.find(P.chain[oi].args[0]);
+      const int K = int(P.values[P.chain[oi].args[1]].items[0]);
+      if (ok && in != tensors.end() && record_maxpool_cascade(ctx, in->second, outs, K)) {
+        pool_skip.insert(pc->second.begin() + 1, pc->second.end());
+        continue;
+      }
+    }
     if (auto at = attn.at.find(oi); at != attn.at.end()) {
       const wgx_tensor *q = tensors[at->second.q], *kt = tensors[at->second.kt],
                        *vt = tensors[at->second.vt], *ot = tensors[at->second.ot];

@@ -242,6 +242,13 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans)
   g.n_oct = (p.OC + g.wrows - 1) / g.wrows;
   g.plane_rows = (long long)g.Hp * g.Wp;
   long long p_out = (long long)(p.OH - 1) * g.Wp + p.OW;
+  if (trans && g.G == 8 && p_out <= 512) {
+    // small planes: 4 M blocks (512 positions) instead of 8, most of whose
+    // positions would lie past the image
+    g.G = 4;
+    g.tile_pos = 128 * g.G;
+    g.acc_cols = g.G * g.NT;
+  }
   g.tiles_per_img = int((p_out + g.tile_pos - 1) / g.tile_pos);
   g.total_tiles = g.tiles_per_img * g.n_oct * g.B;
   long long r = g.tile_pos + (long long)(khs - 1) * g.dH * g.Wp + (long long)(g.KW - 1) * g.dW;
@@ -908,9 +915,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                      __half *__restrict__ out, const __grid_constant__ TmapSet tm) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // transposed variant: output channels per M block (N), M blocks per tile
-  constexpr int NT_C = TRANS > 0 ? TRANS : UN;
-  constexpr int G_C = TRANS == 64 ? 4 : TRANS > 0 ? 8 : 1;
-  constexpr int LG_NT = TRANS == 16 ? 4 : TRANS == 32 ? 5 : 6;
+  // (TRANS = 17 / 33: N = 16 / 32 with 4 M blocks, for planes of at most
+  // 512 positions)
+  constexpr int NT_C = TRANS > 0 ? (TRANS & ~1) : UN;
+  constexpr int G_C = TRANS == 0 ? 1 : (TRANS == 64 || (TRANS & 1)) ? 4 : 8;
+  constexpr int LG_NT = NT_C == 16 ? 4 : NT_C == 32 ? 5 : 6;
   // activation stages first, on a 1024-byte boundary (128-byte swizzle atoms
   // of the direct mode); stage sizes are multiples of 1024 bytes there
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -1018,7 +1027,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // (a = packed weights, b = staged activation rows, whichever MMA
       // operand slot they take)
       const uint32_t idesc = (1u << 4)                                  // D = f32
-                             | (uint32_t((TRANS ? TRANS : UN) >> 3) << 17)  // N
+                             | (uint32_t(NT_C >> 3) << 17)                  // N
                              | (uint32_t(128 >> 4) << 24);              // M; f16 K-major
       const uint32_t a_lbo = uint32_t(g.wrows) * 16;        // chunk plane of the weights
       const uint32_t b_lbo = uint32_t(g.R_alloc) * 16;      // chunk plane of the activations
@@ -1294,21 +1303,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       } else {
-      // the warp's ACC_COLS / 4 columns, in chunks of 32
+      // the warp's ACC_COLS / 4 columns, in chunks of CW = 32 (16 when the
+      // warp owns only 16: N = 16 with 4 M blocks)
       constexpr int ACC_COLS = G_C * NT_C;
-      constexpr int NCHUNK = ACC_COLS / 128;
+      constexpr int CW = ACC_COLS / 4 < 32 ? ACC_COLS / 4 : 32;
+      constexpr int NCHUNK = ACC_COLS / (4 * CW);
       __half *base = out + size_t(b) * g.OC * plane;
 #pragma unroll
       for (int h = 0; h < NCHUNK; ++h) {
-        const int c0 = cq * (ACC_COLS / 4) + h * 32;
-        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * ACC_COLS + c0), r);
+        const int c0 = cq * (ACC_COLS / 4) + h * CW;
+        if constexpr (CW == 32)
+          tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * ACC_COLS + c0), r);
+        else
+          tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * ACC_COLS + c0), r);
         if (h == NCHUNK - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
         }
-        // 32 columns cover one M block (NT >= 32) or two (NT = 16)
-        const int mb0 = c0 >> LG_NT, mb1 = (c0 + 31) >> LG_NT;
+        // CW columns cover one M block (NT >= CW) or two (NT = 16, CW = 32)
+        const int mb0 = c0 >> LG_NT, mb1 = (c0 + CW - 1) >> LG_NT;
         const int pos_a = int(p0) + mb0 * 128 + q * 32 + lane;
         const int pos_b = int(p0) + mb1 * 128 + q * 32 + lane;
         const int oh_a = pos_a / g.Wp, ow_a = pos_a - oh_a * g.Wp;
@@ -1317,9 +1331,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         __half *dst_a = base + size_t(oh_a) * g.OW + ow_a;
         __half *dst_b = base + size_t(oh_b) * g.OW + ow_b;
         // columns j, j+1: channels oc, oc+1 of the same position (NT is even)
-        uint32_t pr[16];
+        uint32_t pr[CW / 2];
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
+        for (int j = 0; j < CW; j += 2) {
           const int oc = (c0 + j) & (NT_C - 1);
           const float2 bb = reinterpret_cast<const float2 *>(sbias)[oc >> 1];
           pr[j / 2] = epi_act2<ACT_T>(r[j], r[j + 1], bb.x, bb.y, g.lo, g.hi);
@@ -1333,7 +1347,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           // consecutive outputs (Wp % 8 == 0: an 8-group never leaves its
           // output row; OW % 8 == 0: it is entirely valid or entirely padding)
 #pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
+          for (int hf = 0; hf < CW / 16; ++hf) {
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const uint32_t v = pr[hf * 8 + k];
@@ -1377,7 +1391,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint4 *slot_a = ok_a ? xs_slot(g, b, 0, oh_a, ow_a) : nullptr;
           uint4 *slot_b = mb1 == mb0 ? slot_a : ok_b ? xs_slot(g, b, 0, oh_b, ow_b) : nullptr;
 #pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8) {
+          for (int q8 = 0; q8 < CW / 8; ++q8) {
             const int c = c0 + 8 * q8;
             const int oc = c & (NT_C - 1);
             uint4 *slot = (c >> LG_NT) != mb0 ? slot_b : slot_a;
@@ -1387,7 +1401,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
+          for (int j = 0; j < CW; j += 2) {
             const int c = c0 + j;
             const int oc = c & (NT_C - 1);
             const bool second = (c >> LG_NT) != mb0;
@@ -1776,11 +1790,13 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
 #define WGX_UMMA_TRANS(T)                                                                  \
   {WGX_UMMA_ROW(0, T), WGX_UMMA_ROW(1, T), WGX_UMMA_ROW(2, T), WGX_UMMA_ROW(3, T),          \
    WGX_UMMA_ROW(0, T), WGX_UMMA_ROW(0, T), WGX_UMMA_ROW(0, T)}
-  // [standard, transposed N = 16 / 32 / 64][filter width][activation]
-  static const KernelFn table[4][7][3] = {
+  // [standard, transposed N = 16 / 32 / 64, N = 16 / 32 with 4 M blocks]
+  // [filter width][activation]
+  static const KernelFn table[6][7][3] = {
       {WGX_UMMA_ROW(0, 0), WGX_UMMA_ROW(1, 0), WGX_UMMA_ROW(2, 0), WGX_UMMA_ROW(3, 0),
        WGX_UMMA_ROW(4, 0), WGX_UMMA_ROW(5, 0), WGX_UMMA_ROW(7, 0)},
-      WGX_UMMA_TRANS(16), WGX_UMMA_TRANS(32), WGX_UMMA_TRANS(64)};
+      WGX_UMMA_TRANS(16), WGX_UMMA_TRANS(32), WGX_UMMA_TRANS(64), WGX_UMMA_TRANS(17),
+      WGX_UMMA_TRANS(33)};
 #undef WGX_UMMA_TRANS
 #undef WGX_UMMA_ROW
   int kw_idx = 0;
@@ -1791,10 +1807,10 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   // residual / split outputs: generic MMA loop, EXT epilogue
 #define WGX_UMMA_EXT(T) \
   { umma_conv_kernel<0, 0, T, 1>, umma_conv_kernel<0, 1, T, 1>, umma_conv_kernel<0, 2, T, 1> }
-  static const KernelFn table_ext[4][3] = {WGX_UMMA_EXT(0), WGX_UMMA_EXT(16), WGX_UMMA_EXT(32),
-                                           WGX_UMMA_EXT(64)};
+  static const KernelFn table_ext[6][3] = {WGX_UMMA_EXT(0),  WGX_UMMA_EXT(16), WGX_UMMA_EXT(32),
+                                           WGX_UMMA_EXT(64), WGX_UMMA_EXT(17), WGX_UMMA_EXT(33)};
 #undef WGX_UMMA_EXT
-  const int nt_idx = !g.trans ? 0 : g.NT == 16 ? 1 : g.NT == 32 ? 2 : 3;
+  const int nt_idx = !g.trans ? 0 : g.NT == 64 ? 3 : (g.NT == 16 ? 1 : 2) + (g.G == 4 ? 3 : 0);
   if (g.trans && g.NT != 16 && g.NT != 32 && g.NT != 64) fail("conv2d: bad transposed tile");
   // 16-byte stores of the transposed epilogue (split pieces and residual
   // loads included)
@@ -1809,8 +1825,8 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   // epilogue
   const bool ext = (g.resid != nullptr || g.nout > 0) && !g.tvec;
   KernelFn kern = ext ? table_ext[nt_idx][act_idx] : table[nt_idx][kw_idx][act_idx];
-  const int kidx = ext ? 84 + nt_idx * 3 + act_idx : (nt_idx * 7 + kw_idx) * 3 + act_idx;
-  static bool attr_set[64][96] = {};
+  const int kidx = ext ? 126 + nt_idx * 3 + act_idx : (nt_idx * 7 + kw_idx) * 3 + act_idx;
+  static bool attr_set[64][144] = {};
   if (dev < 64 && !attr_set[dev][kidx]) {
     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(SMEM_MAX)),
