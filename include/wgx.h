@@ -211,6 +211,12 @@ typedef struct wgx_conv2d_plan {
 } wgx_conv2d_plan;
 
 WGX_API int wgx_conv2d_plan_for(const wgx_conv2d_params *p, wgx_conv2d_plan *out);
+/* A one-line, NUL-terminated description of the kernel configuration that
+ * wgx_conv2d_plan_for selects (variant; for the tensor-core path the tile
+ * orientation, N, M blocks per tile, channels per stage, filter rows per
+ * stage, pipeline stages, resident weights, skipped taps). No counterpart
+ * in the reference (its variant selection is convolution/index.ts:58-310). */
+WGX_API int wgx_conv2d_describe(const wgx_conv2d_params *p, char *buf, int32_t len);
 /* in: NCHW [B,IC,IH,IW]; w: OIHW [OC,IC/groups,KH,KW]; bias: [OC] or NULL;
  * out: NCHW [B,OC,OH,OW]. The packed-weight cache lives in scratch. */
 WGX_API int wgx_conv2d(const wgx_conv2d_params *p, const void *in, const void *w, const void *bias,

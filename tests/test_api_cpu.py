@@ -115,6 +115,34 @@ def test_plan_strided_convs_use_tensor_cores():
     assert down.scratch_bytes >= 64 * 512 * 41 * 41 * 2
 
 
+def describe(**kw):
+    p = _lib.ConvParams()
+    d = dict(B=1, IC=1, IH=1, IW=1, OC=1, OH=1, OW=1, KH=1, KW=1, sH=1, sW=1, pH=0, pW=0, dH=1,
+             dW=1, groups=1, has_bias=1, dtype=1, act=0, out_min=-np.inf, out_max=np.inf)
+    d.update(kw)
+    for k, v in d.items():
+        setattr(p, k, v)
+    buf = ctypes.create_string_buffer(256)
+    _lib.check(_lib.lib.wgx_conv2d_describe(ctypes.byref(p), buf, 256))
+    return buf.value.decode()
+
+
+def test_describe_names_the_selected_configuration():
+    # channels on M, N = 256 positions, weights resident
+    d = describe(B=8, IC=64, IH=160, IW=160, OC=128, OH=160, OW=160, KH=3, KW=3, pH=1, pW=1)
+    assert d.startswith("umma channels-on-M N=256") and "resident" in d
+    # YOLO stem: positions on M, N = 16, 8 M blocks of 128 positions
+    d = describe(B=64, IC=3, IH=640, IW=640, OC=16, OH=320, OW=320, KH=3, KW=3, sH=2, sW=2,
+                 pH=1, pW=1)
+    assert "positions-on-M N=16 G=8" in d
+    # 3x3 / stride 2 with 64 channels: skipped all-zero taps of the space-to-depth view
+    d = describe(B=64, IC=128, IH=80, IW=80, OC=128, OH=40, OW=40, KH=3, KW=3, sH=2, sW=2,
+                 pH=1, pW=1)
+    assert "tapskip" in d
+    assert describe(B=2, IC=8, IH=9, IW=9, OC=8, OH=9, OW=9, KH=3, KW=3, pH=1, pW=1,
+                    groups=8) == "depthwise"
+
+
 def test_plan_rejects_bad_geometry():
     with pytest.raises(wgx.WgxError):
         plan(IC=3, OC=4, groups=2)

@@ -21,6 +21,8 @@
 // and relaunches the instantiated graph on later submits, so the per-submit
 // host cost is one cudaGraphLaunch instead of re-encoding every dispatch.
 #include <cstdio>
+
+#include "umma_conv.h"
 #include <cstring>
 #include <mutex>
 
@@ -640,6 +642,18 @@ int wgx_mm(const void *a, const void *b, void *out, int64_t M, int64_t N, int64_
 
 int wgx_conv2d_plan_for(const wgx_conv2d_params *p, wgx_conv2d_plan *out) {
   return guarded([&] { *out = plan_conv2d(*p); });
+}
+
+int wgx_conv2d_describe(const wgx_conv2d_params *p, char *buf, int32_t len) {
+  return guarded([&] {
+    if (!p || !buf || len <= 0) fail("conv2d describe: null argument");
+    const wgx_conv2d_plan plan = plan_conv2d(*p);
+    static const char *names[] = {"?", "umma", "simt-gemm", "depthwise", "direct", "pointwise1"};
+    std::string d = plan.variant == WGX_CONV_UMMA
+                        ? umma_conv_describe(*p)
+                        : std::string(names[(plan.variant >= 1 && plan.variant <= 5) ? plan.variant : 0]);
+    std::snprintf(buf, size_t(len), "%s", d.c_str());
+  });
 }
 
 int wgx_conv2d(const wgx_conv2d_params *p, const void *in, const void *w, const void *bias,

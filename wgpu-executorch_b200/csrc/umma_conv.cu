@@ -146,7 +146,7 @@ constexpr int kSeqGroups = 8;
 
 static uint32_t smem_need(const UmmaGeom &g) {
   return g.w_region_bytes + uint32_t(g.stages) * g.b_stage_bytes + EPI_BYTES +
-         (2 * g.stages + 5) * 8 + 16 + kMaxGroups * 8 + 1024;
+         (2 * g.stages + 5) * 8 + 16 + kMaxGroups * 8 + kMaxKhg * kMaxPhases * 4 + 1024;
 }
 
 // Geometry for one staging choice: each pipeline stage carries `bk` input
@@ -296,8 +296,15 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans)
   g.tapskip = 0;
   g.cbpp = 1;
   const int nph = g.nphH * g.nphW;
-  if (!trans && nph > 1 && g.xIC % g.bk == 0 && g.n_khg <= kMaxKhg && nph <= kMaxPhases &&
-      g.khs * g.KW <= 16) {
+  // (positions-on-M: only with the generic staging, whose per-stage MMA
+  // group lists are compacted per filter-row group and phase and must fit
+  // the group table after the full list)
+  const int ngroups_ = g.khs * g.KW * (g.bk / 16);
+  const bool spec_ = g.khs == 1 && g.bk == 32 && g.KW <= 3;
+  const bool trans_ok = !spec_ && ngroups_ <= kSeqGroups &&
+                        ngroups_ * (1 + g.n_khg * g.nphH * g.nphW) <= kMaxGroups;
+  if ((!trans || trans_ok) && nph > 1 && g.xIC % g.bk == 0 && g.n_khg <= kMaxKhg &&
+      nph <= kMaxPhases && g.khs * g.KW <= 16) {
     g.cbpp = g.xIC / g.bk;
     for (int khg = 0; khg < g.n_khg; ++khg)
       for (int ph = 0; ph < nph; ++ph) {
@@ -392,6 +399,18 @@ static int sm_count() {
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   check_cuda(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev), "SM count");
   return n;
+}
+
+std::string umma_conv_describe(const wgx_conv2d_params &p) {
+  const UmmaGeom g = make_geom(p);
+  char buf[256];
+  snprintf(buf, sizeof buf,
+           "umma %s N=%d G=%d tile=%d positions bk=%d khs=%d stages=%d/%d kstages=%d%s%s "
+           "Wp=%d tiles=%d",
+           g.trans ? "positions-on-M" : "channels-on-M", g.trans ? g.NT : UN, g.G, g.tile_pos,
+           g.bk, g.khs, g.stages, g.n_kstages, g.n_kstages, g.resident ? " resident" : "",
+           g.tapskip ? " tapskip" : "", g.Wp, g.total_tiles);
+  return buf;
 }
 
 uint64_t umma_conv_grid(const wgx_conv2d_params &p) {
@@ -936,6 +955,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   // generic staging: (activation, weight) descriptor offsets of every MMA
   // group of a stage, in 16-byte units (written and read by the MMA thread)
   uint2 *grp_off = reinterpret_cast<uint2 *>(tmem_slot + 4);
+  // positions-on-M with tap masks: (start, count) of the compacted group list
+  // of each (filter-row group, phase) inside grp_off
+  uint16_t *grp_list = reinterpret_cast<uint16_t *>(grp_off + kMaxGroups);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -1059,6 +1081,19 @@ __global__ void __launch_bounds__(THREADS, 1)
               grp_off[j] = make_uint2((shift * 16 + uint32_t(ks) * 2 * b_lbo) >> 4,
                                       (tap * uint32_t(g.chunks) * a_lbo + uint32_t(ks) * 2 * a_lbo) >> 4);
             }
+        if (TRANS && g.tapskip) {
+          // compacted lists: the groups whose tap meets real filter taps
+          int e = ngroups;
+          for (int khg = 0; khg < g.n_khg; ++khg)
+            for (int ph = 0; ph < g.nphH * g.nphW; ++ph) {
+              const uint32_t m = g.tapmask[khg][ph];
+              const int start = e;
+              for (int jj = 0; jj < ngroups; ++jj)
+                if ((m >> (jj / (g.bk / 16))) & 1) grp_off[e++] = grp_off[jj];
+              grp_list[2 * (khg * kMaxPhases + ph)] = uint16_t(start);
+              grp_list[2 * (khg * kMaxPhases + ph) + 1] = uint16_t(e - start);
+            }
+        }
       }
       int it = 0, slot = S - 1, use = -1;
       for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x, ++it) {
@@ -1149,12 +1184,19 @@ __global__ void __launch_bounds__(THREADS, 1)
             // groups in table order.
             const uint64_t x0 = kmajor_desc(b_base, b_lbo), w0 = kmajor_desc(a_base, a_lbo);
             uint32_t acc_flag = acc_on;
-            if (ngroups <= kSeqGroups) {
+            // the stage's group list: all groups, or the compacted list of
+            // its (filter-row group, phase) under tap masks
+            int gstart = 0, gcount = ngroups;
+            if (TRANS && g.tapskip) {
+              gstart = grp_list[2 * (sw.khg * kMaxPhases + sw.phase)];
+              gcount = grp_list[2 * (sw.khg * kMaxPhases + sw.phase) + 1];
+            }
+            if (gcount <= kSeqGroups) {
               uint2 e[kSeqGroups];
 #pragma unroll
               for (int k = 0; k < kSeqGroups; ++k) {
-                const int j = k - (kSeqGroups - ngroups);
-                e[k] = grp_off[j < 0 ? 0 : j];
+                const int j = k - (kSeqGroups - gcount);
+                e[k] = grp_off[gstart + (j < 0 ? 0 : j)];
               }
 #define WGX_GROUP(K)                                                                      \
   {                                                                                       \
@@ -1167,7 +1209,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }                                                                                     \
     acc_flag = 1;                                                                         \
   }
-              switch (ngroups) {
+              switch (gcount) {
                 case 8: WGX_GROUP(0) [[fallthrough]];
                 case 7: WGX_GROUP(1) [[fallthrough]];
                 case 6: WGX_GROUP(2) [[fallthrough]];

@@ -6,6 +6,7 @@ namespace wgx {
 
 bool umma_conv_supported(const wgx_conv2d_params &p);
 uint64_t umma_conv_grid(const wgx_conv2d_params &p);
+std::string umma_conv_describe(const wgx_conv2d_params &p);
 uint64_t umma_conv_packed_weight_bytes(const wgx_conv2d_params &p);
 uint64_t umma_conv_input_bytes(const wgx_conv2d_params &p);
 void umma_conv_pack_weights(const wgx_conv2d_params &p, const __half *w, void *packed,

@@ -88,6 +88,7 @@ SIGNATURES = {
     "wgx_mm": ([c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p,
                 c_uint64, c_void_p], c_int),
     "wgx_conv2d_plan_for": ([POINTER(ConvParams), POINTER(ConvPlan)], c_int),
+    "wgx_conv2d_describe": ([POINTER(ConvParams), c_char_p, c_int32], c_int),
     "wgx_conv2d": ([POINTER(ConvParams), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                     c_uint64, c_void_p], c_int),
     "wgx_conv2d_noalloc": ([POINTER(ConvParams), c_void_p, c_void_p, c_void_p, c_void_p,
