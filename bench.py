@@ -554,6 +554,8 @@ ONLY_CONV = {
     "yolo_stem": (8, 3, 640, 640, 16, 3, 2, 1, 1, 2),   # YOLO26-N shapes, batch 8
     "yolo_down": (8, 64, 160, 160, 64, 3, 2, 1, 1, 2),
     "yolo_1x1": (8, 48, 160, 160, 64, 1, 1, 0, 1, 2),
+    "yolo_c16": (64, 16, 160, 160, 8, 3, 1, 1, 1, 2),      # small-OC 3x3 (positions on M)
+    "yolo_s2c128": (64, 128, 80, 80, 128, 3, 2, 1, 1, 2),  # stride 2, channels on M
     "yolo_dw20": (64, 256, 20, 20, 256, 3, 1, 1, 256, 2),   # 20x20 depthwise of the neck
 }
 

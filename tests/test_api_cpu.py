@@ -141,6 +141,17 @@ def test_describe_names_the_selected_configuration():
     assert "tapskip" in d
     assert describe(B=2, IC=8, IH=9, IW=9, OC=8, OH=9, OW=9, KH=3, KW=3, pH=1, pW=1,
                     groups=8) == "depthwise"
+    # 3x3 / stride 1, OC <= 64: filter columns folded into N where the MMAs
+    # saved outweigh the longer epilogue (ocp < 14 * ceil(IC / 16))
+    d = describe(B=64, IC=16, IH=160, IW=160, OC=8, OH=160, OW=160, KH=3, KW=3, pH=1, pW=1)
+    assert "positions-on-M N=32 G=8" in d and "kw-folded" in d
+    d = describe(B=64, IC=64, IH=80, IW=80, OC=16, OH=80, OW=80, KH=3, KW=3, pH=1, pW=1)
+    assert "N=48 G=4" in d and "kw-folded" in d
+    d = describe(B=64, IC=256, IH=20, IW=20, OC=64, OH=20, OW=20, KH=3, KW=3, pH=1, pW=1)
+    assert "N=192 G=1" in d and "kw-folded" in d
+    for ic, oc in ((8, 16), (32, 32), (16, 16)):
+        d = describe(B=64, IC=ic, IH=80, IW=80, OC=oc, OH=80, OW=80, KH=3, KW=3, pH=1, pW=1)
+        assert "kw-folded" not in d, (ic, oc, d)
 
 
 def test_plan_rejects_bad_geometry():

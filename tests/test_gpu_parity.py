@@ -121,6 +121,37 @@ def test_dense_f16_tensor_core(ctx, geom):
     check_f16(y, x, w, b, 1, pads, dil, 1)
 
 
+# (B, IC, H, W, OC, pad, dil): 3x3 / stride 1 convolutions whose filter
+# columns are folded into the MMA's N (N = 3 * ocp: 32 / 48 / 96 / 192), with
+# 16-byte NCHW stores (OW % 8 == 0 and a padded row pitch of 8k) or 2-byte ones
+KW_FOLDED_F16 = [
+    (2, 32, 9, 160, 8, (1, 1), (1, 1)),      # N = 32, 8 M blocks, vector stores
+    (2, 48, 13, 17, 16, (1, 1), (1, 1)),     # N = 48, odd sizes
+    (1, 64, 30, 30, 24, (1, 1), (1, 1)),     # N = 96 (24 channels of 32)
+    (1, 80, 9, 40, 40, (1, 1), (1, 1)),      # N = 192, one M block per tile
+    (1, 32, 12, 20, 8, (2, 1), (2, 1)),      # vertical dilation
+    (3, 256, 20, 20, 16, (1, 1), (1, 1)),    # YOLO26-N neck shape
+    (1, 16, 5, 3, 5, (1, 1), (1, 1)),        # planes narrower than the filter rows
+]
+
+
+@pytest.mark.parametrize("geom", KW_FOLDED_F16, ids=[str(g) for g in KW_FOLDED_F16])
+@pytest.mark.parametrize("bias", [True, False])
+def test_kw_folded_f16(ctx, geom, bias):
+    B, IC, H, W, OC, pad, dil = geom
+    p = _lib.ConvParams(B, IC, H, W, OC, H + 2 * pad[0] - 2 * dil[0], W + 2 * pad[1] - 2 * dil[1],
+                        3, 3, 1, 1, pad[0], pad[1], dil[0], dil[1], 1, int(bias), 1,
+                        _lib.ACT_NONE, -np.inf, np.inf)
+    buf = ctypes.create_string_buffer(256)
+    _lib.check(_lib.lib.wgx_conv2d_describe(ctypes.byref(p), buf, 256))
+    assert "kw-folded" in buf.value.decode(), buf.value
+    (x,) = oracle.make_inputs([(B, IC, H, W)], seed=30)
+    w = kaiming((OC, IC, 3, 3), 31)
+    b = oracle.make_inputs([(OC,)], seed=32, scale=0.01)[0] if bias else None
+    y = engine_conv(ctx, x, w, b, 1, pad, dil, 1)
+    check_f16(y, x, w, b, 1, pad, dil, 1)
+
+
 def test_dense_f16_no_bias_and_clamp(ctx):
     (x,) = oracle.make_inputs([(2, 48, 15, 17)], seed=20)
     w = kaiming((40, 48, 3, 3), 21)
@@ -431,13 +462,15 @@ def test_program_conv_sigmoid_mul_fusion(ctx, out_pool, ic, commands):
     assert oracle.rel_err(y, ex) <= 5e-3
 
 
-def test_program_split_and_residual_folded_into_convs(ctx):
+@pytest.mark.parametrize("C,H,W", [(32, 16, 20), (8, 16, 20), (8, 6, 160)])
+def test_program_split_and_residual_folded_into_convs(ctx, C, H, W):
     """C2f-style block: conv1 (+SiLU) -> split [a, b]; conv2 (+SiLU) of b;
     y = b + conv2(b) (residual); cat [a, b, y]. The split and the add are
     done by the convolutions' epilogues; the result equals the program
-    oracle's."""
+    oracle's. (C = 8: conv2 takes the folded-column form, with 2-byte and
+    16-byte residual stores.)"""
     import program_oracle
-    B, C, H, W = 2, 32, 16, 20
+    B = 2
     rng = np.random.default_rng(120)
     x = rng.standard_normal((B, C, H, W)).astype(np.float16)
     w1 = kaiming((2 * C, C, 1, 1), 121)

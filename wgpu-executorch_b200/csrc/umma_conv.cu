@@ -47,7 +47,9 @@
 // Every mbarrier wait is bounded (about 2 s of %globaltimer); on expiry the
 // waiting role sets a bit in the device error word and stops, so a broken
 // pipeline returns an error instead of hanging the GPU.
+#include <cstdlib>
 #include <cstring>
+#include <utility>
 
 #include "tcgen05.h"
 #include "tma.h"
@@ -75,6 +77,10 @@ constexpr int kMaxOut = 4;
 
 // space-to-depth tap masks: filter-row groups x phases
 constexpr int kMaxKhg = 4, kMaxPhases = 16;
+// resident weights arrive in up to this many pieces (consecutive pipeline
+// stages), each on its own barrier, so the first tile's MMAs start once
+// the first piece has landed
+constexpr int kWParts = 8;
 
 struct UmmaGeom {
   // IC, KH, KW, dH, dW, pH, pW describe the stride-1 convolution the MMA
@@ -87,7 +93,18 @@ struct UmmaGeom {
   // tile), output channels on N (NT = OC rounded up to 16/32/64). Used for
   // OC <= 64, where channels on M would leave TMEM lane quadrants idle.
   int trans, NT, G, lgNT;
-  int tile_pos;                      // output positions per tile
+  int tile_pos;                      // positions of one tile's accumulator (M rows)
+  int tile_stride;                   // first positions of consecutive tiles: tile_pos,
+                                     // or tile_pos - 8 when hs > 0 (see below)
+  // hs > 0 (positions on M, stride 1, filter width hs = 3): the filter
+  // columns are folded into N. The MMA pipeline runs the KW = 1 convolution
+  // Y[q][kw*ocp + oc] = sum_{kh,c} xs[q + kh*dH*Wp][c] w[oc][c][kh][kw]
+  // (N = 3*ocp rounded up to 16, ocp = OC rounded up to 8 / 16 / 32 / 64), one MMA per
+  // filter row and 16 channels instead of three, and the epilogue forms
+  // out[p][oc] = Y[p][oc] + Y[p+1][ocp+oc] + Y[p+2][2*ocp+oc]. A tile's
+  // last 8 positions only feed its own outputs, so tiles advance by
+  // tile_pos - 8.
+  int hs, ocp;
   int wrows;                         // packed weight rows per oc tile (UM or NT)
   int acc_cols;                      // TMEM columns per accumulator
   int bk, chunks;                    // channels per stage, 16-byte chunks per stage
@@ -146,7 +163,7 @@ constexpr int kSeqGroups = 8;
 
 static uint32_t smem_need(const UmmaGeom &g) {
   return g.w_region_bytes + uint32_t(g.stages) * g.b_stage_bytes + EPI_BYTES +
-         (2 * g.stages + 5) * 8 + 16 + kMaxGroups * 8 + kMaxKhg * kMaxPhases * 4 + 1024;
+         (2 * g.stages + 6 + kWParts) * 8 + 16 + kMaxGroups * 8 + kMaxKhg * kMaxPhases * 4 + 1024;
 }
 
 // Geometry for one staging choice: each pipeline stage carries `bk` input
@@ -166,7 +183,7 @@ static void phases(int K, int pad, int s, int &n, int *ph, int &d0, int &d1) {
   d1 = floor_div(K - 1 - pad, s);
 }
 
-static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans) {
+static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans, int hs = 0) {
   UmmaGeom g{};
   g.trans = trans;
   if (trans) {
@@ -232,6 +249,22 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans)
       p.KH == 1 && p.KW == 1 && p.sH == 1 && p.sW == 1 && p.pH == 0 && p.pW == 0;
   const int wp8 = (g.Wp + 7) / 8 * 8;
   if (trans && !plain_1x1 && (wp8 - g.Wp) * 20 <= g.Wp) g.Wp = wp8;
+  if (hs) {
+    // filter columns folded into N (stride 1, dW = 1, KW = hs): the
+    // pipeline runs a KW = 1 convolution with N = hs*ocp columns per M block
+    g.hs = hs;
+    // ocp = 8 / 16 / 32 / 64: N = 32 / 48 / 96 / 192 with 8 / 4 / 2 / 1 M
+    // blocks (two accumulators fit TMEM; 8 (M block, 8-channel) epilogue
+    // items per tile)
+    g.ocp = p.OC <= 8 ? 8 : p.OC <= 16 ? 16 : p.OC <= 32 ? 32 : 64;
+    g.NT = (hs * g.ocp + 15) / 16 * 16;
+    g.G = g.ocp == 8 ? 8 : g.ocp == 16 ? 4 : g.ocp == 32 ? 2 : 1;
+    g.lgNT = 0;
+    g.tile_pos = 128 * g.G;
+    g.wrows = g.NT;
+    g.acc_cols = g.G * g.NT;
+    g.KW = 1;
+  }
   if (khs <= 0) khs = g.KH;
   g.bk = bk;
   g.chunks = bk / 8;
@@ -242,14 +275,15 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans)
   g.n_oct = (p.OC + g.wrows - 1) / g.wrows;
   g.plane_rows = (long long)g.Hp * g.Wp;
   long long p_out = (long long)(p.OH - 1) * g.Wp + p.OW;
-  if (trans && g.G == 8 && p_out <= 512) {
+  if (trans && !hs && g.G == 8 && p_out <= 512) {
     // small planes: 4 M blocks (512 positions) instead of 8, most of whose
     // positions would lie past the image
     g.G = 4;
     g.tile_pos = 128 * g.G;
     g.acc_cols = g.G * g.NT;
   }
-  g.tiles_per_img = int((p_out + g.tile_pos - 1) / g.tile_pos);
+  g.tile_stride = hs ? g.tile_pos - 8 : g.tile_pos;
+  g.tiles_per_img = int((p_out + g.tile_stride - 1) / g.tile_stride);
   g.total_tiles = g.tiles_per_img * g.n_oct * g.B;
   long long r = g.tile_pos + (long long)(khs - 1) * g.dH * g.Wp + (long long)(g.KW - 1) * g.dW;
   g.R = r > (1 << 20) ? (1 << 20) : int(r);
@@ -328,6 +362,27 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans)
   return g;
 }
 
+// Filter columns folded into N (UmmaGeom::hs): stride-1 3-wide filters of
+// the positions-on-M variant (OC <= 64) without dilation across, where it
+// pays. The fold cuts the MMAs per position threefold (their cost grows
+// with the 16-channel input blocks) but its epilogue costs about as much
+// per tile and 8 output channels as a 3x3 filter's MMAs per 16 input
+// channels cost unfolded at N = 16 (measured per role on B200: ~3 K cycles
+// per tile and 8-channel chunk, against ~5.8 K cycles of unfolded MMAs per
+// 1024 positions and input block): folded when ocp < 14 * ceil(IC / 16).
+// The environment variable WGX_CONV_HSUM=0 turns the fold off, =2 applies
+// it wherever it is possible (both forms compute the same convolution).
+static bool hsum_eligible(const wgx_conv2d_params &p) {
+  static const int mode = [] {
+    const char *e = std::getenv("WGX_CONV_HSUM");
+    return (e && e[0] == '0') ? 0 : (e && e[0] == '2') ? 2 : 1;
+  }();
+  if (!mode || p.OC > 64 || p.sH != 1 || p.sW != 1 || p.dW != 1 || p.KW != 3 || p.groups != 1)
+    return false;
+  const int ocp = p.OC <= 8 ? 8 : p.OC <= 16 ? 16 : p.OC <= 32 ? 32 : 64;
+  return mode == 2 || ocp < 14 * ((p.IC + 15) / 16);
+}
+
 // Pick the staging: per-filter-row stages of 32 channels measured fastest
 // on config 2 (41 % tensor-pipe activity against 30 % for whole-filter
 // stages of 16 channels); whole-filter and 16-channel stages are the
@@ -335,9 +390,16 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans)
 static UmmaGeom make_geom(const wgx_conv2d_params &p) {
   // (khs, bk); khs 0 = the whole filter. Below 16 (virtual) channels,
   // 16-channel stages halve the zero padding of the K dimension.
-  int cand[3][2] = {{1, 32}, {0, 16}, {1, 16}};
+  int cand[4][2] = {{1, 32}, {0, 16}, {1, 16}, {0, 32}};
   const int trans = p.OC <= 64 ? 1 : 0;
-  if (geom_for(p, 1, 32, trans).IC <= 16) {
+  const int hs = hsum_eligible(p) ? p.KW : 0;
+  if (hs) {
+    // one MMA per filter row: whole-filter stages keep several MMAs per
+    // stage (per-stage waits and commits cost several MMA times)
+    const int c4[4][2] = {{0, 32}, {0, 16}, {1, 32}, {1, 16}};
+    std::memcpy(cand, c4, sizeof cand);
+    if (p.IC <= 16) std::swap(cand[0][1], cand[1][1]);
+  } else if (geom_for(p, 1, 32, trans).IC <= 16) {
     cand[0][1] = 16;
     cand[2][1] = 32;
   }
@@ -345,7 +407,7 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p) {
   bool have = false;
   for (int min_stages : {3, 2}) {
     for (auto &c : cand) {
-      UmmaGeom g = geom_for(p, c[0], c[1], trans);
+      UmmaGeom g = geom_for(p, c[0], c[1], trans, hs);
       if (g.stages >= min_stages && smem_need(g) <= SMEM_MAX && g.R_alloc * 16 < (1 << 18)) {
         return g;
       }
@@ -405,11 +467,11 @@ std::string umma_conv_describe(const wgx_conv2d_params &p) {
   const UmmaGeom g = make_geom(p);
   char buf[256];
   snprintf(buf, sizeof buf,
-           "umma %s N=%d G=%d tile=%d positions bk=%d khs=%d stages=%d/%d kstages=%d%s%s "
+           "umma %s N=%d G=%d tile=%d positions bk=%d khs=%d stages=%d/%d kstages=%d%s%s%s "
            "Wp=%d tiles=%d",
            g.trans ? "positions-on-M" : "channels-on-M", g.trans ? g.NT : UN, g.G, g.tile_pos,
            g.bk, g.khs, g.stages, g.n_kstages, g.n_kstages, g.resident ? " resident" : "",
-           g.tapskip ? " tapskip" : "", g.Wp, g.total_tiles);
+           g.tapskip ? " tapskip" : "", g.hs ? " kw-folded" : "", g.Wp, g.total_tiles);
   return buf;
 }
 
@@ -428,7 +490,7 @@ uint64_t umma_conv_packed_weight_bytes(const wgx_conv2d_params &p) {
 // image only feed output positions that are discarded.
 static uint64_t input_rows_total(const UmmaGeom &g) {
   uint64_t planes = uint64_t(g.B) * (g.C8 / 8);
-  uint64_t last_end = uint64_t(g.tiles_per_img - 1) * g.tile_pos +
+  uint64_t last_end = uint64_t(g.tiles_per_img - 1) * g.tile_stride +
                       uint64_t(g.n_khg - 1) * g.khs * g.dH * g.Wp + g.R;
   uint64_t slack = last_end > uint64_t(g.plane_rows) ? last_end - g.plane_rows : 0;
   return planes * g.plane_rows + slack;
@@ -681,8 +743,21 @@ __device__ __forceinline__ void pack_weights_body(const UmmaGeom &g, const __hal
   const int khg = t % g.n_khg;
   const int oct = t / g.n_khg;
   const int kh = khg * g.khs + khl;
-  const int oc = oct * g.wrows + row;
   __align__(16) __half v[8];
+  if (g.hs) {
+    // folded filter columns: row = kw*ocp + oc (stride 1, one output tile)
+    const int fkw = row / g.ocp, foc = row - fkw * g.ocp;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int c = cb * g.bk + chunk * 8 + e;
+      v[e] = (fkw < g.hs && foc < g.OC && c < g.IC)
+                 ? w[((size_t(foc) * g.IC + c) * g.xKH + kh) * g.xKW + fkw]
+                 : __float2half_rn(0.f);
+    }
+    packed[i] = *reinterpret_cast<const uint4 *>(v);
+    return;
+  }
+  const int oc = oct * g.wrows + row;
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const int cv = cb * g.bk + chunk * 8 + e;  // virtual channel
@@ -910,12 +985,284 @@ struct StageWalk {
   }
 };
 
+// Optional per-role cycle counters (compile with -DWGX_PROF): per CTA,
+// [0] producer waiting for free slots, [1] MMA thread waiting for a free
+// accumulator, [2] MMA thread waiting for staged data, [3] MMA thread
+// issuing, [4] epilogue warp 4 waiting for a full accumulator, [5] epilogue
+// warp 4 working, [6] MMA thread total, [7] tiles of the CTA; folded-column
+// epilogue (warp 4): [8] TMEM loads, [9] exchange wait, [10] outputs.
+#ifdef WGX_PROF
+__device__ unsigned long long g_umma_prof[256][12];
+#define WGX_PROF_T(v) const long long v = clock64()
+#define WGX_PROF_ADD(acc, t0) acc += (unsigned long long)(clock64() - (t0))
+#else
+#define WGX_PROF_T(v)
+#define WGX_PROF_ADD(acc, t0)
+#endif
+
 __device__ __forceinline__ void tile_coords(const UmmaGeom &g, int t, int &b, long long &p0,
                                             int &oct) {
   oct = t % g.n_oct;
   const int rest = t / g.n_oct;
   b = rest / g.tiles_per_img;
-  p0 = (long long)(rest % g.tiles_per_img) * g.tile_pos;
+  p0 = (long long)(rest % g.tiles_per_img) * g.tile_stride;
+}
+
+// ---------------------------------------- epilogue of the folded-column form
+// tcgen05.ld of 8 columns without waiting (completed by tmem_wait_3x8)
+__device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, float *r) {
+  uint32_t *u = reinterpret_cast<uint32_t *>(r);
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]),
+                 "=r"(u[6]), "=r"(u[7])
+               : "r"(taddr));
+}
+// Waits for this thread's outstanding tcgen05.ld's. The 24 destination
+// registers are operands, so no use of them is scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_3x8(float *a, float *b, float *c) {
+  uint32_t *x = reinterpret_cast<uint32_t *>(a), *y = reinterpret_cast<uint32_t *>(b),
+           *z = reinterpret_cast<uint32_t *>(c);
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(x[0]), "+r"(x[1]), "+r"(x[2]), "+r"(x[3]), "+r"(x[4]), "+r"(x[5]),
+                 "+r"(x[6]), "+r"(x[7]), "+r"(y[0]), "+r"(y[1]), "+r"(y[2]), "+r"(y[3]),
+                 "+r"(y[4]), "+r"(y[5]), "+r"(y[6]), "+r"(y[7]), "+r"(z[0]), "+r"(z[1]),
+                 "+r"(z[2]), "+r"(z[3]), "+r"(z[4]), "+r"(z[5]), "+r"(z[6]), "+r"(z[7])
+               :
+               : "memory");
+}
+
+// Exchange area of the folded-column epilogue inside the epilogue staging
+// region (after the bias and the per-warp transpose rows): per tile parity
+// 32 entries (group of 32 positions x 8-channel chunk) of 24 floats: Y's
+// second column group at the group's lane 0, its third at lanes 0 and 1.
+constexpr uint32_t HS_XCH_OFF = 1024 + EPI_WARPS * 1024;
+static_assert(HS_XCH_OFF + 2 * 32 * 24 * 4 <= EPI_BYTES, "folded-column exchange");
+
+// Epilogue of the folded-column form (UmmaGeom::hs). Accumulator column
+// kw*OCP + oc of M block mb holds Y[p][kw][oc] for position p = tile start +
+// mb*128 + TMEM lane; out[p][oc] = Y[p][0][oc] + Y[p+1][1][oc] + Y[p+2][2][oc].
+// Warp w reads TMEM lane quadrant q = w % 4 (positions 32q..32q+31 of every
+// M block). The tile's 8 items (M block, 8-channel chunk) go two to each of
+// the four warps of a quadrant. For an item a lane loads its position's
+// three 8-column groups; the next positions' values come by warp shuffles,
+// and lanes 30 and 31 take them from the next 32-position group's lanes 0
+// and 1, which that group's warp publishes in shared memory (waited for on
+// an mbarrier per tile parity, bounded like every wait here). Outputs:
+// the consumer's re-laid input (one 16-byte slot per position), NCHW through
+// a per-warp transpose (16-byte runs of 8 positions), or 2-byte NCHW stores;
+// residual adds and channel splits in the NCHW paths.
+template <int ACT_T, int NT_C, int G_C>
+__device__ __forceinline__ void hsum_epilogue(const UmmaGeom &g, uint32_t tmem,
+                                              const __half *__restrict__ bias,
+                                              __half *__restrict__ out, uint8_t *sE,
+                                              uint64_t *accf, uint64_t *acce, uint64_t *xbar,
+                                              int warp, int lane) {
+  constexpr int OCP = NT_C == 32 ? 8 : NT_C / 3;
+  constexpr int NCHUNK = OCP / 8;
+  constexpr int ACC_COLS = G_C * NT_C;
+  static_assert(G_C * NCHUNK == 8, "two items per epilogue warp");
+  const int ew = warp - EPI_WARP0;
+  const int q = warp & 3, cq = ew / 4;
+  const size_t plane = size_t(g.OH) * g.OW;
+  float *sbias = reinterpret_cast<float *>(sE);
+  for (int i = threadIdx.x - EPI_WARP0 * 32; i < NT_C; i += EPI_WARPS * 32)
+    sbias[i] = (g.has_bias && i < g.OC) ? __half2float(bias[i]) : 0.f;
+  asm volatile("bar.sync 1, %0;" ::"r"(EPI_WARPS * 32) : "memory");
+  uint16_t *tstage = reinterpret_cast<uint16_t *>(sE + 1024 + ew * 1024);
+  float *xch = reinterpret_cast<float *>(sE + HS_XCH_OFF);
+  const bool tvec = g.tvec != 0;
+  int it = 0;
+  [[maybe_unused]] unsigned long long ph_wait = 0, ph_ld = 0, ph_x = 0, ph_out = 0;
+  for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++it) {
+    const int acc = it & 1, use_acc = it >> 1;
+    int b, oct;
+    long long p0;
+    tile_coords(g, t, b, p0, oct);
+    WGX_PROF_T(th0);
+    if (!mbar_wait(smem_u32(&accf[acc]), use_acc & 1)) {
+      if (lane == 0) atomicOr(g.err, kErrEpilogueTimeout);
+      break;
+    }
+    WGX_PROF_ADD(ph_wait, th0);
+    WGX_PROF_T(th1);
+    tc_fence_after();
+    float y[2][3][8];
+    const uint32_t tq = tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * ACC_COLS);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int item = cq + 4 * k, mb = item / NCHUNK, ch = item % NCHUNK;
+#pragma unroll
+      for (int kw = 0; kw < 3; ++kw)
+        tmem_ld8_nowait(tq + uint32_t(mb * NT_C + kw * OCP + ch * 8), y[k][kw]);
+    }
+    tmem_wait_3x8(y[0][0], y[0][1], y[0][2]);
+    tmem_wait_3x8(y[1][0], y[1][1], y[1][2]);
+    WGX_PROF_ADD(ph_ld, th1);
+    // the accumulator is free again
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
+    // publish what the previous group's lanes 30 and 31 need
+    float *xb = xch + (it & 1) * 32 * 24;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int item = cq + 4 * k, mb = item / NCHUNK, ch = item % NCHUNK;
+      float *e = xb + ((mb * 4 + q) * NCHUNK + ch) * 24;
+      if (lane == 0) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          e[j] = y[k][1][j];
+          e[8 + j] = y[k][2][j];
+        }
+      } else if (lane == 1) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) e[16 + j] = y[k][2][j];
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&xbar[it & 1]));
+    WGX_PROF_T(th2);
+    if (!mbar_wait(smem_u32(&xbar[it & 1]), (it >> 1) & 1)) {
+      if (lane == 0) atomicOr(g.err, kErrEpilogueTimeout);
+      break;
+    }
+    WGX_PROF_ADD(ph_x, th2);
+    WGX_PROF_T(th3);
+    // sums: own column group 0 + next position's group 1 + the one after's
+    // group 2; lanes 30 and 31 patch theirs from the next group's entry
+    float v[2][8];
+    int mbk[2], chk[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int item = cq + 4 * k;
+      mbk[k] = item / NCHUNK;
+      chk[k] = item % NCHUNK;
+      float a1[8], a2[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        a1[j] = __shfl_down_sync(0xffffffffu, y[k][1][j], 1);
+        a2[j] = __shfl_down_sync(0xffffffffu, y[k][2][j], 2);
+      }
+      if (lane >= 30) {
+        // the next 32 positions: quadrant q + 1 of this M block, or quadrant
+        // 0 of the next (none after the tile's last group, whose lanes 30
+        // and 31 lie past the tile's outputs)
+        const int mb = mbk[k];
+        const int ngrp = q < 3 ? mb * 4 + q + 1 : (mb + 1 < G_C ? (mb + 1) * 4 : -1);
+        const float4 *e4 =
+            reinterpret_cast<const float4 *>(xb + (ngrp < 0 ? 0 : (ngrp * NCHUNK + chk[k]) * 24));
+        if (lane == 31) {
+          const float4 p0v = e4[0], p1v = e4[1], p4v = e4[4], p5v = e4[5];
+          a1[0] = p0v.x, a1[1] = p0v.y, a1[2] = p0v.z, a1[3] = p0v.w;
+          a1[4] = p1v.x, a1[5] = p1v.y, a1[6] = p1v.z, a1[7] = p1v.w;
+          a2[0] = p4v.x, a2[1] = p4v.y, a2[2] = p4v.z, a2[3] = p4v.w;
+          a2[4] = p5v.x, a2[5] = p5v.y, a2[6] = p5v.z, a2[7] = p5v.w;
+        } else {
+          const float4 p2v = e4[2], p3v = e4[3];
+          a2[0] = p2v.x, a2[1] = p2v.y, a2[2] = p2v.z, a2[3] = p2v.w;
+          a2[4] = p3v.x, a2[5] = p3v.y, a2[6] = p3v.z, a2[7] = p3v.w;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[k][j] = y[k][0][j] + a1[j] + a2[j];
+    }
+    uint32_t pr[2][4];
+    int ohk[2], owk[2];
+    bool validk[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int oc0 = chk[k] * 8;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        pr[k][j] = epi_act2<ACT_T>(v[k][2 * j], v[k][2 * j + 1], sbias[oc0 + 2 * j],
+                                   sbias[oc0 + 2 * j + 1], g.lo, g.hi);
+      const int i = mbk[k] * 128 + q * 32 + lane;
+      const int pos = int(p0) + i;
+      ohk[k] = pos / g.Wp;
+      owk[k] = pos - ohk[k] * g.Wp;
+      validk[k] = i < g.tile_stride && ohk[k] < g.OH && owk[k] < g.OW;
+    }
+    if (g.omode) {
+      // 8 channels of one position: one slot of the consumer's input
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int oc0 = chk[k] * 8;
+        if (validk[k] && oc0 < g.OC) {
+          uint4 *slot = xs_slot(g, b, oc0, ohk[k], owk[k]);
+          if (slot) *slot = make_uint4(pr[k][0], pr[k][1], pr[k][2], pr[k][3]);
+        }
+      }
+    } else if (tvec) {
+      // [item][channel][32 positions] through the warp's staging rows; lane
+      // -> channel lane / 4 of each item, positions 8 * (lane % 4) .. + 7
+      // (Wp % 8 == 0 and OW % 8 == 0: an 8-group is entirely valid or
+      // entirely padding; tile_stride % 8 == 0: entirely inside or past the
+      // tile's outputs)
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          tstage[(k * 8 + 2 * j) * 32 + lane] = uint16_t(pr[k][j] & 0xFFFFu);
+          tstage[(k * 8 + 2 * j + 1) * 32 + lane] = uint16_t(pr[k][j] >> 16);
+        }
+      __syncwarp();
+      const int row = lane >> 2, part = lane & 3;
+      uint4 val[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) val[k] = reinterpret_cast<const uint4 *>(tstage)[(k * 8 + row) * 4 + part];
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        // (oh, ow) of the group's first position, from the lane holding it
+        const int oh8 = __shfl_sync(0xffffffffu, ohk[k], part * 8);
+        const int ow8 = __shfl_sync(0xffffffffu, owk[k], part * 8);
+        const int i8 = mbk[k] * 128 + q * 32 + part * 8;
+        const int oc = chk[k] * 8 + row;
+        if (i8 < g.tile_stride && oh8 < g.OH && ow8 < g.OW && oc < g.OC) {
+          const size_t off = size_t(oh8) * g.OW + ow8;
+          uint4 w4 = val[k];
+          if (g.resid) {
+            const uint4 rr = *reinterpret_cast<const uint4 *>(
+                g.resid + (size_t(b) * g.OC + oc) * plane + off);
+            w4 = make_uint4(add_resid2(w4.x, rr.x), add_resid2(w4.y, rr.y),
+                            add_resid2(w4.z, rr.z), add_resid2(w4.w, rr.w));
+          }
+          *reinterpret_cast<uint4 *>(out_plane(g, out, b, oc, plane) + off) = w4;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        if (!validk[k]) continue;
+        const size_t posoff = size_t(ohk[k]) * g.OW + owk[k];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int oc = chk[k] * 8 + 2 * j;
+          uint32_t vv = pr[k][j];
+          if (g.resid) {
+            const __half *rp = g.resid + size_t(b) * g.OC * plane + posoff;
+            const uint32_t lo =
+                oc < g.OC ? uint32_t(__half_as_ushort(rp[size_t(oc) * plane])) : 0u;
+            const uint32_t hi =
+                oc + 1 < g.OC ? uint32_t(__half_as_ushort(rp[size_t(oc + 1) * plane])) : 0u;
+            vv = add_resid2(vv, lo | (hi << 16));
+          }
+          const __half2 h2 = *reinterpret_cast<const __half2 *>(&vv);
+          if (oc < g.OC) out_plane(g, out, b, oc, plane)[posoff] = __low2half(h2);
+          if (oc + 1 < g.OC) out_plane(g, out, b, oc + 1, plane)[posoff] = __high2half(h2);
+        }
+      }
+    }
+    WGX_PROF_ADD(ph_out, th3);
+  }
+#ifdef WGX_PROF
+  if (warp == EPI_WARP0 && lane == 0) {
+    g_umma_prof[blockIdx.x][4] = ph_wait;
+    g_umma_prof[blockIdx.x][8] = ph_ld;
+    g_umma_prof[blockIdx.x][9] = ph_x;
+    g_umma_prof[blockIdx.x][10] = ph_out;
+  }
+#endif
 }
 
 // ------------------------------------------------------------ main kernel
@@ -927,7 +1274,7 @@ __device__ __forceinline__ void tile_coords(const UmmaGeom &g, int t, int &b, lo
 // and the packed weights the B operand, with no change to either layout.
 // EXT: NCHW output with a residual add and/or a channel split (separate
 // instantiations keep the common epilogue free of those branches).
-template <int KW_T, int ACT_T, int TRANS, int EXT>
+template <int KW_T, int ACT_T, int TRANS, int EXT, int HS = 0>
 __global__ void __launch_bounds__(THREADS, 1)
     umma_conv_kernel(const UmmaGeom g, const uint8_t *__restrict__ xs,
                      const uint8_t *__restrict__ wpk, const __half *__restrict__ bias,
@@ -937,7 +1284,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   // (TRANS = 17 / 33: N = 16 / 32 with 4 M blocks, for planes of at most
   // 512 positions)
   constexpr int NT_C = TRANS > 0 ? (TRANS & ~1) : UN;
-  constexpr int G_C = TRANS == 0 ? 1 : (TRANS == 64 || (TRANS & 1)) ? 4 : 8;
+  // folded filter columns (HS > 0): N = 32 / 48 / 96 / 192 with 8 / 4 / 2 / 1 M blocks
+  constexpr int G_C = HS > 0 ? (NT_C == 32 ? 8 : NT_C == 48 ? 4 : NT_C == 96 ? 2 : 1)
+                      : TRANS == 0 ? 1 : (TRANS == 64 || (TRANS & 1)) ? 4 : 8;
   constexpr int LG_NT = NT_C == 16 ? 4 : NT_C == 32 ? 5 : 6;
   // activation stages first, on a 1024-byte boundary (128-byte swizzle atoms
   // of the direct mode); stage sizes are multiples of 1024 bytes there
@@ -951,7 +1300,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t *bars = reinterpret_cast<uint64_t *>(sE + EPI_BYTES);
   uint64_t *full = bars, *empty = bars + S;
   uint64_t *accf = bars + 2 * S, *acce = accf + 2, *wbar = acce + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(wbar + 1);
+  uint64_t *xbar = wbar + kWParts;  // folded-column epilogue exchange, per tile parity
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xbar + 2);
+  // resident weight pieces: piece j holds stages [j*n/P, (j+1)*n/P)
+  const int wparts = g.n_kstages < kWParts ? g.n_kstages : kWParts;
   // generic staging: (activation, weight) descriptor offsets of every MMA
   // group of a stage, in 16-byte units (written and read by the MMA thread)
   uint2 *grp_off = reinterpret_cast<uint2 *>(tmem_slot + 4);
@@ -968,7 +1320,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(smem_u32(&accf[a]), 1);
       mbar_init(smem_u32(&acce[a]), EPI_WARPS);
     }
-    mbar_init(smem_u32(wbar), 1);
+    for (int j = 0; j < kWParts; ++j) mbar_init(smem_u32(&wbar[j]), 1);
+    for (int j = 0; j < 2; ++j) mbar_init(smem_u32(&xbar[j]), EPI_WARPS);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -989,12 +1342,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       // ---------------- producer: bulk copies of weights + activation rows
       const uint32_t b_copy = uint32_t(g.R) * 16;
       if (g.resident) {
-        const uint32_t wb = smem_u32(wbar);
-        mbar_expect_tx(wb, g.w_region_bytes);
-        bulk_g2s(smem_u32(sW), wpk, g.w_region_bytes, wb);
+        for (int j = 0; j < wparts; ++j) {
+          const uint32_t s0 = uint32_t(j * g.n_kstages / wparts);
+          const uint32_t s1 = uint32_t((j + 1) * g.n_kstages / wparts);
+          const uint32_t wb = smem_u32(&wbar[j]);
+          mbar_expect_tx(wb, (s1 - s0) * g.a_stage_bytes);
+          bulk_g2s(smem_u32(sW + size_t(s0) * g.a_stage_bytes), wpk + size_t(s0) * g.a_stage_bytes,
+                   (s1 - s0) * g.a_stage_bytes, wb);
+        }
       }
       int slot = S - 1, use = -1;  // pipeline slot and its use count, advanced per loaded stage
       bool ok = true;
+      [[maybe_unused]] unsigned long long pr_empty = 0;
       for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x) {
         int b, oct;
         long long p0;
@@ -1006,11 +1365,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             slot = 0;
             ++use;
           }
+          WGX_PROF_T(tw0);
           if (use > 0 && !mbar_wait(smem_u32(&empty[slot]), (use - 1) & 1)) {
             atomicOr(g.err, kErrLoadTimeout);
             ok = false;
             break;
           }
+          WGX_PROF_ADD(pr_empty, tw0);
           const int khg = sw.khg, cbk = sw.cbk;
           const uint32_t fb = smem_u32(&full[slot]);
           mbar_expect_tx(fb, (g.resident ? 0u : g.a_stage_bytes) + g.chunks * b_copy);
@@ -1042,10 +1403,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
+#ifdef WGX_PROF
+      g_umma_prof[blockIdx.x][0] = pr_empty;
+#endif
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
+      WGX_PROF_T(tm_start);
+      [[maybe_unused]] unsigned long long pm_acce = 0, pm_full = 0, pm_issue = 0, pm_tiles = 0;
       // (a = packed weights, b = staged activation rows, whichever MMA
       // operand slot they take)
       const uint32_t idesc = (1u << 4)                                  // D = f32
@@ -1054,10 +1420,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t a_lbo = uint32_t(g.wrows) * 16;        // chunk plane of the weights
       const uint32_t b_lbo = uint32_t(g.R_alloc) * 16;      // chunk plane of the activations
       bool ok = true;
-      if (g.resident && !mbar_wait(smem_u32(wbar), 0)) {
-        atomicOr(g.err, kErrMmaTimeout);
-        ok = false;
-      }
+      // resident weight pieces waited for so far (first tile only)
+      int wdone = g.resident ? 0 : wparts;
       // per-MMA start-address offsets (16-byte units) of the specialised path:
       // MMA i = (kw, ks) reads A tap kw chunk pair ks, B shifted kw*dW rows
       uint32_t a_off[KW_T > 0 ? 2 * KW_T : 1], b_off[KW_T > 0 ? 2 * KW_T : 1];
@@ -1098,11 +1462,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       int it = 0, slot = S - 1, use = -1;
       for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x, ++it) {
         const int acc = it & 1, use_acc = it >> 1;
+        WGX_PROF_T(ta0);
         if (use_acc > 0 && !mbar_wait(smem_u32(&acce[acc]), (use_acc - 1) & 1)) {
           atomicOr(g.err, kErrMmaTimeout);
           ok = false;
           break;
         }
+        WGX_PROF_ADD(pm_acce, ta0);
+#ifdef WGX_PROF
+        ++pm_tiles;
+#endif
         tc_fence_after();
         const uint32_t d = tmem + uint32_t(acc * g.acc_cols);
         uint32_t acc_on = 0;  // the tile's accumulator already holds a product
@@ -1110,15 +1479,37 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int s = 0; s < g.n_kstages; ++s, sw.next(g)) {
           const uint32_t tmask = sw.taps(g);
           if (!tmask) continue;  // all-zero weights: not loaded, no MMA
+          while (wdone < wparts && wdone * g.n_kstages / wparts <= s) {
+            if (!mbar_wait(smem_u32(&wbar[wdone]), 0)) {
+              atomicOr(g.err, kErrMmaTimeout);
+              ok = false;
+              break;
+            }
+            ++wdone;
+          }
+          if (!ok) break;
           if (++slot == S) {
             slot = 0;
             ++use;
           }
+          WGX_PROF_T(tf0);
           if (!mbar_wait(smem_u32(&full[slot]), use & 1)) {
             atomicOr(g.err, kErrMmaTimeout);
             ok = false;
             break;
           }
+          WGX_PROF_ADD(pm_full, tf0);
+#ifdef WGX_PROF
+          // issue time: from the data's arrival to the stage's commit
+          // (measured at the next stage's wait start: approximated by the
+          // commit below)
+          const long long ti0 = clock64();
+          struct IssueTimer {
+            unsigned long long &acc;
+            long long t0;
+            __device__ ~IssueTimer() { acc += (unsigned long long)(clock64() - t0); }
+          } issue_timer{pm_issue, ti0};
+#endif
           tc_fence_after();
           const uint32_t a_base =
               smem_u32(sW + size_t(g.resident ? s : slot) * g.a_stage_bytes);
@@ -1241,8 +1632,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (ok) mma_commit(smem_u32(&accf[acc]));
       }
+#ifdef WGX_PROF
+      g_umma_prof[blockIdx.x][1] = pm_acce;
+      g_umma_prof[blockIdx.x][2] = pm_full;
+      g_umma_prof[blockIdx.x][3] = pm_issue;
+      g_umma_prof[blockIdx.x][6] = (unsigned long long)(clock64() - tm_start);
+      g_umma_prof[blockIdx.x][7] = pm_tiles;
+#endif
     }
-  } else if (warp >= EPI_WARP0 && TRANS) {
+  } else if (warp >= EPI_WARP0) {
+  if constexpr (HS > 0) {
+    hsum_epilogue<ACT_T, NT_C, G_C>(g, tmem, bias, out, sE, accf, acce, xbar, warp, lane);
+  } else if constexpr (TRANS > 0) {
     // ---------------- epilogue (positions on TMEM lanes): warp w reads lane
     // quadrant w % 4 (32 positions of every M block) and 32 of the 128
     // accumulator columns; column c is channel c % NT of M block c / NT.
@@ -1263,15 +1664,25 @@ __global__ void __launch_bounds__(THREADS, 1)
     const bool tvec = g.tvec != 0;
     float r[EXT ? 16 : 32];
     int it = 0;
+    [[maybe_unused]] unsigned long long pe_wait = 0, pe_work = 0;
+    [[maybe_unused]] long long te_mark = 0;
     for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1, use_acc = it >> 1;
       int b, oct;
       long long p0;
       tile_coords(g, t, b, p0, oct);
+#ifdef WGX_PROF
+      if (warp == EPI_WARP0 && lane == 0 && it > 0) pe_work += (unsigned long long)(clock64() - te_mark);
+#endif
+      WGX_PROF_T(te0);
       if (!mbar_wait(smem_u32(&accf[acc]), use_acc & 1)) {
         if (lane == 0) atomicOr(g.err, kErrEpilogueTimeout);
         break;
       }
+      WGX_PROF_ADD(pe_wait, te0);
+#ifdef WGX_PROF
+      te_mark = clock64();
+#endif
       tc_fence_after();
       if constexpr (EXT) {
       // the warp's acc_cols / 4 columns, 16 at a time (16 columns always lie
@@ -1458,7 +1869,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       }
     }
-  } else if (warp >= EPI_WARP0) {
+#ifdef WGX_PROF
+    if (warp == EPI_WARP0 && lane == 0) {
+      if (it > 0) pe_work += (unsigned long long)(clock64() - te_mark);
+      g_umma_prof[blockIdx.x][4] = pe_wait;
+      g_umma_prof[blockIdx.x][5] = pe_work;
+    }
+#endif
+  } else {
     // ---------------- epilogue: TMEM -> bias + activation -> NCHW fp16.
     // Warp w reads TMEM lane quadrant w % 4 (32 output channels) and one
     // quarter (64 columns) of the accumulator. Per block of 16 positions it
@@ -1622,6 +2040,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
+  }
   }
   tc_fence_before();
   __syncthreads();
@@ -1853,7 +2272,8 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
                                            WGX_UMMA_EXT(64), WGX_UMMA_EXT(17), WGX_UMMA_EXT(33)};
 #undef WGX_UMMA_EXT
   const int nt_idx = !g.trans ? 0 : g.NT == 64 ? 3 : (g.NT == 16 ? 1 : 2) + (g.G == 4 ? 3 : 0);
-  if (g.trans && g.NT != 16 && g.NT != 32 && g.NT != 64) fail("conv2d: bad transposed tile");
+  if (g.trans && !g.hs && g.NT != 16 && g.NT != 32 && g.NT != 64)
+    fail("conv2d: bad transposed tile");
   // 16-byte stores of the transposed epilogue (split pieces and residual
   // loads included)
   {
@@ -1866,9 +2286,23 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   // residual adds and split outputs the vector path cannot store: the EXT
   // epilogue
   const bool ext = (g.resid != nullptr || g.nout > 0) && !g.tvec;
-  KernelFn kern = ext ? table_ext[nt_idx][act_idx] : table[nt_idx][kw_idx][act_idx];
-  const int kidx = ext ? 126 + nt_idx * 3 + act_idx : (nt_idx * 7 + kw_idx) * 3 + act_idx;
-  static bool attr_set[64][144] = {};
+  // folded filter columns: N = 32 / 48 / 96 / 192, generic MMA loop, own
+  // epilogue (residual adds and splits included)
+#define WGX_UMMA_HS(T) \
+  { umma_conv_kernel<0, 0, T, 0, 1>, umma_conv_kernel<0, 1, T, 0, 1>, umma_conv_kernel<0, 2, T, 0, 1> }
+  static const KernelFn table_hs[4][3] = {WGX_UMMA_HS(32), WGX_UMMA_HS(48), WGX_UMMA_HS(96),
+                                          WGX_UMMA_HS(192)};
+#undef WGX_UMMA_HS
+  const int hs_idx = g.NT == 32 ? 0 : g.NT == 48 ? 1 : g.NT == 96 ? 2 : 3;
+  if (g.hs && (g.NT != 32 && g.NT != 48 && g.NT != 96 && g.NT != 192))
+    fail("conv2d: bad folded-column tile");
+  KernelFn kern = g.hs  ? table_hs[hs_idx][act_idx]
+                  : ext ? table_ext[nt_idx][act_idx]
+                        : table[nt_idx][kw_idx][act_idx];
+  const int kidx = g.hs  ? 144 + hs_idx * 3 + act_idx
+                   : ext ? 126 + nt_idx * 3 + act_idx
+                         : (nt_idx * 7 + kw_idx) * 3 + act_idx;
+  static bool attr_set[64][160] = {};
   if (dev < 64 && !attr_set[dev][kidx]) {
     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(SMEM_MAX)),
@@ -1887,3 +2321,13 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
 }
 
 }  // namespace wgx
+
+#ifdef WGX_PROF
+// Reads (and clears) the per-CTA role counters of the last launches.
+extern "C" __attribute__((visibility("default"))) int wgx_umma_prof_read(unsigned long long *out) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return 1;
+  if (cudaMemcpyFromSymbol(out, wgx::g_umma_prof, sizeof(wgx::g_umma_prof)) != cudaSuccess) return 1;
+  static unsigned long long zero[256][12] = {};
+  return cudaMemcpyToSymbol(wgx::g_umma_prof, zero, sizeof(zero)) != cudaSuccess;
+}
+#endif
