@@ -105,6 +105,11 @@ struct UmmaGeom {
   // last 8 positions only feed its own outputs, so tiles advance by
   // tile_pos - 8.
   int hs, ocp;
+  // position -> padded row: pos / Wp = __umulhi(pos, wp_magic) with
+  // wp_magic = ceil(2^32 / Wp), exact for every position the kernel forms
+  // (checked on the host: pos_max * (wp_magic * Wp - 2^32) < 2^32); 0 =
+  // plain division
+  uint32_t wp_magic;
   int wrows;                         // packed weight rows per oc tile (UM or NT)
   int acc_cols;                      // TMEM columns per accumulator
   int bk, chunks;                    // channels per stage, 16-byte chunks per stage
@@ -284,6 +289,13 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans,
   }
   g.tile_stride = hs ? g.tile_pos - 8 : g.tile_pos;
   g.tiles_per_img = int((p_out + g.tile_stride - 1) / g.tile_stride);
+  g.wp_magic = 0;
+  if (g.Wp >= 2) {
+    const uint64_t m = ((1ull << 32) + uint64_t(g.Wp) - 1) / uint64_t(g.Wp);
+    const uint64_t e = m * uint64_t(g.Wp) - (1ull << 32);
+    const uint64_t pos_max = uint64_t(g.tiles_per_img) * g.tile_stride + g.tile_pos;
+    if (m < (1ull << 32) && pos_max * e < (1ull << 32)) g.wp_magic = uint32_t(m);
+  }
   g.total_tiles = g.tiles_per_img * g.n_oct * g.B;
   long long r = g.tile_pos + (long long)(khs - 1) * g.dH * g.Wp + (long long)(g.KW - 1) * g.dW;
   g.R = r > (1 << 20) ? (1 << 20) : int(r);
@@ -919,6 +931,11 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// pos / Wp for a position of the padded plane (see UmmaGeom::wp_magic)
+__device__ __forceinline__ int div_wp(const UmmaGeom &g, int pos) {
+  return g.wp_magic ? int(__umulhi(uint32_t(pos), g.wp_magic)) : pos / g.Wp;
+}
+
 // The consumer's re-layout slot (16 bytes: virtual channels vc..vc+7 of one
 // staged position) that holds output channels [c, c+8) of image b at output
 // position (oh, ow), or null when the consumer stages no such slot (an input
@@ -929,6 +946,12 @@ __device__ __forceinline__ uint4 *xs_slot(const UmmaGeom &g, int b, int c, int o
     hp = oh + g.opH;
     wp = ow + g.opW;
     vc = c;
+  } else if (g.osH == 2 && g.osW == 2) {
+    const int iph = g.ophase_h[oh & 1], ipw = g.ophase_w[ow & 1];
+    if (iph < 0 || ipw < 0) return nullptr;
+    vc = (iph * g.onphW + ipw) * g.oxIC + c;
+    hp = (oh >> 1) + g.opH;
+    wp = (ow >> 1) + g.opW;
   } else {
     const int iph = g.ophase_h[oh % g.osH], ipw = g.ophase_w[ow % g.osW];
     if (iph < 0 || ipw < 0) return nullptr;
@@ -1178,7 +1201,7 @@ __device__ __forceinline__ void hsum_epilogue(const UmmaGeom &g, uint32_t tmem,
                                    sbias[oc0 + 2 * j + 1], g.lo, g.hi);
       const int i = mbk[k] * 128 + q * 32 + lane;
       const int pos = int(p0) + i;
-      ohk[k] = pos / g.Wp;
+      ohk[k] = div_wp(g, pos);
       owk[k] = pos - ohk[k] * g.Wp;
       validk[k] = i < g.tile_stride && ohk[k] < g.OH && owk[k] < g.OW;
     }
@@ -1699,7 +1722,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         const int mb = c0 >> LG_NT;
         const int pos = int(p0) + mb * 128 + q * 32 + lane;
-        const int oh = pos / g.Wp, ow = pos - oh * g.Wp;
+        const int oh = div_wp(g, pos), ow = pos - oh * g.Wp;
         const bool okp = oh < g.OH && ow < g.OW;
         const int oc0 = c0 & (NT_C - 1);  // first of this lane's 16 channels
         // columns 2j, 2j+1: channels oc0+2j, oc0+2j+1 of one position
@@ -1778,8 +1801,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int mb0 = c0 >> LG_NT, mb1 = (c0 + CW - 1) >> LG_NT;
         const int pos_a = int(p0) + mb0 * 128 + q * 32 + lane;
         const int pos_b = int(p0) + mb1 * 128 + q * 32 + lane;
-        const int oh_a = pos_a / g.Wp, ow_a = pos_a - oh_a * g.Wp;
-        const int oh_b = pos_b / g.Wp, ow_b = pos_b - oh_b * g.Wp;
+        const int oh_a = div_wp(g, pos_a), ow_a = pos_a - oh_a * g.Wp;
+        const int oh_b = div_wp(g, pos_b), ow_b = pos_b - oh_b * g.Wp;
         const bool ok_a = oh_a < g.OH && ow_a < g.OW, ok_b = oh_b < g.OH && ow_b < g.OW;
         __half *dst_a = base + size_t(oh_a) * g.OW + ow_a;
         __half *dst_b = base + size_t(oh_b) * g.OW + ow_b;
@@ -1817,7 +1840,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               const int c = c0 + hf * 16 + row;
               const int oc = c & (NT_C - 1);
               const int pos = int(p0) + (c >> LG_NT) * 128 + q * 32 + part * 8;
-              const int oh = pos / g.Wp, ow = pos - oh * g.Wp;
+              const int oh = div_wp(g, pos), ow = pos - oh * g.Wp;
               if (oc < g.OC && oh < g.OH && ow < g.OW) {
                 const size_t off = size_t(oh) * g.OW + ow;
                 uint4 v = val;
@@ -1913,7 +1936,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __half *rowp = out + (size_t(b) * g.OC + oc0 + rsel) * plane;
       // (oh, ow) of this lane's first position pair; advanced per block
       const int pos0 = int(p0) + colh * WCOLS + 2 * sub;
-      int oh = pos0 / g.Wp, ow = pos0 - oh * g.Wp;
+      int oh = div_wp(g, pos0), ow = pos0 - oh * g.Wp;
       constexpr int NBLK = WCOLS / EPI_COLS;
       // TMEM reads are software-pipelined: block blk + 1 is requested right
       // after block blk has arrived, so its latency hides behind blk's stores
@@ -1956,7 +1979,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               wv[e] = lo | (hi << 16);
             }
             const int P = int(p0) + col0 + pos;
-            const int ohh = P / g.Wp, oww = P - ohh * g.Wp;
+            const int ohh = div_wp(g, P), oww = P - ohh * g.Wp;
             const int c = oc0 + grp * 8;
             if (ohh < g.OH && oww < g.OW && c < g.OC) {
               uint4 *slot = xs_slot(g, b, c, ohh, oww);
