@@ -1779,115 +1779,108 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       } else {
-      // the warp's ACC_COLS / 4 columns, in chunks of CW = 32 (16 when the
-      // warp owns only 16: N = 16 with 4 M blocks)
+      // the warp's ACC_COLS / 4 columns in pieces of 16 (each within one M
+      // block, NT >= 16). TMEM reads are software-pipelined: piece h + 1 is
+      // requested as soon as piece h has arrived, so its latency hides
+      // behind piece h's conversion and stores.
       constexpr int ACC_COLS = G_C * NT_C;
-      constexpr int CW = ACC_COLS / 4 < 32 ? ACC_COLS / 4 : 32;
-      constexpr int NCHUNK = ACC_COLS / (4 * CW);
+      constexpr int WC = ACC_COLS / 4;
+      constexpr int NP = WC / 16;
       __half *base = out + size_t(b) * g.OC * plane;
+      float rb[2][16];
+      const uint32_t tw = tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * ACC_COLS + cq * WC);
+      tmem_ld16_async(tw, rb[0]);
 #pragma unroll
-      for (int h = 0; h < NCHUNK; ++h) {
-        const int c0 = cq * (ACC_COLS / 4) + h * CW;
-        if constexpr (CW == 32)
-          tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * ACC_COLS + c0), r);
-        else
-          tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * ACC_COLS + c0), r);
-        if (h == NCHUNK - 1) {
+      for (int h = 0; h < NP; ++h) {
+        float *rr = rb[h & 1];
+        tmem_wait16(rr);
+        if (h + 1 < NP) tmem_ld16_async(tw + uint32_t((h + 1) * 16), rb[(h + 1) & 1]);
+        if (h == NP - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
         }
-        // CW columns cover one M block (NT >= CW) or two (NT = 16, CW = 32)
-        const int mb0 = c0 >> LG_NT, mb1 = (c0 + CW - 1) >> LG_NT;
-        const int pos_a = int(p0) + mb0 * 128 + q * 32 + lane;
-        const int pos_b = int(p0) + mb1 * 128 + q * 32 + lane;
-        const int oh_a = div_wp(g, pos_a), ow_a = pos_a - oh_a * g.Wp;
-        const int oh_b = div_wp(g, pos_b), ow_b = pos_b - oh_b * g.Wp;
-        const bool ok_a = oh_a < g.OH && ow_a < g.OW, ok_b = oh_b < g.OH && ow_b < g.OW;
-        __half *dst_a = base + size_t(oh_a) * g.OW + ow_a;
-        __half *dst_b = base + size_t(oh_b) * g.OW + ow_b;
-        // columns j, j+1: channels oc, oc+1 of the same position (NT is even)
-        uint32_t pr[CW / 2];
+        const int c0 = cq * WC + h * 16;
+        const int mb = c0 >> LG_NT;
+        const int oc0 = c0 & (NT_C - 1);  // first of the piece's 16 channels
+        const int pos = int(p0) + mb * 128 + q * 32 + lane;
+        const int oh = div_wp(g, pos), ow = pos - oh * g.Wp;
+        const bool okp = oh < g.OH && ow < g.OW;
+        // columns 2j, 2j+1: channels oc0 + 2j, oc0 + 2j + 1 of this lane's position
+        uint32_t pr[8];
 #pragma unroll
-        for (int j = 0; j < CW; j += 2) {
-          const int oc = (c0 + j) & (NT_C - 1);
-          const float2 bb = reinterpret_cast<const float2 *>(sbias)[oc >> 1];
-          pr[j / 2] = epi_act2<ACT_T>(r[j], r[j + 1], bb.x, bb.y, g.lo, g.hi);
+        for (int j = 0; j < 8; ++j) {
+          const float2 bb = reinterpret_cast<const float2 *>(sbias)[(oc0 >> 1) + j];
+          pr[j] = epi_act2<ACT_T>(rr[2 * j], rr[2 * j + 1], bb.x, bb.y, g.lo, g.hi);
         }
         if (tvec) {
-          // transpose through the warp's staging rows, 16 columns a round:
-          // lanes l, l^1 swap halves so that even lanes hold positions
-          // (l, l+1) of column 2k and odd lanes positions (l-1, l) of column
-          // 2k+1; row = column (64 bytes: 32 positions). Then lane -> row
-          // lane/4 (+8), 8 positions from (lane%4)*8: one 16-byte store of 8
-          // consecutive outputs (Wp % 8 == 0: an 8-group never leaves its
-          // output row; OW % 8 == 0: it is entirely valid or entirely padding)
+          // transpose through the warp's staging rows: lanes l, l^1 swap
+          // halves so that even lanes hold positions (l, l+1) of column 2k
+          // and odd lanes positions (l-1, l) of column 2k+1; row = column
+          // (64 bytes: 32 positions). Then lane -> row lane/4 (+8), 8
+          // positions from (lane%4)*8: one 16-byte store of 8 consecutive
+          // outputs (Wp % 8 == 0: an 8-group never leaves its output row;
+          // OW % 8 == 0: it is entirely valid or entirely padding)
 #pragma unroll
-          for (int hf = 0; hf < CW / 16; ++hf) {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const uint32_t v = pr[hf * 8 + k];
-              const uint32_t o = __shfl_xor_sync(0xffffffffu, v, 1);
-              const bool odd = lane & 1;
-              tstage[(2 * k + (odd ? 1 : 0)) * 16 + (lane >> 1)] =
-                  odd ? __byte_perm(o, v, 0x7632) : __byte_perm(v, o, 0x5410);
-            }
-            __syncwarp();
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-              const int row = (lane >> 2) + 8 * k, part = lane & 3;
-              const uint4 val = reinterpret_cast<const uint4 *>(tstage)[row * 4 + part];
-              const int c = c0 + hf * 16 + row;
-              const int oc = c & (NT_C - 1);
-              const int pos = int(p0) + (c >> LG_NT) * 128 + q * 32 + part * 8;
-              const int oh = div_wp(g, pos), ow = pos - oh * g.Wp;
-              if (oc < g.OC && oh < g.OH && ow < g.OW) {
-                const size_t off = size_t(oh) * g.OW + ow;
-                uint4 v = val;
-                if (g.resid) {
-                  // residual add after the activation, one rounding (as the
-                  // separate add would compute it)
-                  const uint4 rr = *reinterpret_cast<const uint4 *>(
-                      g.resid + (size_t(b) * g.OC + oc) * plane + off);
-                  v = make_uint4(add_resid2(val.x, rr.x), add_resid2(val.y, rr.y),
-                                 add_resid2(val.z, rr.z), add_resid2(val.w, rr.w));
-                }
-                *reinterpret_cast<uint4 *>(out_plane(g, out, b, oc, plane) + off) = v;
-              }
-            }
-            __syncwarp();
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t v = pr[k];
+            const uint32_t o = __shfl_xor_sync(0xffffffffu, v, 1);
+            const bool odd = lane & 1;
+            tstage[(2 * k + (odd ? 1 : 0)) * 16 + (lane >> 1)] =
+                odd ? __byte_perm(o, v, 0x7632) : __byte_perm(v, o, 0x5410);
           }
+          __syncwarp();
+          const int part = lane & 3;
+          // (oh, ow) of the 8-group's first position, from the lane holding it
+          const int oh8 = __shfl_sync(0xffffffffu, oh, part * 8);
+          const int ow8 = __shfl_sync(0xffffffffu, ow, part * 8);
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int row = (lane >> 2) + 8 * k;
+            const uint4 val = reinterpret_cast<const uint4 *>(tstage)[row * 4 + part];
+            const int oc = oc0 + row;
+            if (oc < g.OC && oh8 < g.OH && ow8 < g.OW) {
+              const size_t off = size_t(oh8) * g.OW + ow8;
+              uint4 v = val;
+              if (g.resid) {
+                // residual add after the activation, one rounding (as the
+                // separate add would compute it)
+                const uint4 rr4 = *reinterpret_cast<const uint4 *>(
+                    g.resid + (size_t(b) * g.OC + oc) * plane + off);
+                v = make_uint4(add_resid2(val.x, rr4.x), add_resid2(val.y, rr4.y),
+                               add_resid2(val.z, rr4.z), add_resid2(val.w, rr4.w));
+              }
+              *reinterpret_cast<uint4 *>(out_plane(g, out, b, oc, plane) + off) = v;
+            }
+          }
+          __syncwarp();
           continue;
         }
+        if (!okp) continue;
         if (g.omode) {
           // 8 consecutive columns = 8 channels of one position: one 16-byte
           // slot; the slot of channel c is that of channel 0 plus c / 8
           // planes (the consumer's channel count is a multiple of 8)
           const size_t pstride = size_t(g.oHp) * g.oWp;
-          uint4 *slot_a = ok_a ? xs_slot(g, b, 0, oh_a, ow_a) : nullptr;
-          uint4 *slot_b = mb1 == mb0 ? slot_a : ok_b ? xs_slot(g, b, 0, oh_b, ow_b) : nullptr;
+          uint4 *slot = xs_slot(g, b, 0, oh, ow);
+          if (slot) {
 #pragma unroll
-          for (int q8 = 0; q8 < CW / 8; ++q8) {
-            const int c = c0 + 8 * q8;
-            const int oc = c & (NT_C - 1);
-            uint4 *slot = (c >> LG_NT) != mb0 ? slot_b : slot_a;
-            if (slot && oc < g.OC)
-              slot[size_t(oc >> 3) * pstride] =
-                  make_uint4(pr[4 * q8], pr[4 * q8 + 1], pr[4 * q8 + 2], pr[4 * q8 + 3]);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < CW; j += 2) {
-            const int c = c0 + j;
-            const int oc = c & (NT_C - 1);
-            const bool second = (c >> LG_NT) != mb0;
-            const __half2 h2 = *reinterpret_cast<const __half2 *>(&pr[j / 2]);
-            if (second ? ok_b : ok_a) {
-              __half *d = (second ? dst_b : dst_a) + size_t(oc) * plane;
-              if (oc < g.OC) d[0] = __low2half(h2);
-              if (oc + 1 < g.OC) d[plane] = __high2half(h2);
+            for (int q8 = 0; q8 < 2; ++q8) {
+              const int oc = oc0 + 8 * q8;
+              if (oc < g.OC)
+                slot[size_t(oc >> 3) * pstride] =
+                    make_uint4(pr[4 * q8], pr[4 * q8 + 1], pr[4 * q8 + 2], pr[4 * q8 + 3]);
             }
           }
+          continue;
+        }
+        __half *d = base + size_t(oh) * g.OW + ow;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int oc = oc0 + 2 * j;
+          const __half2 h2 = *reinterpret_cast<const __half2 *>(&pr[j]);
+          if (oc < g.OC) d[size_t(oc) * plane] = __low2half(h2);
+          if (oc + 1 < g.OC) d[size_t(oc + 1) * plane] = __high2half(h2);
         }
       }
       }
