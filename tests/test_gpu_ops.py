@@ -321,9 +321,10 @@ def test_sigmoid(ctx, shape):
     assert np.max(np.abs(out.numpy().reshape(shape).astype(np.float64) - ref)) <= 1e-3
 
 
-def pool_chain_program(shape, K, n):
+def pool_chain_program(shape, K, n, idx_out=True):
     """n chained max_pool2d_with_indices (K x K, stride 1, same padding), the
-    SPPF spelling; outputs every stage's values and the last indices."""
+    SPPF spelling; outputs every stage's values and (idx_out) the last
+    indices."""
     vals = [{"type": "tensor", "shape": list(shape), "dtype": "float16", "memObjId": 0},
             {"type": "list", "items": [K, K]}, {"type": "list", "items": [1, 1]},
             {"type": "list", "items": [(K - 1) // 2] * 2}, {"type": "list", "items": [1, 1]},
@@ -341,16 +342,22 @@ def pool_chain_program(shape, K, n):
         src = v
     nb = int(np.prod(shape)) * 4
     return {"version": "1", "chain": chain, "values": vals, "inputIds": [0],
-            "outputIds": outs + [outs[-1] + 1],
+            "outputIds": outs + ([outs[-1] + 1] if idx_out else []),
             "memoryPlan": {"pools": [{"id": i, "size": nb} for i in range(1 + 2 * n)]}}
 
 
-@pytest.mark.parametrize("shape,K,n", [((2, 8, 20, 20), 5, 3), ((1, 6, 9, 13), 3, 2)])
-def test_maxpool_cascade_program(ctx, shape, K, n):
+@pytest.mark.parametrize("shape,K,n,idx_out", [((2, 8, 20, 20), 5, 3, True),
+                                               ((1, 6, 9, 13), 3, 2, True),
+                                               ((3, 16, 20, 20), 5, 3, False),
+                                               ((2, 5, 11, 7), 7, 2, False)])
+def test_maxpool_cascade_program(ctx, shape, K, n, idx_out):
+    """(idx_out False: no operator reads the indices and none is a program
+    output, so the cascade writes none and tracks no maximising position.)"""
     x = rnd(shape)
     ys = [empty(ctx, shape, "float16") for _ in range(n)]
     last_idx = empty(ctx, shape, "int32")
-    ctx.recordProgram(pool_chain_program(shape, K, n), b"", [T(ctx, x)] + ys + [last_idx])
+    ctx.recordProgram(pool_chain_program(shape, K, n, idx_out), b"",
+                      [T(ctx, x)] + ys + ([last_idx] if idx_out else []))
     names = ctx.command_names()
     assert sum(nm.endswith("(cascade)") for nm in names) == 1, names
     ctx.submit()
@@ -361,4 +368,5 @@ def test_maxpool_cascade_program(ctx, shape, K, n):
         y, idx = maxpool_ref(cur, (K, K), (1, 1), (p, p), (1, 1), False, True)
         np.testing.assert_array_equal(ys[s].numpy().reshape(shape).astype(np.float32), y)
         cur = y.astype(np.float16)
-    np.testing.assert_array_equal(last_idx.numpy().reshape(shape), idx)
+    if idx_out:
+        np.testing.assert_array_equal(last_idx.numpy().reshape(shape), idx)

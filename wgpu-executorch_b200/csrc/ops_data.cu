@@ -566,17 +566,20 @@ __global__ void __launch_bounds__(256) maxpool_plane_kernel(PoolGeom g, const T 
   }
 }
 
-// Stride-1, dilation-1, K x K pooling of small planes (compile-time K): the
-// same two passes as maxpool_plane_kernel (row maxima with the first
-// maximising column, then a top-to-bottom scan of those with strict '>'),
-// but a thread takes a whole row (pass 1) or a whole column (pass 2) of a
-// plane, so the index arithmetic is paid once per row or column and every
-// window is K unrolled shared-memory reads. Values are compared in their
-// storage type (the order of fp16 values is that of their fp32 images).
-// `ppb` consecutive planes per CTA. A cascade of o.n same-size poolings
-// (the SPPF block: pool(x), pool(pool(x)), ...) runs in one launch: each
-// stage's output also replaces the staged tile as the next stage's input,
-// and every stage writes its own values and indices.
+// Stride-1, dilation-1, K x K pooling of small planes (compile-time K), in
+// the same two passes as maxpool_plane_kernel: row maxima with the first
+// maximising column, then a top-to-bottom scan of those with strict '>'
+// (the first maximum in (kh, kw) order, as max-pool-2d's shader scans).
+// The CTA's `ppb` consecutive planes are staged in shared memory padded by
+// (pH, pW) with the start value, which never wins a strict '>', so no tap
+// needs a bounds check; threads map to (row, column) pairs of a plane
+// (consecutive threads take consecutive columns: coalesced global stores)
+// and every output is independent work. Values are compared in fp32 (the
+// order of fp16 values is that of their fp32 images). A cascade of o.n
+// same-size poolings (the SPPF block: pool(x), pool(pool(x)), ...) runs in
+// one launch: each stage's output also replaces the staged tile's interior
+// as the next stage's input. IDX = false: no stage writes indices (the
+// caller found them unread), so no maximising position is tracked.
 template <class T>
 struct MpOut {
   T *y[3];
@@ -584,77 +587,101 @@ struct MpOut {
   int n;
 };
 
-template <class T, int K>
+template <class T, int K, bool IDX>
 __global__ void __launch_bounds__(256) maxpool_rows_kernel(PoolGeom g, const T *__restrict__ x,
                                                            MpOut<T> o, int ppb, long long planes) {
   extern __shared__ __align__(16) unsigned char mp_smem[];
-  const int hw = g.IH * g.IW, rw = g.IH * g.OW, ohw = g.OH * g.OW;
+  const int IH = g.IH, IW = g.IW, OH = g.OH, OW = g.OW, pH = g.pH, pW = g.pW;
+  const int Hp = IH + 2 * pH, Wp = IW + 2 * pW;  // OH = Hp - K + 1, OW = Wp - K + 1
   const long long plane0 = (long long)blockIdx.x * ppb;
   const int np = int(min((long long)ppb, planes - plane0));
-  T *tile = reinterpret_cast<T *>(mp_smem);
-  T *rmax = tile + size_t(ppb) * hw;
-  int16_t *rarg = reinterpret_cast<int16_t *>(rmax + size_t(ppb) * rw);
-  const T *xp = x + plane0 * hw;
-  for (int i = threadIdx.x; i < np * hw; i += 256) tile[i] = xp[i];
-  __syncthreads();
+  T *tile = reinterpret_cast<T *>(mp_smem);              // [ppb][Hp][Wp]
+  T *rmax = tile + size_t(ppb) * Hp * Wp;                 // [ppb][Hp][OW]
+  int8_t *rarg = reinterpret_cast<int8_t *>(rmax + size_t(ppb) * Hp * OW);  // [ppb][Hp][OW]
   const float start = sizeof(T) == 2 ? -65504.0f : -3.402823466e38f;
+  const T startv = sf<T>(start);
+  // padding (and the row-maxima of the pad rows, which never change)
+  for (int i = threadIdx.x; i < np * Hp * Wp; i += 256) tile[i] = startv;
+  for (int i = threadIdx.x; i < np * Hp * OW; i += 256) rmax[i] = startv;
+  __syncthreads();
+  // (row, column) mappings of the 256 threads for rows of IW and of OW
+  // columns (the host keeps IW, OW <= 256)
+  const int ic = threadIdx.x % IW, ir0 = threadIdx.x / IW, irs = 256 / IW;
+  const int oc = threadIdx.x % OW, or0 = threadIdx.x / OW, ors = 256 / OW;
+  for (int pl = 0; pl < np; ++pl) {
+    const T *xp = x + (plane0 + pl) * IH * IW;
+    T *tp = tile + (size_t(pl) * Hp + pH) * Wp + pW;
+    for (int r = ir0; r < IH && ir0 < irs; r += irs) tp[r * Wp + ic] = xp[r * IW + ic];
+  }
+  __syncthreads();
   for (int st = 0; st < o.n; ++st) {
-    // pass 1: one (plane, input row) per thread
-    for (int it = threadIdx.x; it < np * g.IH; it += 256) {
-      const T *trow = tile + size_t(it) * g.IW;  // plane-major rows: it = p * IH + ih
-      T *mrow = rmax + size_t(it) * g.OW;
-      int16_t *arow = rarg + size_t(it) * g.OW;
-      for (int ow = 0; ow < g.OW; ++ow) {
-        float best = start;
-        int arg = -1;
+    // pass 1: row maxima of the real rows
+    if (or0 < ors) {
+      for (int pl = 0; pl < np; ++pl) {
+#pragma unroll 2
+        for (int r = pH + or0; r < pH + IH; r += ors) {
+          const T *src = tile + (size_t(pl) * Hp + r) * Wp + oc;
+          float best = start;
+          int arg = -1;
 #pragma unroll
-        for (int kw = 0; kw < K; ++kw) {
-          const int iw = ow - g.pW + kw;
-          if (iw < 0 || iw >= g.IW) continue;
-          const float v = lf(trow[iw]);
-          if (v > best) {
-            best = v;
-            arg = iw;
+          for (int kw = 0; kw < K; ++kw) {
+            const float v = lf(src[kw]);
+            if (v > best) {
+              best = v;
+              if (IDX) arg = kw;
+            }
           }
+          const size_t ri = (size_t(pl) * Hp + r) * OW + oc;
+          rmax[ri] = sf<T>(best);
+          if (IDX) rarg[ri] = int8_t(arg);
         }
-        mrow[ow] = sf<T>(best);
-        arow[ow] = int16_t(arg);
       }
     }
     __syncthreads();
-    // pass 2: one (plane, output column) per thread; consecutive threads
-    // store consecutive columns of a row
+    // pass 2: column scans of the row maxima
     T *y = o.y[st];
-    int32_t *idx = o.idx[st];
+    int32_t *idx = IDX ? o.idx[st] : nullptr;
     const bool next = st + 1 < o.n;  // (same-size poolings: OH = IH, OW = IW)
-    for (int it = threadIdx.x; it < np * g.OW; it += 256) {
-      const int pl = it / g.OW, ow = it - pl * g.OW;
-      const T *mcol = rmax + size_t(pl) * rw + ow;
-      const int16_t *acol = rarg + size_t(pl) * rw + ow;
-      T *ycol = y + (plane0 + pl) * ohw + ow;
-      T *tcol = tile + size_t(pl) * hw + ow;
-      int32_t *icol = idx ? idx + (plane0 + pl) * ohw + ow : nullptr;
-      for (int oh = 0; oh < g.OH; ++oh) {
-        float best = start;
-        int best_idx = 0;
+    if (or0 < ors) {
+      for (int pl = 0; pl < np; ++pl) {
+        T *yp = y + (plane0 + pl) * OH * OW;
+        int32_t *ip = idx ? idx + (plane0 + pl) * OH * OW : nullptr;
+#pragma unroll 2
+        for (int oh = or0; oh < OH; oh += ors) {
+          const T *col = rmax + (size_t(pl) * Hp + oh) * OW + oc;
+          float best = start;
+          int bk = -1;
 #pragma unroll
-        for (int kh = 0; kh < K; ++kh) {
-          const int ih = oh - g.pH + kh;
-          if (ih < 0 || ih >= g.IH) continue;
-          const float v = lf(mcol[size_t(ih) * g.OW]);
-          if (v > best) {
-            best = v;
-            best_idx = ih * g.IW + acol[size_t(ih) * g.OW];
+          for (int kh = 0; kh < K; ++kh) {
+            const float v = lf(col[kh * OW]);
+            if (v > best) {
+              best = v;
+              if (IDX) bk = kh;
+            }
+          }
+          const T bv = sf<T>(best);
+          yp[oh * OW + oc] = bv;
+          if (next) tile[(size_t(pl) * Hp + oh + pH) * Wp + oc + pW] = bv;
+          if (IDX && ip) {
+            int bi = 0;
+            if (bk >= 0) {
+              const int ih = oh + bk - pH;
+              const int iw = oc + rarg[(size_t(pl) * Hp + oh + bk) * OW + oc] - pW;
+              bi = ih * IW + iw;
+            }
+            ip[oh * OW + oc] = bi;
           }
         }
-        const T bv = sf<T>(best);
-        ycol[size_t(oh) * g.OW] = bv;
-        if (next) tcol[size_t(oh) * g.OW] = bv;
-        if (icol) icol[size_t(oh) * g.OW] = best_idx;
       }
     }
     __syncthreads();
   }
+}
+
+// Shared memory of one plane for maxpool_rows_kernel.
+static size_t mp_rows_plane_bytes(const PoolGeom &g, size_t esz) {
+  const size_t Hp = size_t(g.IH) + 2 * g.pH, Wp = size_t(g.IW) + 2 * g.pW;
+  return Hp * Wp * esz + Hp * g.OW * esz + Hp * g.OW;
 }
 
 void parse_hw(const std::vector<int64_t> &v, const char *name, const char *what, int *h, int *w) {
@@ -716,17 +743,18 @@ void record_maxpool(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   const int Kp = g.kH;
   if (g.sH == 1 && g.sW == 1 && g.dH == 1 && g.dW == 1 && g.kW == Kp &&
       (Kp == 3 || Kp == 5 || Kp == 7) && (long long)g.IH * g.IW <= 4096 &&
-      (long long)g.IH * g.OW <= 4096 && g.IW <= 32767 && planes > 0 && planes < (1ll << 31)) {
+      (long long)g.IH * g.OW <= 4096 && g.IW <= 256 && g.OW <= 256 && g.OW >= 1 &&
+      g.OH >= 1 && planes > 0 && planes < (1ll << 31)) {
     // about 40 KB of planes per block
     const size_t esz = dt == WGX_FLOAT16 ? 2 : 4;
-    const size_t per_plane = (size_t(g.IH) * g.IW + size_t(g.IH) * g.OW) * esz +
-                             size_t(g.IH) * g.OW * 2;
+    const size_t per_plane = mp_rows_plane_bytes(g, esz);
     const int ppb = int(std::max<size_t>(1, std::min<size_t>(64, 40 * 1024 / per_plane)));
     const size_t smem = per_plane * ppb + 16;
+    if (smem > 48 * 1024) fail(std::string(name) + ": plane too large for the tiled kernel");
     const long long blocks = (planes + ppb - 1) / ppb;
     push(ctx, name, 1, [=](const ExecEnv &env) {
 #define WGX_MP_ROWS(TT, KK)                                                             \
-  maxpool_rows_kernel<TT, KK><<<unsigned(blocks), 256, smem, env.stream>>>(              \
+  maxpool_rows_kernel<TT, KK, true><<<unsigned(blocks), 256, smem, env.stream>>>(        \
       g, (const TT *)px, MpOut<TT>{{(TT *)py, nullptr, nullptr}, {pi, nullptr, nullptr}, 1}, \
       ppb, planes)
       if (dt == WGX_FLOAT16) {
@@ -1119,18 +1147,24 @@ void record_pad(wgx_context *ctx, const std::vector<wgx_arg> &a) {
 // A cascade of 2 or 3 same-size max-pools (stride 1, dilation 1, K x K with
 // K in {3, 5, 7}, padding (K-1)/2), each reading the previous one's values
 // (the SPPF block): one launch of maxpool_rows_kernel that writes every
-// stage's values and indices. False (nothing recorded) when the shapes do
-// not qualify; the caller then records the operators one by one.
+// stage's values and indices. An index tensor given as null is one that no
+// later operator reads and that is no program output: it is not written
+// (with all of them null, no maximising position is tracked). False
+// (nothing recorded) when the shapes do not qualify; the caller then
+// records the operators one by one.
 bool record_maxpool_cascade(wgx_context *ctx, wgx_tensor *in,
                             const std::vector<std::pair<wgx_tensor *, wgx_tensor *>> &outs, int K) {
   const int n = int(outs.size());
   if (n < 2 || n > 3 || (K != 3 && K != 5 && K != 7)) return false;
   if (in->ndim != 4 || (in->dtype != WGX_FLOAT16 && in->dtype != WGX_FLOAT32)) return false;
+  bool any_idx = false;
   for (auto &o : outs) {
     const wgx_tensor *v = o.first, *ix = o.second;
-    if (v->dtype != in->dtype || ix->dtype != WGX_INT32 || v->ndim != 4 || ix->ndim != 4) return false;
+    if (v->dtype != in->dtype || v->ndim != 4) return false;
+    if (ix && (ix->dtype != WGX_INT32 || ix->ndim != 4)) return false;
     for (int d = 0; d < 4; ++d)
-      if (v->shape[d] != in->shape[d] || ix->shape[d] != in->shape[d]) return false;
+      if (v->shape[d] != in->shape[d] || (ix && ix->shape[d] != in->shape[d])) return false;
+    any_idx = any_idx || ix != nullptr;
   }
   PoolGeom g{};
   g.N = int(in->shape[0]);
@@ -1141,17 +1175,19 @@ bool record_maxpool_cascade(wgx_context *ctx, wgx_tensor *in,
   g.sH = g.sW = g.dH = g.dW = 1;
   g.pH = g.pW = (K - 1) / 2;
   const long long planes = (long long)g.N * g.C;
-  if ((long long)g.IH * g.IW > 4096 || planes <= 0 || planes >= (1ll << 31)) return false;
+  if ((long long)g.IH * g.IW > 4096 || g.IW > 256 || planes <= 0 || planes >= (1ll << 31))
+    return false;
   const size_t esz = in->dtype == WGX_FLOAT16 ? 2 : 4;
-  const size_t per_plane = size_t(g.IH) * g.IW * (2 * esz + 2);
+  const size_t per_plane = mp_rows_plane_bytes(g, esz);
   const int ppb = int(std::max<size_t>(1, std::min<size_t>(64, 40 * 1024 / per_plane)));
   const size_t smem = per_plane * ppb + 16;
+  if (smem > 48 * 1024) return false;
   const long long blocks = (planes + ppb - 1) / ppb;
   const void *px = in->data();
   void *py[3] = {}, *pi[3] = {};
   for (int k = 0; k < n; ++k) {
     py[k] = outs[k].first->data();
-    pi[k] = outs[k].second->data();
+    pi[k] = outs[k].second ? outs[k].second->data() : nullptr;
   }
   const int dt = in->dtype;
   std::string name = "aten.max_pool2d_with_indices.default x" + std::to_string(n) + " (cascade)";
@@ -1159,20 +1195,26 @@ bool record_maxpool_cascade(wgx_context *ctx, wgx_tensor *in,
   c.name = name;
   c.kernel_launches = 1;
   c.run = [=](const ExecEnv &env) {
-#define WGX_MP_CASCADE(TT, KK)                                                              \
-  maxpool_rows_kernel<TT, KK><<<unsigned(blocks), 256, smem, env.stream>>>(                 \
+#define WGX_MP_CASCADE(TT, KK, ID)                                                          \
+  maxpool_rows_kernel<TT, KK, ID><<<unsigned(blocks), 256, smem, env.stream>>>(             \
       g, (const TT *)px,                                                                    \
       MpOut<TT>{{(TT *)py[0], (TT *)py[1], (TT *)py[2]},                                   \
                 {(int32_t *)pi[0], (int32_t *)pi[1], (int32_t *)pi[2]}, n},                 \
       ppb, planes)
     if (dt == WGX_FLOAT16) {
-      if (K == 3) WGX_MP_CASCADE(__half, 3);
-      else if (K == 5) WGX_MP_CASCADE(__half, 5);
-      else WGX_MP_CASCADE(__half, 7);
+      if (any_idx) {
+        if (K == 3) WGX_MP_CASCADE(__half, 3, true);
+        else if (K == 5) WGX_MP_CASCADE(__half, 5, true);
+        else WGX_MP_CASCADE(__half, 7, true);
+      } else {
+        if (K == 3) WGX_MP_CASCADE(__half, 3, false);
+        else if (K == 5) WGX_MP_CASCADE(__half, 5, false);
+        else WGX_MP_CASCADE(__half, 7, false);
+      }
     } else {
-      if (K == 3) WGX_MP_CASCADE(float, 3);
-      else if (K == 5) WGX_MP_CASCADE(float, 5);
-      else WGX_MP_CASCADE(float, 7);
+      if (K == 3) WGX_MP_CASCADE(float, 3, true);
+      else if (K == 5) WGX_MP_CASCADE(float, 5, true);
+      else WGX_MP_CASCADE(float, 7, true);
     }
 #undef WGX_MP_CASCADE
     check_cuda(cudaGetLastError(), "maxpool launch");

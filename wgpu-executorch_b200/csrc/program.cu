@@ -555,6 +555,24 @@ struct PoolCascades {
   std::map<size_t, std::vector<size_t>> at;  // first op -> the ops of its cascade
 };
 
+// Whether value v is named by an operator other than `producer` (directly or
+// inside a tensor list) or is a program output: a value for which neither
+// holds is never observed, so its producer need not write it.
+bool value_used_elsewhere(const Program &P, int64_t v, size_t producer) {
+  for (int64_t o : P.output_ids)
+    if (o == v) return true;
+  for (size_t j = 0; j < P.chain.size(); ++j) {
+    if (j == producer) continue;
+    for (int64_t a : P.chain[j].args) {
+      if (a == v) return true;
+      if (a >= 0 && size_t(a) < P.values.size() && P.values[a].kind == PValue::TensorList)
+        for (int64_t t : P.values[a].items)
+          if (t == v) return true;
+    }
+  }
+  return false;
+}
+
 PoolCascades plan_pool_cascades(const Program &P) {
   PoolCascades C;
   auto items_of = [&](int64_t v) -> const std::vector<int64_t> * {
@@ -928,7 +946,10 @@ static void record_program_impl(wgx_context *ctx, const char *text, uint64_t len
           ok = false;
           break;
         }
-        outs.emplace_back(v->second, ix->second);
+        // indices no operator reads (the SPPF block keeps only the values)
+        // are not written
+        outs.emplace_back(v->second,
+                          value_used_elsewhere(P, items[1], k) ? ix->second : nullptr);
       }
       auto in = tensors.find(P.chain[oi].args[0]);
       const int K = int(P.values[P.chain[oi].args[1]].items[0]);
