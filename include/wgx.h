@@ -159,6 +159,32 @@ WGX_API int wgx_context_stats(const wgx_context *ctx, int64_t *n_commands, int64
  * submits only (utils/benchmark/main.ts:60-77); this is the per-command
  * breakdown of that figure. */
 WGX_API int wgx_context_profile(wgx_context *ctx, int repeats, double *ms, int capacity, int *count);
+/* Pipelined serving steps of a recorded program. No counterpart in the
+ * reference: there, writeBuffer (Tensor.setData, src/tensor.ts:115-135),
+ * the dispatches of submit() (src/context.ts:323-370) and the readback of
+ * getData (src/tensor.ts:142-158) are ordered on the one WebGPU queue, and
+ * wgx_tensor_set_data / wgx_submit / wgx_tensor_get_data keep that order.
+ * A pipeline runs the same three parts of consecutive steps on three
+ * streams so that they overlap: step k uploads host_in into a device
+ * staging slot (upload stream) while step k-1 computes; the context stream
+ * copies the slot into `input`, replays the recorded commands and copies
+ * `output` into an output slot; the download stream copies that slot to
+ * host_out while step k+1 computes. Every step still moves all of its input
+ * and output across the host link. `input` and `output` are the tensors the
+ * recorded program reads and writes (bound by wgx_record_program); depth
+ * (>= 2) staging slots of each are allocated on the device. host_in and
+ * host_out (pinned memory for the copies to overlap) belong to the step
+ * until `depth` further steps have been issued or wgx_pipeline_sync has
+ * returned: wgx_pipeline_step first waits for the step issued `depth`
+ * steps earlier to finish its download. */
+typedef struct wgx_pipeline wgx_pipeline;
+WGX_API int wgx_pipeline_create(wgx_context *ctx, wgx_tensor *input, wgx_tensor *output,
+                                int depth, wgx_pipeline **out);
+WGX_API int wgx_pipeline_step(wgx_pipeline *p, const void *host_in, void *host_out);
+/* waits for every issued step (and reports device errors like wgx_sync) */
+WGX_API int wgx_pipeline_sync(wgx_pipeline *p);
+/* waits for the issued steps and frees the pipeline's streams and slots */
+WGX_API int wgx_pipeline_destroy(wgx_pipeline *p);
 /* the op name of recorded command `index` (NULL when out of range); the
  * string lives until the context is reset or destroyed */
 WGX_API const char *wgx_context_command_name(const wgx_context *ctx, int index);

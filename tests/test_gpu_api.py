@@ -229,3 +229,67 @@ def test_failed_record_leaves_no_commands(ctx):
     with pytest.raises(WgxError):
         ctx.recordProgram(bad, b"", [a, b, c, ctx.tensor("float32", [2, 2])])
     assert ctx.stats()["commands"] == 0
+
+
+def _conv_program(B=2, C=16, H=12, W=12, OC=8, seed=5):
+    """One-input, one-output program: a 3x3 convolution with constant weights."""
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((OC, C, 3, 3)) * 0.1).astype(np.float16)
+    b = (rng.standard_normal(OC) * 0.01).astype(np.float16)
+    vals = [{"type": "tensor", "shape": [B, C, H, W], "dtype": "float16", "memObjId": 0},
+            {"type": "tensor", "shape": [OC, C, 3, 3], "dtype": "float16", "weightsOffset": 0,
+             "weightsLength": w.nbytes},
+            {"type": "tensor", "shape": [OC], "dtype": "float16", "weightsOffset": w.nbytes,
+             "weightsLength": b.nbytes},
+            {"type": "list", "items": [1, 1]}, {"type": "list", "items": [1, 1]},
+            {"type": "list", "items": [1, 1]}, {"type": "scalar", "value": False},
+            {"type": "list", "items": [0, 0]}, {"type": "scalar", "value": 1},
+            {"type": "tensor", "shape": [B, OC, H, W], "dtype": "float16", "memObjId": 1}]
+    prog = {"version": "1",
+            "chain": [{"name": "aten.convolution.default", "args": list(range(10))}],
+            "values": vals, "inputIds": [0], "outputIds": [9],
+            "memoryPlan": {"pools": [{"id": 0, "size": B * C * H * W * 2},
+                                     {"id": 1, "size": B * OC * H * W * 2}]}}
+    return prog, w.tobytes() + b.tobytes(), (B, C, H, W), (B, OC, H, W)
+
+
+@pytest.mark.parametrize("depth,steps", [(2, 5), (3, 7)])
+def test_pipeline_matches_serial_steps(ctx, depth, steps):
+    """Pipelined steps (upload, compute and download of neighbouring steps
+    overlapping, device slots reused) give exactly the outputs of
+    setData / submit / getData run step by step on the same inputs."""
+    prog, wb, xs_shape, ys_shape = _conv_program()
+    inp = ctx.tensor("float16", xs_shape)
+    out = ctx.tensor("float16", ys_shape)
+    ctx.recordProgram(prog, wb, [inp, out])
+    rng = np.random.default_rng(9)
+    xs = [rng.standard_normal(xs_shape).astype(np.float16) for _ in range(steps)]
+    ref = []
+    for x in xs:
+        inp.setData(x)
+        ctx.submit()
+        ref.append(out.numpy().copy())
+    pipe = ctx.pipeline(inp, out, depth)
+    try:
+        hout = [np.full(ys_shape, np.nan, np.float16) for _ in range(steps)]
+        for i, x in enumerate(xs):
+            pipe.step(x, hout[i])
+        pipe.sync()
+        for i in range(steps):
+            np.testing.assert_array_equal(hout[i], ref[i])
+    finally:
+        pipe.destroy()
+
+
+def test_pipeline_rejects_bad_arguments(ctx):
+    prog, wb, xs_shape, ys_shape = _conv_program()
+    inp = ctx.tensor("float16", xs_shape)
+    out = ctx.tensor("float16", ys_shape)
+    ctx.recordProgram(prog, wb, [inp, out])
+    with pytest.raises(wgx.WgxError, match="depth"):
+        ctx.pipeline(inp, out, 1)
+    pipe = ctx.pipeline(inp, out, 2)
+    with pytest.raises(wgx.WgxError, match="smaller"):
+        pipe.step(np.zeros(4, np.float16), np.zeros(ys_shape, np.float16))
+    pipe.destroy()
+    pipe.destroy()  # idempotent

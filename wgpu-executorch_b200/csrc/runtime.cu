@@ -575,6 +575,145 @@ const char *wgx_context_command_name(const wgx_context *ctx, int index) {
   return ctx->commands[size_t(index)].name.c_str();
 }
 
+// ------------------------------------------------------------ pipeline
+// Pipelined steps (see wgx_pipeline_create in wgx.h). Slot k = step % depth.
+// Ordering per slot, with events:
+//   upload stream:   wait in_free[k]; H2D host_in -> sin[k]; record uploaded[k]
+//   context stream:  wait uploaded[k]; sin[k] -> input; record in_free[k];
+//                    graph; wait out_free[k]; output -> sout[k]; record computed[k]
+//   download stream: wait computed[k]; D2H sout[k] -> host_out; record out_free[k]
+// The host waits for out_free[k] of the slot's previous step before reusing
+// slot k (and so before the caller reuses that step's host buffers).
+struct wgx_pipeline {
+  wgx_context *ctx = nullptr;
+  wgx_tensor *input = nullptr, *output = nullptr;
+  int depth = 0;
+  uint64_t in_bytes = 0, out_bytes = 0;
+  cudaStream_t up = nullptr, down = nullptr;
+  std::vector<void *> sin, sout;
+  std::vector<cudaEvent_t> uploaded, in_free, computed, out_free;
+  std::vector<bool> used;  // slot has an issued step
+  int64_t steps = 0;
+};
+
+static void pipeline_release(wgx_pipeline *p) {
+  cudaSetDevice(p->ctx->device);
+  if (p->up) cudaStreamSynchronize(p->up);
+  if (p->down) cudaStreamSynchronize(p->down);
+  for (void *b : p->sin) cudaFree(b);
+  for (void *b : p->sout) cudaFree(b);
+  for (auto *v : {&p->uploaded, &p->in_free, &p->computed, &p->out_free})
+    for (cudaEvent_t e : *v)
+      if (e) cudaEventDestroy(e);
+  if (p->up) cudaStreamDestroy(p->up);
+  if (p->down) cudaStreamDestroy(p->down);
+  p->sin.clear();
+  p->sout.clear();
+  p->up = p->down = nullptr;
+}
+
+int wgx_pipeline_create(wgx_context *ctx, wgx_tensor *input, wgx_tensor *output, int depth,
+                        wgx_pipeline **out) {
+  return guarded([&] {
+    assert_alive(ctx);
+    if (!input || !output || !out) fail("pipeline: null argument");
+    if (depth < 2 || depth > 16) fail("pipeline: depth must be in [2, 16]");
+    if (input->buffer->device != ctx->device || output->buffer->device != ctx->device)
+      fail("pipeline: tensors must live on the context's device");
+    set_device(ctx->device);
+    auto p = std::make_unique<wgx_pipeline>();
+    p->ctx = ctx;
+    p->input = input;
+    p->output = output;
+    p->depth = depth;
+    p->in_bytes = input->byte_length();
+    p->out_bytes = output->byte_length();
+    try {
+      check_cuda(cudaStreamCreateWithFlags(&p->up, cudaStreamNonBlocking), "pipeline stream");
+      check_cuda(cudaStreamCreateWithFlags(&p->down, cudaStreamNonBlocking), "pipeline stream");
+      p->sin.assign(depth, nullptr);
+      p->sout.assign(depth, nullptr);
+      for (auto *v : {&p->uploaded, &p->in_free, &p->computed, &p->out_free})
+        v->assign(depth, nullptr);
+      p->used.assign(depth, false);
+      for (int k = 0; k < depth; ++k) {
+        check_cuda(cudaMalloc(&p->sin[k], std::max<uint64_t>(p->in_bytes, 16)),
+                   "pipeline staging (input)");
+        check_cuda(cudaMalloc(&p->sout[k], std::max<uint64_t>(p->out_bytes, 16)),
+                   "pipeline staging (output)");
+        for (auto *v : {&p->uploaded, &p->in_free, &p->computed, &p->out_free})
+          check_cuda(cudaEventCreateWithFlags(&(*v)[k], cudaEventDisableTiming),
+                     "pipeline event");
+      }
+    } catch (...) {
+      pipeline_release(p.get());
+      throw;
+    }
+    *out = p.release();
+  });
+}
+
+int wgx_pipeline_step(wgx_pipeline *p, const void *host_in, void *host_out) {
+  return guarded([&] {
+    if (!p) fail("pipeline: null pipeline");
+    assert_alive(p->ctx);
+    if ((!host_in && p->in_bytes) || (!host_out && p->out_bytes)) fail("pipeline: null host buffer");
+    wgx_context *ctx = p->ctx;
+    set_device(ctx->device);
+    const int k = int(p->steps % p->depth);
+    if (p->used[k]) {
+      // the slot's previous step has finished its download: its buffers
+      // (device and host) are free
+      check_cuda(cudaEventSynchronize(p->out_free[k]), "pipeline wait");
+      check_cuda(cudaStreamWaitEvent(p->up, p->in_free[k], 0), "pipeline wait");
+    }
+    if (p->in_bytes)
+      check_cuda(cudaMemcpyAsync(p->sin[k], host_in, p->in_bytes, cudaMemcpyHostToDevice, p->up),
+                 "pipeline upload");
+    check_cuda(cudaEventRecord(p->uploaded[k], p->up), "pipeline event");
+    check_cuda(cudaStreamWaitEvent(ctx->stream, p->uploaded[k], 0), "pipeline wait");
+    if (p->in_bytes)
+      check_cuda(cudaMemcpyAsync(p->input->data(), p->sin[k], p->in_bytes,
+                                 cudaMemcpyDeviceToDevice, ctx->stream),
+                 "pipeline input copy");
+    check_cuda(cudaEventRecord(p->in_free[k], ctx->stream), "pipeline event");
+    if (const int rc = wgx_submit(ctx)) fail(wgx_last_error(), rc);
+    if (p->used[k]) check_cuda(cudaStreamWaitEvent(ctx->stream, p->out_free[k], 0), "pipeline wait");
+    if (p->out_bytes)
+      check_cuda(cudaMemcpyAsync(p->sout[k], p->output->data(), p->out_bytes,
+                                 cudaMemcpyDeviceToDevice, ctx->stream),
+                 "pipeline output copy");
+    check_cuda(cudaEventRecord(p->computed[k], ctx->stream), "pipeline event");
+    check_cuda(cudaStreamWaitEvent(p->down, p->computed[k], 0), "pipeline wait");
+    if (p->out_bytes)
+      check_cuda(cudaMemcpyAsync(host_out, p->sout[k], p->out_bytes, cudaMemcpyDeviceToHost,
+                                 p->down),
+                 "pipeline download");
+    check_cuda(cudaEventRecord(p->out_free[k], p->down), "pipeline event");
+    p->used[k] = true;
+    ++p->steps;
+  });
+}
+
+int wgx_pipeline_sync(wgx_pipeline *p) {
+  return guarded([&] {
+    if (!p) fail("pipeline: null pipeline");
+    assert_alive(p->ctx);
+    set_device(p->ctx->device);
+    check_cuda(cudaStreamSynchronize(p->down), "pipeline sync");
+    check_cuda(cudaStreamSynchronize(p->up), "pipeline sync");
+    if (const int rc = wgx_sync(p->ctx)) fail(wgx_last_error(), rc);
+  });
+}
+
+int wgx_pipeline_destroy(wgx_pipeline *p) {
+  return guarded([&] {
+    if (!p) return;
+    std::unique_ptr<wgx_pipeline> owned(p);
+    pipeline_release(p);
+  });
+}
+
 int wgx_context_stream(const wgx_context *ctx, void **stream) {
   return guarded([&] {
     assert_alive(ctx);

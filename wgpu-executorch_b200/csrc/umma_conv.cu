@@ -77,10 +77,6 @@ constexpr int kMaxOut = 4;
 
 // space-to-depth tap masks: filter-row groups x phases
 constexpr int kMaxKhg = 4, kMaxPhases = 16;
-// resident weights arrive in up to this many pieces (consecutive pipeline
-// stages), each on its own barrier, so the first tile's MMAs start once
-// the first piece has landed
-constexpr int kWParts = 8;
 
 struct UmmaGeom {
   // IC, KH, KW, dH, dW, pH, pW describe the stride-1 convolution the MMA
@@ -168,7 +164,7 @@ constexpr int kSeqGroups = 8;
 
 static uint32_t smem_need(const UmmaGeom &g) {
   return g.w_region_bytes + uint32_t(g.stages) * g.b_stage_bytes + EPI_BYTES +
-         (2 * g.stages + 6 + kWParts) * 8 + 16 + kMaxGroups * 8 + kMaxKhg * kMaxPhases * 4 + 1024;
+         (2 * g.stages + 7) * 8 + 16 + kMaxGroups * 8 + kMaxKhg * kMaxPhases * 4 + 1024;
 }
 
 // Geometry for one staging choice: each pipeline stage carries `bk` input
@@ -1323,10 +1319,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t *bars = reinterpret_cast<uint64_t *>(sE + EPI_BYTES);
   uint64_t *full = bars, *empty = bars + S;
   uint64_t *accf = bars + 2 * S, *acce = accf + 2, *wbar = acce + 2;
-  uint64_t *xbar = wbar + kWParts;  // folded-column epilogue exchange, per tile parity
+  uint64_t *xbar = wbar + 1;  // folded-column epilogue exchange, per tile parity
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xbar + 2);
-  // resident weight pieces: piece j holds stages [j*n/P, (j+1)*n/P)
-  const int wparts = g.n_kstages < kWParts ? g.n_kstages : kWParts;
   // generic staging: (activation, weight) descriptor offsets of every MMA
   // group of a stage, in 16-byte units (written and read by the MMA thread)
   uint2 *grp_off = reinterpret_cast<uint2 *>(tmem_slot + 4);
@@ -1343,7 +1337,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(smem_u32(&accf[a]), 1);
       mbar_init(smem_u32(&acce[a]), EPI_WARPS);
     }
-    for (int j = 0; j < kWParts; ++j) mbar_init(smem_u32(&wbar[j]), 1);
+    mbar_init(smem_u32(wbar), 1);
     for (int j = 0; j < 2; ++j) mbar_init(smem_u32(&xbar[j]), EPI_WARPS);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1365,14 +1359,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       // ---------------- producer: bulk copies of weights + activation rows
       const uint32_t b_copy = uint32_t(g.R) * 16;
       if (g.resident) {
-        for (int j = 0; j < wparts; ++j) {
-          const uint32_t s0 = uint32_t(j * g.n_kstages / wparts);
-          const uint32_t s1 = uint32_t((j + 1) * g.n_kstages / wparts);
-          const uint32_t wb = smem_u32(&wbar[j]);
-          mbar_expect_tx(wb, (s1 - s0) * g.a_stage_bytes);
-          bulk_g2s(smem_u32(sW + size_t(s0) * g.a_stage_bytes), wpk + size_t(s0) * g.a_stage_bytes,
-                   (s1 - s0) * g.a_stage_bytes, wb);
-        }
+        // (one copy: splitting it into per-stage pieces, each on its own
+        // barrier, measured slower on B200)
+        const uint32_t wb = smem_u32(wbar);
+        mbar_expect_tx(wb, g.w_region_bytes);
+        bulk_g2s(smem_u32(sW), wpk, g.w_region_bytes, wb);
       }
       int slot = S - 1, use = -1;  // pipeline slot and its use count, advanced per loaded stage
       bool ok = true;
@@ -1443,8 +1434,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t a_lbo = uint32_t(g.wrows) * 16;        // chunk plane of the weights
       const uint32_t b_lbo = uint32_t(g.R_alloc) * 16;      // chunk plane of the activations
       bool ok = true;
-      // resident weight pieces waited for so far (first tile only)
-      int wdone = g.resident ? 0 : wparts;
+      if (g.resident && !mbar_wait(smem_u32(wbar), 0)) {
+        atomicOr(g.err, kErrMmaTimeout);
+        ok = false;
+      }
       // per-MMA start-address offsets (16-byte units) of the specialised path:
       // MMA i = (kw, ks) reads A tap kw chunk pair ks, B shifted kw*dW rows
       uint32_t a_off[KW_T > 0 ? 2 * KW_T : 1], b_off[KW_T > 0 ? 2 * KW_T : 1];
@@ -1502,15 +1495,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int s = 0; s < g.n_kstages; ++s, sw.next(g)) {
           const uint32_t tmask = sw.taps(g);
           if (!tmask) continue;  // all-zero weights: not loaded, no MMA
-          while (wdone < wparts && wdone * g.n_kstages / wparts <= s) {
-            if (!mbar_wait(smem_u32(&wbar[wdone]), 0)) {
-              atomicOr(g.err, kErrMmaTimeout);
-              ok = false;
-              break;
-            }
-            ++wdone;
-          }
-          if (!ok) break;
           if (++slot == S) {
             slot = 0;
             ++use;

@@ -28,7 +28,8 @@ from typing import Any, Callable, Dict, Mapping, Sequence, Union
 import numpy as np
 
 from ._lib import (ARG_BOOL, ARG_INT_LIST, ARG_NULL, ARG_NUMBER, ARG_STRING, ARG_TENSOR,
-                   ARG_TENSOR_LIST, DTYPE_BYTESIZE, DTYPE_CODE, DTYPES, WgxArg, WgxError, check,
+                   ARG_TENSOR_LIST, DTYPE_BYTESIZE, DTYPE_CODE, DTYPES, WGX_ERR_INVALID, WgxArg,
+                   WgxError, check,
                    device_count, lib)
 
 MAX_NDIM = 8
@@ -409,7 +410,56 @@ class WgpuExecutionContext:
         check(lib.wgx_context_stream(self._h, byref(s)))
         return s.value or 0
 
+    def pipeline(self, input: Tensor, output: Tensor, depth: int = 2) -> "Pipeline":
+        """Pipelined serving steps of the recorded program (wgx_pipeline_* in
+        wgx.h): each ``step(host_in, host_out)`` uploads one input, replays
+        the recorded commands and downloads the output, overlapping the
+        copies of neighbouring steps with this step's compute. ``input`` and
+        ``output`` are the tensors the program was recorded with."""
+        self._assert_alive()
+        return Pipeline(self, input, output, depth)
+
+
+class Pipeline:
+    """Overlapped upload / compute / download of consecutive steps. The host
+    arrays of a step (pinned for the copies to overlap) stay in use until
+    ``depth`` further steps have been issued or ``sync()`` has returned."""
+
+    def __init__(self, ctx: "WgpuExecutionContext", input: Tensor, output: Tensor, depth: int):
+        self._ctx = ctx
+        self._in_bytes = input.byteLength
+        self._out_bytes = output.byteLength
+        h = c_void_p()
+        check(lib.wgx_pipeline_create(ctx._h, input._h, output._h, int(depth), byref(h)))
+        self._h = h
+        self._keep = [input, output]
+
+    def step(self, host_in: np.ndarray, host_out: np.ndarray) -> None:
+        if self._h is None:
+            raise WgxError(WGX_ERR_INVALID, "pipeline is destroyed")
+        if not (host_in.flags.c_contiguous and host_out.flags.c_contiguous):
+            raise WgxError(WGX_ERR_INVALID, "pipeline: host arrays must be contiguous")
+        if host_in.nbytes < self._in_bytes or host_out.nbytes < self._out_bytes:
+            raise WgxError(WGX_ERR_INVALID, "pipeline: host array smaller than its tensor")
+        check(lib.wgx_pipeline_step(self._h, host_in.ctypes.data_as(c_void_p),
+                                    host_out.ctypes.data_as(c_void_p)))
+
+    def sync(self) -> None:
+        if self._h is not None:
+            check(lib.wgx_pipeline_sync(self._h))
+
+    def destroy(self) -> None:
+        if self._h is not None:
+            check(lib.wgx_pipeline_destroy(self._h))
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
 
 __all__ = ["WgpuExecutionContext", "Tensor", "Shader", "Buffer", "Device", "requestDevice",
            "shaders", "shaderRegistry", "MAX_NDIM", "DTYPE_BYTESIZE", "GPUBufferUsage",
-           "WgxError", "device_count", "DTYPES"]
+           "WgxError", "device_count", "DTYPES", "Pipeline"]

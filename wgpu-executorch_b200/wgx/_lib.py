@@ -84,6 +84,10 @@ SIGNATURES = {
     "wgx_context_stream": ([c_void_p, POINTER(c_void_p)], c_int),
     "wgx_context_profile": ([c_void_p, c_int, POINTER(c_double), c_int, POINTER(c_int)], c_int),
     "wgx_context_command_name": ([c_void_p, c_int], c_char_p),
+    "wgx_pipeline_create": ([c_void_p, c_void_p, c_void_p, c_int, POINTER(c_void_p)], c_int),
+    "wgx_pipeline_step": ([c_void_p, c_void_p, c_void_p], c_int),
+    "wgx_pipeline_sync": ([c_void_p], c_int),
+    "wgx_pipeline_destroy": ([c_void_p], c_int),
     "wgx_mm_scratch_bytes": ([c_int64, c_int64, c_int64, c_int, POINTER(c_uint64)], c_int),
     "wgx_mm": ([c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p,
                 c_uint64, c_void_p], c_int),
