@@ -752,8 +752,18 @@ static bool dw_tiling(const wgx_conv2d_params &p, int esize, DwTile &d) {
   d.rows = d.n_rg * DW_R + K - 1;
   d.P = 1;
   if (d.bands == 1) {
+    // planes per CTA: of floor and ceil of 256 / (items per plane), the one
+    // whose items (4 x 8 outputs each) fill the rounds of the CTA's 256
+    // threads best, the larger on a tie (20 x 20 planes: 17 planes = 255
+    // items in one round rather than 18 = 270 in two; 80 x 80: 2 planes =
+    // 400 items in two rounds, as full as 1 plane's one)
     const int per_plane = d.n_rg * d.n_cg;
-    const int want = std::max(1, (256 + per_plane - 1) / per_plane);
+    auto fill = [&](int np) {
+      const int items = np * per_plane;
+      return double(items) / (double((items + 255) / 256) * 256.0);
+    };
+    const int lo = std::max(1, 256 / per_plane), hi = std::max(1, (256 + per_plane - 1) / per_plane);
+    const int want = fill(lo) > fill(hi) + 1e-9 ? lo : hi;
     const int fit = int(size_t(DW_SMEM) / tile_bytes(TH));
     d.P = std::max(1, std::min(want, fit));
   }

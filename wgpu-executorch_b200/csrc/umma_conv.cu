@@ -243,13 +243,18 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans,
   // transposed variant: the padded row pitch is rounded up to a multiple of
   // 8 (extra zero columns, whose outputs are discarded), so that 8-position
   // groups never straddle an output row (vector epilogue stores), when that
-  // adds at most 5 % positions (the extra MMA work outweighs the cheaper
-  // stores above that). 1x1 stride-1 unpadded convolutions keep Wp = IW:
-  // the direct mode reads NCHW rows as they are.
+  // adds at most 1/6 of the positions for unfolded stride-1 filters, whose
+  // NCHW and residual stores otherwise take the 2-byte path (YOLO26-N
+  // bottlenecks on 80^2 / 40^2 planes: pitch 82 -> 88, 42 -> 48, 30 % faster
+  // measured), and at most 5 % for strided and folded ones, whose MMA work
+  // grows with the pitch while their stores gain less. 1x1 stride-1
+  // unpadded convolutions keep Wp = IW: the direct mode reads NCHW rows as
+  // they are.
   const bool plain_1x1 =
       p.KH == 1 && p.KW == 1 && p.sH == 1 && p.sW == 1 && p.pH == 0 && p.pW == 0;
   const int wp8 = (g.Wp + 7) / 8 * 8;
-  if (trans && !plain_1x1 && (wp8 - g.Wp) * 20 <= g.Wp) g.Wp = wp8;
+  const int pitch_div = (hs || p.sH != 1 || p.sW != 1) ? 20 : 6;
+  if (trans && !plain_1x1 && (wp8 - g.Wp) * pitch_div <= g.Wp) g.Wp = wp8;
   if (hs) {
     // filter columns folded into N (stride 1, dW = 1, KW = hs): the
     // pipeline runs a KW = 1 convolution with N = hs*ocp columns per M block
