@@ -346,14 +346,22 @@ def pool_chain_program(shape, K, n, idx_out=True):
             "memoryPlan": {"pools": [{"id": i, "size": nb} for i in range(1 + 2 * n)]}}
 
 
-@pytest.mark.parametrize("shape,K,n,idx_out", [((2, 8, 20, 20), 5, 3, True),
-                                               ((1, 6, 9, 13), 3, 2, True),
-                                               ((3, 16, 20, 20), 5, 3, False),
-                                               ((2, 5, 11, 7), 7, 2, False)])
-def test_maxpool_cascade_program(ctx, shape, K, n, idx_out):
+@pytest.mark.parametrize("shape,K,n,idx_out,ties", [((2, 8, 20, 20), 5, 3, True, False),
+                                                    ((1, 6, 9, 13), 3, 2, True, False),
+                                                    ((3, 16, 20, 20), 5, 3, False, False),
+                                                    ((2, 8, 12, 16), 5, 3, False, True),
+                                                    ((2, 5, 11, 7), 7, 2, False, False)])
+def test_maxpool_cascade_program(ctx, shape, K, n, idx_out, ties):
     """(idx_out False: no operator reads the indices and none is a program
-    output, so the cascade writes none and tracks no maximising position.)"""
-    x = rnd(shape)
+    output, so the cascade writes none and tracks no maximising position;
+    fp16 planes of even width then take the packed half2 kernel. ties: a
+    few integer values and -inf, so equal maxima are everywhere.)"""
+    if ties:
+        rng = np.random.default_rng(77)
+        x = rng.integers(-2, 3, size=shape).astype(np.float16)
+        x[rng.random(shape) < 0.1] = -np.inf
+    else:
+        x = rnd(shape)
     ys = [empty(ctx, shape, "float16") for _ in range(n)]
     last_idx = empty(ctx, shape, "int32")
     ctx.recordProgram(pool_chain_program(shape, K, n, idx_out), b"",

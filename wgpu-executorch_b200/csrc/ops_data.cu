@@ -678,6 +678,83 @@ __global__ void __launch_bounds__(256) maxpool_rows_kernel(PoolGeom g, const T *
   }
 }
 
+// fp16 form of maxpool_rows_kernel without indices (IW, OW and pW even):
+// a thread takes two adjacent output columns as one half2 word. The window
+// of output columns 2c, 2c+1 and tap kw is the word at half 2c + kw (even
+// kw) or the two halves straddling two words (odd kw, one byte permute);
+// each tap is one packed compare (__hgt2_mask, strict '>', false for NaN)
+// and a bitwise select, so values and ties resolve exactly as the scalar
+// kernel's fp32 compares do. Same shared-memory layout (the index plane is
+// left unused).
+template <int K>
+__global__ void __launch_bounds__(256) maxpool_rows_h2_kernel(PoolGeom g,
+                                                              const __half *__restrict__ x,
+                                                              MpOut<__half> o, int ppb,
+                                                              long long planes) {
+  extern __shared__ __align__(16) unsigned char mp_smem[];
+  const int IH = g.IH, IW = g.IW, OH = g.OH, OW = g.OW, pH = g.pH;
+  const int Hp = IH + 2 * pH, Wp2 = (IW + 2 * g.pW) / 2, OW2 = OW / 2, IW2 = IW / 2;
+  const int pW2 = g.pW / 2;
+  const long long plane0 = (long long)blockIdx.x * ppb;
+  const int np = int(min((long long)ppb, planes - plane0));
+  uint32_t *tile = reinterpret_cast<uint32_t *>(mp_smem);  // [ppb][Hp][Wp/2] half pairs
+  uint32_t *rmax = tile + size_t(ppb) * Hp * Wp2;          // [ppb][Hp][OW/2]
+  constexpr uint32_t kStart = 0xFBFFFBFFu;                 // (-65504, -65504)
+  for (int i = threadIdx.x; i < np * Hp * Wp2; i += 256) tile[i] = kStart;
+  for (int i = threadIdx.x; i < np * Hp * OW2; i += 256) rmax[i] = kStart;
+  __syncthreads();
+  const int ic = threadIdx.x % IW2, ir0 = threadIdx.x / IW2, irs = 256 / IW2;
+  const int oc = threadIdx.x % OW2, or0 = threadIdx.x / OW2, ors = 256 / OW2;
+  for (int pl = 0; pl < np; ++pl) {
+    const uint32_t *xp = reinterpret_cast<const uint32_t *>(x + (plane0 + pl) * IH * IW);
+    uint32_t *tp = tile + (size_t(pl) * Hp + pH) * Wp2 + pW2;
+    for (int r = ir0; r < IH && ir0 < irs; r += irs) tp[r * Wp2 + ic] = xp[r * IW2 + ic];
+  }
+  __syncthreads();
+  auto take = [](uint32_t v, uint32_t best) {
+    const uint32_t m = __hgt2_mask(*reinterpret_cast<const __half2 *>(&v),
+                                   *reinterpret_cast<const __half2 *>(&best));
+    return (v & m) | (best & ~m);
+  };
+  for (int st = 0; st < o.n; ++st) {
+    if (or0 < ors) {
+      for (int pl = 0; pl < np; ++pl) {
+#pragma unroll 2
+        for (int r = pH + or0; r < pH + IH; r += ors) {
+          const uint32_t *src = tile + (size_t(pl) * Hp + r) * Wp2 + oc;
+          uint32_t w[(K + 1) / 2];
+#pragma unroll
+          for (int j = 0; j < (K + 1) / 2; ++j) w[j] = src[j];
+          uint32_t best = kStart;
+#pragma unroll
+          for (int kw = 0; kw < K; ++kw)
+            best = take((kw & 1) ? __byte_perm(w[kw >> 1], w[(kw >> 1) + 1], 0x5432) : w[kw >> 1],
+                        best);
+          rmax[(size_t(pl) * Hp + r) * OW2 + oc] = best;
+        }
+      }
+    }
+    __syncthreads();
+    uint32_t *y = reinterpret_cast<uint32_t *>(o.y[st]);
+    const bool next = st + 1 < o.n;  // (same-size poolings: OH = IH, OW = IW)
+    if (or0 < ors) {
+      for (int pl = 0; pl < np; ++pl) {
+        uint32_t *yp = y + (plane0 + pl) * OH * OW2;
+#pragma unroll 2
+        for (int oh = or0; oh < OH; oh += ors) {
+          const uint32_t *col = rmax + (size_t(pl) * Hp + oh) * OW2 + oc;
+          uint32_t best = kStart;
+#pragma unroll
+          for (int kh = 0; kh < K; ++kh) best = take(col[kh * OW2], best);
+          yp[oh * OW2 + oc] = best;
+          if (next) tile[(size_t(pl) * Hp + oh + pH) * Wp2 + oc + pW2] = best;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // Shared memory of one plane for maxpool_rows_kernel.
 static size_t mp_rows_plane_bytes(const PoolGeom &g, size_t esz) {
   const size_t Hp = size_t(g.IH) + 2 * g.pH, Wp = size_t(g.IW) + 2 * g.pW;
@@ -1190,6 +1267,10 @@ bool record_maxpool_cascade(wgx_context *ctx, wgx_tensor *in,
     pi[k] = outs[k].second ? outs[k].second->data() : nullptr;
   }
   const int dt = in->dtype;
+  // packed fp16 form: no indices, even widths and padding, 4-byte aligned planes
+  bool h2 = dt == WGX_FLOAT16 && !any_idx && g.IW % 2 == 0 && g.pW % 2 == 0 &&
+            g.IW / 2 <= 256 && (reinterpret_cast<uintptr_t>(px) & 3) == 0;
+  for (int k = 0; k < n; ++k) h2 = h2 && (reinterpret_cast<uintptr_t>(py[k]) & 3) == 0;
   std::string name = "aten.max_pool2d_with_indices.default x" + std::to_string(n) + " (cascade)";
   Command c;
   c.name = name;
@@ -1201,7 +1282,19 @@ bool record_maxpool_cascade(wgx_context *ctx, wgx_tensor *in,
       MpOut<TT>{{(TT *)py[0], (TT *)py[1], (TT *)py[2]},                                   \
                 {(int32_t *)pi[0], (int32_t *)pi[1], (int32_t *)pi[2]}, n},                 \
       ppb, planes)
-    if (dt == WGX_FLOAT16) {
+    if (h2) {
+      const MpOut<__half> mo{{(__half *)py[0], (__half *)py[1], (__half *)py[2]},
+                             {nullptr, nullptr, nullptr}, n};
+      if (K == 3)
+        maxpool_rows_h2_kernel<3><<<unsigned(blocks), 256, smem, env.stream>>>(
+            g, (const __half *)px, mo, ppb, planes);
+      else if (K == 5)
+        maxpool_rows_h2_kernel<5><<<unsigned(blocks), 256, smem, env.stream>>>(
+            g, (const __half *)px, mo, ppb, planes);
+      else
+        maxpool_rows_h2_kernel<7><<<unsigned(blocks), 256, smem, env.stream>>>(
+            g, (const __half *)px, mo, ppb, planes);
+    } else if (dt == WGX_FLOAT16) {
       if (any_idx) {
         if (K == 3) WGX_MP_CASCADE(__half, 3, true);
         else if (K == 5) WGX_MP_CASCADE(__half, 5, true);

@@ -1014,9 +1014,11 @@ struct StageWalk {
 // accumulator, [2] MMA thread waiting for staged data, [3] MMA thread
 // issuing, [4] epilogue warp 4 waiting for a full accumulator, [5] epilogue
 // warp 4 working, [6] MMA thread total, [7] tiles of the CTA; folded-column
-// epilogue (warp 4): [8] TMEM loads, [9] exchange wait, [10] outputs.
+// epilogue (warp 4): [8] TMEM loads, [9] exchange wait, [10] outputs;
+// %globaltimer (ns) at [11] kernel entry, [12] end of the set-up, [13] the
+// MMA thread's last commit, [14] the end of epilogue warp 4, [15] kernel exit.
 #ifdef WGX_PROF
-__device__ unsigned long long g_umma_prof[256][12];
+__device__ unsigned long long g_umma_prof[256][16];
 #define WGX_PROF_T(v) const long long v = clock64()
 #define WGX_PROF_ADD(acc, t0) acc += (unsigned long long)(clock64() - (t0))
 #else
@@ -1304,6 +1306,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                      const uint8_t *__restrict__ wpk, const __half *__restrict__ bias,
                      __half *__restrict__ out, const __grid_constant__ TmapSet tm) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+#ifdef WGX_PROF
+  if (threadIdx.x == 0) g_umma_prof[blockIdx.x][11] = global_ns();
+#endif
   // transposed variant: output channels per M block (N), M blocks per tile
   // (TRANS = 17 / 33: N = 16 / 32 with 4 M blocks, for planes of at most
   // 512 positions)
@@ -1358,6 +1363,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+#ifdef WGX_PROF
+  if (threadIdx.x == 0) g_umma_prof[blockIdx.x][12] = global_ns();
+#endif
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1649,6 +1657,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       g_umma_prof[blockIdx.x][2] = pm_full;
       g_umma_prof[blockIdx.x][3] = pm_issue;
       g_umma_prof[blockIdx.x][6] = (unsigned long long)(clock64() - tm_start);
+      g_umma_prof[blockIdx.x][13] = global_ns();
       g_umma_prof[blockIdx.x][7] = pm_tiles;
 #endif
     }
@@ -2047,8 +2056,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   }
   }
+#ifdef WGX_PROF
+  if (warp == EPI_WARP0 && lane == 0) g_umma_prof[blockIdx.x][14] = global_ns();
+#endif
   tc_fence_before();
   __syncthreads();
+#ifdef WGX_PROF
+  if (threadIdx.x == 0) g_umma_prof[blockIdx.x][15] = global_ns();
+#endif
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -2332,7 +2347,7 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
 extern "C" __attribute__((visibility("default"))) int wgx_umma_prof_read(unsigned long long *out) {
   if (cudaDeviceSynchronize() != cudaSuccess) return 1;
   if (cudaMemcpyFromSymbol(out, wgx::g_umma_prof, sizeof(wgx::g_umma_prof)) != cudaSuccess) return 1;
-  static unsigned long long zero[256][12] = {};
+  static unsigned long long zero[256][16] = {};
   return cudaMemcpyToSymbol(wgx::g_umma_prof, zero, sizeof(zero)) != cudaSuccess;
 }
 #endif
