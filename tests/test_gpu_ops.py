@@ -312,9 +312,12 @@ def test_elementwise_binary(ctx, dt, op, sa, sb):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("shape", [(4, 80, 400), (3, 5, 7)])
-def test_sigmoid(ctx, shape):
-    x = rnd(shape)
+@pytest.mark.parametrize("shape,scale", [((4, 80, 400), 1.0), ((3, 5, 7), 1.0),
+                                         ((2, 80, 8400), 6.0)])
+def test_sigmoid(ctx, shape, scale):
+    """(scale 6: inputs out to about +-25, both tails saturated; the vector
+    fp16 path evaluates 0.5 * tanh(x / 2) + 0.5)"""
+    x = (rnd(shape).astype(np.float32) * scale).astype(np.float16)
     out = empty(ctx, shape, "float16")
     run(ctx, wgx.shaders.sigmoid, [T(ctx, x), out])
     ref = 1.0 / (1.0 + np.exp(-x.astype(np.float64)))
