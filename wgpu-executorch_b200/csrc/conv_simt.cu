@@ -1031,9 +1031,78 @@ uint64_t mm_scratch_bytes(int64_t M, int64_t N, int64_t K, int dtype) {
   return conv2d_scratch_bytes(mm_params(M, N, K, dtype), true);
 }
 
+// fp32 aten.mm, C[M,N] = A[M,K] B[K,N] row-major (mm-64x64.wgsl.ts's GEMM,
+// fp32 FMAs in K order as there): a 32x32 output tile per CTA of 256
+// threads, 2x2 outputs per thread, 64-deep K steps through shared memory,
+// the next step's global loads held in registers while this step's FMAs
+// run. 32x32 tiles give a 512 x 512 product 256 CTAs (64x64 tiles: 64 CTAs
+// for 148 SMs, each with a long serial K loop). A is stored k-major
+// (As[k][m], one pad column: conflict-free transposing stores), B as is.
+namespace {
+constexpr int MM_T = 32, MM_BK = 64, MM_LD = MM_T * MM_BK / 256;  // loads per thread and operand
+
+__global__ void __launch_bounds__(256) mm_f32_kernel(const float *__restrict__ A,
+                                                     const float *__restrict__ B,
+                                                     float *__restrict__ C, int M, int N, int K) {
+  __shared__ float As[MM_BK][MM_T + 1];
+  __shared__ __align__(16) float Bs[MM_BK][MM_T];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.y * MM_T, n0 = blockIdx.x * MM_T;
+  float ra[MM_LD], rb[MM_LD];
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < MM_LD; ++u) {
+      const int e = tid + 256 * u;
+      const int ar = e / MM_BK, ac = e % MM_BK;  // A: row m, column k
+      const int br = e / MM_T, bc = e % MM_T;    // B: row k, column n
+      ra[u] = (m0 + ar < M && k0 + ac < K) ? A[size_t(m0 + ar) * K + k0 + ac] : 0.f;
+      rb[u] = (k0 + br < K && n0 + bc < N) ? B[size_t(k0 + br) * N + n0 + bc] : 0.f;
+    }
+  };
+  float acc[2][2] = {};
+  load(0);
+  for (int k0 = 0; k0 < K; k0 += MM_BK) {
+#pragma unroll
+    for (int u = 0; u < MM_LD; ++u) {
+      const int e = tid + 256 * u;
+      As[e % MM_BK][e / MM_BK] = ra[u];
+      Bs[e / MM_T][e % MM_T] = rb[u];
+    }
+    __syncthreads();
+    if (k0 + MM_BK < K) load(k0 + MM_BK);
+#pragma unroll
+    for (int kk = 0; kk < MM_BK; ++kk) {
+      const float a0 = As[kk][2 * ty], a1 = As[kk][2 * ty + 1];
+      const float2 b = *reinterpret_cast<const float2 *>(&Bs[kk][2 * tx]);
+      acc[0][0] = fmaf(a0, b.x, acc[0][0]);
+      acc[0][1] = fmaf(a0, b.y, acc[0][1]);
+      acc[1][0] = fmaf(a1, b.x, acc[1][0]);
+      acc[1][1] = fmaf(a1, b.y, acc[1][1]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int m = m0 + 2 * ty + i, n = n0 + 2 * tx + j;
+      if (m < M && n < N) C[size_t(m) * N + n] = acc[i][j];
+    }
+}
+}  // namespace
+
 void launch_mm(const void *a, const void *b, void *out, int64_t M, int64_t N, int64_t K,
                int dtype, void *scratch, uint64_t scratch_bytes, cudaStream_t stream) {
   wgx_conv2d_params p = mm_params(M, N, K, dtype);
+  if (dtype == WGX_FLOAT32) {
+    const int64_t gy = (M + MM_T - 1) / MM_T, gx = (N + MM_T - 1) / MM_T;
+    if (gy > 65535 || gx > INT32_MAX) fail("aten.mm.default: matrix too large");
+    mm_f32_kernel<<<dim3(unsigned(gx), unsigned(gy)), 256, 0, stream>>>(
+        static_cast<const float *>(a), static_cast<const float *>(b), static_cast<float *>(out),
+        int(M), int(N), int(K));
+    check_cuda(cudaGetLastError(), "mm launch");
+    return;
+  }
   launch_conv2d(p, b, a, nullptr, nullptr, out, scratch, scratch_bytes, stream);
 }
 
