@@ -413,8 +413,18 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p) {
     std::memcpy(cand, c4, sizeof cand);
     if (p.IC <= 16) std::swap(cand[0][1], cand[1][1]);
   } else if (geom_for(p, 1, 32, trans).IC <= 16) {
-    cand[0][1] = 16;
-    cand[2][1] = 32;
+    if (trans) {
+      // positions on M with at most 16 (virtual) channels: one stage per
+      // filter row carries only KW x G MMAs, and each stage's wait, fence
+      // and commit cost several MMA times; whole-filter stages measured
+      // faster on every such YOLO26-N layer (stem 235 -> 225 us, 8 -> 16
+      // channels at 160^2 74 -> 63 us, 16 -> 16 at 80^2 41 -> 37 us)
+      const int c4[4][2] = {{0, 16}, {1, 16}, {1, 32}, {0, 32}};
+      std::memcpy(cand, c4, sizeof cand);
+    } else {
+      cand[0][1] = 16;
+      cand[2][1] = 32;
+    }
   }
   UmmaGeom best{};
   bool have = false;
