@@ -425,6 +425,13 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p) {
       cand[0][1] = 16;
       cand[2][1] = 32;
     }
+  } else if (trans && (p.sH > 1 || p.sW > 1)) {
+    // strided, positions on M, more than 16 virtual channels: whole-filter
+    // stages of 32 channels first (the 64 -> 64 / stride-2 layer of
+    // YOLO26-N at 160^2: 102 -> 85 us against 16-channel stages; stride-1
+    // layers measured neutral and keep the per-row order)
+    const int c4[4][2] = {{0, 32}, {0, 16}, {1, 32}, {1, 16}};
+    std::memcpy(cand, c4, sizeof cand);
   }
   UmmaGeom best{};
   bool have = false;
