@@ -149,6 +149,9 @@ def test_describe_names_the_selected_configuration():
     assert "N=48 G=4" in d and "kw-folded" in d
     d = describe(B=64, IC=256, IH=20, IW=20, OC=64, OH=20, OW=20, KH=3, KW=3, pH=1, pW=1)
     assert "N=192 G=1" in d and "kw-folded" in d
+    # small planes (at most 512 positions): folded up to ocp = 16 * ceil(IC / 16)
+    d = describe(B=64, IC=64, IH=20, IW=20, OC=64, OH=20, OW=20, KH=3, KW=3, pH=1, pW=1)
+    assert "N=192 G=1" in d and "kw-folded" in d
     for ic, oc in ((8, 16), (32, 32), (16, 16)):
         d = describe(B=64, IC=ic, IH=80, IW=80, OC=oc, OH=80, OW=80, KH=3, KW=3, pH=1, pW=1)
         assert "kw-folded" not in d, (ic, oc, d)

@@ -131,6 +131,7 @@ KW_FOLDED_F16 = [
     (1, 80, 9, 40, 40, (1, 1), (1, 1)),      # N = 192, one M block per tile
     (1, 32, 12, 20, 8, (2, 1), (2, 1)),      # vertical dilation
     (3, 256, 20, 20, 16, (1, 1), (1, 1)),    # YOLO26-N neck shape
+    (2, 64, 20, 20, 64, (1, 1), (1, 1)),     # small plane: folded at ocp = 16 * ceil(IC/16)
     (1, 16, 5, 3, 5, (1, 1), (1, 1)),        # planes narrower than the filter rows
 ]
 

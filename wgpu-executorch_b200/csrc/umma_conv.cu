@@ -382,7 +382,8 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans,
 // per tile and 8 output channels as a 3x3 filter's MMAs per 16 input
 // channels cost unfolded at N = 16 (measured per role on B200: ~3 K cycles
 // per tile and 8-channel chunk, against ~5.8 K cycles of unfolded MMAs per
-// 1024 positions and input block): folded when ocp < 14 * ceil(IC / 16).
+// 1024 positions and input block): folded when ocp < 14 * ceil(IC / 16),
+// and on small planes up to ocp = 16 * ceil(IC / 16) (below).
 // The environment variable WGX_CONV_HSUM=0 turns the fold off, =2 applies
 // it wherever it is possible (both forms compute the same convolution).
 static bool hsum_eligible(const wgx_conv2d_params &p) {
@@ -393,7 +394,13 @@ static bool hsum_eligible(const wgx_conv2d_params &p) {
   if (!mode || p.OC > 64 || p.sH != 1 || p.sW != 1 || p.dW != 1 || p.KW != 3 || p.groups != 1)
     return false;
   const int ocp = p.OC <= 8 ? 8 : p.OC <= 16 ? 16 : p.OC <= 32 ? 32 : 64;
-  return mode == 2 || ocp < 14 * ((p.IC + 15) / 16);
+  const int c16 = (p.IC + 15) / 16;
+  // planes of at most 512 flattened positions fit inside one unfolded tile
+  // of 4 M blocks; the fold's smaller tiles spread them over more SMs
+  // (64 -> 64 channels at 20^2: 31 -> 23 us measured), so there it is
+  // taken up to ocp = 16 * ceil(IC / 16)
+  const long long p_out = (long long)(p.OH - 1) * (p.IW + 2 * p.pW) + p.OW;
+  return mode == 2 || ocp < 14 * c16 || (p_out <= 512 && ocp <= 16 * c16);
 }
 
 // Pick the staging: per-filter-row stages of 32 channels measured fastest
