@@ -27,10 +27,19 @@ weights (wgx.programs.random_init, seed 0); inputs are seeded U[0,1) images.
 * ``cpu_baseline``: the CPU program oracle (oracle/program_oracle.py: the
   reference operators restated in C and numpy, all host threads) on one
   image of the same program, rank 0 at N = 1 only.
+* ``e2e.host_copy_ceiling``: the same bytes per step copied host <-> device
+  by every rank at once with no compute (the host link's bound for e2e).
+* ``models``: BASELINE configs[4] (DepthART-shaped encoder-decoder, 256^2,
+  16 images per GPU, full recordProgram path, random-init weights) with its
+  own value / e2e / roofline / cpu_baseline, and configs[3] at B = 1
+  (YOLO26-N single-image latency, replicas only).
 * ``kernels``: the single-kernel configurations of the metric's
   "conv/mm TFLOP/s vs roofline" part: configs[1] (fp16 conv + SiLU),
-  configs[2] (depthwise 5x5 + 1x1 pointwise) and configs[0] (fp32 mm), each
-  timed with CUDA events with L2 flushed between steps.
+  configs[2] (depthwise 5x5 + 1x1 pointwise) and configs[0] (fp32 mm,
+  against the nominal FFMA peak), each timed with CUDA events with L2
+  flushed between steps.
+
+Each rank first pins its host threads to the CPUs local to its GPU.
 
 ``--impl reference`` times only the CPU program oracle (rank 0; other ranks
 exit) on the same metric and config; WebGPU is unavailable on this box, so
@@ -77,6 +86,14 @@ def peaks():
     return 1590.0, 6650.0, "fallback"
 
 
+def FFMA_PEAK_TFLOPS():
+    """Nominal FP32 FFMA peak: 148 SMs x 128 lanes x 2 FLOP x the max SM
+    clock recorded in MEASURED_PEAKS.json (1965 MHz when absent)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    mhz = float(json.load(open(p)).get("sm_max_mhz", 1965.0)) if os.path.exists(p) else 1965.0
+    return 148 * 128 * 2 * mhz * 1e6 / 1e12
+
+
 def profiled(name, key):
     """A number recorded in a committed ncu summary under profiles/."""
     p = os.path.join(ROOT, "profiles", name)
@@ -102,6 +119,23 @@ def load_model(batch):
     w = open(os.path.join(MODEL_DIR, "weights-fp16.bin"), "rb").read()
     w = programs.random_init(prog, w, seed=0)
     return prog, programs.batch_lift(prog, batch), w
+
+
+DEPTHART_DIR = os.path.join(ROOT, "tests", "golden", "_assets", "depthart")
+DA_PER_GPU = 16   # B = 128 over 8 GPUs
+DA_HW = 256
+
+
+def load_depthart(batch):
+    """the shipped DepthART export converted to fp16,
+    re-shaped to 256x256 (programs.respatial), seeded random-init weights,
+    batch-lifted. Returns (batch-1 program, batch-`batch` program, weights)."""
+    from wgx import programs
+    prog = json.load(open(os.path.join(DEPTHART_DIR, "program-fp16.json")))
+    w = open(os.path.join(DEPTHART_DIR, "weights-fp16.bin"), "rb").read()
+    w = programs.random_init(prog, w, seed=0)
+    p1 = programs.respatial(prog, DA_HW, DA_HW)
+    return p1, programs.batch_lift(p1, batch), w
 
 
 def images(seed, shape):
@@ -408,10 +442,248 @@ def kernel_configs(ctx, local, steps, peak_tf, peak_hbm):
                ctypes.c_void_p(c.data_ptr()), M, N, Kd, 0, ctypes.c_void_p(scr.data_ptr()),
                ctypes.c_uint64(need.value), ctypes.c_void_p(ctx.stream))
     ms_mm = timed(lambda: _lib.check(_lib.lib.wgx_mm(*mm_args)), steps)
+    mm_tf = 2.0 * M * N * Kd / (ms_mm * 1e-3) / 1e12
+    ffma_peak = FFMA_PEAK_TFLOPS()
     out["configs[0]_mm_fp32"] = {"workload": "fp32 mm [512,512] @ [512,512]",
-                                 "value": 2.0 * M * N * Kd / (ms_mm * 1e-3) / 1e12,
-                                 "unit": "TFLOP/s", "ms_per_call": ms_mm,
-                                 "path": "FFMA (fp32 accumulate)"}
+                                 "value": mm_tf, "unit": "TFLOP/s", "ms_per_call": ms_mm,
+                                 "path": "FFMA (fp32 accumulate)",
+                                 "roofline": {"bound": "fp32 CUDA cores", "kernel": "mm_f32_kernel",
+                                              "achieved": mm_tf, "peak": ffma_peak,
+                                              "unit": "TFLOP/s", "frac": mm_tf / ffma_peak,
+                                              "peak_source": "nominal: 148 SMs x 128 FP32 lanes "
+                                                             "x 2 FLOP x max SM clock (not "
+                                                             "measured)"}}
+    return out
+
+
+# ------------------------------------------------ host placement
+def place_on_gpu_node(local):
+    """Pins this rank's host threads to the CPUs local to its GPU (the PCI
+    device's local_cpulist), so pinned host buffers allocated afterwards are
+    first touched on the GPU's NUMA node. Returns (numa node, cpu count)."""
+    import torch
+    pr = torch.cuda.get_device_properties(local)
+    bus = "%04x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+    base = os.path.join("/sys/bus/pci/devices", bus)
+    try:
+        node = int(open(os.path.join(base, "numa_node")).read().strip())
+        cpus = set()
+        for part in open(os.path.join(base, "local_cpulist")).read().strip().split(","):
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return node, len(os.sched_getaffinity(0))
+    except (OSError, ValueError):
+        return None, len(os.sched_getaffinity(0))
+
+
+def host_copy_ceiling(local, ws, in_bytes, out_bytes, steps):
+    """The host link's bound for e2e steps: every rank at once copies a
+    step's input bytes host -> device and its output bytes device -> host
+    (pinned buffers, one stream per direction, concurrently), `steps` times;
+    max over ranks of the device time. Returns (steps per second of one
+    rank, GB/s per rank)."""
+    import torch
+    dev = torch.device("cuda", local)
+    h_in = torch.empty(in_bytes, dtype=torch.uint8, pin_memory=True)
+    h_out = torch.empty(out_bytes, dtype=torch.uint8, pin_memory=True)
+    d_in = torch.empty(in_bytes, dtype=torch.uint8, device=dev)
+    d_out = torch.empty(out_bytes, dtype=torch.uint8, device=dev)
+    s_up, s_dn = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    for _ in range(2):
+        with torch.cuda.stream(s_up):
+            d_in.copy_(h_in, non_blocking=True)
+        with torch.cuda.stream(s_dn):
+            h_out.copy_(d_out, non_blocking=True)
+    barrier(ws)
+    e0u, e1u = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0d, e1d = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0u.record(s_up)
+    e0d.record(s_dn)
+    for _ in range(steps):
+        with torch.cuda.stream(s_up):
+            d_in.copy_(h_in, non_blocking=True)
+        with torch.cuda.stream(s_dn):
+            h_out.copy_(d_out, non_blocking=True)
+    e1u.record(s_up)
+    e1d.record(s_dn)
+    barrier(ws)
+    ms = max(e0u.elapsed_time(e1u), e0d.elapsed_time(e1d))
+    (ms,) = reduce_max([ms], ws)
+    return steps / (ms * 1e-3), (in_bytes + out_bytes) * steps / (ms * 1e-3) / 1e9
+
+
+def l2_flusher(local):
+    import torch
+    dev = f"cuda:{local}"
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    flush_rd = torch.ones(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+
+    def run(i):
+        flush.fill_(i)
+        flush_rd.max()
+    return run
+
+
+def program_bench(local, ws, prog, w, x, steps, warmup, flush_l2, e2e_mode):
+    """One recorded program: device-resident steps (one submit each, CUDA
+    events per step on the context stream; L2 flushed between steps when
+    `flush_l2`), end-to-end steps through the public API, and the tensor-core
+    convolution kernel's time from an eager replay. e2e_mode "pipeline":
+    wgx.Pipeline steps (depth 3); "serial": setData / submit / getData per
+    step (the reference's one-queue order: a latency)."""
+    import torch
+
+    import wgx
+    from wgx import _lib
+    v_in = prog["values"][prog["inputIds"][0]]
+    v_out = prog["values"][prog["outputIds"][0]]
+    out_bytes = int(np.prod(v_out["shape"])) * 2
+    ctx = wgx.WgpuExecutionContext(local)
+    ext = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
+    inp = ctx.tensor("float16", v_in["shape"]).setData(x)
+    out = ctx.tensor("float16", v_out["shape"])
+    ctx.recordProgram(prog, w, [inp, out])
+    st = ctx.stats()
+    flush = l2_flusher(local) if flush_l2 else None
+    for _ in range(warmup):
+        ctx.submit()
+    ctx.sync()
+    barrier(ws)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        if flush:
+            with torch.cuda.stream(ext):
+                flush(i)
+        starts[i].record(ext)
+        ctx.submit()
+        ends[i].record(ext)
+    barrier(ws)
+    dev_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
+    DEPTH = 3
+    if e2e_mode == "pipeline":
+        pins_in = [torch.empty(x.nbytes, dtype=torch.uint8, pin_memory=True).numpy()
+                   for _ in range(DEPTH)]
+        pins_out = [torch.empty(out_bytes, dtype=torch.uint8, pin_memory=True).numpy()
+                    for _ in range(DEPTH)]
+        for pin in pins_in:
+            pin[:] = x.view(np.uint8).reshape(-1)
+        pipe = ctx.pipeline(inp, out, DEPTH)
+        for i in range(DEPTH):
+            pipe.step(pins_in[i], pins_out[i])
+        pipe.sync()
+        barrier(ws)
+        t0 = time.perf_counter()
+        for i in range(steps):
+            pipe.step(pins_in[i % DEPTH], pins_out[i % DEPTH])
+        pipe.sync()
+        barrier(ws)
+        e2e_s = time.perf_counter() - t0
+        pipe.destroy()
+    else:
+        # pinned host arrays; setData and getDataInto block like the
+        # reference's writeBuffer + mapAsync round trip
+        h_in = torch.empty(x.nbytes, dtype=torch.uint8, pin_memory=True).numpy()
+        h_in[:] = x.view(np.uint8).reshape(-1)
+        h_out = torch.empty(out_bytes, dtype=torch.uint8, pin_memory=True).numpy()
+        for _ in range(3):
+            inp.setData(h_in)
+            ctx.submit()
+            out.getDataInto(h_out)
+        barrier(ws)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            inp.setData(h_in)
+            ctx.submit()
+            out.getDataInto(h_out)
+        barrier(ws)
+        e2e_s = time.perf_counter() - t0
+    _lib.check(_lib.lib.wgx_kernel_timing(1))
+    _lib.check(_lib.lib.wgx_kernel_timing_read(b"", None, None, 1))
+    reps = max(3, min(20, steps // 5))
+    prof = ctx.profile(reps)
+    kms, kcnt = ctypes.c_double(), ctypes.c_int64()
+    _lib.check(_lib.lib.wgx_kernel_timing_read(b"umma_conv_kernel", ctypes.byref(kms),
+                                                ctypes.byref(kcnt), 1))
+    _lib.check(_lib.lib.wgx_kernel_timing(0))
+    conv_ms = kms.value / reps
+    eager_ms = sum(t for _, t in prof)
+    dev_ms, e2e_s = reduce_max([dev_ms, e2e_s], ws)
+    ctx.destroy()
+    return {"dev_ms": dev_ms, "e2e_s": e2e_s, "conv_ms": conv_ms, "eager_ms": eager_ms,
+            "stats": st, "in_bytes": x.nbytes, "out_bytes": out_bytes, "reps": reps}
+
+
+def model_workloads(local, ws, rank, steps, warmup, peak_tf, peak_hbm):
+    """BASELINE configs[4] (DepthART 256^2, 16 images per GPU) and configs[3]
+    at B = 1 (YOLO26-N single-image latency; replicas only)."""
+    out = {}
+    # ---- configs[4]: DepthART-shaped encoder-decoder, 256^2, fp16
+    p1, pb, w = load_depthart(DA_PER_GPU)
+    x = images(2000 + rank, pb["values"][pb["inputIds"][0]]["shape"])
+    r = program_bench(local, ws, pb, w, x, steps, warmup, True, "pipeline")
+    dense_f, dense_b, n_dense, dw_b, n_dw = conv_work(pb)
+    imgs = DA_PER_GPU * ws * steps
+    ach = dense_b / (r["conv_ms"] * 1e-3) / 1e9
+    cpu = None
+    if ws == 1 and rank == 0:
+        rate, secs, threads = cpu_image_rate(p1, w)
+        cpu = {"value": rate, "unit": "imgs/s", "cores": threads, "kind": "port",
+               "sample": f"1 image of the batch-1 256x256 program, {secs:.2f} s (CPU program "
+                         "oracle: reference operators restated in C/numpy, fp64 accumulation)"}
+    out["configs[4]_depthart_256"] = {
+        "workload": f"BASELINE configs[4]: DepthART-shaped encoder-decoder fp16, input "
+                    f"[{DA_PER_GPU},3,{DA_HW},{DA_HW}] per GPU (B = {DA_PER_GPU * ws} global; "
+                    "shipped export converted to fp16, re-shaped to 256^2, batch-lifted, "
+                    "seeded random-init weights), full recordProgram path",
+        "value": imgs / (r["dev_ms"] * 1e-3), "unit": "imgs/s",
+        "ms_per_step": r["dev_ms"] / steps, "global_batch": DA_PER_GPU * ws,
+        "l2": "flushed (256 MiB write + 256 MiB read) before every timed step",
+        "commands": r["stats"]["commands"], "kernel_launches_per_step": r["stats"]["kernel_launches"],
+        "e2e": {"value": imgs / r["e2e_s"], "unit": "imgs/s", "h2d_bytes_per_step": r["in_bytes"],
+                "d2h_bytes_per_step": r["out_bytes"], "ms_per_step": r["e2e_s"] / steps * 1e3,
+                "path": "wgx.Pipeline steps (depth 3), pinned host buffers"},
+        "roofline": {"bound": "hbm", "kernel": "umma_conv_kernel", "achieved": ach,
+                     "peak": peak_hbm, "unit": "GB/s", "frac": ach / peak_hbm,
+                     "launches_per_step": n_dense,
+                     "algorithmic_bytes_per_launch": dense_b / max(1, n_dense),
+                     "avg_launch_ms": r["conv_ms"] / max(1, n_dense),
+                     "flop_rate_tflops": dense_f / (r["conv_ms"] * 1e-3) / 1e12,
+                     "step_share": r["conv_ms"] / r["eager_ms"],
+                     "timing": f"eager replay, {r['reps']} reps, CUDA events per launch"},
+        "cpu_baseline": cpu,
+        "gpu_launches": (steps + r["reps"]) * r["stats"]["kernel_launches"] * ws,
+    }
+    # ---- configs[3] at B = 1: single-image latency (replicas only)
+    p1y, _, wy = load_model(1)
+    xy = images(3000 + rank, p1y["values"][p1y["inputIds"][0]]["shape"])
+    r1 = program_bench(local, ws, p1y, wy, xy, steps, warmup, True, "serial")
+    dense_f, dense_b, n_dense, _, _ = conv_work(p1y)
+    ach1 = dense_b / (r1["conv_ms"] * 1e-3) / 1e9
+    out["configs[3]_yolo26n_b1"] = {
+        "workload": "BASELINE configs[3] at B = 1: YOLO26-N fp16, [1,3,640,640], one image per "
+                    "GPU (replicas only: one image does not shard)",
+        "value": r1["dev_ms"] / steps, "unit": "ms/image", "higher_is_better": False,
+        "imgs_per_s_per_gpu": steps / (r1["dev_ms"] * 1e-3),
+        "l2": "flushed (256 MiB write + 256 MiB read) before every timed step",
+        "path": "submit() = one CUDA-graph replay; max over ranks",
+        "kernel_launches_per_step": r1["stats"]["kernel_launches"],
+        "e2e": {"value": r1["e2e_s"] / steps * 1e3, "unit": "ms/image",
+                "h2d_bytes_per_step": r1["in_bytes"], "d2h_bytes_per_step": r1["out_bytes"],
+                "path": "setData (pinned host array) -> submit -> getData (pinned), one step "
+                        "at a time"},
+        "roofline": {"bound": "hbm", "kernel": "umma_conv_kernel", "achieved": ach1,
+                     "peak": peak_hbm, "unit": "GB/s", "frac": ach1 / peak_hbm,
+                     "launches_per_step": n_dense,
+                     "avg_launch_ms": r1["conv_ms"] / max(1, n_dense),
+                     "step_share": r1["conv_ms"] / r1["eager_ms"]},
+        "reference_published_ms": {"value": 14.0, "hardware": "NVIDIA Turing, Chrome WebGPU, fp16",
+                                   "source": "benchmark-results.json:21-29 of the reference"},
+        "gpu_launches": (steps + 3 + r1["reps"]) * r1["stats"]["kernel_launches"] * ws,
+    }
     return out
 
 
@@ -423,6 +695,7 @@ def run_ours(args, ws, rank, local):
     from wgx import _lib
 
     torch.cuda.set_device(local)
+    numa_node, n_cpus = place_on_gpu_node(local)
     prog1, progb, w = load_model(PER_GPU)
     v_in = progb["values"][progb["inputIds"][0]]
     v_out = progb["values"][progb["outputIds"][0]]
@@ -483,7 +756,8 @@ def run_ours(args, ws, rank, local):
     barrier(ws)
     e2e_s = time.perf_counter() - t0
     pipe.destroy()
-    clocks = sampler.stop() if sampler else None
+    # the host link's bound for the same bytes per step, all ranks at once
+    ceil_steps_s, ceil_gbs = host_copy_ceiling(local, ws, in_bytes, out_bytes, args.steps)
 
     # ---- per-kernel CUDA events: the same program replayed eagerly
     _lib.check(_lib.lib.wgx_kernel_timing(1))
@@ -505,7 +779,9 @@ def run_ours(args, ws, rank, local):
     peak_tf, peak_hbm, peak_kind = peaks()
     dense_f, dense_b, n_dense, dw_b, n_dw = conv_work(progb)
     ach = dense_b / (conv_main_ms * 1e-3) / 1e9
+    models = model_workloads(local, ws, rank, args.steps, args.warmup, peak_tf, peak_hbm)
     kernels = kernel_configs(ctx, local, max(20, min(200, args.steps)), peak_tf, peak_hbm)
+    clocks = sampler.stop() if sampler else None
     if rank != 0:
         ctx.destroy()
         return 0
@@ -548,9 +824,19 @@ def run_ours(args, ws, rank, local):
                      "depthwise_gbs": dw_b / (dw_ms * 1e-3) / 1e9 if dw_ms else None},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "imgs/s", "h2d_bytes_per_step": in_bytes,
-                "d2h_bytes_per_step": out_bytes, "ms_per_step": e2e_s / args.steps * 1e3},
-        "gpu_launches": 2 * args.steps * st["kernel_launches"] * ws,
+                "d2h_bytes_per_step": out_bytes, "ms_per_step": e2e_s / args.steps * 1e3,
+                "host_copy_ceiling": {
+                    "value": ceil_steps_s * PER_GPU * ws, "unit": "imgs/s",
+                    "gbs_per_rank": ceil_gbs,
+                    "how": "every rank at once: the step's input bytes H2D and output bytes D2H "
+                           "from/to pinned host memory, one stream per direction, CUDA events, "
+                           "max over ranks; no compute",
+                    "numa_node_of_gpu": numa_node, "host_cpus_of_rank": n_cpus},
+                "frac_of_host_copy_ceiling": e2e_value / (ceil_steps_s * PER_GPU * ws)},
+        "gpu_launches": 2 * args.steps * st["kernel_launches"] * ws + sum(
+            m.get("gpu_launches", 0) for m in models.values()),
         "clocks": clocks,
+        "models": models,
         "kernels": kernels,
     }
     print(json.dumps(line), flush=True)
@@ -578,8 +864,11 @@ def run_only(args):
 
     import wgx
     ctx = wgx.WgpuExecutionContext(0)
-    if args.only == "yolo":
-        _, progb, w = load_model(args.batch or PER_GPU)
+    if args.only in ("yolo", "depthart"):
+        if args.only == "yolo":
+            _, progb, w = load_model(args.batch or PER_GPU)
+        else:
+            _, progb, w = load_depthart(args.batch or DA_PER_GPU)
         v_in = progb["values"][progb["inputIds"][0]]
         v_out = progb["values"][progb["outputIds"][0]]
         inp = ctx.tensor("float16", v_in["shape"]).setData(images(1000, v_in["shape"]))
@@ -588,7 +877,7 @@ def run_only(args):
         for _ in range(args.warmup + args.steps):
             ctx.submit()
         ctx.sync()
-        print(json.dumps({"only": "yolo", "steps": args.steps, "warmup": args.warmup,
+        print(json.dumps({"only": args.only, "steps": args.steps, "warmup": args.warmup,
                           "kernel_launches_per_step": ctx.stats()["kernel_launches"]}))
     else:
         rng = np.random.default_rng(0)
@@ -611,7 +900,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--only", default=None, choices=["yolo"] + sorted(ONLY_CONV),
+    ap.add_argument("--only", default=None, choices=["yolo", "depthart"] + sorted(ONLY_CONV),
                     help="run one workload's launches only (for profilers)")
     ap.add_argument("--batch", type=int, default=0,
                     help="images per GPU for --only (default: 64 for yolo, the listed batch otherwise)")

@@ -256,7 +256,9 @@ WGX_API int wgx_conv2d(const wgx_conv2d_params *p, const void *in, const void *w
  * The first call on a device looks the buffer up (once per device); make
  * that first call before any stream capture. All calls on a device share
  * the buffer: calls that overlap on the GPU race, so order them on one
- * stream. */
+ * stream. The looked-up address (like the device error word's) is cached
+ * for the life of the process: do not use the library across a
+ * cudaDeviceReset of a device it has already run on. */
 WGX_API int wgx_conv2d_noalloc(const wgx_conv2d_params *p, const void *in, const void *w,
                                const void *bias, void *out, void *stream);
 
@@ -275,6 +277,23 @@ WGX_API int wgx_kernel_timing_read(const char *kernel, double *total_ms, int64_t
 /* hanging; wgx_sync reports it.                                        */
 /* ------------------------------------------------------------------ */
 WGX_API int wgx_device_error(int device, uint32_t *code, int clear);
+
+/* ------------------------------------------------------------------ */
+/* Fault injection for failure-detection tests. No counterpart in the  */
+/* reference (whose errors are synchronous throws, context.ts:52-56,   */
+/* 226-230, 296-298). Process-wide; wgx_debug_inject(0) clears it.      */
+/*  WGX_INJECT_ALLOC_FAIL: the next device allocation of the library    */
+/*    fails as cudaMalloc's out-of-memory would (WGX_ERR_NOMEM); one    */
+/*    shot, nothing is allocated, the context stays usable.             */
+/*  WGX_INJECT_SKIP_LOADS: tensor-core convolution kernels launched     */
+/*    while it is set issue none of their copies, so their bounded      */
+/*    mbarrier waits run out (after ~2 s); the kernel records the        */
+/*    timeout in the device error word and returns, and the next        */
+/*    wgx_sync reports WGX_ERR_DEVICE. No trap, no fault.               */
+/* ------------------------------------------------------------------ */
+#define WGX_INJECT_ALLOC_FAIL 1u
+#define WGX_INJECT_SKIP_LOADS 2u
+WGX_API int wgx_debug_inject(uint32_t flags);
 
 #ifdef __cplusplus
 }

@@ -322,9 +322,85 @@ static void conv_plane(void *vctx, long idx) {
   }
 }
 
+/* Exact mode, plane-wise: for output plane (b, oc) the products of the
+ * stored inputs (pre-widened to double once, `xd`) are accumulated in a
+ * double plane, input channel and filter tap outermost, so the inner loop
+ * runs over contiguous output columns of one row with the in-bounds column
+ * range computed up front. Same value as the per-output loop of conv_plane
+ * (double sums of the same products; only the order of the additions
+ * differs, far below one rounding of the storage type). */
+typedef struct {
+  const conv_job *j;
+  const double *xd;
+} exact_job;
+
+static void conv_plane_exact(void *vctx, long idx) {
+  const exact_job *e = vctx;
+  const conv_job *j = e->j;
+  const conv_params *p = j->p;
+  const int dt = p->dtype;
+  const int icpg = p->IC / p->groups, ocpg = p->OC / p->groups;
+  const long ohw = (long)p->OH * p->OW, ihw = (long)p->IH * p->IW;
+  const int tile32_bug = j->bug_tile32 && !j->is_clamp_op && uses_tile32_layout(p);
+  const int b = (int)(idx / p->OC), oc = (int)(idx % p->OC);
+  const int g = oc / ocpg;
+  double *acc = calloc((size_t)ohw, sizeof(double));
+  if (!acc) abort();
+  for (int c = 0; c < icpg; ++c) {
+    const double *xp = e->xd + ((long)b * p->IC + g * icpg + c) * ihw;
+    for (int kh = 0; kh < p->KH; ++kh)
+      for (int kw = 0; kw < p->KW; ++kw) {
+        const double wv = ld(dt, j->w, (((long)oc * icpg + c) * p->KH + kh) * p->KW + kw);
+        /* in-bounds output columns: 0 <= ow*sW + off < IW */
+        const int off = kw * p->dW - p->pW;
+        int ow0 = off >= 0 ? 0 : (-off + p->sW - 1) / p->sW;
+        int ow1 = (p->IW - 1 - off) >= 0 ? (p->IW - 1 - off) / p->sW + 1 : 0;
+        if (ow1 > p->OW) ow1 = p->OW;
+        for (int oh = 0; oh < p->OH; ++oh) {
+          const int ih = oh * p->sH - p->pH + kh * p->dH;
+          if (ih < 0 || ih >= p->IH) continue;
+          const double *row = xp + (long)ih * p->IW + off;
+          double *a = acc + (long)oh * p->OW;
+          for (int ow = ow0; ow < ow1; ++ow) a[ow] += row[(long)ow * p->sW] * wv;
+        }
+      }
+  }
+  const double bv = p->has_bias ? ld(dt, j->bias, oc) : 0.0;
+  for (long i = 0; i < ohw; ++i) {
+    long oidx = ((long)b * p->OC + oc) * ohw + i;
+    if (tile32_bug) oidx = (long)oc * ((long)p->B * ohw) + (long)b * ohw + i;
+    st(dt, j->out, oidx, act_d(p->act, acc[i] + bv, p->out_min, p->out_max));
+  }
+  free(acc);
+}
+
+typedef struct {
+  int dt;
+  const void *src;
+  double *dst;
+  long n, chunk;
+} widen_job;
+
+static void widen_chunk(void *vctx, long c) {
+  const widen_job *w = vctx;
+  const long i0 = c * w->chunk, i1 = i0 + w->chunk < w->n ? i0 + w->chunk : w->n;
+  for (long i = i0; i < i1; ++i) w->dst[i] = ld(w->dt, w->src, i);
+}
+
 void oracle_conv2d(int mode, int is_clamp_op, const conv_params *p, const void *x, const void *w,
                    const void *bias, void *out, int bug_tile32) {
   conv_job j = {mode, is_clamp_op, bug_tile32, p, x, w, bias, out};
+  if (mode == ORACLE_EXACT) {
+    const long n = (long)p->B * p->IC * p->IH * p->IW;
+    double *xd = malloc((size_t)(n > 0 ? n : 1) * sizeof(double));
+    if (!xd) abort();
+    widen_job wj = {p->dtype, x, xd, n, 1 << 16};
+    parallel_for((n + wj.chunk - 1) / wj.chunk, widen_chunk, &wj);
+    exact_job e = {&j, xd};
+    parallel_for((long)p->B * p->OC, conv_plane_exact, &e);
+    free(xd);
+    return;
+  }
   parallel_for((long)p->B * p->OC, conv_plane, &j);
 }
 

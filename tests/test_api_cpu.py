@@ -40,6 +40,15 @@ def test_version_and_device_count():
     assert wgx.device_count() >= 0
 
 
+def test_debug_inject_flags():
+    """The test-only fault injection accepts its two flags and rejects
+    others (host state only: no GPU call)."""
+    assert _lib.lib.wgx_debug_inject(_lib.INJECT_ALLOC_FAIL | _lib.INJECT_SKIP_LOADS) == 0
+    assert _lib.lib.wgx_debug_inject(0) == 0
+    assert _lib.lib.wgx_debug_inject(8) == _lib.WGX_ERR_INVALID
+    assert "unknown flags" in _lib.lib.wgx_last_error().decode()
+
+
 @pytest.mark.skipif(wgx.device_count() > 0, reason="a GPU is present")
 def test_context_without_gpu_raises_cleanly():
     with pytest.raises(wgx.WgxError, match="no CUDA device"):

@@ -173,6 +173,35 @@ def test_depthart_256_batch_lift_runs(ctx):
         np.testing.assert_array_equal(y[i], y[0])
 
 
+def test_headline_program_matches_program_oracle(ctx):
+    """The benchmarked program itself: the shipped YOLO26-N export converted
+    to fp16, seeded Kaiming-normal random-init weights (random_init, seed 0)
+    and batch-lifted, here to 2 images of seeded U[0,1) input (the bench's
+    image generator), against the CPU program oracle at the fp16 bound. The
+    box rows (0-3, pixel coordinates up to 640) and the class-score rows
+    (4-83, sigmoids near 0.5) are checked each against their own scale."""
+    import program_oracle
+    from wgx import programs
+    prog, w = load("yolo26n", True)
+    w = programs.random_init(prog, w.tobytes(), seed=0)
+    prog = programs.batch_lift(prog, 2)
+    x = np.random.default_rng(1000).random([2, 3, 640, 640], dtype=np.float32).astype(np.float16)
+    inp = ctx.tensor("float16", [2, 3, 640, 640]).setData(x)
+    out = ctx.tensor("float16", [2, 84, 8400])
+    ctx.recordProgram(prog, w, [inp, out])
+    ctx.submit()
+    ctx.sync()
+    y = out.numpy().astype(np.float64)
+    (ref,) = program_oracle.run_program(prog, w, [x])
+    ref = ref.astype(np.float64)
+    assert np.all(np.isfinite(y))
+    for name, rows in (("boxes", slice(0, 4)), ("scores", slice(4, 84))):
+        err = np.abs(y[:, rows] - ref[:, rows]).max()
+        scale = np.abs(ref[:, rows]).max()
+        print(f"headline {name}: max abs err {err:.3e}, scale {scale:.3e}")
+        assert err / scale <= 2e-2, f"{name}: {err / scale}"
+
+
 @pytest.mark.parametrize("model,fp16,hw,batch", [
     ("yolo26n", True, None, 2),
     ("depthart", True, (256, 256), 2),

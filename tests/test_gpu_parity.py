@@ -360,6 +360,30 @@ def test_config2_full_batch_properties(ctx):
     for i in (3, 7):
         yi, _ = c_conv(ctx, x[i:i + 1], w, b, 1, _lib.ACT_SILU)
         np.testing.assert_array_equal(yi[0], y[i])
+    # the whole batch against the exact oracle
+    check_f16(y, x, w, b, 1, 1, 1, 1, act=oracle.ACT_SILU)
+
+
+def test_config3_full_size_depthwise(ctx):
+    """BASELINE config 3 depthwise at the benchmarked size: [16,256,80,80] x
+    [256,1,5,5], stride 1, pad 2, groups 256, N(0,1) input, N(0,0.1)
+    weights, against the exact oracle and the reference's f16 arithmetic."""
+    (x,) = oracle.make_inputs([(16, 256, 80, 80)], seed=90)
+    (w, b) = oracle.make_inputs([(256, 1, 5, 5), (256,)], seed=91, scale=[0.1, 0.01])
+    y = engine_conv(ctx, x, w, b, 1, 2, 1, 256)
+    check_f16(y, x, w, b, 1, 2, 1, 256)
+
+
+def test_config3_full_size_pointwise(ctx):
+    """BASELINE config 3's 1x1 pointwise at the benchmarked size:
+    [16,256,80,80] x [256,256,1,1] (Kaiming weights), through the TMA direct
+    mode, against the exact oracle and the reference's f16 arithmetic (its
+    conv2d-tile64-f16 kernel for B > 1)."""
+    (x,) = oracle.make_inputs([(16, 256, 80, 80)], seed=92)
+    w = kaiming((256, 256, 1, 1), 93)
+    (b,) = oracle.make_inputs([(256,)], seed=94, scale=0.01)
+    y = engine_conv(ctx, x, w, b, 1, 0, 1, 1)
+    check_f16(y, x, w, b, 1, 0, 1, 1)
 
 
 # --------------------------------------------------- program fusion

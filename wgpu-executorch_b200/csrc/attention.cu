@@ -22,6 +22,8 @@
 // Softmax runs in fp32 on fp32 scores, both products accumulate in fp32;
 // the reference computes all three steps in f16 (bmm-64x64-f16,
 // softmax-last-dim-f16.wgsl.ts).
+#include <mutex>
+
 #include "internal.h"
 #include "tcgen05.h"
 
@@ -299,12 +301,17 @@ void launch_attention(const __half *Q, const __half *KT, const __half *VT, __hal
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   g.err = device_error_word(dev);
-  static bool attr_set[64] = {};
-  if (dev < 64 && !attr_set[dev]) {
-    check_cuda(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    int(kAttnSmemMax)),
-               "attention smem attr");
-    attr_set[dev] = true;
+  {
+    // once per device; host threads share the table, so under a lock
+    static std::mutex setup_mu;
+    static bool attr_set[64] = {};
+    std::lock_guard<std::mutex> lock(setup_mu);
+    if (dev >= 64 || !attr_set[dev]) {
+      check_cuda(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(kAttnSmemMax)),
+                 "attention smem attr");
+      if (dev < 64) attr_set[dev] = true;
+    }
   }
   const unsigned grid = unsigned(n);  // one CTA per head, looping over query blocks
   int th = timer_begin("attention_kernel", stream);

@@ -46,6 +46,14 @@ enum DeviceErrorBits : uint32_t {
 };
 uint32_t *device_error_word(int device);
 
+// Device allocations of the library go through device_malloc, which
+// honours the test-only fault injection of wgx_debug_inject
+// (WGX_INJECT_ALLOC_FAIL fails the next one with cudaErrorMemoryAllocation).
+cudaError_t device_malloc(void **p, uint64_t bytes);
+// WGX_INJECT_SKIP_LOADS is set: tensor-core kernels launched now issue no
+// copies, so their bounded waits run out (failure-detection tests).
+bool inject_skip_loads();
+
 // Opt-in CUDA-event timing of individual kernels (wgx_kernel_timing). Both
 // are no-ops unless timing is enabled and the stream is not capturing.
 int timer_begin(const char *kernel, cudaStream_t stream);

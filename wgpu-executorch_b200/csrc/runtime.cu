@@ -24,6 +24,7 @@
 
 #include "umma_conv.h"
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "internal.h"
@@ -128,6 +129,23 @@ void timer_end(int handle, cudaStream_t stream) {
   t.pending[handle].closed = true;
 }
 
+// ------------------------------------------------ fault injection (tests)
+static std::atomic<uint32_t> g_inject{0};
+
+cudaError_t device_malloc(void **p, uint64_t bytes) {
+  uint32_t f = g_inject.load();
+  while (f & WGX_INJECT_ALLOC_FAIL) {
+    // one-shot: the flag is consumed by the allocation it fails
+    if (g_inject.compare_exchange_weak(f, f & ~uint32_t(WGX_INJECT_ALLOC_FAIL))) {
+      *p = nullptr;
+      return cudaErrorMemoryAllocation;
+    }
+  }
+  return cudaMalloc(p, bytes);
+}
+
+bool inject_skip_loads() { return (g_inject.load() & WGX_INJECT_SKIP_LOADS) != 0; }
+
 }  // namespace wgx
 
 using namespace wgx;
@@ -135,7 +153,7 @@ using namespace wgx;
 void *wgx_context::alloc_device(uint64_t bytes) {
   void *p = nullptr;
   if (bytes == 0) bytes = 16;
-  check_cuda(cudaMalloc(&p, bytes), "cudaMalloc");
+  check_cuda(device_malloc(&p, bytes), "cudaMalloc");
   allocations.push_back(p);
   return p;
 }
@@ -179,7 +197,7 @@ static wgx_buffer *make_buffer(wgx_context *ctx, int device, uint64_t size, uint
   b->usage = usage;
   b->device = device;
   set_device(device);
-  cudaError_t e = cudaMalloc(&b->dptr, size);
+  cudaError_t e = device_malloc(&b->dptr, size);
   if (e != cudaSuccess) {
     delete b;
     cudaGetLastError();
@@ -196,6 +214,14 @@ extern "C" {
 const char *wgx_last_error(void) { return g_last_error.c_str(); }
 
 int wgx_version(void) { return 1; }
+
+int wgx_debug_inject(uint32_t flags) {
+  return guarded([&] {
+    if (flags & ~uint32_t(WGX_INJECT_ALLOC_FAIL | WGX_INJECT_SKIP_LOADS))
+      fail("wgx_debug_inject: unknown flags");
+    g_inject.store(flags);
+  });
+}
 
 int wgx_device_count(int *count) {
   return guarded([&] {
@@ -458,7 +484,7 @@ static ExecEnv ensure_workspace(wgx_context *ctx) {
     if (ctx->workspace) cudaFree(ctx->workspace);
     ctx->workspace = nullptr;
     ctx->workspace_bytes = 0;
-    check_cuda(cudaMalloc(&ctx->workspace, ws), "cudaMalloc(workspace)");
+    check_cuda(device_malloc(&ctx->workspace, ws), "cudaMalloc(workspace)");
     ctx->workspace_bytes = ws;
   }
   return ExecEnv{ctx->stream, ctx->workspace, ctx->workspace_bytes};
@@ -637,9 +663,9 @@ int wgx_pipeline_create(wgx_context *ctx, wgx_tensor *input, wgx_tensor *output,
         v->assign(depth, nullptr);
       p->used.assign(depth, false);
       for (int k = 0; k < depth; ++k) {
-        check_cuda(cudaMalloc(&p->sin[k], std::max<uint64_t>(p->in_bytes, 16)),
+        check_cuda(device_malloc(&p->sin[k], std::max<uint64_t>(p->in_bytes, 16)),
                    "pipeline staging (input)");
-        check_cuda(cudaMalloc(&p->sout[k], std::max<uint64_t>(p->out_bytes, 16)),
+        check_cuda(device_malloc(&p->sout[k], std::max<uint64_t>(p->out_bytes, 16)),
                    "pipeline staging (output)");
         for (auto *v : {&p->uploaded, &p->in_free, &p->computed, &p->out_free})
           check_cuda(cudaEventCreateWithFlags(&(*v)[k], cudaEventDisableTiming),

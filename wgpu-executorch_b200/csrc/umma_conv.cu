@@ -49,6 +49,7 @@
 // pipeline returns an error instead of hanging the GPU.
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <utility>
 
 #include "tcgen05.h"
@@ -153,6 +154,9 @@ struct UmmaGeom {
   int nout;
   int out_c0[kMaxOut + 1];
   __half *outp[kMaxOut];
+  // failure-detection tests (WGX_INJECT_SKIP_LOADS): the producer issues no
+  // copies, so the other roles' bounded waits run out
+  int inject_skip;
 };
 
 // MMA groups (filter tap x 16-channel step) of one stage whose descriptor
@@ -164,7 +168,7 @@ constexpr int kSeqGroups = 8;
 
 static uint32_t smem_need(const UmmaGeom &g) {
   return g.w_region_bytes + uint32_t(g.stages) * g.b_stage_bytes + EPI_BYTES +
-         (2 * g.stages + 7) * 8 + 16 + kMaxGroups * 8 + kMaxKhg * kMaxPhases * 4 + 1024;
+         (2 * g.stages + 8) * 8 + 16 + kMaxGroups * 8 + kMaxKhg * kMaxPhases * 4 + 1024;
 }
 
 // Geometry for one staging choice: each pipeline stage carries `bk` input
@@ -1354,7 +1358,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t *full = bars, *empty = bars + S;
   uint64_t *accf = bars + 2 * S, *acce = accf + 2, *wbar = acce + 2;
   uint64_t *xbar = wbar + 1;  // folded-column epilogue exchange, per tile parity
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xbar + 2);
+  uint64_t *dbar = xbar + 2;  // MMA thread's drain of its MMAs after a timeout
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(dbar + 1);
   // generic staging: (activation, weight) descriptor offsets of every MMA
   // group of a stage, in 16-byte units (written and read by the MMA thread)
   uint2 *grp_off = reinterpret_cast<uint2 *>(tmem_slot + 4);
@@ -1373,6 +1378,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     mbar_init(smem_u32(wbar), 1);
     for (int j = 0; j < 2; ++j) mbar_init(smem_u32(&xbar[j]), EPI_WARPS);
+    mbar_init(smem_u32(dbar), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -1392,7 +1398,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #endif
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (lane == 0 && !g.inject_skip) {
       // ---------------- producer: bulk copies of weights + activation rows
       const uint32_t b_copy = uint32_t(g.R) * 16;
       if (g.resident) {
@@ -1420,6 +1426,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (use > 0 && !mbar_wait(smem_u32(&empty[slot]), (use - 1) & 1)) {
             atomicOr(g.err, kErrLoadTimeout);
             ok = false;
+            // this stage was not issued: step back so the drain below
+            // waits only for copies in flight
+            if (slot == 0) {
+              slot = S - 1;
+              --use;
+            } else {
+              --slot;
+            }
             break;
           }
           WGX_PROF_ADD(pr_empty, tw0);
@@ -1452,6 +1466,18 @@ __global__ void __launch_bounds__(THREADS, 1)
             bulk_g2s(smem_u32(sB + size_t(slot) * g.b_stage_bytes + size_t(ch) * g.R_alloc * 16),
                      xs + (plane * g.plane_rows + row0) * 16, b_copy, fb);
           }
+        }
+      }
+      // Before the CTA exits, every copy this thread issued must have landed
+      // (bounded waits). Slot j's last fill is use (j <= slot) or use - 1;
+      // its barrier completed no later phase, so the parity test is exact.
+      // On the normal path every wait succeeds at its first try.
+      if (g.resident && !mbar_wait(smem_u32(wbar), 0)) atomicOr(g.err, kErrLoadTimeout);
+      for (int j = 0; j < S; ++j) {
+        const int last = j <= slot ? use : use - 1;
+        if (last >= 0 && !mbar_wait(smem_u32(&full[j]), uint32_t(last) & 1)) {
+          atomicOr(g.err, kErrLoadTimeout);
+          break;
         }
       }
 #ifdef WGX_PROF
@@ -1675,6 +1701,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           mma_commit(smem_u32(&empty[slot]));
         }
         if (ok) mma_commit(smem_u32(&accf[acc]));
+      }
+      if (!ok) {
+        // a wait ran out: let the MMAs already issued finish (bounded)
+        // before TMEM is released at the end of the kernel
+        mma_commit(smem_u32(dbar));
+        if (!mbar_wait(smem_u32(dbar), 0)) atomicOr(g.err, kErrMmaTimeout);
       }
 #ifdef WGX_PROF
       g_umma_prof[blockIdx.x][1] = pm_acce;
@@ -2119,6 +2151,7 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   g.err = device_error_word(dev);
+  g.inject_skip = inject_skip_loads() ? 1 : 0;
   if ((reinterpret_cast<uintptr_t>(xs) & 15) || (reinterpret_cast<uintptr_t>(packed) & 15))
     fail("conv2d: scratch must be 16-byte aligned");
   // ---- input sources
@@ -2346,16 +2379,23 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   const int kidx = g.hs  ? 144 + hs_idx * 3 + act_idx
                    : ext ? 126 + nt_idx * 3 + act_idx
                          : (nt_idx * 7 + kw_idx) * 3 + act_idx;
+  // per (device, kernel) set-up, cached; host threads launching on one
+  // device share the tables, so they are read and written under a lock
+  static std::mutex setup_mu;
   static bool attr_set[64][160] = {};
-  if (dev < 64 && !attr_set[dev][kidx]) {
-    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    int(SMEM_MAX)),
-               "umma_conv smem attr");
-    attr_set[dev][kidx] = true;
-  }
   static int sms[64] = {};
-  if (dev < 64 && !sms[dev]) sms[dev] = sm_count();
-  const int n_sm = dev < 64 ? sms[dev] : sm_count();
+  int n_sm = 0;
+  {
+    std::lock_guard<std::mutex> lock(setup_mu);
+    if (dev >= 64 || !attr_set[dev][kidx]) {
+      check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(SMEM_MAX)),
+                 "umma_conv smem attr");
+      if (dev < 64) attr_set[dev][kidx] = true;
+    }
+    if (dev < 64 && !sms[dev]) sms[dev] = sm_count();
+    n_sm = dev < 64 ? sms[dev] : sm_count();
+  }
   const int grid = g.total_tiles < n_sm ? g.total_tiles : n_sm;
   int th = timer_begin("umma_conv_kernel", stream);
   kern<<<grid, THREADS, smem, stream>>>(g, static_cast<const uint8_t *>(xs),

@@ -1,8 +1,10 @@
 """ctypes binding of the C ABI declared in include/wgx.h.
 
-Loads the in-tree ``lib/libwgx.so``. There is no fallback: when the library
-is missing this module raises at import, so nothing can silently run on a
-CPU path.
+Maps the in-tree ``lib/libwgx.so`` on first use: importing the package
+(e.g. for the pure-Python program transforms in ``wgx.programs``) maps
+nothing, and the first call through ``lib`` loads the library. There is no
+fallback: when the library is missing, that first call raises ImportError,
+so nothing can silently run on a CPU path. ``load()`` maps it eagerly.
 """
 from __future__ import annotations
 
@@ -29,6 +31,7 @@ DTYPE_BYTESIZE = {"float32": 4, "float16": 2, "float64": 8, "int32": 4, "int64":
 ARG_NULL, ARG_TENSOR, ARG_NUMBER, ARG_BOOL, ARG_INT_LIST, ARG_TENSOR_LIST, ARG_STRING = range(7)
 
 ACT_NONE, ACT_CLAMP, ACT_SILU = 0, 1, 2
+INJECT_ALLOC_FAIL, INJECT_SKIP_LOADS = 1, 2
 CONV_UMMA, CONV_SIMT_GEMM, CONV_DEPTHWISE, CONV_DIRECT, CONV_POINTWISE1 = 1, 2, 3, 4, 5
 
 
@@ -98,6 +101,7 @@ SIGNATURES = {
     "wgx_conv2d_noalloc": ([POINTER(ConvParams), c_void_p, c_void_p, c_void_p, c_void_p,
                             c_void_p], c_int),
     "wgx_device_error": ([c_int, POINTER(c_uint32), c_int], c_int),
+    "wgx_debug_inject": ([c_uint32], c_int),
     "wgx_kernel_timing": ([c_int], c_int),
     "wgx_kernel_timing_read": ([c_char_p, POINTER(c_double), POINTER(c_int64), c_int], c_int),
 }
@@ -123,7 +127,25 @@ def _load() -> ctypes.CDLL:
     return lib
 
 
-lib = _load()
+class _Library:
+    """The C ABI, mapped on first attribute access (see the module
+    docstring)."""
+
+    _cdll = None
+
+    def __getattr__(self, name):
+        if _Library._cdll is None:
+            _Library._cdll = _load()
+        return getattr(_Library._cdll, name)
+
+
+lib = _Library()
+
+
+def load() -> ctypes.CDLL:
+    """Maps the library now (raises ImportError when it is not built)."""
+    lib.wgx_last_error  # noqa: B018  (first access maps it)
+    return _Library._cdll
 
 
 def check(code: int) -> None:
