@@ -238,6 +238,9 @@ def test_dense_f16_cuda_core_fallback(ctx, geom):
     (1, 12, 24, 24, 3, 1, 2, 2),
     (3, 32, 40, 40, 3, 1, 1, 1),
     (1, 4, 224, 224, 3, 2, 1, 1),
+    (2, 16, 24, 32, 7, 1, 3, 1),     # fp16 sliding-window kernel, K = 7
+    (1, 4, 160, 320, 3, 1, 1, 1),    # sliding-window kernel in row bands
+    (3, 5, 16, 40, 5, 1, 2, 1),      # planes that do not fill a CTA
 ])
 @pytest.mark.parametrize("dtype", [np.float16, np.float32])
 def test_depthwise(ctx, geom, dtype):
@@ -302,6 +305,23 @@ def engine_mm(ctx, a, b):
 def test_mm_fp32_config1(ctx):
     # A[512,512] @ B[512,512], U(-1,1), seed 0
     a, b = oracle.make_inputs([(512, 512), (512, 512)], seed=0, dist="uniform", dtype=np.float32)
+    y = engine_mm(ctx, a, b)
+    assert oracle.rel_err(y, oracle.mm(a, b, "exact")) <= F32_TOL
+    assert oracle.rel_err(y, oracle.mm(a, b, "wgsl")) <= F32_TOL
+
+
+@pytest.mark.parametrize("mkn", [
+    (64, 4096, 64),     # one tile: K split over a cluster of 8 CTAs
+    (100, 300, 72),     # K % 4 == 0, N % 4 == 0, partial tiles
+    (1000, 129, 515),   # K and N not multiples of 4: scalar loads
+    (7, 1000, 9),
+    (640, 64, 640),     # 100 tiles, K too short to split
+    (1, 2048, 1),
+])
+def test_mm_fp32_shapes(ctx, mkn):
+    """The split-K cluster FFMA kernel against both oracle modes."""
+    M, K, N = mkn
+    a, b = oracle.make_inputs([(M, K), (K, N)], seed=81, dist="uniform", dtype=np.float32)
     y = engine_mm(ctx, a, b)
     assert oracle.rel_err(y, oracle.mm(a, b, "exact")) <= F32_TOL
     assert oracle.rel_err(y, oracle.mm(a, b, "wgsl")) <= F32_TOL

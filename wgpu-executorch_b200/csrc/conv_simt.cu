@@ -17,6 +17,7 @@
 // All of them apply bias, then the activation (clamp or SiLU) in fp32 and
 // round once to the storage type.
 #include <algorithm>
+#include <mutex>
 
 #include "internal.h"
 #include "umma_conv.h"
@@ -721,6 +722,222 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ------------------------------- fp16 depthwise, sliding window per thread
+// Stride 1, dilation 1, square K in {3, 5, 7} with "same" padding
+// (pH = pW = (K-1)/2), rows of whole 16-byte vectors (IW % 8 == 0), 16-byte
+// aligned tensors. Same arithmetic as depthwise_tiled_h2 (and the
+// reference's conv2d-depthwise-f16.wgsl.ts: f16 accumulator started at the
+// bias, taps added in (kh, kw) order), so the results are identical; what
+// changes is the work per instruction, which the half2 FMA pipe bounds:
+//  * one CTA stages P whole planes (or a band of TH output rows of one
+//    plane) with cp.async 16-byte copies, zero-filled outside the image
+//    (no per-element index arithmetic; the loop steps are precomputed);
+//  * each thread owns 8 output columns x RB output rows and slides down
+//    RB + K - 1 staged input rows: per input row three shared loads (the 8
+//    + K - 1 columns it needs), the odd-offset column pairs by one byte
+//    permute each, and K*K*4 HFMA2 into the (at most K) output rows the
+//    row feeds, with the K*K weight pairs in registers; an output row is
+//    stored (16 bytes) as soon as its last input row is added.
+// Staged column 8 + iw holds input column iw; columns 0-7 and those past
+// the image are zero (the halo).
+struct DwSlide {
+  int P, TH, bands, rows, TWs, n_cg, n_rb, threads;
+  long long planes;
+};
+constexpr int DWS_RB = 8;  // output rows per thread
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  const int n = valid ? 16 : 0;  // 0: no bytes read, 16 zero bytes written
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n)
+               : "memory");
+}
+
+template <int K>
+__global__ void __launch_bounds__(256, 2)
+    depthwise_slide_h2(ConvGeom g, DwSlide d, const __half *__restrict__ x,
+                       const __half *__restrict__ w, const __half *__restrict__ bias,
+                       __half *__restrict__ out) {
+  constexpr int PW = (K - 1) / 2;
+  constexpr int RB = DWS_RB;
+  constexpr int KK1 = K * K + 1;  // weights + bias of one plane
+  extern __shared__ __align__(16) unsigned char dw_smem[];
+  __half *tile = reinterpret_cast<__half *>(dw_smem);
+  const int tid = threadIdx.x;
+  const long long plane0 = (long long)(blockIdx.x / d.bands) * d.P;
+  const int oh0 = int(blockIdx.x % d.bands) * d.TH;
+  const int np = int(min((long long)d.P, d.planes - plane0));
+  const int plane_tile = d.rows * d.TWs;
+  __half2 *wsm = reinterpret_cast<__half2 *>(tile + size_t(d.P) * plane_tile);
+  {
+    // staging: thread -> (vector column v, first row r0), rows step rstep
+    const int vrow = d.TWs / 8;
+    const int v = tid % vrow, r0 = tid / vrow, rstep = blockDim.x / vrow;
+    const int iw0 = v * 8 - 8;
+    const bool col_in = iw0 >= 0 && iw0 < g.IW;
+    const size_t hw = size_t(g.IH) * g.IW;
+    if (r0 < rstep) {
+      for (int p = 0; p < np; ++p) {
+        const __half *src = x + size_t(plane0 + p) * hw;
+        __half *dst = tile + p * plane_tile + v * 8;
+        for (int r = r0; r < d.rows; r += rstep) {
+          const int ih = oh0 - PW + r;
+          const bool ok = col_in && ih >= 0 && ih < g.IH;
+          cp_async16(dst + r * d.TWs, ok ? src + size_t(ih) * g.IW + iw0 : src, ok);
+        }
+      }
+    }
+  }
+  for (int i = tid; i < np * KK1; i += blockDim.x) {
+    const int p = i / KK1, t = i - p * KK1;
+    const int c = int((plane0 + p) % g.OC);
+    const __half v = t < K * K ? w[size_t(c) * K * K + t]
+                               : (g.has_bias ? bias[c] : __float2half_rn(0.f));
+    wsm[i] = __halves2half2(v, v);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  // compute: thread -> (plane p, row block rb, column group cg)
+  const int cg = tid % d.n_cg;
+  const int rest = tid / d.n_cg;
+  const int rb = rest % d.n_rb, p = rest / d.n_rb;
+  if (p >= np) return;
+  const int ow0 = cg * 8, r0 = rb * RB;  // r0: first output row of the block in the band
+  const int oh_end = min(oh0 + d.TH, g.OH);
+  __half2 wv[K * K];
+  const __half2 *wp = wsm + p * KK1;
+#pragma unroll
+  for (int t = 0; t < K * K; ++t) wv[t] = wp[t];
+  const __half2 b2 = wp[K * K];
+  // staged columns ow0 .. ow0 + 23 (input columns ow0 - 8 .. ow0 + 15)
+  const __half *rowp = tile + p * plane_tile + r0 * d.TWs + ow0;
+  __half *op = out + size_t(plane0 + p) * g.OH * g.OW + ow0;
+  __half2 acc[RB][4];
+#pragma unroll
+  for (int r = 0; r < RB; ++r)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[r][j] = b2;
+#pragma unroll
+  for (int ir = 0; ir < RB + K - 1; ++ir) {
+    // window words wd[k] = staged halves 2k, 2k + 1 of the row from column
+    // ow0; only those the filter reaches are loaded
+    const __half *src = rowp + ir * d.TWs;
+    uint32_t wd[12];
+    {
+      const uint4 bq = *reinterpret_cast<const uint4 *>(src + 8);
+      wd[4] = bq.x, wd[5] = bq.y, wd[6] = bq.z, wd[7] = bq.w;
+      if constexpr (PW <= 2) {
+        wd[3] = *reinterpret_cast<const uint32_t *>(src + 6);
+        wd[8] = *reinterpret_cast<const uint32_t *>(src + 16);
+      } else {
+        const uint2 a = *reinterpret_cast<const uint2 *>(src + 4);
+        const uint2 c = *reinterpret_cast<const uint2 *>(src + 16);
+        wd[2] = a.x, wd[3] = a.y, wd[8] = c.x, wd[9] = c.y;
+      }
+    }
+    // pair i = input columns ow0 - PW + i, +1 (odd offsets: one permute);
+    // (output pair j, tap kw) reads pair 2j + kw <= K + 5
+    uint32_t pr[K + 6];
+#pragma unroll
+    for (int i = 0; i < K + 6; ++i) {
+      const int h = 8 - PW + i;
+      pr[i] = (h & 1) ? __byte_perm(wd[h >> 1], wd[(h >> 1) + 1], 0x5432) : wd[h >> 1];
+    }
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      const int kh = ir - r;
+      if (kh < 0 || kh >= K) continue;
+#pragma unroll
+      for (int kw = 0; kw < K; ++kw)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          acc[r][j] = __hfma2(*reinterpret_cast<const __half2 *>(&pr[2 * j + kw]),
+                              wv[kh * K + kw], acc[r][j]);
+    }
+    // output row ir - (K - 1) is complete
+    if (ir >= K - 1) {
+      const int r = ir - (K - 1);
+      const int oh = oh0 + r0 + r;
+      if (oh < oh_end) {
+        uint32_t res[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          __half2 v = acc[r][j];
+          if (g.act == WGX_ACT_SILU) {
+            // v * sigmoid(v) = h + h * tanh(h), h = v / 2
+            const __half2 h = __hmul2(v, __float2half2_rn(0.5f));
+            const uint32_t hu = *reinterpret_cast<const uint32_t *>(&h);
+            uint32_t tu;
+            asm("tanh.approx.f16x2 %0, %1;" : "=r"(tu) : "r"(hu));
+            v = __hfma2(h, *reinterpret_cast<const __half2 *>(&tu), h);
+          } else if (g.act == WGX_ACT_CLAMP) {
+            const float2 f = __half22float2(v);
+            v = __floats2half2_rn(fminf(fmaxf(f.x, g.lo), g.hi), fminf(fmaxf(f.y, g.lo), g.hi));
+          }
+          res[j] = *reinterpret_cast<const uint32_t *>(&v);
+        }
+        *reinterpret_cast<uint4 *>(op + size_t(oh) * g.OW) =
+            make_uint4(res[0], res[1], res[2], res[3]);
+      }
+    }
+  }
+}
+
+// Tiling of depthwise_slide_h2 (see there), or false when it does not apply.
+static int dw_sm_count() {
+  int dev = 0, n = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  check_cuda(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev), "SM count");
+  return n > 0 ? n : 1;
+}
+
+static bool dw_slide_tiling(const wgx_conv2d_params &p, DwSlide &d, size_t &smem, int n_sm) {
+  const int K = p.KH;
+  if (p.dtype != WGX_FLOAT16 || p.KW != K || (K != 3 && K != 5 && K != 7)) return false;
+  if (p.sH != 1 || p.sW != 1 || p.dH != 1 || p.dW != 1) return false;
+  if (p.pH != (K - 1) / 2 || p.pW != (K - 1) / 2 || p.IW % 8 != 0) return false;
+  if (p.OH != p.IH || p.OW != p.IW) return false;
+  d.n_cg = p.OW / 8;
+  // staged row: 8 zero columns, the interior, then zeros up to the last
+  // column group's window end (ow0 + 24)
+  d.TWs = 8 * d.n_cg + 16;
+  d.planes = (long long)p.B * p.OC;
+  const size_t wbytes = size_t(K * K + 1) * 4;
+  // whole planes when one plane's items fit 256 threads and its tile fits
+  // the shared-memory budget, else bands of TH output rows
+  const int budget = 96 * 1024;
+  int TH = p.OH;
+  auto items = [&](int th) { return d.n_cg * ((th + DWS_RB - 1) / DWS_RB); };
+  auto tbytes = [&](int th) {
+    return size_t((th + DWS_RB - 1) / DWS_RB * DWS_RB + K - 1) * d.TWs * 2 + wbytes;
+  };
+  while (TH > DWS_RB && (items(TH) > 256 || tbytes(TH) > size_t(budget)))
+    TH = (TH / 2 + DWS_RB - 1) / DWS_RB * DWS_RB;
+  if (items(TH) > 256 || tbytes(TH) > size_t(budget)) return false;
+  d.TH = TH;
+  d.bands = (p.OH + TH - 1) / TH;
+  d.n_rb = (TH + DWS_RB - 1) / DWS_RB;
+  d.rows = d.n_rb * DWS_RB + K - 1;
+  d.P = 1;
+  if (d.bands == 1) {
+    // as many planes as fill 256 threads and the budget, but no fewer than
+    // two CTAs per SM when there are planes enough (small planes: 16^2 has
+    // 4 items per plane)
+    const long long per_sm2 = (d.planes + 2ll * n_sm - 1) / (2ll * n_sm);
+    d.P = int(std::max(1ll, std::min<long long>({(long long)(256 / items(TH)),
+                                                  (long long)(budget / tbytes(TH)), d.planes,
+                                                  per_sm2})));
+  }
+  const int vrow = d.TWs / 8;
+  auto threads_for = [&](int P) {
+    return std::min(256, std::max((P * items(TH) + 31) / 32 * 32, (vrow + 31) / 32 * 32));
+  };
+  d.threads = threads_for(d.P);
+  smem = size_t(d.P) * (size_t(d.rows) * d.TWs * 2 + wbytes);
+  const long long ctas = (d.planes + d.P - 1) / d.P * d.bands;
+  return ctas < (1ll << 31) && vrow <= d.threads && d.P * items(TH) <= d.threads;
+}
+
 // Tiling of depthwise_tiled for p (stride 1, dilation 1, square K in
 // {3,5,7}, pW <= DW_PADL), or false when it does not apply.
 static bool dw_tiling(const wgx_conv2d_params &p, int esize, DwTile &d) {
@@ -817,10 +1034,16 @@ bool conv2d_in_place_safe(const wgx_conv2d_params &p) {
   if (plan.variant == WGX_CONV_UMMA) return true;
   // tiled depthwise with whole planes per CTA: each CTA stages its planes in
   // shared memory before writing them, and no other CTA reads those planes
+  // (either depthwise kernel may run: the sliding-window one when the
+  // pointers are 16-byte aligned; both must stage whole planes)
   DwTile d{};
+  DwSlide ds{};
+  size_t ds_smem = 0;
   const int esize = p.dtype == WGX_FLOAT16 ? 2 : 4;
+  // (the band split does not depend on the SM count)
+  const bool slide_whole = !dw_slide_tiling(p, ds, ds_smem, 1) || ds.bands == 1;
   return plan.variant == WGX_CONV_DEPTHWISE && dw_tiling(p, esize, d) && d.bands == 1 &&
-         p.OH == p.IH && p.OW == p.IW;
+         slide_whole && p.OH == p.IH && p.OW == p.IW;
 }
 
 uint64_t conv2d_packed_weight_bytes(const wgx_conv2d_params &p) {
@@ -853,6 +1076,8 @@ static void launch_simt(const wgx_conv2d_params &p, int variant, const T *in, co
                         const T *bias, T *out, cudaStream_t s) {
   ConvGeom g = geom_of(p);
   DwTile dt{};
+  DwSlide ds{};
+  size_t ds_smem = 0;
   if (variant == WGX_CONV_SIMT_GEMM) {
     long long N = (long long)p.B * p.OH * p.OW;
     dim3 grid(unsigned((N + 63) / 64), unsigned((p.OC + 63) / 64));
@@ -863,6 +1088,32 @@ static void launch_simt(const wgx_conv2d_params &p, int variant, const T *in, co
     if (p.B > 65535) fail("conv2d: batch too large for the single-channel kernel");
     dim3 grid(unsigned((hw + 255) / 256), unsigned(p.B));
     pointwise_single<T><<<grid, 256, 0, s>>>(g, in, w, bias, out);
+  } else if (variant == WGX_CONV_DEPTHWISE && sizeof(T) == 2 &&
+             ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) == 0 &&
+             dw_slide_tiling(p, ds, ds_smem, dw_sm_count())) {
+    const __half *hin = reinterpret_cast<const __half *>(in);
+    const __half *hw = reinterpret_cast<const __half *>(w);
+    const __half *hb = reinterpret_cast<const __half *>(bias);
+    __half *hout = reinterpret_cast<__half *>(out);
+    auto fn = p.KH == 3 ? depthwise_slide_h2<3> : p.KH == 5 ? depthwise_slide_h2<5> : depthwise_slide_h2<7>;
+    static std::mutex mu;
+    static bool attr[3] = {};
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      if (!attr[p.KH / 2 - 1]) {
+        check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024),
+                   "depthwise smem attr");
+        attr[p.KH / 2 - 1] = true;
+      }
+    }
+    if (ds_smem > 100 * 1024) fail("conv2d: depthwise tile exceeds 100 KB");
+    const unsigned grid = unsigned((ds.planes + ds.P - 1) / ds.P * ds.bands);
+    if (p.KH == 3)
+      depthwise_slide_h2<3><<<grid, ds.threads, ds_smem, s>>>(g, ds, hin, hw, hb, hout);
+    else if (p.KH == 5)
+      depthwise_slide_h2<5><<<grid, ds.threads, ds_smem, s>>>(g, ds, hin, hw, hb, hout);
+    else
+      depthwise_slide_h2<7><<<grid, ds.threads, ds_smem, s>>>(g, ds, hin, hw, hb, hout);
   } else if (variant == WGX_CONV_DEPTHWISE && dw_tiling(p, int(sizeof(T)), dt)) {
     constexpr int V = 16 / sizeof(T);
     // staging: 1 = whole-vector rows, 3 = whole 8-byte-unit rows, 2 = vector
@@ -1031,63 +1282,172 @@ uint64_t mm_scratch_bytes(int64_t M, int64_t N, int64_t K, int dtype) {
   return conv2d_scratch_bytes(mm_params(M, N, K, dtype), true);
 }
 
-// fp32 aten.mm, C[M,N] = A[M,K] B[K,N] row-major (mm-64x64.wgsl.ts's GEMM,
-// fp32 FMAs in K order as there): a 32x32 output tile per CTA of 256
-// threads, 2x2 outputs per thread, 64-deep K steps through shared memory,
-// the next step's global loads held in registers while this step's FMAs
-// run. 32x32 tiles give a 512 x 512 product 256 CTAs (64x64 tiles: 64 CTAs
-// for 148 SMs, each with a long serial K loop). A is stored k-major
-// (As[k][m], one pad column: conflict-free transposing stores), B as is.
+// fp32 aten.mm, C[M,N] = A[M,K] B[K,N] row-major (mm-64x64.wgsl.ts's GEMM:
+// fp32 FMAs, K ascending within each part). A 64x64 output tile per CTA of
+// 256 threads, 4x4 outputs per thread. K advances in 32-deep steps through a
+// 4-stage cp.async pipeline (A rows [64][32 + 4 pad], B rows [32][64], zero
+// fill past the matrix), so three steps' loads are in flight while one
+// step's FMAs run; per 4 k a thread reads its 4 A rows and 4 B rows as
+// 16-byte words (8 shared loads for 64 FMAs). The K range is split over the
+// S CTAs of a thread-block cluster (S = 1, 2, 4 or 8, chosen so that the grid
+// covers the SMs: a 512 x 512 product has 64 tiles, S = 4 gives 256 CTAs);
+// each CTA leaves its partial tile in shared memory and, after a cluster
+// barrier, CTA r sums rows [r*64/S, (r+1)*64/S) of the S partials in rank
+// order through distributed shared memory (deterministic) and stores them.
 namespace {
-constexpr int MM_T = 32, MM_BK = 64, MM_LD = MM_T * MM_BK / 256;  // loads per thread and operand
+constexpr int MM_T = 64, MM_BK = 32, MM_AS = MM_BK + 4, MM_NS = 4;
+constexpr int MM_STAGE_FLOATS = MM_T * MM_AS + MM_BK * MM_T;
+constexpr uint32_t MM_SMEM = MM_NS * MM_STAGE_FLOATS * 4;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// the shared-memory address `p` of this CTA, seen in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t dsmem_addr(const void *p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+               : "=r"(out)
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+// 4 consecutive floats src[0..3] into shared memory: one 16-byte copy when
+// `vec`, else four 4-byte copies. Elements i >= valid (past the matrix) are
+// zero-filled and read nothing; their copies take the (aligned) matrix base
+// `base` as their source address.
+__device__ __forceinline__ void cp_async_f4(float *dst, const float *src, const float *base,
+                                            bool vec, int valid) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  if (vec) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d),
+                 "l"(valid >= 4 ? src : base), "r"(valid >= 4 ? 16 : 0)
+                 : "memory");
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d + 4 * i),
+                   "l"(i < valid ? src + i : base), "r"(i < valid ? 4 : 0)
+                   : "memory");
+  }
+}
 
 __global__ void __launch_bounds__(256) mm_f32_kernel(const float *__restrict__ A,
                                                      const float *__restrict__ B,
-                                                     float *__restrict__ C, int M, int N, int K) {
-  __shared__ float As[MM_BK][MM_T + 1];
-  __shared__ __align__(16) float Bs[MM_BK][MM_T];
+                                                     float *__restrict__ C, int M, int N, int K,
+                                                     int kchunk, int avec, int bvec) {
+  extern __shared__ __align__(16) float mm_smem[];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int m0 = blockIdx.y * MM_T, n0 = blockIdx.x * MM_T;
-  float ra[MM_LD], rb[MM_LD];
-  auto load = [&](int k0) {
+  const int S = gridDim.z;
+  const int kb = blockIdx.z * kchunk, ke = min(K, kb + kchunk);
+  const int nsteps = ke > kb ? (ke - kb + MM_BK - 1) / MM_BK : 0;
+  // copies per stage: A rows m = tid/8 and tid/8 + 32, k quad tid%8; B rows
+  // k = tid/16 and tid/16 + 16, column quad tid%16
+  // (avec / bvec: 16-byte copies; K % 4 == 0 / N % 4 == 0 and 16-byte
+  // aligned bases, checked on the host)
+  auto issue = [&](int step) {
+    float *As = mm_smem + (step % MM_NS) * MM_STAGE_FLOATS;
+    float *Bs = As + MM_T * MM_AS;
+    const int k0 = kb + step * MM_BK;
 #pragma unroll
-    for (int u = 0; u < MM_LD; ++u) {
-      const int e = tid + 256 * u;
-      const int ar = e / MM_BK, ac = e % MM_BK;  // A: row m, column k
-      const int br = e / MM_T, bc = e % MM_T;    // B: row k, column n
-      ra[u] = (m0 + ar < M && k0 + ac < K) ? A[size_t(m0 + ar) * K + k0 + ac] : 0.f;
-      rb[u] = (k0 + br < K && n0 + bc < N) ? B[size_t(k0 + br) * N + n0 + bc] : 0.f;
+    for (int h = 0; h < 2; ++h) {
+      const int m = (tid >> 3) + 32 * h, kq = (tid & 7) * 4;
+      const int k = k0 + kq;
+      const int valid = (m0 + m < M) ? max(0, min(4, ke - k)) : 0;
+      cp_async_f4(As + m * MM_AS + kq, valid > 0 ? A + size_t(m0 + m) * K + k : A, A, avec != 0,
+                  valid);
+      const int kr = (tid >> 4) + 16 * h, nq = (tid & 15) * 4;
+      const int kk = k0 + kr;
+      const int bvalid = (kk < ke) ? max(0, min(4, N - (n0 + nq))) : 0;
+      cp_async_f4(Bs + kr * MM_T + nq, bvalid > 0 ? B + size_t(kk) * N + n0 + nq : B, B,
+                  bvec != 0, bvalid);
     }
   };
-  float acc[2][2] = {};
-  load(0);
-  for (int k0 = 0; k0 < K; k0 += MM_BK) {
+  float acc[4][4] = {};
 #pragma unroll
-    for (int u = 0; u < MM_LD; ++u) {
-      const int e = tid + 256 * u;
-      As[e % MM_BK][e / MM_BK] = ra[u];
-      Bs[e / MM_T][e % MM_T] = rb[u];
-    }
-    __syncthreads();
-    if (k0 + MM_BK < K) load(k0 + MM_BK);
-#pragma unroll
-    for (int kk = 0; kk < MM_BK; ++kk) {
-      const float a0 = As[kk][2 * ty], a1 = As[kk][2 * ty + 1];
-      const float2 b = *reinterpret_cast<const float2 *>(&Bs[kk][2 * tx]);
-      acc[0][0] = fmaf(a0, b.x, acc[0][0]);
-      acc[0][1] = fmaf(a0, b.y, acc[0][1]);
-      acc[1][0] = fmaf(a1, b.x, acc[1][0]);
-      acc[1][1] = fmaf(a1, b.y, acc[1][1]);
-    }
-    __syncthreads();
+  for (int st = 0; st < MM_NS - 1; ++st) {
+    if (st < nsteps) issue(st);
+    asm volatile("cp.async.commit_group;" ::: "memory");
   }
+  for (int step = 0; step < nsteps; ++step) {
+    // step's copies are complete once at most MM_NS - 2 newer groups remain
+    asm volatile("cp.async.wait_group %0;" ::"n"(MM_NS - 2) : "memory");
+    __syncthreads();
+    // refill the stage consumed one step ago (every thread is past it)
+    if (step + MM_NS - 1 < nsteps) issue(step + MM_NS - 1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const float *As = mm_smem + (step % MM_NS) * MM_STAGE_FLOATS;
+    const float *Bs = As + MM_T * MM_AS;
 #pragma unroll
-  for (int i = 0; i < 2; ++i)
+    for (int k4 = 0; k4 < MM_BK; k4 += 4) {
+      float4 a[4], b[4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int m = m0 + 2 * ty + i, n = n0 + 2 * tx + j;
-      if (m < M && n < N) C[size_t(m) * N + n] = acc[i][j];
+      for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4 *>(As + (ty * 4 + i) * MM_AS + k4);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) b[kk] = *reinterpret_cast<const float4 *>(Bs + (k4 + kk) * MM_T + tx * 4);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float bv[4] = {b[kk].x, b[kk].y, b[kk].z, b[kk].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float av = kk == 0 ? a[i].x : kk == 1 ? a[i].y : kk == 2 ? a[i].z : a[i].w;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av, bv[j], acc[i][j]);
+        }
+      }
     }
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  if (S == 1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
+        if (m < M && n < N) C[size_t(m) * N + n] = acc[i][j];
+      }
+    return;
+  }
+  // the partial tile [64][64] over the (now idle) pipeline stages
+  __syncthreads();
+  float *Ps = mm_smem;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    *reinterpret_cast<float4 *>(Ps + (ty * 4 + i) * MM_T + tx * 4) =
+        make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+  cluster_sync_all();
+  // rows [r*64/S, (r+1)*64/S) of the tile: sum of the S partials, rank order
+  const uint32_t r = cluster_rank();
+  const int rows = MM_T / S, row0 = int(r) * rows;
+  for (int e = tid; e < rows * (MM_T / 4); e += blockDim.x) {
+    const int row = row0 + e / (MM_T / 4), c4 = (e % (MM_T / 4)) * 4;
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < S; ++q) {
+      const float4 v = ld_dsmem_f4(dsmem_addr(Ps + row * MM_T + c4, uint32_t(q)));
+      sum.x += v.x, sum.y += v.y, sum.z += v.z, sum.w += v.w;
+    }
+    const int m = m0 + row;
+    if (m < M) {
+      const float sv[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (n0 + c4 + j < N) C[size_t(m) * N + n0 + c4 + j] = sv[j];
+    }
+  }
+  // no CTA leaves while another may still read its partial
+  cluster_sync_all();
 }
 }  // namespace
 
@@ -1097,10 +1457,43 @@ void launch_mm(const void *a, const void *b, void *out, int64_t M, int64_t N, in
   if (dtype == WGX_FLOAT32) {
     const int64_t gy = (M + MM_T - 1) / MM_T, gx = (N + MM_T - 1) / MM_T;
     if (gy > 65535 || gx > INT32_MAX) fail("aten.mm.default: matrix too large");
-    mm_f32_kernel<<<dim3(unsigned(gx), unsigned(gy)), 256, 0, stream>>>(
-        static_cast<const float *>(a), static_cast<const float *>(b), static_cast<float *>(out),
-        int(M), int(N), int(K));
-    check_cuda(cudaGetLastError(), "mm launch");
+    // split K over a cluster of S CTAs until the grid covers the SMs
+    // (S divides the tile's 64 rows; each part keeps at least 64 of K)
+    const int64_t tiles = gx * gy;
+    int S = 1;
+    while (S < 8 && tiles * S < dw_sm_count() && K / (2 * S) >= 64) S *= 2;
+    const int kchunk = int(((K + S - 1) / S + MM_BK - 1) / MM_BK * MM_BK);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(gx), unsigned(gy), unsigned(S));
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.dynamicSmemBytes = MM_SMEM;
+    cfg.stream = stream;
+    {
+      static std::mutex mu;
+      static bool attr_set[64] = {};
+      int dev = 0;
+      check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+      std::lock_guard<std::mutex> lock(mu);
+      if (dev >= 64 || !attr_set[dev]) {
+        check_cuda(cudaFuncSetAttribute(mm_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(MM_SMEM)),
+                   "mm smem attr");
+        if (dev < 64) attr_set[dev] = true;
+      }
+    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = unsigned(S);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    check_cuda(cudaLaunchKernelEx(&cfg, mm_f32_kernel, static_cast<const float *>(a),
+                                  static_cast<const float *>(b), static_cast<float *>(out), int(M),
+                                  int(N), int(K), kchunk,
+                                  int(K % 4 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0),
+                                  int(N % 4 == 0 && (reinterpret_cast<uintptr_t>(b) & 15) == 0)),
+               "mm launch");
     return;
   }
   launch_conv2d(p, b, a, nullptr, nullptr, out, scratch, scratch_bytes, stream);
