@@ -580,6 +580,31 @@ __global__ void pack_input(UmmaGeom g, const __half *__restrict__ x, uint4 *__re
   xs[i] = *reinterpret_cast<const uint4 *>(v);
 }
 
+// Warp-cooperative store of 4 consecutive 16-byte slots per lane: lane l's
+// slots k (lo_l <= k < hi_l) go to dst_l + k. Written directly, every warp
+// store would put 16 bytes into each of 32 lines 64 bytes apart; staged in
+// the warp's 2 KB of shared memory (16-byte units XOR-swizzled within each
+// 128 bytes: conflict-free both ways), each store instruction writes 32
+// consecutive entries (lane l's run continues lane l + 1's when they share a
+// row, which is the common case). All 32 lanes must call it.
+__device__ __forceinline__ int slot_swz(int j) { return j ^ ((j >> 3) & 7); }
+__device__ __forceinline__ void warp_store4(uint4 *wbuf, const uint4 (&v)[4], uint4 *dst, int lo,
+                                            int hi) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) wbuf[slot_swz(lane * 4 + k)] = v[k];
+  __syncwarp();
+  const unsigned long long dptr = reinterpret_cast<unsigned long long>(dst);
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const int j = m * 32 + lane, t = j >> 2, k = j & 3;
+    const unsigned long long d = __shfl_sync(0xffffffffu, dptr, t);
+    const int tlo = __shfl_sync(0xffffffffu, lo, t), thi = __shfl_sync(0xffffffffu, hi, t);
+    if (k >= tlo && k < thi) reinterpret_cast<uint4 *>(d)[k] = wbuf[slot_swz(j)];
+  }
+  __syncwarp();
+}
+
 // Vector form of pack_input for IW % 4 == 0: one thread re-lays 4
 // consecutive padded positions of one 8-channel block. The first position
 // wp0 = 4t + (pW % 4) - 4 is chosen so that its input column iw0 = wp0 - pW
@@ -587,10 +612,13 @@ __global__ void pack_input(UmmaGeom g, const __half *__restrict__ x, uint4 *__re
 // the 8x4 block is transposed in registers (prmt) and written as four
 // 16-byte slots (64 contiguous bytes). Positions outside [0, Wp) are
 // skipped; padding positions and channels >= IC are written as zeros.
-__global__ void pack_input_v4(UmmaGeom g, const __half *__restrict__ x, uint4 *__restrict__ xs,
-                              int groups_per_row, long long n_threads) {
+__global__ void __launch_bounds__(256)
+    pack_input_v4(UmmaGeom g, const __half *__restrict__ x, uint4 *__restrict__ xs,
+                  int groups_per_row, long long n_threads) {
+  __shared__ uint4 wstage[8][128];
   long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n_threads) return;
+  const bool active = i < n_threads;
+  if (!active) i = n_threads - 1;  // inactive lanes still join the warp store
   const int t = int(i % groups_per_row);
   long long r = i / groups_per_row;
   const int hp = int(r % g.Hp);
@@ -621,19 +649,21 @@ __global__ void pack_input_v4(UmmaGeom g, const __half *__restrict__ x, uint4 *_
       }
     }
   }
-  uint4 *dst = xs + ((b * (g.C8 / 8) + cb) * g.Hp + hp) * (long long)g.Wp;
+  uint4 *dst = xs + ((b * (g.C8 / 8) + cb) * g.Hp + hp) * (long long)g.Wp + wp0;
+  uint4 vv[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int wp = wp0 + k;
-    if (wp < 0 || wp >= g.Wp) continue;
     // halves of position k: low (k even) or high (k odd) half of word k/2
     const uint32_t sel = (k & 1) ? 0x7632u : 0x5410u;
     const bool lo = k < 2;
-    dst[wp] = make_uint4(__byte_perm(lo ? ch[0].x : ch[0].y, lo ? ch[1].x : ch[1].y, sel),
-                         __byte_perm(lo ? ch[2].x : ch[2].y, lo ? ch[3].x : ch[3].y, sel),
-                         __byte_perm(lo ? ch[4].x : ch[4].y, lo ? ch[5].x : ch[5].y, sel),
-                         __byte_perm(lo ? ch[6].x : ch[6].y, lo ? ch[7].x : ch[7].y, sel));
+    vv[k] = make_uint4(__byte_perm(lo ? ch[0].x : ch[0].y, lo ? ch[1].x : ch[1].y, sel),
+                       __byte_perm(lo ? ch[2].x : ch[2].y, lo ? ch[3].x : ch[3].y, sel),
+                       __byte_perm(lo ? ch[4].x : ch[4].y, lo ? ch[5].x : ch[5].y, sel),
+                       __byte_perm(lo ? ch[6].x : ch[6].y, lo ? ch[7].x : ch[7].y, sel));
   }
+  // positions outside [0, Wp) are skipped
+  const int klo = active ? max(0, -wp0) : 4, khi = active ? min(4, g.Wp - wp0) : 0;
+  warp_store4(wstage[threadIdx.x >> 5], vv, dst, klo, khi);
 }
 
 // Vector form of pack_input for IW % 8 == 0: one thread re-lays 8
@@ -650,7 +680,16 @@ __device__ __forceinline__ void pack_weights_body(const UmmaGeom &g, const __hal
 // (blocks past n_in_blocks): the small weight packing costs no launch of its
 // own on the per-call path. Each input thread handles one 8-position group
 // of one padded row (b, 8-channel block, hp); index math is 32-bit (the
-// host checks the ranges).
+// host checks the ranges). The CTA's items are consecutive (row, group)
+// pairs, so the slots they write form one contiguous run of xs: the threads
+// put their slots in shared memory (16-byte units XOR-swizzled within each
+// 128 bytes, so that a thread's 8 consecutive slots and 8 threads' equal
+// slots fall in distinct banks) and the CTA then stores the run with
+// coalesced 16-byte writes (a thread's own 8 slots, written directly, would
+// make every warp store touch 32 different 128-byte lines).
+constexpr int PACK_SLOTS = 256 * 8;
+__device__ __forceinline__ int pack_swz(int s) { return s ^ ((s >> 3) & 7); }
+
 __global__ void __launch_bounds__(256, 4)
     pack_input_v8(UmmaGeom g, const __half *__restrict__ x, uint4 *__restrict__ xs,
                   int groups_per_row, int n_items, int n_in_blocks,
@@ -660,23 +699,30 @@ __global__ void __launch_bounds__(256, 4)
     if (w && i < n_w) pack_weights_body(g, w, packed, i);
     return;
   }
-  const int item = blockIdx.x * 256 + threadIdx.x;
-  if (item >= n_items) return;
-  const int row = item / groups_per_row;
-  const int t = item - row * groups_per_row;
-  const int ncb = g.C8 / 8;
-  const int hp = row % g.Hp;
-  const int rest = row / g.Hp;
-  const int cb = rest % ncb, b = rest / ncb;
-  const int ih = hp - g.pH;
-  const bool row_in = ih >= 0 && ih < g.IH;
-  const int nch = min(8, g.IC - cb * 8);
-  const size_t cstride = size_t(g.IH) * g.IW;
-  // every 8-channel block lies in one source (source boundaries are multiples of 8)
-  const __half *src0 = (nch > 0 ? src_plane(g, b, cb * 8) : x) + size_t(row_in ? ih : 0) * g.IW;
-  uint4 *dst = xs + size_t(row) * g.Wp;
-  {
-    const int wp0 = 8 * t + (g.pW & 7) - 8;
+  __shared__ uint4 stage[PACK_SLOTS];
+  const int ipw = g.pW & 7;
+  // the CTA's slot run [s0, s1]
+  const int item0 = blockIdx.x * 256;
+  const int item1 = min(n_items, item0 + 256) - 1;
+  const int r0 = item0 / groups_per_row, r1 = item1 / groups_per_row;
+  const long long s0 = (long long)r0 * g.Wp + max(0, 8 * (item0 - r0 * groups_per_row) + ipw - 8);
+  const long long s1 =
+      (long long)r1 * g.Wp + min(g.Wp - 1, 8 * (item1 - r1 * groups_per_row) + ipw - 1);
+  const int item = item0 + threadIdx.x;
+  if (item < n_items) {
+    const int row = item / groups_per_row;
+    const int t = item - row * groups_per_row;
+    const int ncb = g.C8 / 8;
+    const int hp = row % g.Hp;
+    const int rest = row / g.Hp;
+    const int cb = rest % ncb, b = rest / ncb;
+    const int ih = hp - g.pH;
+    const bool row_in = ih >= 0 && ih < g.IH;
+    const int nch = min(8, g.IC - cb * 8);
+    const size_t cstride = size_t(g.IH) * g.IW;
+    // every 8-channel block lies in one source (source boundaries are multiples of 8)
+    const __half *src0 = (nch > 0 ? src_plane(g, b, cb * 8) : x) + size_t(row_in ? ih : 0) * g.IW;
+    const int wp0 = 8 * t + ipw - 8;
     const int iw0 = wp0 - g.pW;  // a multiple of 8
     // IW % 8 == 0 and iw0 % 8 == 0: the 16-byte chunk [iw0, iw0 + 8) lies
     // either entirely inside the input row or entirely in the padding
@@ -686,6 +732,7 @@ __global__ void __launch_bounds__(256, 4)
     for (int e = 0; e < 8; ++e)
       ch[e] = (inside && e < nch) ? *reinterpret_cast<const uint4 *>(src0 + e * cstride + iw0)
                                   : make_uint4(0u, 0u, 0u, 0u);
+    const int srow = int((long long)row * g.Wp - s0);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int wp = wp0 + k;
@@ -698,10 +745,15 @@ __global__ void __launch_bounds__(256, 4)
         const uint4 &v = ch[e];
         wd[e] = (k >> 1) == 0 ? v.x : (k >> 1) == 1 ? v.y : (k >> 1) == 2 ? v.z : v.w;
       }
-      dst[wp] = make_uint4(__byte_perm(wd[0], wd[1], sel), __byte_perm(wd[2], wd[3], sel),
-                           __byte_perm(wd[4], wd[5], sel), __byte_perm(wd[6], wd[7], sel));
+      stage[pack_swz(srow + wp)] =
+          make_uint4(__byte_perm(wd[0], wd[1], sel), __byte_perm(wd[2], wd[3], sel),
+                     __byte_perm(wd[4], wd[5], sel), __byte_perm(wd[6], wd[7], sel));
     }
   }
+  __syncthreads();
+  const int n = int(s1 - s0 + 1);
+  uint4 *dst = xs + s0;
+  for (int i = threadIdx.x; i < n; i += 256) dst[i] = stage[pack_swz(i)];
 }
 
 // Space-to-depth re-layout for stride 2 with few input channels (XIC < 8,
@@ -715,8 +767,10 @@ template <int XIC>
 __global__ void __launch_bounds__(256)
     pack_input_s2d_small(UmmaGeom g, uint4 *__restrict__ xs, int groups_per_row, int qbase,
                          int n_items) {
-  const int item = blockIdx.x * 256 + threadIdx.x;
-  if (item >= n_items) return;
+  __shared__ uint4 wstage[8][128];
+  int item = blockIdx.x * 256 + threadIdx.x;
+  const bool active = item < n_items;
+  if (!active) item = n_items - 1;  // inactive lanes still join the warp stores
   const int t = item % groups_per_row;
   const int r = item / groups_per_row;
   const int hp = r % g.Hp, b = r / g.Hp;
@@ -735,13 +789,15 @@ __global__ void __launch_bounds__(256)
   }
   const int planes = g.C8 / 8;
   const size_t plane_rows = size_t(g.Hp) * g.Wp;
+  const int wp0 = q0 + g.pW;
+  // positions outside [0, Wp) are skipped
+  const int klo = active ? max(0, -wp0) : 4, khi = active ? min(4, g.Wp - wp0) : 0;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int wp = q0 + k + g.pW;
-    if (wp < 0 || wp >= g.Wp) continue;
+  for (int pl = 0; pl < 4; ++pl) {
+    if (pl >= planes) break;  // uniform across the CTA
+    uint4 vv[4];
 #pragma unroll
-    for (int pl = 0; pl < 4; ++pl) {
-      if (pl >= planes) break;
+    for (int k = 0; k < 4; ++k) {
       uint32_t w32[4];
 #pragma unroll
       for (int e2 = 0; e2 < 4; ++e2) {
@@ -761,9 +817,10 @@ __global__ void __launch_bounds__(256)
         }
         w32[e2] = h2;
       }
-      xs[(size_t(b) * planes + pl) * plane_rows + size_t(hp) * g.Wp + wp] =
-          make_uint4(w32[0], w32[1], w32[2], w32[3]);
+      vv[k] = make_uint4(w32[0], w32[1], w32[2], w32[3]);
     }
+    warp_store4(wstage[threadIdx.x >> 5], vv,
+                xs + (size_t(b) * planes + pl) * plane_rows + size_t(hp) * g.Wp + wp0, klo, khi);
   }
 }
 
@@ -860,8 +917,10 @@ __global__ void pack_input_s2d(UmmaGeom g, const __half *__restrict__ x, uint4 *
 __global__ void __launch_bounds__(256)
     pack_input_s2d_v8(UmmaGeom g, const __half *__restrict__ x, uint4 *__restrict__ xs,
                       int groups_per_row, int qbase, int n_items) {
-  const int item = blockIdx.x * 256 + threadIdx.x;
-  if (item >= n_items) return;
+  __shared__ uint4 wstage[8][128];
+  int item = blockIdx.x * 256 + threadIdx.x;
+  const bool active = item < n_items;
+  if (!active) item = n_items - 1;  // inactive lanes still join the warp stores
   const int t = item % groups_per_row;
   int r = item / groups_per_row;
   const int iph = r % g.nphH;
@@ -882,16 +941,18 @@ __global__ void __launch_bounds__(256)
     ch[e] = inside ? *reinterpret_cast<const uint4 *>(src0 + e * cstride)
                    : make_uint4(0u, 0u, 0u, 0u);
   const size_t plane_rows = size_t(g.Hp) * g.Wp;
+  const int wp0 = q0 + g.pW;
+  // positions outside [0, Wp) are skipped
+  const int klo = active ? max(0, -wp0) : 4, khi = active ? min(4, g.Wp - wp0) : 0;
 #pragma unroll
   for (int pw = 0; pw < 2; ++pw) {
     // virtual block of phase (iph, pw), real block cb
     const int vb = (iph * 2 + pw) * nb + cb;
-    uint4 *dst = xs + (size_t(b) * (g.C8 / 8) + vb) * plane_rows + size_t(hp) * g.Wp;
+    uint4 *dst = xs + (size_t(b) * (g.C8 / 8) + vb) * plane_rows + size_t(hp) * g.Wp + wp0;
     const uint32_t sel = pw ? 0x7632u : 0x5410u;
+    uint4 vv[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int wp = q0 + k + g.pW;
-      if (wp < 0 || wp >= g.Wp) continue;
       // column 2k+pw of each channel: half pw of word k
       uint32_t wd[8];
 #pragma unroll
@@ -899,9 +960,10 @@ __global__ void __launch_bounds__(256)
         const uint4 &v = ch[e];
         wd[e] = k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
       }
-      dst[wp] = make_uint4(__byte_perm(wd[0], wd[1], sel), __byte_perm(wd[2], wd[3], sel),
-                           __byte_perm(wd[4], wd[5], sel), __byte_perm(wd[6], wd[7], sel));
+      vv[k] = make_uint4(__byte_perm(wd[0], wd[1], sel), __byte_perm(wd[2], wd[3], sel),
+                         __byte_perm(wd[4], wd[5], sel), __byte_perm(wd[6], wd[7], sel));
     }
+    warp_store4(wstage[threadIdx.x >> 5], vv, dst, klo, khi);
   }
 }
 
