@@ -91,6 +91,31 @@ def test_bmm(ctx, bmkn, dt):
     assert err <= (2e-3 if dt == np.float16 else 1e-5)
 
 
+@pytest.mark.parametrize("bmkn", [
+    (2, 400, 32, 400),   # YOLO26-N PSA shapes of one image: channels on the MMA M side
+    (2, 64, 400, 400),   # positions on M (M <= 64), TMA reads of the [K][N] images
+    (3, 96, 64, 50),     # N % 8 != 0: re-laid input
+    (4, 130, 24, 72),    # two M tiles, K not a multiple of 16
+    (5, 16, 8, 64),
+])
+def test_bmm_fp16_tensor_cores(ctx, bmkn):
+    """fp16 aten.bmm on the tcgen05 pipeline (per-image weights): one weight
+    pack + the tensor-core kernel (+ re-layout when N % 8 != 0), against the
+    exact oracle batch by batch (fp16 bound of the tensor-core path)."""
+    import oracle
+    b, m, k, n = bmkn
+    a, bb = oracle.make_inputs([(b, m, k), (b, k, n)], seed=95, dist="uniform")
+    out = empty(ctx, (b, m, n), "float16")
+    ctx.recordShader(wgx.shaders.bmm, [T(ctx, a), T(ctx, bb), out])
+    assert ctx.stats()["kernel_launches"] == (2 if n % 8 == 0 else 3)
+    ctx.submit()
+    ctx.sync()
+    y = out.numpy()
+    ctx.reset()
+    for i in range(b):
+        assert oracle.rel_err(y[i], oracle.mm(a[i], bb[i], "exact")) <= 2e-3, i
+
+
 def maxpool_ref(x, k, s, p, d, ceil_mode, f16):
     N, C, H, W = x.shape
     def osz(n, kk, ss, pp, dd):

@@ -20,6 +20,7 @@
 #include <cmath>
 
 #include "internal.h"
+#include "umma_conv.h"
 
 namespace wgx {
 
@@ -453,6 +454,21 @@ void record_bmm(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   const void *pa = A->data(), *pb = B->data();
   void *pc = out->data();
   const int dt = A->dtype;
+  if (dt == WGX_FLOAT16 && umma_bmm_supported(batch, m, k, n)) {
+    // tcgen05 path: one weight-pack launch and the tensor-core kernel (plus
+    // the input re-layout when N % 8 != 0)
+    Command c;
+    c.name = name;
+    c.workspace_bytes = umma_bmm_scratch_bytes(batch, m, k, n);
+    c.kernel_launches = n % 8 == 0 ? 2 : 3;
+    c.run = [=](const ExecEnv &env) {
+      umma_bmm_run(static_cast<const __half *>(pa), static_cast<const __half *>(pb),
+                   static_cast<__half *>(pc), batch, m, k, n, env.workspace, env.workspace_bytes,
+                   env.stream);
+    };
+    ctx->commands.push_back(std::move(c));
+    return;
+  }
   const dim3 grid(unsigned((n + 63) / 64), unsigned((m + 63) / 64), unsigned(batch));
   push(ctx, name, 1, [=](const ExecEnv &env) {
     if (dt == WGX_FLOAT16)

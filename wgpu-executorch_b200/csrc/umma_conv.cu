@@ -157,6 +157,9 @@ struct UmmaGeom {
   // failure-detection tests (WGX_INJECT_SKIP_LOADS): the producer issues no
   // copies, so the other roles' bounded waits run out
   int inject_skip;
+  // per-image weights (a batched GEMM: aten.bmm as a 1x1 convolution whose
+  // weights differ per image): packed weight bytes per image, 0 = shared
+  uint64_t w_img_bytes;
 };
 
 // MMA groups (filter tap x 16-channel step) of one stage whose descriptor
@@ -188,7 +191,8 @@ static void phases(int K, int pad, int s, int &n, int *ph, int &d0, int &d1) {
   d1 = floor_div(K - 1 - pad, s);
 }
 
-static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans, int hs = 0) {
+static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans, int hs = 0,
+                         bool no_resident = false) {
   UmmaGeom g{};
   g.trans = trans;
   if (trans) {
@@ -312,7 +316,7 @@ static UmmaGeom geom_for(const wgx_conv2d_params &p, int khs, int bk, int trans,
   uint64_t w_all = uint64_t(g.n_kstages) * g.a_stage_bytes;
   g.resident = 0;
   g.stages = 0;
-  if (g.n_oct == 1 && w_all < SMEM_MAX) {
+  if (g.n_oct == 1 && w_all < SMEM_MAX && !no_resident) {
     g.w_region_bytes = uint32_t(w_all);
     g.stages = 2;
     if (smem_need(g) <= SMEM_MAX) {
@@ -411,7 +415,9 @@ static bool hsum_eligible(const wgx_conv2d_params &p) {
 // on config 2 (41 % tensor-pipe activity against 30 % for whole-filter
 // stages of 16 channels); whole-filter and 16-channel stages are the
 // fallbacks for shapes where fewer than three 32-channel stages fit.
-static UmmaGeom make_geom(const wgx_conv2d_params &p) {
+// per_image_w: the weights differ per image (batched GEMM), so they are
+// streamed per stage, never resident.
+static UmmaGeom make_geom(const wgx_conv2d_params &p, bool per_image_w = false) {
   // (khs, bk); khs 0 = the whole filter. Below 16 (virtual) channels,
   // 16-channel stages halve the zero padding of the K dimension.
   int cand[4][2] = {{1, 32}, {0, 16}, {1, 16}, {0, 32}};
@@ -448,7 +454,7 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p) {
   bool have = false;
   for (int min_stages : {3, 2}) {
     for (auto &c : cand) {
-      UmmaGeom g = geom_for(p, c[0], c[1], trans, hs);
+      UmmaGeom g = geom_for(p, c[0], c[1], trans, hs, per_image_w);
       if (g.stages >= min_stages && smem_need(g) <= SMEM_MAX && g.R_alloc * 16 < (1 << 18)) {
         return g;
       }
@@ -468,7 +474,7 @@ static uint32_t smem_bytes(const UmmaGeom &g) {
   return need < 120u * 1024u ? 120u * 1024u : need;
 }
 
-bool umma_conv_supported(const wgx_conv2d_params &p) {
+bool umma_conv_supported(const wgx_conv2d_params &p, bool per_image_w) {
   if (p.dtype != WGX_FLOAT16 || p.groups != 1) return false;
   if (p.sH < 1 || p.sW < 1 || p.sH > 4 || p.sW > 4) return false;
   if (p.dH < 1 || p.dW < 1 || p.pH < 0 || p.pW < 0) return false;
@@ -484,7 +490,7 @@ bool umma_conv_supported(const wgx_conv2d_params &p) {
     if (p.OH != (p.IH + 2 * p.pH - p.KH) / p.sH + 1) return false;
     if (p.OW != (p.IW + 2 * p.pW - p.KW) / p.sW + 1) return false;
   }
-  UmmaGeom g = make_geom(p);
+  UmmaGeom g = make_geom(p, per_image_w);
   if (g.KW > MAX_KW || g.IC < 8) return false;
   if (g.khs * g.KW * (g.bk / 16) > kMaxGroups) return false;
   if (g.stages < 2) return false;
@@ -521,8 +527,8 @@ uint64_t umma_conv_grid(const wgx_conv2d_params &p) {
   return uint64_t(g.total_tiles);
 }
 
-uint64_t umma_conv_packed_weight_bytes(const wgx_conv2d_params &p) {
-  UmmaGeom g = make_geom(p);
+uint64_t umma_conv_packed_weight_bytes(const wgx_conv2d_params &p, bool per_image_w) {
+  UmmaGeom g = make_geom(p, per_image_w);
   return uint64_t(g.n_oct) * g.n_kstages * g.a_stage_bytes;
 }
 
@@ -537,8 +543,8 @@ static uint64_t input_rows_total(const UmmaGeom &g) {
   return planes * g.plane_rows + slack;
 }
 
-uint64_t umma_conv_input_bytes(const wgx_conv2d_params &p) {
-  UmmaGeom g = make_geom(p);
+uint64_t umma_conv_input_bytes(const wgx_conv2d_params &p, bool per_image_w) {
+  UmmaGeom g = make_geom(p, per_image_w);
   return (input_rows_total(g) * 16 + 255) / 256 * 256;
 }
 
@@ -971,6 +977,17 @@ __global__ void pack_weights(UmmaGeom g, const __half *__restrict__ w, uint4 *__
                              int n_slots) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n_slots) pack_weights_body(g, w, packed, i);
+}
+
+// Per-image weights (batched GEMM): image img's OIHW weights at
+// w + img * w_img_elems pack into packed + img * n_img_slots.
+__global__ void pack_weights_batched(UmmaGeom g, const __half *__restrict__ w,
+                                     uint4 *__restrict__ packed, int n_img_slots,
+                                     long long w_img_elems, long long n_slots) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_slots) return;
+  const long long img = i / n_img_slots;
+  pack_weights_body(g, w + img * w_img_elems, packed + img * n_img_slots, int(i - img * n_img_slots));
 }
 
 // PTX helpers: tcgen05.h
@@ -1504,8 +1521,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_expect_tx(fb, (g.resident ? 0u : g.a_stage_bytes) + g.chunks * b_copy);
           if (!g.resident)
             bulk_g2s(smem_u32(sW + size_t(slot) * g.a_stage_bytes),
-                     wpk + (size_t(oct) * g.n_kstages + s) * g.a_stage_bytes, g.a_stage_bytes,
-                     fb);
+                     wpk + size_t(b) * g.w_img_bytes +
+                         (size_t(oct) * g.n_kstages + s) * g.a_stage_bytes,
+                     g.a_stage_bytes, fb);
           if (g.direct) {
             // TMA boxes of 64 positions x dbox channels: atom j (64 positions,
             // bk rows of 128 bytes) at j * bk * 128, channel group rows inside
@@ -2208,8 +2226,10 @@ bool umma_conv_link_ok(const wgx_conv2d_params &prod, const wgx_conv2d_params &c
 void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
                    const __half *w_to_pack, const __half *bias, __half *out, void *xs,
                    cudaStream_t stream, const UmmaLink *link) {
-  if (!umma_conv_supported(p)) fail("conv2d: shape not supported by the tensor-core path");
-  UmmaGeom g = make_geom(p);
+  const bool per_image_w = link && link->per_image_weights;
+  if (!umma_conv_supported(p, per_image_w))
+    fail("conv2d: shape not supported by the tensor-core path");
+  UmmaGeom g = make_geom(p, per_image_w);
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   g.err = device_error_word(dev);
@@ -2306,7 +2326,23 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
         encode_nchw_tmap(&tm.m[k], g.src[k], p.B, g.src_c0[k + 1] - g.src_c0[k], int(hw), dbox);
     }
   }
-  const uint64_t n_w64 = w_to_pack ? umma_conv_packed_weight_bytes(p) / 16 : 0;
+  // per-image weights: packed image after image (streamed per stage)
+  g.w_img_bytes = 0;
+  if (per_image_w) {
+    g.w_img_bytes = umma_conv_packed_weight_bytes(p, true);
+    if (w_to_pack) {
+      const long long n_img = (long long)(g.w_img_bytes / 16);
+      if (n_img >= (1ll << 31)) fail("conv2d: weights too large for the tensor-core path");
+      const long long total = n_img * p.B;
+      pack_weights_batched<<<unsigned((total + 255) / 256), 256, 0, stream>>>(
+          g, w_to_pack, static_cast<uint4 *>(packed), int(n_img),
+          (long long)p.OC * p.IC * p.KH * p.KW, total);
+      check_cuda(cudaGetLastError(), "pack_weights launch");
+    }
+  }
+  // shared weights still to pack (fused into the re-layout launch where it can be)
+  const __half *wtp = per_image_w ? nullptr : w_to_pack;
+  const uint64_t n_w64 = wtp ? umma_conv_packed_weight_bytes(p) / 16 : 0;
   if (n_w64 >= (1ull << 31)) fail("conv2d: weights too large for the tensor-core path");
   const int n_w = int(n_w64);
   const bool strided = g.sH != 1 || g.sW != 1;
@@ -2315,13 +2351,13 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
     // re-laid by the producer
   } else if (g.direct) {
     // read from NCHW by the kernel's TMA loads; only the weights may need packing
-    if (w_to_pack)
+    if (wtp)
       pack_weights<<<unsigned((n_w + 255) / 256), 256, 0, stream>>>(
-          g, w_to_pack, static_cast<uint4 *>(packed), n_w);
+          g, wtp, static_cast<uint4 *>(packed), n_w);
   } else if (strided) {
-    if (w_to_pack)
+    if (wtp)
       pack_weights<<<unsigned((n_w + 255) / 256), 256, 0, stream>>>(
-          g, w_to_pack, static_cast<uint4 *>(packed), n_w);
+          g, wtp, static_cast<uint4 *>(packed), n_w);
     if (g.sW == 2 && g.nphW == 2 && g.phW[0] == 0 && g.phW[1] == 1 && g.xIC % 8 == 0 &&
         g.IW % 8 == 0 && g.C8 == g.IC && srcs_aligned) {
       const int qbase = -4 * ((g.pW + 3) / 4);
@@ -2361,12 +2397,12 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
     const int n_in_blocks = int((n_items + 255) / 256);
     const int n_wblk = (n_w + 255) / 256;
     pack_input_v8<<<unsigned(n_in_blocks + n_wblk), 256, 0, stream>>>(
-        g, in, static_cast<uint4 *>(xs), groups_per_row, int(n_items), n_in_blocks, w_to_pack,
+        g, in, static_cast<uint4 *>(xs), groups_per_row, int(n_items), n_in_blocks, wtp,
         static_cast<uint4 *>(packed), n_w);
   } else {
-    if (w_to_pack)
+    if (wtp)
       pack_weights<<<unsigned((n_w + 255) / 256), 256, 0, stream>>>(
-          g, w_to_pack, static_cast<uint4 *>(packed), n_w);
+          g, wtp, static_cast<uint4 *>(packed), n_w);
     if (g.IW % 4 == 0 && srcs_aligned) {
       const int groups_per_row = (g.Wp - (g.pW & 3) + 4 + 3) / 4;
       long long n = (long long)g.B * (g.C8 / 8) * g.Hp * groups_per_row;
@@ -2464,6 +2500,61 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
                                         static_cast<const uint8_t *>(packed), bias, out, tm);
   check_cuda(cudaGetLastError(), "umma_conv launch");
   timer_end(th, stream);
+}
+
+// ------------------------------------------------------- batched GEMM
+// aten.bmm in fp16 on the tensor cores (src/shaders/bmm/index.ts:33-55:
+// C[b] = A[b] B[b], A [batch, M, K], B [batch, K, N], row-major): the 1x1
+// convolution of image b = B[b] (K channels of N positions, 1 x N) with
+// the per-image weights A[b] (M output channels x K input channels), so the
+// same tcgen05 pipeline, TMA reads of the [K][N] image (N % 8 == 0) and
+// epilogue serve it; each image's packed weights stream per stage.
+static wgx_conv2d_params bmm_params(int64_t batch, int64_t M, int64_t K, int64_t N) {
+  wgx_conv2d_params p{};
+  p.B = int(batch);
+  p.IC = int(K);
+  p.IH = 1;
+  p.IW = int(N);
+  p.OC = int(M);
+  p.OH = 1;
+  p.OW = int(N);
+  p.KH = p.KW = 1;
+  p.sH = p.sW = 1;
+  p.dH = p.dW = 1;
+  p.groups = 1;
+  p.has_bias = 0;
+  p.dtype = WGX_FLOAT16;
+  p.act = WGX_ACT_NONE;
+  p.out_min = -INFINITY;
+  p.out_max = INFINITY;
+  return p;
+}
+
+bool umma_bmm_supported(int64_t batch, int64_t M, int64_t K, int64_t N) {
+  if (batch < 1 || M < 1 || K < 1 || N < 1 || batch > INT32_MAX || M > INT32_MAX ||
+      K > INT32_MAX || N > INT32_MAX)
+    return false;
+  return umma_conv_supported(bmm_params(batch, M, K, N), true);
+}
+
+static uint64_t align256(uint64_t v) { return (v + 255) / 256 * 256; }
+
+uint64_t umma_bmm_scratch_bytes(int64_t batch, int64_t M, int64_t K, int64_t N) {
+  const wgx_conv2d_params p = bmm_params(batch, M, K, N);
+  return align256(uint64_t(batch) * umma_conv_packed_weight_bytes(p, true)) +
+         umma_conv_input_bytes(p, true);
+}
+
+void umma_bmm_run(const __half *A, const __half *B, __half *C, int64_t batch, int64_t M, int64_t K,
+                  int64_t N, void *scratch, uint64_t scratch_bytes, cudaStream_t stream) {
+  const wgx_conv2d_params p = bmm_params(batch, M, K, N);
+  if (scratch_bytes < umma_bmm_scratch_bytes(batch, M, K, N))
+    fail("aten.bmm.default: scratch too small");
+  UmmaLink link;
+  link.per_image_weights = true;
+  char *base = static_cast<char *>(scratch);
+  void *xs = base + align256(uint64_t(batch) * umma_conv_packed_weight_bytes(p, true));
+  umma_conv_run(p, B, base, A, nullptr, C, xs, stream, &link);
 }
 
 }  // namespace wgx
