@@ -879,6 +879,19 @@ def run_only(args):
         ctx.sync()
         print(json.dumps({"only": args.only, "steps": args.steps, "warmup": args.warmup,
                           "kernel_launches_per_step": ctx.stats()["kernel_launches"]}))
+    elif args.only == "mm0":
+        # fp32 mm 512^3 through wgx_mm
+        from wgx import _lib
+        M = N = Kd = 512
+        a = torch.rand(M, Kd, device="cuda:0") * 2 - 1
+        bm = torch.rand(Kd, N, device="cuda:0") * 2 - 1
+        c = torch.empty(M, N, device="cuda:0")
+        for _ in range(args.warmup + args.steps):
+            _lib.check(_lib.lib.wgx_mm(ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(bm.data_ptr()),
+                                       ctypes.c_void_p(c.data_ptr()), M, N, Kd, 0, None,
+                                       ctypes.c_uint64(0), ctypes.c_void_p(ctx.stream)))
+        ctx.sync()
+        print(json.dumps({"only": "mm0", "steps": args.steps, "warmup": args.warmup}))
     else:
         rng = np.random.default_rng(0)
         cfg = ONLY_CONV[args.only]
@@ -900,7 +913,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--only", default=None, choices=["yolo", "depthart"] + sorted(ONLY_CONV),
+    ap.add_argument("--only", default=None, choices=["yolo", "depthart", "mm0"] + sorted(ONLY_CONV),
                     help="run one workload's launches only (for profilers)")
     ap.add_argument("--batch", type=int, default=0,
                     help="images per GPU for --only (default: 64 for yolo, the listed batch otherwise)")

@@ -41,7 +41,9 @@
 // its A block. Two TMEM accumulators of 256 columns ping-pong, so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
 // Warp roles: warp 0 issues bulk copies, warp 1 owns TMEM and issues
-// tcgen05.mma, warps 4-19 drain TMEM (four warps per TMEM lane quadrant,
+// tcgen05.mma (with positions on M and several M blocks per tile, warp 2
+// issues every other M block: two issuers keep the tensor pipe busier on
+// short MMAs), warps 4-19 drain TMEM (four warps per TMEM lane quadrant,
 // 64 columns each) through bias + activation to NCHW global memory.
 //
 // Every mbarrier wait is bounded (about 2 s of %globaltimer); on expiry the
@@ -171,7 +173,7 @@ constexpr int kSeqGroups = 8;
 
 static uint32_t smem_need(const UmmaGeom &g) {
   return g.w_region_bytes + uint32_t(g.stages) * g.b_stage_bytes + EPI_BYTES +
-         (2 * g.stages + 8) * 8 + 16 + kMaxGroups * 8 + kMaxKhg * kMaxPhases * 4 + 1024;
+         (2 * g.stages + 9) * 8 + 16 + kMaxGroups * 8 + kMaxKhg * kMaxPhases * 4 + 1024;
 }
 
 // Geometry for one staging choice: each pipeline stage carries `bk` input
@@ -1424,6 +1426,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   constexpr int G_C = HS > 0 ? (NT_C == 32 ? 8 : NT_C == 48 ? 4 : NT_C == 96 ? 2 : 1)
                       : TRANS == 0 ? 1 : (TRANS == 64 || (TRANS & 1)) ? 4 : 8;
   constexpr int LG_NT = NT_C == 16 ? 4 : NT_C == 32 ? 5 : 6;
+  // positions on M with several M blocks per tile: two MMA threads (warps 1
+  // and 2), each issuing every other M block of every stage; a single
+  // thread's back-to-back tcgen05.mma issue (~56 cycles per MMA measured)
+  // is slower than the tensor pipe takes short MMAs from two issuers (~40
+  // cycles for N <= 32)
+  constexpr bool DUAL = TRANS > 0 && G_C >= 2;
+  constexpr int NISS = DUAL ? 2 : 1;
   // activation stages first, on a 1024-byte boundary (128-byte swizzle atoms
   // of the direct mode); stage sizes are multiples of 1024 bytes there
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -1437,8 +1446,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t *full = bars, *empty = bars + S;
   uint64_t *accf = bars + 2 * S, *acce = accf + 2, *wbar = acce + 2;
   uint64_t *xbar = wbar + 1;  // folded-column epilogue exchange, per tile parity
-  uint64_t *dbar = xbar + 2;  // MMA thread's drain of its MMAs after a timeout
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(dbar + 1);
+  uint64_t *dbar = xbar + 2;  // each MMA thread's drain of its MMAs after a timeout
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(dbar + 2);
   // generic staging: (activation, weight) descriptor offsets of every MMA
   // group of a stage, in 16-byte units (written and read by the MMA thread)
   uint2 *grp_off = reinterpret_cast<uint2 *>(tmem_slot + 4);
@@ -1449,17 +1458,48 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
-      mbar_init(smem_u32(&empty[s]), 1);
+      mbar_init(smem_u32(&empty[s]), NISS);
     }
     for (int a = 0; a < 2; ++a) {
-      mbar_init(smem_u32(&accf[a]), 1);
+      mbar_init(smem_u32(&accf[a]), NISS);
       mbar_init(smem_u32(&acce[a]), EPI_WARPS);
     }
     mbar_init(smem_u32(wbar), 1);
     for (int j = 0; j < 2; ++j) mbar_init(smem_u32(&xbar[j]), EPI_WARPS);
-    mbar_init(smem_u32(dbar), 1);
+    mbar_init(smem_u32(&dbar[0]), 1);
+    mbar_init(smem_u32(&dbar[1]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if constexpr (KW_T == 0) {
+    if (threadIdx.x == 32) {
+      // generic staging: the (activation, weight) descriptor offsets of every
+      // MMA group of a stage, read by the MMA thread(s) after the barrier
+      const uint32_t a_lbo = uint32_t(g.wrows) * 16, b_lbo = uint32_t(g.R_alloc) * 16;
+      const int ngroups = g.khs * g.KW * (g.bk / 16);
+      int j = 0;
+      for (int khl = 0; khl < g.khs; ++khl)
+        for (int kw = 0; kw < g.KW; ++kw)
+          for (int ks = 0; ks < g.bk / 16; ++ks, ++j) {
+            const uint32_t tap = uint32_t(khl * g.KW + kw);
+            const uint32_t shift = uint32_t(khl * g.dH * g.Wp + kw * g.dW);
+            grp_off[j] = make_uint2((shift * 16 + uint32_t(ks) * 2 * b_lbo) >> 4,
+                                    (tap * uint32_t(g.chunks) * a_lbo + uint32_t(ks) * 2 * a_lbo) >> 4);
+          }
+      if (TRANS && g.tapskip) {
+        // compacted lists: the groups whose tap meets real filter taps
+        int e = ngroups;
+        for (int khg = 0; khg < g.n_khg; ++khg)
+          for (int ph = 0; ph < g.nphH * g.nphW; ++ph) {
+            const uint32_t m = g.tapmask[khg][ph];
+            const int start = e;
+            for (int jj = 0; jj < ngroups; ++jj)
+              if ((m >> (jj / (g.bk / 16))) & 1) grp_off[e++] = grp_off[jj];
+            grp_list[2 * (khg * kMaxPhases + ph)] = uint16_t(start);
+            grp_list[2 * (khg * kMaxPhases + ph) + 1] = uint16_t(e - start);
+          }
+      }
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -1564,9 +1604,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       g_umma_prof[blockIdx.x][0] = pr_empty;
 #endif
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || (DUAL && warp == 2)) {
     if (lane == 0) {
-      // ---------------- MMA issuer
+      // ---------------- MMA issuer (iss 0: warp 1; with DUAL, iss 1: warp 2,
+      // the odd M blocks)
+      const int iss = warp - 1;
       WGX_PROF_T(tm_start);
       [[maybe_unused]] unsigned long long pm_acce = 0, pm_full = 0, pm_issue = 0, pm_tiles = 0;
       // (a = packed weights, b = staged activation rows, whichever MMA
@@ -1594,30 +1636,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
       }
       const int ngroups = g.khs * g.KW * (g.bk / 16);
-      if constexpr (KW_T == 0) {
-        int j = 0;
-        for (int khl = 0; khl < g.khs; ++khl)
-          for (int kw = 0; kw < g.KW; ++kw)
-            for (int ks = 0; ks < g.bk / 16; ++ks, ++j) {
-              const uint32_t tap = uint32_t(khl * g.KW + kw);
-              const uint32_t shift = uint32_t(khl * g.dH * g.Wp + kw * g.dW);
-              grp_off[j] = make_uint2((shift * 16 + uint32_t(ks) * 2 * b_lbo) >> 4,
-                                      (tap * uint32_t(g.chunks) * a_lbo + uint32_t(ks) * 2 * a_lbo) >> 4);
-            }
-        if (TRANS && g.tapskip) {
-          // compacted lists: the groups whose tap meets real filter taps
-          int e = ngroups;
-          for (int khg = 0; khg < g.n_khg; ++khg)
-            for (int ph = 0; ph < g.nphH * g.nphW; ++ph) {
-              const uint32_t m = g.tapmask[khg][ph];
-              const int start = e;
-              for (int jj = 0; jj < ngroups; ++jj)
-                if ((m >> (jj / (g.bk / 16))) & 1) grp_off[e++] = grp_off[jj];
-              grp_list[2 * (khg * kMaxPhases + ph)] = uint16_t(start);
-              grp_list[2 * (khg * kMaxPhases + ph) + 1] = uint16_t(e - start);
-            }
-        }
-      }
       int it = 0, slot = S - 1, use = -1;
       for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x, ++it) {
         const int acc = it & 1, use_acc = it >> 1;
@@ -1675,10 +1693,12 @@ __global__ void __launch_bounds__(THREADS, 1)
               const uint32_t xaddr = b_base + uint32_t(ks) * 2 * 1024;
               if constexpr (TRANS) {
 #pragma unroll
-                for (int mb = 0; mb < G_C; ++mb)
+                for (int k2 = 0; k2 < G_C / NISS; ++k2) {
+                  const int mb = k2 * NISS + iss;
                   mma_f16(d + uint32_t(mb * NT_C),
                           sw128_mn_desc(xaddr + uint32_t(mb) * 2 * x_lbo, x_lbo, 1024), wdesc,
                           idesc_mn, (acc_on | ks) != 0);
+                }
               } else {
                 mma_f16(d, wdesc, sw128_mn_desc(xaddr, x_lbo, 1024), idesc_mn, (acc_on | ks) != 0);
               }
@@ -1699,9 +1719,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
               for (int i = 0; i < 2 * KW_T; ++i)
 #pragma unroll
-                for (int mb = 0; mb < G_C; ++mb)
+                for (int k2 = 0; k2 < G_C / NISS; ++k2) {
+                  const int mb = k2 * NISS + iss;
                   mma_f16(d + uint32_t(mb * NT_C), b0 + uint64_t(mb * 128) + b_off[i],
                           a0 + a_off[i], idesc, (acc_on | i) != 0);
+                }
               acc_on = 1;
             } else {
               // (taps whose weights are all zero are skipped: tapskip)
@@ -1743,8 +1765,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   {                                                                                       \
     const uint64_t xd = x0 + e[K].x, wd = w0 + e[K].y;                                    \
     if constexpr (TRANS) {                                                                \
-      _Pragma("unroll") for (int mb = 0; mb < G_C; ++mb)                                  \
-          mma_f16(d + uint32_t(mb * NT_C), xd + uint64_t(mb * 128), wd, idesc, acc_flag); \
+      _Pragma("unroll") for (int k2 = 0; k2 < G_C / NISS; ++k2)                          \
+          mma_f16(d + uint32_t((k2 * NISS + iss) * NT_C), xd + uint64_t((k2 * NISS + iss) * 128), \
+                  wd, idesc, acc_flag);                                                   \
     } else {                                                                              \
       mma_f16(d, wd, xd, idesc, acc_flag);                                                \
     }                                                                                     \
@@ -1768,8 +1791,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint64_t xd = x0 + o.x, wd = w0 + o.y;
                 if constexpr (TRANS) {
 #pragma unroll
-                  for (int mb = 0; mb < G_C; ++mb)
+                  for (int k2 = 0; k2 < G_C / NISS; ++k2) {
+                    const int mb = k2 * NISS + iss;
                     mma_f16(d + uint32_t(mb * NT_C), xd + uint64_t(mb * 128), wd, idesc, acc_flag);
+                  }
                 } else {
                   mma_f16(d, wd, xd, idesc, acc_flag);
                 }
@@ -1785,16 +1810,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) {
         // a wait ran out: let the MMAs already issued finish (bounded)
         // before TMEM is released at the end of the kernel
-        mma_commit(smem_u32(dbar));
-        if (!mbar_wait(smem_u32(dbar), 0)) atomicOr(g.err, kErrMmaTimeout);
+        mma_commit(smem_u32(&dbar[iss]));
+        if (!mbar_wait(smem_u32(&dbar[iss]), 0)) atomicOr(g.err, kErrMmaTimeout);
       }
 #ifdef WGX_PROF
+      if (iss == 0) {
       g_umma_prof[blockIdx.x][1] = pm_acce;
       g_umma_prof[blockIdx.x][2] = pm_full;
       g_umma_prof[blockIdx.x][3] = pm_issue;
       g_umma_prof[blockIdx.x][6] = (unsigned long long)(clock64() - tm_start);
       g_umma_prof[blockIdx.x][13] = global_ns();
       g_umma_prof[blockIdx.x][7] = pm_tiles;
+      }
 #endif
     }
   } else if (warp >= EPI_WARP0) {
