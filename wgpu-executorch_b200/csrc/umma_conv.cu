@@ -1019,12 +1019,14 @@ __device__ __forceinline__ float epi_act(float acc, float bias, float hb, float 
 // half precision after one rounding of h = (acc + bias)/2: one
 // tanh.approx.f16x2 for both values and y = h + h*tanh(h) as one HFMA2
 // (the output is fp16, so the half-precision tail adds at most about one
-// fp16 rounding); the other activations round once from fp32.
+// fp16 rounding); the other activations round once from fp32. For SiLU the
+// bias arguments are the HALF biases (bias/2, staged that way by the
+// epilogues: one FMA per value).
 template <int ACT>
 __device__ __forceinline__ uint32_t epi_act2(float a0, float a1, float b0, float b1, float lo,
                                              float hi) {
   if constexpr (ACT == WGX_ACT_SILU) {
-    const __half2 h = __floats2half2_rn(fmaf(a0, 0.5f, 0.5f * b0), fmaf(a1, 0.5f, 0.5f * b1));
+    const __half2 h = __floats2half2_rn(fmaf(a0, 0.5f, b0), fmaf(a1, 0.5f, b1));
     const uint32_t hu = *reinterpret_cast<const uint32_t *>(&h);
     uint32_t tu;
     asm("tanh.approx.f16x2 %0, %1;" : "=r"(tu) : "r"(hu));
@@ -1201,7 +1203,8 @@ __device__ __forceinline__ void hsum_epilogue(const UmmaGeom &g, uint32_t tmem,
   const size_t plane = size_t(g.OH) * g.OW;
   float *sbias = reinterpret_cast<float *>(sE);
   for (int i = threadIdx.x - EPI_WARP0 * 32; i < NT_C; i += EPI_WARPS * 32)
-    sbias[i] = (g.has_bias && i < g.OC) ? __half2float(bias[i]) : 0.f;
+    sbias[i] = ((g.has_bias && i < g.OC) ? __half2float(bias[i]) : 0.f) *
+                (ACT_T == WGX_ACT_SILU ? 0.5f : 1.f);
   asm volatile("bar.sync 1, %0;" ::"r"(EPI_WARPS * 32) : "memory");
   uint16_t *tstage = reinterpret_cast<uint16_t *>(sE + 1024 + ew * 1024);
   float *xch = reinterpret_cast<float *>(sE + HS_XCH_OFF);
@@ -1840,7 +1843,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     // otherwise unused epilogue staging area
     float *sbias = reinterpret_cast<float *>(sE);
     for (int i = threadIdx.x - EPI_WARP0 * 32; i < NT_C; i += EPI_WARPS * 32)
-      sbias[i] = (g.has_bias && i < g.OC) ? __half2float(bias[i]) : 0.f;
+      sbias[i] = ((g.has_bias && i < g.OC) ? __half2float(bias[i]) : 0.f) *
+                (ACT_T == WGX_ACT_SILU ? 0.5f : 1.f);
     asm volatile("bar.sync 1, %0;" ::"r"(EPI_WARPS * 32) : "memory");
     // per-warp transpose rows of the vector-store path: 16 rows x 64 bytes
     // after the bias (1 KB reserved), 16 KB in all
@@ -2084,7 +2088,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int oc0 = oct * UM + q * 32;  // first channel of this quadrant
       const int oc_lane = oc0 + lane;
-      const float bv = (g.has_bias && oc_lane < g.OC) ? __half2float(bias[oc_lane]) : 0.f;
+      // (halved for SiLU: see epi_act2)
+      const float bv = ((g.has_bias && oc_lane < g.OC) ? __half2float(bias[oc_lane]) : 0.f) *
+                       (ACT_T == WGX_ACT_SILU ? 0.5f : 1.f);
       const int nrows = min(32, g.OC - oc0);  // valid channel rows of the quadrant
       // this lane stores rows rsel, rsel+4, ..., rsel+28 of the quadrant
       __half *rowp = out + (size_t(b) * g.OC + oc0 + rsel) * plane;
