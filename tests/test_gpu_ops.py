@@ -211,6 +211,39 @@ def test_upsample_bilinear(ctx, align):
     assert np.abs(out.numpy() - ref).max() <= 1e-5
 
 
+@pytest.mark.parametrize("align", [True, False])
+@pytest.mark.parametrize("shape,out_hw", [((2, 6, 32, 40), (64, 80)),    # 16-byte row groups
+                                          ((16, 24, 128, 128), (256, 256)),  # DepthART decoder
+                                          ((2, 5, 14, 14), (28, 21))])   # per-element path
+def test_upsample_bilinear_f16(ctx, align, shape, out_hw):
+    """fp16 bilinear (fp32 interpolation, one rounding) against an fp64
+    restatement of the same source-index rule."""
+    x = rnd(shape)
+    N, C, H, W = shape
+    OH, OW = out_hw
+    def src(o, n_in, n_out):
+        o = np.arange(o, dtype=np.float64)
+        if align:
+            return o * (n_in - 1) / (n_out - 1)
+        return (o + 0.5) * n_in / n_out - 0.5
+    sh, sw = src(OH, H, OH), src(OW, W, OW)
+    h0, w0 = np.floor(sh).astype(int), np.floor(sw).astype(int)
+    lh, lw = sh - h0, sw - w0
+    c = lambda v, n: np.clip(v, 0, n - 1)
+    xd = x.astype(np.float64)
+    v00 = xd[:, :, c(h0, H)][:, :, :, c(w0, W)]
+    v01 = xd[:, :, c(h0, H)][:, :, :, c(w0 + 1, W)]
+    v10 = xd[:, :, c(h0 + 1, H)][:, :, :, c(w0, W)]
+    v11 = xd[:, :, c(h0 + 1, H)][:, :, :, c(w0 + 1, W)]
+    top = v00 + (v01 - v00) * lw
+    bot = v10 + (v11 - v10) * lw
+    ref = top + (bot - top) * lh[:, None]
+    out = empty(ctx, (N, C, OH, OW), "float16")
+    run(ctx, wgx.shaders.upsampleBilinear2d, [T(ctx, x), [OH, OW], align, None, out])
+    y = out.numpy().astype(np.float64)
+    assert np.abs(y - ref).max() <= 2e-3 * np.abs(ref).max()
+
+
 def test_softmax_and_mean(ctx):
     x = rnd((2, 2, 40, 400))
     out = empty(ctx, x.shape, "float16")

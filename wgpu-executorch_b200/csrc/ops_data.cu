@@ -994,6 +994,40 @@ __global__ void bilinear_kernel(Resample r, const T *__restrict__ x, T *__restri
   }
 }
 
+// Bilinear, fp16, OW % 8 == 0, 32-bit index range: each thread writes 8
+// consecutive outputs of one output row with one 16-byte store. The row's
+// source rows and weight (h0, h1, lh) are computed once per thread and the
+// column terms per output, with the same fp32 arithmetic as bilinear_kernel
+// (identical results); thread -> (row, group) by one 32-bit division.
+__global__ void __launch_bounds__(256) bilinear_v8_kernel(Resample r, const __half *__restrict__ x,
+                                                          uint4 *__restrict__ y, int n8) {
+  const int i = blockIdx.x * 256 + threadIdx.x;
+  if (i >= n8) return;
+  const int ow8 = r.OW / 8;
+  const int row = i / ow8, g = i - row * ow8;
+  const int plane = row / r.OH, oh = row - plane * r.OH;
+  const float sh = src_index(oh, r.IH, r.OH, r.align);
+  const int h0 = int(floorf(sh));
+  const float lh = sh - float(h0);
+  const int h0c = min(max(h0, 0), r.IH - 1), h1c = min(max(h0 + 1, 0), r.IH - 1);
+  const __half *p0 = x + (size_t(plane) * r.IH + h0c) * r.IW;
+  const __half *p1 = x + (size_t(plane) * r.IH + h1c) * r.IW;
+  __align__(16) __half v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int ow = 8 * g + k;
+    const float sw = src_index(ow, r.IW, r.OW, r.align);
+    const int w0 = int(floorf(sw));
+    const float lw = sw - float(w0);
+    const int w0c = min(max(w0, 0), r.IW - 1), w1c = min(max(w0 + 1, 0), r.IW - 1);
+    const float v00 = __half2float(__ldg(p0 + w0c)), v01 = __half2float(__ldg(p0 + w1c));
+    const float v10 = __half2float(__ldg(p1 + w0c)), v11 = __half2float(__ldg(p1 + w1c));
+    const float top = v00 + (v01 - v00) * lw, bot = v10 + (v11 - v10) * lw;
+    v[k] = __float2half_rn(top + (bot - top) * lh);
+  }
+  y[i] = *reinterpret_cast<const uint4 *>(v);
+}
+
 // fp16, OW % 8 == 0: each thread writes 8 consecutive outputs of one row
 // with one 16-byte store (the 8 source reads hit the same cache lines).
 __global__ void nearest_v8_kernel(Resample r, const __half *__restrict__ x, uint4 *__restrict__ y,
@@ -1092,8 +1126,15 @@ void record_bilinear(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   void *py = out->data();
   const long long n = out->numel;
   const int dt = in->dtype;
+  const bool v8 = dt == WGX_FLOAT16 && r.OW % 8 == 0 && n / 8 < (1ll << 31) - 256 &&
+                  (reinterpret_cast<uintptr_t>(py) & 15) == 0 &&
+                  (long long)r.N * r.C * r.OH < (1ll << 31);
   push(ctx, name, 1, [=](const ExecEnv &env) {
-    if (dt == WGX_FLOAT16)
+    if (v8) {
+      const int n8 = int(n / 8);
+      bilinear_v8_kernel<<<unsigned((n8 + 255) / 256), 256, 0, env.stream>>>(
+          r, (const __half *)px, (uint4 *)py, n8);
+    } else if (dt == WGX_FLOAT16)
       bilinear_kernel<__half><<<blocks_for(n), 256, 0, env.stream>>>(r, (const __half *)px,
                                                                      (__half *)py, n);
     else
