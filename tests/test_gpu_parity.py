@@ -241,6 +241,8 @@ def test_dense_f16_cuda_core_fallback(ctx, geom):
     (2, 16, 24, 32, 7, 1, 3, 1),     # fp16 sliding-window kernel, K = 7
     (1, 4, 160, 320, 3, 1, 1, 1),    # sliding-window kernel in row bands
     (3, 5, 16, 40, 5, 1, 2, 1),      # planes that do not fill a CTA
+    (3, 40, 16, 16, 3, 2, 1, 1),     # strided, many small planes per CTA (DepthART shapes)
+    (2, 24, 32, 32, 5, 2, 2, 1),
 ])
 @pytest.mark.parametrize("dtype", [np.float16, np.float32])
 def test_depthwise(ctx, geom, dtype):

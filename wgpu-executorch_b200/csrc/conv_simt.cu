@@ -239,70 +239,86 @@ constexpr int DW_MAX_TAPS = 64;
 
 template <class T>
 __global__ void __launch_bounds__(DW_THREADS)
-    depthwise_conv(ConvGeom g, int TH, int TWs, const T *__restrict__ x, const T *__restrict__ w,
-                   const T *__restrict__ bias, T *__restrict__ out, int vec_in, int vec_out) {
+    depthwise_conv(ConvGeom g, int TH, int TWs, int P, long long planes, const T *__restrict__ x,
+                   const T *__restrict__ w, const T *__restrict__ bias, T *__restrict__ out,
+                   int vec_in, int vec_out) {
+  // P planes per CTA (small planes: one band each), or one plane's band of
+  // TH output rows (P = 1)
   extern __shared__ __align__(16) unsigned char dw_smem[];
-  float *wsm = reinterpret_cast<float *>(dw_smem);  // KH*KW weights
-  T *tile = reinterpret_cast<T *>(dw_smem + DW_MAX_TAPS * sizeof(float));
-  const int plane = blockIdx.x;  // b*C + c
-  const int c = plane % g.OC;
+  float *wsm = reinterpret_cast<float *>(dw_smem);  // [P][DW_MAX_TAPS] weights
+  T *tile = reinterpret_cast<T *>(dw_smem + size_t(P) * DW_MAX_TAPS * sizeof(float));
+  const long long plane0 = (long long)blockIdx.x * P;
+  const int np = int(min((long long)P, planes - plane0));
   const int oh0 = blockIdx.y * TH;
   const int taps = g.KH * g.KW;
-  for (int i = threadIdx.x; i < taps; i += blockDim.x) wsm[i] = ld_f(&w[(long long)c * taps + i]);
+  for (int i = threadIdx.x; i < np * taps; i += blockDim.x) {
+    const int pp = i / taps, t = i - pp * taps;
+    const int c = int((plane0 + pp) % g.OC);
+    wsm[pp * DW_MAX_TAPS + t] = ld_f(&w[(long long)c * taps + t]);
+  }
   const int rows = (TH - 1) * g.sH + (g.KH - 1) * g.dH + 1;
   const int ih0 = oh0 * g.sH - g.pH;
-  const T *xp = x + (long long)plane * g.IH * g.IW;
-  // stage rows [ih0, ih0+rows) x cols [-pW, -pW+TWs) into the tile; column j
-  // of the tile is input column j - pW.
-  if (vec_in) {
-    // interior: 16-byte vectors of 8 (f16) / 4 (f32) elements
-    constexpr int V = 16 / sizeof(T);
-    const int nvec = g.IW / V;
-    for (int idx = threadIdx.x; idx < rows * nvec; idx += blockDim.x) {
-      int r = idx / nvec, v = idx % nvec;
-      int ih = ih0 + r;
-      T *dst = tile + (long long)r * TWs + g.pW + v * V;
-      if (ih >= 0 && ih < g.IH) {
-        uint4 val = *reinterpret_cast<const uint4 *>(xp + (long long)ih * g.IW + v * V);
-        const T *vv = reinterpret_cast<const T *>(&val);
+  const size_t ptile = size_t(rows) * TWs;
+  // stage rows [ih0, ih0+rows) x cols [-pW, -pW+TWs) of each plane; column
+  // j of a tile is input column j - pW.
+  for (int pp = 0; pp < np; ++pp) {
+    const T *xp = x + (plane0 + pp) * (long long)g.IH * g.IW;
+    T *tl = tile + pp * ptile;
+    if (vec_in) {
+      // interior: 16-byte vectors of 8 (f16) / 4 (f32) elements
+      constexpr int V = 16 / sizeof(T);
+      const int nvec = g.IW / V;
+      for (int idx = threadIdx.x; idx < rows * nvec; idx += blockDim.x) {
+        int r = idx / nvec, v = idx % nvec;
+        int ih = ih0 + r;
+        T *dst = tl + (long long)r * TWs + g.pW + v * V;
+        if (ih >= 0 && ih < g.IH) {
+          uint4 val = *reinterpret_cast<const uint4 *>(xp + (long long)ih * g.IW + v * V);
+          const T *vv = reinterpret_cast<const T *>(&val);
 #pragma unroll
-        for (int e = 0; e < V; ++e) dst[e] = vv[e];
-      } else {
+          for (int e = 0; e < V; ++e) dst[e] = vv[e];
+        } else {
 #pragma unroll
-        for (int e = 0; e < V; ++e) dst[e] = to_t<T>(0.f);
+          for (int e = 0; e < V; ++e) dst[e] = to_t<T>(0.f);
+        }
       }
-    }
-    // left/right padding columns
-    const int padc = TWs - g.IW;
-    for (int idx = threadIdx.x; idx < rows * padc; idx += blockDim.x) {
-      int r = idx / padc, j = idx % padc;
-      int col = j < g.pW ? j : g.IW + j;
-      tile[(long long)r * TWs + col] = to_t<T>(0.f);
-    }
-  } else {
-    for (int idx = threadIdx.x; idx < rows * TWs; idx += blockDim.x) {
-      int r = idx / TWs, j = idx % TWs;
-      int ih = ih0 + r, iw = j - g.pW;
-      T v = to_t<T>(0.f);
-      if (ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW) v = xp[(long long)ih * g.IW + iw];
-      tile[(long long)r * TWs + j] = v;
+      // left/right padding columns
+      const int padc = TWs - g.IW;
+      for (int idx = threadIdx.x; idx < rows * padc; idx += blockDim.x) {
+        int r = idx / padc, j = idx % padc;
+        int col = j < g.pW ? j : g.IW + j;
+        tl[(long long)r * TWs + col] = to_t<T>(0.f);
+      }
+    } else {
+      for (int idx = threadIdx.x; idx < rows * TWs; idx += blockDim.x) {
+        int r = idx / TWs, j = idx % TWs;
+        int ih = ih0 + r, iw = j - g.pW;
+        T v = to_t<T>(0.f);
+        if (ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW) v = xp[(long long)ih * g.IW + iw];
+        tl[(long long)r * TWs + j] = v;
+      }
     }
   }
   __syncthreads();
-  const float bv = g.has_bias ? ld_f(&bias[c]) : 0.f;
   const int ohn = min(TH, g.OH - oh0);
   const int ngrp = (g.OW + 7) / 8;
-  T *op = out + (long long)plane * g.OH * g.OW;
-  for (int idx = threadIdx.x; idx < ohn * ngrp; idx += blockDim.x) {
-    int r = idx / ngrp, q = idx % ngrp;
+  const int per_plane = ohn * ngrp;
+  for (int idx = threadIdx.x; idx < np * per_plane; idx += blockDim.x) {
+    const int pp = idx / per_plane, rq = idx - pp * per_plane;
+    const int r = rq / ngrp, q = rq - r * ngrp;
+    const int c = int((plane0 + pp) % g.OC);
+    const float bv = g.has_bias ? ld_f(&bias[c]) : 0.f;
+    const float *wp = wsm + pp * DW_MAX_TAPS;
+    const T *tl = tile + pp * ptile;
+    T *op = out + (plane0 + pp) * (long long)g.OH * g.OW;
     int ow0 = q * 8;
     float acc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = bv;
     for (int kh = 0; kh < g.KH; ++kh) {
-      const T *trow = tile + (long long)(r * g.sH + kh * g.dH) * TWs;
+      const T *trow = tl + (long long)(r * g.sH + kh * g.dH) * TWs;
       for (int kw = 0; kw < g.KW; ++kw) {
-        float wv = wsm[kh * g.KW + kw];
+        float wv = wp[kh * g.KW + kw];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           int col = (ow0 + e) * g.sW + kw * g.dW;  // tile column (input col + pW)
@@ -1175,7 +1191,18 @@ static void launch_simt(const wgx_conv2d_params &p, int variant, const T *in, co
     };
     while (TH > 1 && tile_bytes(TH) > 40 * 1024) TH /= 2;
     if (TH > p.OH) TH = p.OH;
-    uint64_t smem = DW_MAX_TAPS * sizeof(float) + tile_bytes(TH) + 16;
+    long long planes = (long long)p.B * p.OC;
+    // small planes (one band): several per CTA, so that the CTA's 256
+    // threads have work (a 16x16 -> 8x8 plane has 8 items of 8 outputs)
+    int P = 1;
+    if (TH >= p.OH) {
+      const long long items = (long long)p.OH * ((p.OW + 7) / 8);
+      const uint64_t per_plane = DW_MAX_TAPS * sizeof(float) + tile_bytes(TH);
+      P = int(std::max<long long>(1, std::min<long long>({(long long)(DW_THREADS / items),
+                                                          (long long)(40 * 1024 / per_plane),
+                                                          planes})));
+    }
+    uint64_t smem = uint64_t(P) * (DW_MAX_TAPS * sizeof(float) + tile_bytes(TH)) + 16;
     if (smem > 200 * 1024) fail("conv2d: depthwise plane too wide");
     if (smem > 48 * 1024)
       check_cuda(cudaFuncSetAttribute(depthwise_conv<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1189,13 +1216,12 @@ static void launch_simt(const wgx_conv2d_params &p, int variant, const T *in, co
     // alignment matters.
     int vec_out = (p.OW % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0) &&
                   (((long long)p.OH * p.OW) % 8 == 0);
-    long long planes = (long long)p.B * p.OC;
     if (planes > 0x7fffffffLL) fail("conv2d: too many depthwise planes");
     if ((p.OH + TH - 1) / TH > 65535) fail("conv2d: depthwise plane too tall");
-    // planes on x (up to 2^31-1 blocks), row bands on y
-    dim3 grid(unsigned(planes), unsigned((p.OH + TH - 1) / TH));
-    depthwise_conv<T><<<grid, DW_THREADS, smem, s>>>(g, TH, TWs, in, w, bias, out, vec_in,
-                                                      vec_out);
+    // plane groups on x (up to 2^31-1 blocks), row bands on y
+    dim3 grid(unsigned((planes + P - 1) / P), unsigned((p.OH + TH - 1) / TH));
+    depthwise_conv<T><<<grid, DW_THREADS, smem, s>>>(g, TH, TWs, P, planes, in, w, bias, out,
+                                                      vec_in, vec_out);
   } else {
     long long total = (long long)p.B * p.OC * p.OH * p.OW;
     direct_conv<T><<<unsigned((total + 255) / 256), 256, 0, s>>>(g, in, w, bias, out, total);

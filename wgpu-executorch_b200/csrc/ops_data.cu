@@ -995,12 +995,26 @@ __global__ void bilinear_kernel(Resample r, const T *__restrict__ x, T *__restri
 }
 
 // Bilinear, fp16, OW % 8 == 0, 32-bit index range: each thread writes 8
-// consecutive outputs of one output row with one 16-byte store. The row's
-// source rows and weight (h0, h1, lh) are computed once per thread and the
-// column terms per output, with the same fp32 arithmetic as bilinear_kernel
-// (identical results); thread -> (row, group) by one 32-bit division.
+// consecutive outputs of one output row with one 16-byte store. The CTA
+// first tabulates every output column's source columns and weight in shared
+// memory (one fp32 division per column instead of per output); the row's
+// source rows and weight (h0, h1, lh) are computed once per thread. Same
+// fp32 arithmetic as bilinear_kernel (identical results); thread -> (row,
+// group) by one 32-bit division.
+struct BilinCol {
+  int16_t w0, w1;
+  float lw;
+};
 __global__ void __launch_bounds__(256) bilinear_v8_kernel(Resample r, const __half *__restrict__ x,
                                                           uint4 *__restrict__ y, int n8) {
+  extern __shared__ BilinCol bcol[];
+  for (int ow = threadIdx.x; ow < r.OW; ow += 256) {
+    const float sw = src_index(ow, r.IW, r.OW, r.align);
+    const int w0 = int(floorf(sw));
+    bcol[ow] = BilinCol{int16_t(min(max(w0, 0), r.IW - 1)), int16_t(min(max(w0 + 1, 0), r.IW - 1)),
+                        sw - float(w0)};
+  }
+  __syncthreads();
   const int i = blockIdx.x * 256 + threadIdx.x;
   if (i >= n8) return;
   const int ow8 = r.OW / 8;
@@ -1015,13 +1029,10 @@ __global__ void __launch_bounds__(256) bilinear_v8_kernel(Resample r, const __ha
   __align__(16) __half v[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    const int ow = 8 * g + k;
-    const float sw = src_index(ow, r.IW, r.OW, r.align);
-    const int w0 = int(floorf(sw));
-    const float lw = sw - float(w0);
-    const int w0c = min(max(w0, 0), r.IW - 1), w1c = min(max(w0 + 1, 0), r.IW - 1);
-    const float v00 = __half2float(__ldg(p0 + w0c)), v01 = __half2float(__ldg(p0 + w1c));
-    const float v10 = __half2float(__ldg(p1 + w0c)), v11 = __half2float(__ldg(p1 + w1c));
+    const BilinCol cc = bcol[8 * g + k];
+    const float lw = cc.lw;
+    const float v00 = __half2float(__ldg(p0 + cc.w0)), v01 = __half2float(__ldg(p0 + cc.w1));
+    const float v10 = __half2float(__ldg(p1 + cc.w0)), v11 = __half2float(__ldg(p1 + cc.w1));
     const float top = v00 + (v01 - v00) * lw, bot = v10 + (v11 - v10) * lw;
     v[k] = __float2half_rn(top + (bot - top) * lh);
   }
@@ -1126,14 +1137,16 @@ void record_bilinear(wgx_context *ctx, const std::vector<wgx_arg> &a) {
   void *py = out->data();
   const long long n = out->numel;
   const int dt = in->dtype;
+  // (the column table: 8 bytes per output column in shared memory; int16
+  // source columns)
   const bool v8 = dt == WGX_FLOAT16 && r.OW % 8 == 0 && n / 8 < (1ll << 31) - 256 &&
                   (reinterpret_cast<uintptr_t>(py) & 15) == 0 &&
-                  (long long)r.N * r.C * r.OH < (1ll << 31);
+                  (long long)r.N * r.C * r.OH < (1ll << 31) && r.OW <= 6144 && r.IW <= 32767;
   push(ctx, name, 1, [=](const ExecEnv &env) {
     if (v8) {
       const int n8 = int(n / 8);
-      bilinear_v8_kernel<<<unsigned((n8 + 255) / 256), 256, 0, env.stream>>>(
-          r, (const __half *)px, (uint4 *)py, n8);
+      bilinear_v8_kernel<<<unsigned((n8 + 255) / 256), 256, size_t(r.OW) * sizeof(BilinCol),
+                           env.stream>>>(r, (const __half *)px, (uint4 *)py, n8);
     } else if (dt == WGX_FLOAT16)
       bilinear_kernel<__half><<<blocks_for(n), 256, 0, env.stream>>>(r, (const __half *)px,
                                                                      (__half *)py, n);
