@@ -295,6 +295,14 @@ WGX_API int wgx_device_error(int device, uint32_t *code, int clear);
 #define WGX_INJECT_SKIP_LOADS 2u
 WGX_API int wgx_debug_inject(uint32_t flags);
 
+/* How the loaded library was built (no counterpart in the reference):
+ * WGX_BUILD_BOUNDS is set in the bounds-checking debug build
+ * (lib/libwgx_bounds.so, `make bounds`), whose hot-path kernels skip any
+ * global access outside its buffer and report it as WGX_ERR_DEVICE at the
+ * next wgx_sync. */
+#define WGX_BUILD_BOUNDS 1u
+WGX_API int wgx_build_flags(uint32_t *flags);
+
 #ifdef __cplusplus
 }
 #endif

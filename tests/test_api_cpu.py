@@ -49,6 +49,26 @@ def test_debug_inject_flags():
     assert "unknown flags" in _lib.lib.wgx_last_error().decode()
 
 
+def test_normal_build_reports_no_bounds_checks():
+    if os.environ.get("WGX_LIBRARY") == "bounds":
+        assert _lib.build_flags() == _lib.BUILD_BOUNDS
+    else:
+        assert _lib.build_flags() == 0
+
+
+def test_bounds_build_exports_the_same_symbols():
+    """lib/libwgx_bounds.so (-DWGX_BOUNDS) is a drop-in for lib/libwgx.so:
+    same exports, and it says which build it is."""
+    path = os.path.join(_lib.PKG_DIR, "lib", "libwgx_bounds.so")
+    if not os.path.exists(path):
+        pytest.skip("bounds build not compiled (make -C wgpu-executorch_b200 bounds)")
+    blib = ctypes.CDLL(path)
+    missing = [s for s in header_symbols() if not hasattr(blib, s)]
+    assert not missing, missing
+    flags = ctypes.c_uint32(7)
+    assert blib.wgx_build_flags(ctypes.byref(flags)) == 0 and flags.value == _lib.BUILD_BOUNDS
+
+
 @pytest.mark.skipif(wgx.device_count() > 0, reason="a GPU is present")
 def test_context_without_gpu_raises_cleanly():
     with pytest.raises(wgx.WgxError, match="no CUDA device"):

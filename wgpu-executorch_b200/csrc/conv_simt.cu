@@ -759,6 +759,10 @@ __global__ void __launch_bounds__(256)
 struct DwSlide {
   int P, TH, bands, rows, TWs, n_cg, n_rb, threads;
   long long planes;
+  // extents of x and out in bytes and the device error word (bounds-checking
+  // build)
+  uint64_t in_bytes, out_bytes;
+  uint32_t *err;
 };
 constexpr int DWS_RB = 8;  // output rows per thread
 
@@ -799,7 +803,9 @@ __global__ void __launch_bounds__(256, 2)
         for (int r = r0; r < d.rows; r += rstep) {
           const int ih = oh0 - PW + r;
           const bool ok = col_in && ih >= 0 && ih < g.IH;
-          cp_async16(dst + r * d.TWs, ok ? src + size_t(ih) * g.IW + iw0 : src, ok);
+          const __half *gsrc = ok ? src + size_t(ih) * g.IW + iw0 : src;
+          cp_async16(dst + r * d.TWs, gsrc,
+                     ok && WGX_IN_BOUNDS(gsrc, 16, x, d.in_bytes, d.err));
         }
       }
     }
@@ -892,8 +898,9 @@ __global__ void __launch_bounds__(256, 2)
           }
           res[j] = *reinterpret_cast<const uint32_t *>(&v);
         }
-        *reinterpret_cast<uint4 *>(op + size_t(oh) * g.OW) =
-            make_uint4(res[0], res[1], res[2], res[3]);
+        if (WGX_IN_BOUNDS(op + size_t(oh) * g.OW, 16, out, d.out_bytes, d.err))
+          *reinterpret_cast<uint4 *>(op + size_t(oh) * g.OW) =
+              make_uint4(res[0], res[1], res[2], res[3]);
       }
     }
   }
@@ -1111,6 +1118,13 @@ static void launch_simt(const wgx_conv2d_params &p, int variant, const T *in, co
     const __half *hw = reinterpret_cast<const __half *>(w);
     const __half *hb = reinterpret_cast<const __half *>(bias);
     __half *hout = reinterpret_cast<__half *>(out);
+    {
+      int dev = 0;
+      check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+      ds.err = device_error_word(dev);
+      ds.in_bytes = uint64_t(p.B) * p.IC * p.IH * p.IW * 2;
+      ds.out_bytes = uint64_t(p.B) * p.OC * p.OH * p.OW * 2;
+    }
     auto fn = p.KH == 3 ? depthwise_slide_h2<3> : p.KH == 5 ? depthwise_slide_h2<5> : depthwise_slide_h2<7>;
     static std::mutex mu;
     static bool attr[3] = {};

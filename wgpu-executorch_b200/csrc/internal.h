@@ -43,7 +43,29 @@ enum DeviceErrorBits : uint32_t {
   kErrLoadTimeout = 1u << 1,
   kErrEpilogueTimeout = 1u << 2,
   kErrTmemAlloc = 1u << 3,
+  kErrBounds = 1u << 4,  // bounds-checking build: an access outside its buffer was skipped
 };
+
+// Bounds-checking debug build (-DWGX_BOUNDS; `make bounds` builds
+// lib/libwgx_bounds.so). The hot-path kernels check their global accesses
+// against the extent of the buffer they belong to; an access outside it is
+// skipped and kErrBounds is set in the device error word, so the next sync()
+// fails with WGX_ERR_DEVICE instead of the kernel writing (or reading) out of
+// bounds. compute-sanitizer is closed on this pool; this build and the
+// odd-shape parity tests stand in for it. In the normal build the checks
+// compile to nothing.
+#ifdef WGX_BOUNDS
+__device__ __forceinline__ bool bounds_ok(const void *p, uint64_t n, const void *base,
+                                          uint64_t extent, uint32_t *err) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p), b = reinterpret_cast<uintptr_t>(base);
+  if (base != nullptr && a >= b && a + n <= b + extent) return true;
+  if (err) atomicOr(err, kErrBounds);
+  return false;
+}
+#define WGX_IN_BOUNDS(p, n, base, extent, err) ::wgx::bounds_ok((p), (n), (base), (extent), (err))
+#else
+#define WGX_IN_BOUNDS(p, n, base, extent, err) true
+#endif
 uint32_t *device_error_word(int device);
 
 // Device allocations of the library go through device_malloc, which

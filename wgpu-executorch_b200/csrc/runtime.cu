@@ -215,6 +215,17 @@ const char *wgx_last_error(void) { return g_last_error.c_str(); }
 
 int wgx_version(void) { return 1; }
 
+int wgx_build_flags(uint32_t *flags) {
+  return guarded([&] {
+    if (!flags) fail("wgx_build_flags: null pointer");
+#ifdef WGX_BOUNDS
+    *flags = WGX_BUILD_BOUNDS;
+#else
+    *flags = 0;
+#endif
+  });
+}
+
 int wgx_debug_inject(uint32_t flags) {
   return guarded([&] {
     if (flags & ~uint32_t(WGX_INJECT_ALLOC_FAIL | WGX_INJECT_SKIP_LOADS))
@@ -531,7 +542,8 @@ int wgx_sync(wgx_context *ctx) {
       uint32_t zero = 0;
       cudaMemcpy(w, &zero, 4, cudaMemcpyHostToDevice);
       fail("device reported error code " + std::to_string(code) +
-               " (a bounded wait inside a kernel ran out)",
+               ((code & kErrBounds) ? " (an access outside its buffer was skipped)"
+                                    : " (a bounded wait inside a kernel ran out)"),
            WGX_ERR_DEVICE);
     }
   });

@@ -162,7 +162,32 @@ struct UmmaGeom {
   // per-image weights (a batched GEMM: aten.bmm as a 1x1 convolution whose
   // weights differ per image): packed weight bytes per image, 0 = shared
   uint64_t w_img_bytes;
+  // buffer extents in bytes, checked by the bounds-checking build
+  // (WGX_BOUNDS): out (and resid), the re-laid input xs, the consumer's xs,
+  // the packed weights, the split pieces
+  uint64_t out_bytes, xs_bytes, oxs_bytes, wpk_bytes, outp_bytes[kMaxOut];
 };
+
+// Bounds checks of the epilogue stores (WGX_BOUNDS build; true otherwise):
+// an NCHW store lands in `out` or, with split outputs, in one of the pieces.
+__device__ __forceinline__ bool out_ok(const UmmaGeom &g, const __half *out, const void *p,
+                                       int n) {
+#ifdef WGX_BOUNDS
+  if (g.nout == 0) return bounds_ok(p, uint64_t(n), out, g.out_bytes, g.err);
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  for (int k = 0; k < kMaxOut; ++k) {
+    const uintptr_t b = reinterpret_cast<uintptr_t>(g.outp[k]);
+    if (k < g.nout && a >= b && a + uint64_t(n) <= b + g.outp_bytes[k]) return true;
+  }
+  atomicOr(g.err, kErrBounds);
+  return false;
+#else
+  return true;
+#endif
+}
+__device__ __forceinline__ bool oxs_ok(const UmmaGeom &g, const void *p) {
+  return WGX_IN_BOUNDS(p, 16, g.oxs, g.oxs_bytes, g.err);
+}
 
 // MMA groups (filter tap x 16-channel step) of one stage whose descriptor
 // offsets the generic staging keeps in shared memory
@@ -585,7 +610,7 @@ __global__ void pack_input(UmmaGeom g, const __half *__restrict__ x, uint4 *__re
     v[e] = (inside && c < g.IC) ? src_plane(g, b, c)[(long long)ih * g.IW + iw]
                                 : __float2half_rn(0.f);
   }
-  xs[i] = *reinterpret_cast<const uint4 *>(v);
+  if (WGX_IN_BOUNDS(xs + i, 16, xs, g.xs_bytes, g.err)) xs[i] = *reinterpret_cast<const uint4 *>(v);
 }
 
 // Warp-cooperative store of 4 consecutive 16-byte slots per lane: lane l's
@@ -596,8 +621,8 @@ __global__ void pack_input(UmmaGeom g, const __half *__restrict__ x, uint4 *__re
 // consecutive entries (lane l's run continues lane l + 1's when they share a
 // row, which is the common case). All 32 lanes must call it.
 __device__ __forceinline__ int slot_swz(int j) { return j ^ ((j >> 3) & 7); }
-__device__ __forceinline__ void warp_store4(uint4 *wbuf, const uint4 (&v)[4], uint4 *dst, int lo,
-                                            int hi) {
+__device__ __forceinline__ void warp_store4(const UmmaGeom &g, const uint4 *xs, uint4 *wbuf,
+                                            const uint4 (&v)[4], uint4 *dst, int lo, int hi) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int k = 0; k < 4; ++k) wbuf[slot_swz(lane * 4 + k)] = v[k];
@@ -608,7 +633,9 @@ __device__ __forceinline__ void warp_store4(uint4 *wbuf, const uint4 (&v)[4], ui
     const int j = m * 32 + lane, t = j >> 2, k = j & 3;
     const unsigned long long d = __shfl_sync(0xffffffffu, dptr, t);
     const int tlo = __shfl_sync(0xffffffffu, lo, t), thi = __shfl_sync(0xffffffffu, hi, t);
-    if (k >= tlo && k < thi) reinterpret_cast<uint4 *>(d)[k] = wbuf[slot_swz(j)];
+    if (k >= tlo && k < thi &&
+        WGX_IN_BOUNDS(reinterpret_cast<uint4 *>(d) + k, 16, xs, g.xs_bytes, g.err))
+      reinterpret_cast<uint4 *>(d)[k] = wbuf[slot_swz(j)];
   }
   __syncwarp();
 }
@@ -671,7 +698,7 @@ __global__ void __launch_bounds__(256)
   }
   // positions outside [0, Wp) are skipped
   const int klo = active ? max(0, -wp0) : 4, khi = active ? min(4, g.Wp - wp0) : 0;
-  warp_store4(wstage[threadIdx.x >> 5], vv, dst, klo, khi);
+  warp_store4(g, xs, wstage[threadIdx.x >> 5], vv, dst, klo, khi);
 }
 
 // Vector form of pack_input for IW % 8 == 0: one thread re-lays 8
@@ -761,7 +788,8 @@ __global__ void __launch_bounds__(256, 4)
   __syncthreads();
   const int n = int(s1 - s0 + 1);
   uint4 *dst = xs + s0;
-  for (int i = threadIdx.x; i < n; i += 256) dst[i] = stage[pack_swz(i)];
+  for (int i = threadIdx.x; i < n; i += 256)
+    if (WGX_IN_BOUNDS(dst + i, 16, xs, g.xs_bytes, g.err)) dst[i] = stage[pack_swz(i)];
 }
 
 // Space-to-depth re-layout for stride 2 with few input channels (XIC < 8,
@@ -827,7 +855,7 @@ __global__ void __launch_bounds__(256)
       }
       vv[k] = make_uint4(w32[0], w32[1], w32[2], w32[3]);
     }
-    warp_store4(wstage[threadIdx.x >> 5], vv,
+    warp_store4(g, xs, wstage[threadIdx.x >> 5], vv,
                 xs + (size_t(b) * planes + pl) * plane_rows + size_t(hp) * g.Wp + wp0, klo, khi);
   }
 }
@@ -912,7 +940,7 @@ __global__ void pack_input_s2d(UmmaGeom g, const __half *__restrict__ x, uint4 *
     }
     v[e] = val;
   }
-  xs[i] = *reinterpret_cast<const uint4 *>(v);
+  if (WGX_IN_BOUNDS(xs + i, 16, xs, g.xs_bytes, g.err)) xs[i] = *reinterpret_cast<const uint4 *>(v);
 }
 
 // Vector form for stride 2 across with both column phases used, IC % 8 == 0
@@ -971,7 +999,7 @@ __global__ void __launch_bounds__(256)
       vv[k] = make_uint4(__byte_perm(wd[0], wd[1], sel), __byte_perm(wd[2], wd[3], sel),
                          __byte_perm(wd[4], wd[5], sel), __byte_perm(wd[6], wd[7], sel));
     }
-    warp_store4(wstage[threadIdx.x >> 5], vv, dst, klo, khi);
+    warp_store4(g, xs, wstage[threadIdx.x >> 5], vv, dst, klo, khi);
   }
 }
 
@@ -1327,7 +1355,7 @@ __device__ __forceinline__ void hsum_epilogue(const UmmaGeom &g, uint32_t tmem,
         const int oc0 = chk[k] * 8;
         if (validk[k] && oc0 < g.OC) {
           uint4 *slot = xs_slot(g, b, oc0, ohk[k], owk[k]);
-          if (slot) *slot = make_uint4(pr[k][0], pr[k][1], pr[k][2], pr[k][3]);
+          if (slot && oxs_ok(g, slot)) *slot = make_uint4(pr[k][0], pr[k][1], pr[k][2], pr[k][3]);
         }
       }
     } else if (tvec) {
@@ -1360,12 +1388,15 @@ __device__ __forceinline__ void hsum_epilogue(const UmmaGeom &g, uint32_t tmem,
           const size_t off = size_t(oh8) * g.OW + ow8;
           uint4 w4 = val[k];
           if (g.resid) {
-            const uint4 rr = *reinterpret_cast<const uint4 *>(
-                g.resid + (size_t(b) * g.OC + oc) * plane + off);
+            const __half *rsrc = g.resid + (size_t(b) * g.OC + oc) * plane + off;
+            const uint4 rr = WGX_IN_BOUNDS(rsrc, 16, g.resid, g.out_bytes, g.err)
+                                 ? *reinterpret_cast<const uint4 *>(rsrc)
+                                 : make_uint4(0u, 0u, 0u, 0u);
             w4 = make_uint4(add_resid2(w4.x, rr.x), add_resid2(w4.y, rr.y),
                             add_resid2(w4.z, rr.z), add_resid2(w4.w, rr.w));
           }
-          *reinterpret_cast<uint4 *>(out_plane(g, out, b, oc, plane) + off) = w4;
+          __half *dst16 = out_plane(g, out, b, oc, plane) + off;
+          if (out_ok(g, out, dst16, 16)) *reinterpret_cast<uint4 *>(dst16) = w4;
         }
       }
     } else {
@@ -1386,8 +1417,10 @@ __device__ __forceinline__ void hsum_epilogue(const UmmaGeom &g, uint32_t tmem,
             vv = add_resid2(vv, lo | (hi << 16));
           }
           const __half2 h2 = *reinterpret_cast<const __half2 *>(&vv);
-          if (oc < g.OC) out_plane(g, out, b, oc, plane)[posoff] = __low2half(h2);
-          if (oc + 1 < g.OC) out_plane(g, out, b, oc + 1, plane)[posoff] = __high2half(h2);
+          if (oc < g.OC && out_ok(g, out, out_plane(g, out, b, oc, plane) + posoff, 2))
+            out_plane(g, out, b, oc, plane)[posoff] = __low2half(h2);
+          if (oc + 1 < g.OC && out_ok(g, out, out_plane(g, out, b, oc + 1, plane) + posoff, 2))
+            out_plane(g, out, b, oc + 1, plane)[posoff] = __high2half(h2);
         }
       }
     }
@@ -1528,7 +1561,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         // barrier, measured slower on B200)
         const uint32_t wb = smem_u32(wbar);
         mbar_expect_tx(wb, g.w_region_bytes);
-        bulk_g2s(smem_u32(sW), wpk, g.w_region_bytes, wb);
+        if (WGX_IN_BOUNDS(wpk, g.w_region_bytes, wpk, g.wpk_bytes, g.err))
+          bulk_g2s(smem_u32(sW), wpk, g.w_region_bytes, wb);
       }
       int slot = S - 1, use = -1;  // pipeline slot and its use count, advanced per loaded stage
       bool ok = true;
@@ -1562,11 +1596,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int khg = sw.khg, cbk = sw.cbk;
           const uint32_t fb = smem_u32(&full[slot]);
           mbar_expect_tx(fb, (g.resident ? 0u : g.a_stage_bytes) + g.chunks * b_copy);
-          if (!g.resident)
-            bulk_g2s(smem_u32(sW + size_t(slot) * g.a_stage_bytes),
-                     wpk + size_t(b) * g.w_img_bytes +
-                         (size_t(oct) * g.n_kstages + s) * g.a_stage_bytes,
-                     g.a_stage_bytes, fb);
+          if (!g.resident) {
+            const uint8_t *wsrc = wpk + size_t(b) * g.w_img_bytes +
+                                  (size_t(oct) * g.n_kstages + s) * g.a_stage_bytes;
+            if (WGX_IN_BOUNDS(wsrc, g.a_stage_bytes, wpk, g.wpk_bytes, g.err))
+              bulk_g2s(smem_u32(sW + size_t(slot) * g.a_stage_bytes), wsrc, g.a_stage_bytes, fb);
+          }
           if (g.direct) {
             // TMA boxes of 64 positions x dbox channels: atom j (64 positions,
             // bk rows of 128 bytes) at j * bk * 128, channel group rows inside
@@ -1586,8 +1621,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           const long long row0 = p0 + (long long)khg * g.khs * g.dH * g.Wp;
           for (int ch = 0; ch < g.chunks; ++ch) {
             const long long plane = (long long)b * (g.C8 / 8) + cbk * g.chunks + ch;
-            bulk_g2s(smem_u32(sB + size_t(slot) * g.b_stage_bytes + size_t(ch) * g.R_alloc * 16),
-                     xs + (plane * g.plane_rows + row0) * 16, b_copy, fb);
+            const uint8_t *xsrc = xs + (plane * g.plane_rows + row0) * 16;
+            if (WGX_IN_BOUNDS(xsrc, b_copy, xs, g.xs_bytes, g.err))
+              bulk_g2s(smem_u32(sB + size_t(slot) * g.b_stage_bytes + size_t(ch) * g.R_alloc * 16),
+                       xsrc, b_copy, fb);
           }
         }
       }
@@ -1905,7 +1942,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int oc = oc0 + 8 * q8;
             if (oc >= g.OC) continue;
             uint4 *slot = xs_slot(g, b, oc, oh, ow);
-            if (slot) *slot = make_uint4(pr[4 * q8], pr[4 * q8 + 1], pr[4 * q8 + 2], pr[4 * q8 + 3]);
+            if (slot && oxs_ok(g, slot))
+              *slot = make_uint4(pr[4 * q8], pr[4 * q8 + 1], pr[4 * q8 + 2], pr[4 * q8 + 3]);
           }
           continue;
         }
@@ -1916,8 +1954,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int j = 0; j < 8; ++j) {
             const int oc = oc0 + 2 * j;
             const __half2 h2 = *reinterpret_cast<const __half2 *>(&pr[j]);
-            if (oc < g.OC) d[size_t(oc) * plane] = __low2half(h2);
-            if (oc + 1 < g.OC) d[size_t(oc + 1) * plane] = __high2half(h2);
+            if (oc < g.OC && out_ok(g, out, d + size_t(oc) * plane, 2))
+              d[size_t(oc) * plane] = __low2half(h2);
+            if (oc + 1 < g.OC && out_ok(g, out, d + size_t(oc + 1) * plane, 2))
+              d[size_t(oc + 1) * plane] = __high2half(h2);
           }
           continue;
         }
@@ -1939,8 +1979,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int oc = oc0 + 2 * j;
           const uint32_t v = g.resid ? add_resid2(pr[j], rres[j]) : pr[j];
           const __half2 h2 = *reinterpret_cast<const __half2 *>(&v);
-          if (oc < g.OC) out_plane(g, out, b, oc, plane)[posoff] = __low2half(h2);
-          if (oc + 1 < g.OC) out_plane(g, out, b, oc + 1, plane)[posoff] = __high2half(h2);
+          if (oc < g.OC && out_ok(g, out, out_plane(g, out, b, oc, plane) + posoff, 2))
+            out_plane(g, out, b, oc, plane)[posoff] = __low2half(h2);
+          if (oc + 1 < g.OC && out_ok(g, out, out_plane(g, out, b, oc + 1, plane) + posoff, 2))
+            out_plane(g, out, b, oc + 1, plane)[posoff] = __high2half(h2);
         }
       }
       } else {
@@ -2010,12 +2052,15 @@ __global__ void __launch_bounds__(THREADS, 1)
               if (g.resid) {
                 // residual add after the activation, one rounding (as the
                 // separate add would compute it)
-                const uint4 rr4 = *reinterpret_cast<const uint4 *>(
-                    g.resid + (size_t(b) * g.OC + oc) * plane + off);
+                const __half *rsrc = g.resid + (size_t(b) * g.OC + oc) * plane + off;
+                const uint4 rr4 = WGX_IN_BOUNDS(rsrc, 16, g.resid, g.out_bytes, g.err)
+                                      ? *reinterpret_cast<const uint4 *>(rsrc)
+                                      : make_uint4(0u, 0u, 0u, 0u);
                 v = make_uint4(add_resid2(val.x, rr4.x), add_resid2(val.y, rr4.y),
                                add_resid2(val.z, rr4.z), add_resid2(val.w, rr4.w));
               }
-              *reinterpret_cast<uint4 *>(out_plane(g, out, b, oc, plane) + off) = v;
+              __half *dst16 = out_plane(g, out, b, oc, plane) + off;
+              if (out_ok(g, out, dst16, 16)) *reinterpret_cast<uint4 *>(dst16) = v;
             }
           }
           __syncwarp();
@@ -2033,7 +2078,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int q8 = 0; q8 < 2; ++q8) {
               const int oc = oc0 + 8 * q8;
               if (oc < g.OC)
-                slot[size_t(oc >> 3) * pstride] =
+                if (oxs_ok(g, slot + size_t(oc >> 3) * pstride))
+                  slot[size_t(oc >> 3) * pstride] =
                     make_uint4(pr[4 * q8], pr[4 * q8 + 1], pr[4 * q8 + 2], pr[4 * q8 + 3]);
             }
           }
@@ -2044,8 +2090,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int j = 0; j < 8; ++j) {
           const int oc = oc0 + 2 * j;
           const __half2 h2 = *reinterpret_cast<const __half2 *>(&pr[j]);
-          if (oc < g.OC) d[size_t(oc) * plane] = __low2half(h2);
-          if (oc + 1 < g.OC) d[size_t(oc + 1) * plane] = __high2half(h2);
+          if (oc < g.OC && out_ok(g, out, d + size_t(oc) * plane, 2))
+            d[size_t(oc) * plane] = __low2half(h2);
+          if (oc + 1 < g.OC && out_ok(g, out, d + size_t(oc + 1) * plane, 2))
+            d[size_t(oc + 1) * plane] = __high2half(h2);
         }
       }
       }
@@ -2143,7 +2191,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int c = oc0 + grp * 8;
             if (ohh < g.OH && oww < g.OW && c < g.OC) {
               uint4 *slot = xs_slot(g, b, c, ohh, oww);
-              if (slot) *slot = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+              if (slot && oxs_ok(g, slot)) *slot = make_uint4(wv[0], wv[1], wv[2], wv[3]);
             }
           }
           __syncwarp();
@@ -2190,11 +2238,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             __half *orow = g.nout ? out_plane(g, out, b, c, plane) : rowp + size_t(r4) * 4 * plane;
             if (g.resid) val = add_resid2(val, rv[r4]);
             if (pairs) {
-              if (v0) *reinterpret_cast<uint32_t *>(orow + off0) = val;
+              if (v0 && out_ok(g, out, orow + off0, 4))
+                *reinterpret_cast<uint32_t *>(orow + off0) = val;
             } else {
               const __half2 h2 = *reinterpret_cast<const __half2 *>(&val);
-              if (v0) orow[off0] = __low2half(h2);
-              if (v1) orow[off1] = __high2half(h2);
+              if (v0 && out_ok(g, out, orow + off0, 2)) orow[off0] = __low2half(h2);
+              if (v1 && out_ok(g, out, orow + off1, 2)) orow[off1] = __high2half(h2);
             }
           }
         }
@@ -2206,11 +2255,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (4 * r4 + rsel < nrows) {
             __half *orow = rowp + size_t(r4) * 4 * plane;
             if (pairs) {
-              if (v0) *reinterpret_cast<uint32_t *>(orow + off0) = val;
+              if (v0 && out_ok(g, out, orow + off0, 4))
+                *reinterpret_cast<uint32_t *>(orow + off0) = val;
             } else {
               const __half2 h2 = *reinterpret_cast<const __half2 *>(&val);
-              if (v0) orow[off0] = __low2half(h2);
-              if (v1) orow[off1] = __high2half(h2);
+              if (v0 && out_ok(g, out, orow + off0, 2)) orow[off0] = __low2half(h2);
+              if (v1 && out_ok(g, out, orow + off1, 2)) orow[off1] = __high2half(h2);
             }
           }
         }
@@ -2267,6 +2317,10 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   g.err = device_error_word(dev);
   g.inject_skip = inject_skip_loads() ? 1 : 0;
+  // extents for the bounds-checking build
+  g.out_bytes = uint64_t(p.B) * p.OC * p.OH * p.OW * 2;
+  g.xs_bytes = umma_conv_input_bytes(p, per_image_w);
+  g.wpk_bytes = uint64_t(per_image_w ? p.B : 1) * umma_conv_packed_weight_bytes(p, per_image_w);
   if ((reinterpret_cast<uintptr_t>(xs) & 15) || (reinterpret_cast<uintptr_t>(packed) & 15))
     fail("conv2d: scratch must be 16-byte aligned");
   // ---- input sources
@@ -2313,6 +2367,7 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
       for (int k = 0; k < c.nphW; ++k) g.ophase_w[c.phW[k]] = k;
     }
     g.oxs = static_cast<uint4 *>(link->consumer_xs);
+    g.oxs_bytes = umma_conv_input_bytes(*link->consumer);
   }
   const bool xs_ready = link && link->xs_ready;
   if (xs_ready && w_to_pack) fail("conv2d: weights must be packed before a linked launch");
@@ -2327,6 +2382,7 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
       for (int k = 0; k < link->nout; ++k) {
         g.outp[k] = link->outp[k];
         g.out_c0[k + 1] = g.out_c0[k] + link->out_ch[k];
+        g.outp_bytes[k] = uint64_t(p.B) * link->out_ch[k] * p.OH * p.OW * 2;
       }
       if (g.out_c0[g.nout] != p.OC) fail("conv2d: output pieces do not add up to OC");
     }

@@ -14,7 +14,10 @@ from ctypes import (POINTER, Structure, Union, c_char_p, c_double, c_float, c_in
                     c_int64, c_uint32, c_uint64, c_void_p)
 
 PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-LIB_PATH = os.path.join(PKG_DIR, "lib", "libwgx.so")
+# WGX_LIBRARY=bounds loads the bounds-checking debug build (lib/libwgx_bounds.so,
+# `make -C wgpu-executorch_b200 bounds`) instead of the normal library.
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libwgx_bounds.so" if os.environ.get("WGX_LIBRARY") ==
+                        "bounds" else "libwgx.so")
 
 WGX_OK = 0
 WGX_ERR_INVALID = 1
@@ -32,6 +35,7 @@ ARG_NULL, ARG_TENSOR, ARG_NUMBER, ARG_BOOL, ARG_INT_LIST, ARG_TENSOR_LIST, ARG_S
 
 ACT_NONE, ACT_CLAMP, ACT_SILU = 0, 1, 2
 INJECT_ALLOC_FAIL, INJECT_SKIP_LOADS = 1, 2
+BUILD_BOUNDS = 1
 CONV_UMMA, CONV_SIMT_GEMM, CONV_DEPTHWISE, CONV_DIRECT, CONV_POINTWISE1 = 1, 2, 3, 4, 5
 
 
@@ -102,6 +106,7 @@ SIGNATURES = {
                             c_void_p], c_int),
     "wgx_device_error": ([c_int, POINTER(c_uint32), c_int], c_int),
     "wgx_debug_inject": ([c_uint32], c_int),
+    "wgx_build_flags": ([POINTER(c_uint32)], c_int),
     "wgx_kernel_timing": ([c_int], c_int),
     "wgx_kernel_timing_read": ([c_char_p, POINTER(c_double), POINTER(c_int64), c_int], c_int),
 }
@@ -158,3 +163,11 @@ def device_count() -> int:
     n = c_int(0)
     check(lib.wgx_device_count(ctypes.byref(n)))
     return n.value
+
+
+def build_flags() -> int:
+    """WGX_BUILD_* bits of the loaded library (BUILD_BOUNDS: the
+    bounds-checking debug build)."""
+    f = c_uint32(0)
+    check(lib.wgx_build_flags(ctypes.byref(f)))
+    return f.value
