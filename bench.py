@@ -550,11 +550,11 @@ def program_bench(local, ws, prog, w, x, steps, warmup, flush_l2, e2e_mode):
     inp = ctx.tensor("float16", v_in["shape"]).setData(x)
     out = ctx.tensor("float16", v_out["shape"])
     ctx.recordProgram(prog, w, [inp, out])
-    st = ctx.stats()
     flush = l2_flusher(local) if flush_l2 else None
     for _ in range(warmup):
         ctx.submit()
     ctx.sync()
+    st = ctx.stats()  # after a submit: the captured graph's kernel nodes
     barrier(ws)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -712,7 +712,6 @@ def run_ours(args, ws, rank, local):
     inp = ctx.tensor("float16", v_in["shape"]).setData(x)
     out = ctx.tensor("float16", v_out["shape"])
     ctx.recordProgram(progb, w, [inp, out])
-    st = ctx.stats()
     # end to end: pipelined steps through the public API (wgx.Pipeline): each
     # step uploads its input from pinned host memory, replays the program and
     # downloads its output; neighbouring steps' copies overlap this step's
@@ -733,6 +732,7 @@ def run_ours(args, ws, rank, local):
         pipe.step(pins_in[i], pins_out[i])
     pipe.sync()
     torch.cuda.synchronize()
+    st = ctx.stats()  # after a submit: the captured graph's kernel nodes
 
     gpus = [int(g) for g in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if g.strip()]
     sampler = ClockSampler(gpus if gpus else list(range(max(ws, 1)))) if rank == 0 else None

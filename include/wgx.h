@@ -150,7 +150,9 @@ WGX_API int wgx_submit(wgx_context *ctx);
 WGX_API int wgx_sync(wgx_context *ctx);
 /* reset() (src/context.ts:386-389) */
 WGX_API int wgx_reset(wgx_context *ctx);
-/* number of recorded commands and of kernel launches one submit replays */
+/* number of recorded commands and of kernel launches one submit replays
+ * (after the first submit: the kernel nodes of the captured CUDA graph;
+ * before it: the recorders' per-command counts, an upper bound) */
 WGX_API int wgx_context_stats(const wgx_context *ctx, int64_t *n_commands, int64_t *n_kernel_launches);
 /* Replays the recorded commands eagerly (outside the captured graph)
  * `repeats` times with a CUDA event pair around each command and writes the

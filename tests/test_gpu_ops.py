@@ -110,6 +110,8 @@ def test_bmm_fp16_tensor_cores(ctx, bmkn):
     assert ctx.stats()["kernel_launches"] == (2 if n % 8 == 0 else 3)
     ctx.submit()
     ctx.sync()
+    # after the submit: counted from the captured graph's kernel nodes
+    assert ctx.stats()["kernel_launches"] == (2 if n % 8 == 0 else 3)
     y = out.numpy()
     ctx.reset()
     for i in range(b):
@@ -439,3 +441,22 @@ def test_maxpool_cascade_program(ctx, shape, K, n, idx_out, ties):
         cur = y.astype(np.float16)
     if idx_out:
         np.testing.assert_array_equal(last_idx.numpy().reshape(shape), idx)
+
+
+@pytest.mark.parametrize("k", [1, 3])
+def test_launch_count_is_the_graph_kernel_nodes(ctx, k):
+    """Before the first submit the stats give the recorders' counts (a
+    tensor-core convolution counts a re-layout launch, which the 1x1
+    direct mode, reading NCHW through TMA, does without); after it, the
+    kernel nodes of the captured graph, never more."""
+    x = rnd((2, 64, 32, 32))
+    w = rnd((32, 64, k, k)) * 0.05
+    y = empty(ctx, (2, 32, 32, 32), "float16")
+    ctx.recordShader(wgx.shaders.convolution, [T(ctx, x), T(ctx, w), None, [1, 1],
+                                               [k // 2, k // 2], [1, 1], False, [0, 0], 1, y])
+    before = ctx.stats()["kernel_launches"]
+    ctx.submit()
+    ctx.sync()
+    after = ctx.stats()["kernel_launches"]
+    ctx.reset()
+    assert 1 <= after <= before

@@ -501,14 +501,28 @@ static ExecEnv ensure_workspace(wgx_context *ctx) {
   return ExecEnv{ctx->stream, ctx->workspace, ctx->workspace_bytes};
 }
 
+// Kernel launches one replay of a captured graph makes: its kernel nodes
+// (copies and memsets are not kernels).
+static int64_t kernel_nodes(cudaGraph_t graph) {
+  size_t n = 0;
+  check_cuda(cudaGraphGetNodes(graph, nullptr, &n), "cudaGraphGetNodes");
+  std::vector<cudaGraphNode_t> nodes(n);
+  if (n) check_cuda(cudaGraphGetNodes(graph, nodes.data(), &n), "cudaGraphGetNodes");
+  int64_t k = 0;
+  for (size_t i = 0; i < n; ++i) {
+    cudaGraphNodeType t;
+    check_cuda(cudaGraphNodeGetType(nodes[i], &t), "cudaGraphNodeGetType");
+    if (t == cudaGraphNodeTypeKernel) ++k;
+  }
+  return k;
+}
+
 int wgx_submit(wgx_context *ctx) {
   return guarded([&] {
     assert_alive(ctx);
     if (ctx->commands.empty()) return;  // context.ts:325-327
     set_device(ctx->device);
     if (!ctx->graph_valid) {
-      int64_t launches = 0;
-      for (auto &c : ctx->commands) launches += c.kernel_launches;
       ExecEnv env = ensure_workspace(ctx);
       check_cuda(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal),
                  "cudaStreamBeginCapture");
@@ -524,7 +538,7 @@ int wgx_submit(wgx_context *ctx) {
       check_cuda(cudaStreamEndCapture(ctx->stream, &ctx->graph), "cudaStreamEndCapture");
       check_cuda(cudaGraphInstantiate(&ctx->graph_exec, ctx->graph, 0), "cudaGraphInstantiate");
       ctx->graph_valid = true;
-      ctx->launches_per_submit = launches;
+      ctx->launches_per_submit = kernel_nodes(ctx->graph);
     }
     check_cuda(cudaGraphLaunch(ctx->graph_exec, ctx->stream), "cudaGraphLaunch");
   });
@@ -562,8 +576,15 @@ int wgx_reset(wgx_context *ctx) {
 int wgx_context_stats(const wgx_context *ctx, int64_t *n_commands, int64_t *n_kernel_launches) {
   return guarded([&] {
     if (!ctx) fail("null context");
+    // after the first submit: the kernel nodes of the captured graph;
+    // before it: the recorders' per-command counts (the tensor-core
+    // convolution counts its re-layout launch, which the direct mode skips)
     int64_t launches = 0;
-    for (auto &c : ctx->commands) launches += c.kernel_launches;
+    if (ctx->graph_valid) {
+      launches = ctx->launches_per_submit;
+    } else {
+      for (auto &c : ctx->commands) launches += c.kernel_launches;
+    }
     if (n_commands) *n_commands = int64_t(ctx->commands.size());
     if (n_kernel_launches) *n_kernel_launches = launches;
   });
