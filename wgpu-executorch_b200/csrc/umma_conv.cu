@@ -1157,7 +1157,7 @@ struct StageWalk {
 // %globaltimer (ns) at [11] kernel entry, [12] end of the set-up, [13] the
 // MMA thread's last commit, [14] the end of epilogue warp 4, [15] kernel exit.
 #ifdef WGX_PROF
-__device__ unsigned long long g_umma_prof[256][16];
+__device__ unsigned long long g_umma_prof[256][20];
 #define WGX_PROF_T(v) const long long v = clock64()
 #define WGX_PROF_ADD(acc, t0) acc += (unsigned long long)(clock64() - (t0))
 #else
@@ -1659,10 +1659,17 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t a_lbo = uint32_t(g.wrows) * 16;        // chunk plane of the weights
       const uint32_t b_lbo = uint32_t(g.R_alloc) * 16;      // chunk plane of the activations
       bool ok = true;
+      WGX_PROF_T(tw_res);
       if (g.resident && !mbar_wait(smem_u32(wbar), 0)) {
         atomicOr(g.err, kErrMmaTimeout);
         ok = false;
       }
+#ifdef WGX_PROF
+      if (iss == 0) {
+        g_umma_prof[blockIdx.x][16] = (unsigned long long)(clock64() - tw_res);
+        g_umma_prof[blockIdx.x][17] = global_ns();
+      }
+#endif
       // per-MMA start-address offsets (16-byte units) of the specialised path:
       // MMA i = (kw, ks) reads A tap kw chunk pair ks, B shifted kw*dW rows
       uint32_t a_off[KW_T > 0 ? 2 * KW_T : 1], b_off[KW_T > 0 ? 2 * KW_T : 1];
@@ -1708,6 +1715,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           WGX_PROF_ADD(pm_full, tf0);
 #ifdef WGX_PROF
+          if (iss == 0 && it == 0 && g_umma_prof[blockIdx.x][18] == 0)
+            g_umma_prof[blockIdx.x][18] = global_ns();  // first stage landed
           // issue time: from the data's arrival to the stage's commit
           // (measured at the next stage's wait start: approximated by the
           // commit below)
@@ -2133,6 +2142,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) atomicOr(g.err, kErrEpilogueTimeout);
         break;
       }
+#ifdef WGX_PROF
+      if (it == 0 && ew == 0 && lane == 0) g_umma_prof[blockIdx.x][19] = global_ns();
+#endif
       tc_fence_after();
       const int oc0 = oct * UM + q * 32;  // first channel of this quadrant
       const int oc_lane = oc0 + lane;
@@ -2653,7 +2665,7 @@ void umma_bmm_run(const __half *A, const __half *B, __half *C, int64_t batch, in
 extern "C" __attribute__((visibility("default"))) int wgx_umma_prof_read(unsigned long long *out) {
   if (cudaDeviceSynchronize() != cudaSuccess) return 1;
   if (cudaMemcpyFromSymbol(out, wgx::g_umma_prof, sizeof(wgx::g_umma_prof)) != cudaSuccess) return 1;
-  static unsigned long long zero[256][16] = {};
+  static unsigned long long zero[256][20] = {};
   return cudaMemcpyToSymbol(wgx::g_umma_prof, zero, sizeof(zero)) != cudaSuccess;
 }
 #endif
