@@ -438,6 +438,25 @@ static bool hsum_eligible(const wgx_conv2d_params &p) {
   return mode == 2 || ocp < 14 * c16 || (p_out <= 512 && ocp <= 16 * c16);
 }
 
+// 64-channel stages for channels-on-M convolutions (input channels a
+// multiple of 64): WGX_CONV_BK64=0 never, =1 (default) 1x1 filters with at
+// least 256 input channels, =2 1x1 filters with at least 192, =3 1x1
+// filters, =4 every filter size (all forms compute the same convolution).
+static bool bk64_wanted(const wgx_conv2d_params &p) {
+  static const int mode = [] {
+    const char *e = std::getenv("WGX_CONV_BK64");
+    return (e && e[0] >= '0' && e[0] <= '4') ? e[0] - '0' : 1;
+  }();
+  const bool one = p.KH == 1 && p.KW == 1;
+  switch (mode) {
+    case 0: return false;
+    case 1: return one && p.IC >= 256;
+    case 2: return one && p.IC >= 192;
+    case 3: return one;
+    default: return true;
+  }
+}
+
 // Pick the staging: per-filter-row stages of 32 channels measured fastest
 // on config 2 (41 % tensor-pipe activity against 30 % for whole-filter
 // stages of 16 channels); whole-filter and 16-channel stages are the
@@ -469,6 +488,18 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p, bool per_image_w = false) 
       cand[0][1] = 16;
       cand[2][1] = 32;
     }
+  } else if (!trans && p.IC % 64 == 0 && bk64_wanted(p)) {
+    // channels on M, input channels a multiple of 64: 64-channel stages.
+    // The per-SM copy engine finishes pipeline stages at a roughly fixed
+    // cost per barrier round and per copy (measured on B200: 4 KB copies,
+    // four to a stage, feed ~11 B/clk per SM; 8 KB copies ~20 B/clk), so
+    // twice the bytes per stage and per copy (8 KB boxes, 8 KB chunk rows)
+    // nearly double what the tensor cores are fed (1x1 layers of YOLO26-N
+    // at batch 64: 512 -> 256 at 20^2 40.0 -> 29.8 us, 384 -> 128 at 40^2
+    // 48.1 -> 40.2 us). With at most two stages per tile (128 input
+    // channels) and for 3x3 filters they measured slower.
+    const int c4[4][2] = {{1, 64}, {1, 32}, {0, 16}, {1, 16}};
+    std::memcpy(cand, c4, sizeof cand);
   } else if (trans && (p.sH > 1 || p.sW > 1)) {
     // strided, positions on M, more than 16 virtual channels: whole-filter
     // stages of 32 channels first (the 64 -> 64 / stride-2 layer of
@@ -1469,6 +1500,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   // cycles for N <= 32)
   constexpr bool DUAL = TRANS > 0 && G_C >= 2;
   constexpr int NISS = DUAL ? 2 : 1;
+  // copy-issuing threads (see the producer)
+  constexpr int NPI = DUAL ? 2 : 3;
   // activation stages first, on a 1024-byte boundary (128-byte swizzle atoms
   // of the direct mode); stage sizes are multiples of 1024 bytes there
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -1493,7 +1526,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&full[s]), NPI);
       mbar_init(smem_u32(&empty[s]), NISS);
     }
     for (int a = 0; a < 2; ++a) {
@@ -1552,11 +1585,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) g_umma_prof[blockIdx.x][12] = global_ns();
 #endif
 
-  if (warp == 0) {
+  if (warp == 0 || warp == 3 || (!DUAL && warp == 2)) {
     if (lane == 0 && !g.inject_skip) {
-      // ---------------- producer: bulk copies of weights + activation rows
+      // ---------------- producers: bulk copies of weights + activation rows.
+      // NPI threads (lane 0 of warps 0, 3 and, without a second MMA issuer,
+      // 2) walk the same stage sequence and split each stage's copies: the
+      // per-SM copy engine takes copies from several issuing threads faster
+      // than from one (measured on B200: eight 4 KB copies per stage, one
+      // issuer ~16 B/clk per SM, four issuers ~22 B/clk). Each issuer
+      // arrives on the stage's full barrier once with its own byte count;
+      // issuer 0 also copies the weights.
+      const int pi = warp == 0 ? 0 : warp == 3 ? 1 : 2;
       const uint32_t b_copy = uint32_t(g.R) * 16;
-      if (g.resident) {
+      if (g.resident && pi == 0) {
         // (one copy: splitting it into per-stage pieces, each on its own
         // barrier, measured slower on B200)
         const uint32_t wb = smem_u32(wbar);
@@ -1564,6 +1605,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (WGX_IN_BOUNDS(wpk, g.w_region_bytes, wpk, g.wpk_bytes, g.err))
           bulk_g2s(smem_u32(sW), wpk, g.w_region_bytes, wb);
       }
+      // this issuer's share of a stage: chunk copies ch = pi, pi + NPI, ...;
+      // direct-mode boxes q = pi, pi + NPI, ... of the stage's box list
+      const int my_chunks = g.chunks > pi ? (g.chunks - pi + NPI - 1) / NPI : 0;
+      const int nj = (g.tile_pos + 63) / 64, nq = g.direct ? (g.bk / g.dbox) * nj : 0;
+      const int my_boxes = g.direct && nq > pi ? (nq - pi + NPI - 1) / NPI : 0;
+      const uint32_t my_bytes =
+          (g.resident || pi != 0 ? 0u : g.a_stage_bytes) +
+          (g.direct ? uint32_t(my_boxes) * uint32_t(g.dbox) * 128u : uint32_t(my_chunks) * b_copy);
       int slot = S - 1, use = -1;  // pipeline slot and its use count, advanced per loaded stage
       bool ok = true;
       [[maybe_unused]] unsigned long long pr_empty = 0;
@@ -1595,8 +1644,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           WGX_PROF_ADD(pr_empty, tw0);
           const int khg = sw.khg, cbk = sw.cbk;
           const uint32_t fb = smem_u32(&full[slot]);
-          mbar_expect_tx(fb, (g.resident ? 0u : g.a_stage_bytes) + g.chunks * b_copy);
-          if (!g.resident) {
+          mbar_expect_tx(fb, my_bytes);
+          if (!g.resident && pi == 0) {
             const uint8_t *wsrc = wpk + size_t(b) * g.w_img_bytes +
                                   (size_t(oct) * g.n_kstages + s) * g.a_stage_bytes;
             if (WGX_IN_BOUNDS(wsrc, g.a_stage_bytes, wpk, g.wpk_bytes, g.err))
@@ -1606,20 +1655,20 @@ __global__ void __launch_bounds__(THREADS, 1)
             // TMA boxes of 64 positions x dbox channels: atom j (64 positions,
             // bk rows of 128 bytes) at j * bk * 128, channel group rows inside
             uint8_t *stage = sB + size_t(slot) * g.b_stage_bytes;
-            for (int c = cbk * g.bk; c < (cbk + 1) * g.bk; c += g.dbox) {
+            for (int q = pi; q < nq; q += NPI) {
+              const int c = cbk * g.bk + (q / nj) * g.dbox, j = q % nj;
               int src = 0;
               for (int k = 1; k < g.nsrc; ++k)
                 if (c >= g.src_c0[k]) src = k;
               const int y = c - g.src_c0[src];
               const int row = c - cbk * g.bk;
-              for (int j = 0; j < g.tile_pos / 64; ++j)
-                tma_load_3d(smem_u32(stage + size_t(j) * g.bk * 128 + size_t(row) * 128),
-                            &tm.m[src], int(p0) + 64 * j, y, b, fb);
+              tma_load_3d(smem_u32(stage + size_t(j) * g.bk * 128 + size_t(row) * 128),
+                          &tm.m[src], int(p0) + 64 * j, y, b, fb);
             }
             continue;
           }
           const long long row0 = p0 + (long long)khg * g.khs * g.dH * g.Wp;
-          for (int ch = 0; ch < g.chunks; ++ch) {
+          for (int ch = pi; ch < g.chunks; ch += NPI) {
             const long long plane = (long long)b * (g.C8 / 8) + cbk * g.chunks + ch;
             const uint8_t *xsrc = xs + (plane * g.plane_rows + row0) * 16;
             if (WGX_IN_BOUNDS(xsrc, b_copy, xs, g.xs_bytes, g.err))
@@ -1632,7 +1681,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       // (bounded waits). Slot j's last fill is use (j <= slot) or use - 1;
       // its barrier completed no later phase, so the parity test is exact.
       // On the normal path every wait succeeds at its first try.
-      if (g.resident && !mbar_wait(smem_u32(wbar), 0)) atomicOr(g.err, kErrLoadTimeout);
+      if (g.resident && pi == 0 && !mbar_wait(smem_u32(wbar), 0))
+        atomicOr(g.err, kErrLoadTimeout);
       for (int j = 0; j < S; ++j) {
         const int last = j <= slot ? use : use - 1;
         if (last >= 0 && !mbar_wait(smem_u32(&full[j]), uint32_t(last) & 1)) {
@@ -1641,7 +1691,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
 #ifdef WGX_PROF
-      g_umma_prof[blockIdx.x][0] = pr_empty;
+      if (pi == 0) g_umma_prof[blockIdx.x][0] = pr_empty;
 #endif
     }
   } else if (warp == 1 || (DUAL && warp == 2)) {
