@@ -497,7 +497,9 @@ static UmmaGeom make_geom(const wgx_conv2d_params &p, bool per_image_w = false) 
     // nearly double what the tensor cores are fed (1x1 layers of YOLO26-N
     // at batch 64: 512 -> 256 at 20^2 40.0 -> 29.8 us, 384 -> 128 at 40^2
     // 48.1 -> 40.2 us). With at most two stages per tile (128 input
-    // channels) and for 3x3 filters they measured slower.
+    // channels) and for 3x3 filters they measured slower, and 128-channel
+    // stages for 512 input channels and whole-filter 32-channel stages
+    // for 3x3 filters no faster.
     const int c4[4][2] = {{1, 64}, {1, 32}, {0, 16}, {1, 16}};
     std::memcpy(cand, c4, sizeof cand);
   } else if (trans && (p.sH > 1 || p.sW > 1)) {
@@ -1599,7 +1601,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t b_copy = uint32_t(g.R) * 16;
       if (g.resident && pi == 0) {
         // (one copy: splitting it into per-stage pieces, each on its own
-        // barrier, measured slower on B200)
+        // barrier, or into one piece per issuer, measured no faster on B200)
         const uint32_t wb = smem_u32(wbar);
         mbar_expect_tx(wb, g.w_region_bytes);
         if (WGX_IN_BOUNDS(wpk, g.w_region_bytes, wpk, g.wpk_bytes, g.err))
@@ -1853,12 +1855,15 @@ __global__ void __launch_bounds__(THREADS, 1)
               gstart = grp_list[2 * (sw.khg * kMaxPhases + sw.phase)];
               gcount = grp_list[2 * (sw.khg * kMaxPhases + sw.phase) + 1];
             }
-            if (gcount <= kSeqGroups) {
+            // batches of at most kSeqGroups groups (a branch between
+            // batches, none inside one)
+            for (int base = 0; base < gcount; base += kSeqGroups) {
+              const int nb = gcount - base < kSeqGroups ? gcount - base : kSeqGroups;
               uint2 e[kSeqGroups];
 #pragma unroll
               for (int k = 0; k < kSeqGroups; ++k) {
-                const int j = k - (kSeqGroups - gcount);
-                e[k] = grp_off[gstart + (j < 0 ? 0 : j)];
+                const int j = k - (kSeqGroups - nb);
+                e[k] = grp_off[gstart + base + (j < 0 ? 0 : j)];
               }
 #define WGX_GROUP(K)                                                                      \
   {                                                                                       \
@@ -1872,7 +1877,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }                                                                                     \
     acc_flag = 1;                                                                         \
   }
-              switch (gcount) {
+              switch (nb) {
                 case 8: WGX_GROUP(0) [[fallthrough]];
                 case 7: WGX_GROUP(1) [[fallthrough]];
                 case 6: WGX_GROUP(2) [[fallthrough]];
@@ -1883,22 +1888,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 default: WGX_GROUP(7)
               }
 #undef WGX_GROUP
-            } else {
-#pragma unroll 2
-              for (int j = 0; j < ngroups; ++j) {
-                const uint2 o = grp_off[j];
-                const uint64_t xd = x0 + o.x, wd = w0 + o.y;
-                if constexpr (TRANS) {
-#pragma unroll
-                  for (int k2 = 0; k2 < G_C / NISS; ++k2) {
-                    const int mb = k2 * NISS + iss;
-                    mma_f16(d + uint32_t(mb * NT_C), xd + uint64_t(mb * 128), wd, idesc, acc_flag);
-                  }
-                } else {
-                  mma_f16(d, wd, xd, idesc, acc_flag);
-                }
-                acc_flag = 1;
-              }
             }
           }
           acc_on = 1;

@@ -15,9 +15,10 @@ from ctypes import (POINTER, Structure, Union, c_char_p, c_double, c_float, c_in
 
 PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 # WGX_LIBRARY=bounds loads the bounds-checking debug build (lib/libwgx_bounds.so,
-# `make -C wgpu-executorch_b200 bounds`) instead of the normal library.
-LIB_PATH = os.path.join(PKG_DIR, "lib", "libwgx_bounds.so" if os.environ.get("WGX_LIBRARY") ==
-                        "bounds" else "libwgx.so")
+# `make -C wgpu-executorch_b200 bounds`) instead of the normal library;
+# WGX_LIBRARY_PATH names any other build of the same C ABI.
+LIB_PATH = os.environ.get("WGX_LIBRARY_PATH") or os.path.join(
+    PKG_DIR, "lib", "libwgx_bounds.so" if os.environ.get("WGX_LIBRARY") == "bounds" else "libwgx.so")
 
 WGX_OK = 0
 WGX_ERR_INVALID = 1
