@@ -159,6 +159,9 @@ struct UmmaGeom {
   // failure-detection tests (WGX_INJECT_SKIP_LOADS): the producer issues no
   // copies, so the other roles' bounded waits run out
   int inject_skip;
+  // split = 1: each stage's copies are split across several issuing threads
+  // (see the producer); 0: one issuer
+  int split;
   // per-image weights (a batched GEMM: aten.bmm as a 1x1 convolution whose
   // weights differ per image): packed weight bytes per image, 0 = shared
   uint64_t w_img_bytes;
@@ -455,6 +458,16 @@ static bool bk64_wanted(const wgx_conv2d_params &p) {
     case 3: return one;
     default: return true;
   }
+}
+
+// Copy issue of the activation stages: WGX_CONV_SPLIT=0 one issuing
+// thread, =1 (default) several (the same copies either way).
+static int split_mode() {
+  static const int mode = [] {
+    const char *e = std::getenv("WGX_CONV_SPLIT");
+    return (e && e[0] >= '0' && e[0] <= '1') ? e[0] - '0' : 1;
+  }();
+  return mode;
 }
 
 // Pick the staging: per-filter-row stages of 32 channels measured fastest
@@ -1504,6 +1517,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   constexpr int NISS = DUAL ? 2 : 1;
   // copy-issuing threads (see the producer)
   constexpr int NPI = DUAL ? 2 : 3;
+  const int npi = g.split ? NPI : 1;
   // activation stages first, on a 1024-byte boundary (128-byte swizzle atoms
   // of the direct mode); stage sizes are multiples of 1024 bytes there
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -1528,7 +1542,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&full[s]), NPI);
+      mbar_init(smem_u32(&full[s]), npi);
       mbar_init(smem_u32(&empty[s]), NISS);
     }
     for (int a = 0; a < 2; ++a) {
@@ -1588,7 +1602,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #endif
 
   if (warp == 0 || warp == 3 || (!DUAL && warp == 2)) {
-    if (lane == 0 && !g.inject_skip) {
+    const int pi = warp == 0 ? 0 : warp == 3 ? 1 : 2;
+    if (lane == 0 && !g.inject_skip && pi < npi) {
       // ---------------- producers: bulk copies of weights + activation rows.
       // NPI threads (lane 0 of warps 0, 3 and, without a second MMA issuer,
       // 2) walk the same stage sequence and split each stage's copies: the
@@ -1596,8 +1611,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       // than from one (measured on B200: eight 4 KB copies per stage, one
       // issuer ~16 B/clk per SM, four issuers ~22 B/clk). Each issuer
       // arrives on the stage's full barrier once with its own byte count;
-      // issuer 0 also copies the weights.
-      const int pi = warp == 0 ? 0 : warp == 3 ? 1 : 2;
+      // issuer 0 also copies the weights. In the direct mode the issuers
+      // take every npi-th 64-position atom of each channel box (YOLO26-N
+      // batch 64, 1x1 layers over concatenations of 16-channel sources:
+      // 48 -> 64 at 160^2 105 -> 86 us against one issuer).
       const uint32_t b_copy = uint32_t(g.R) * 16;
       if (g.resident && pi == 0) {
         // (one copy: splitting it into per-stage pieces, each on its own
@@ -1607,11 +1624,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (WGX_IN_BOUNDS(wpk, g.w_region_bytes, wpk, g.wpk_bytes, g.err))
           bulk_g2s(smem_u32(sW), wpk, g.w_region_bytes, wb);
       }
-      // this issuer's share of a stage: chunk copies ch = pi, pi + NPI, ...;
-      // direct-mode boxes q = pi, pi + NPI, ... of the stage's box list
-      const int my_chunks = g.chunks > pi ? (g.chunks - pi + NPI - 1) / NPI : 0;
-      const int nj = (g.tile_pos + 63) / 64, nq = g.direct ? (g.bk / g.dbox) * nj : 0;
-      const int my_boxes = g.direct && nq > pi ? (nq - pi + NPI - 1) / NPI : 0;
+      // this issuer's share of a stage: chunk copies ch = pi, pi + npi, ...;
+      // direct-mode atoms j = pi, pi + npi, ... of every channel box
+      const int my_chunks = g.chunks > pi ? (g.chunks - pi + npi - 1) / npi : 0;
+      const int nj = g.tile_pos / 64;
+      const int my_boxes = g.direct && nj > pi ? (g.bk / g.dbox) * ((nj - pi + npi - 1) / npi) : 0;
       const uint32_t my_bytes =
           (g.resident || pi != 0 ? 0u : g.a_stage_bytes) +
           (g.direct ? uint32_t(my_boxes) * uint32_t(g.dbox) * 128u : uint32_t(my_chunks) * b_copy);
@@ -1656,21 +1673,25 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (g.direct) {
             // TMA boxes of 64 positions x dbox channels: atom j (64 positions,
             // bk rows of 128 bytes) at j * bk * 128, channel group rows inside
-            uint8_t *stage = sB + size_t(slot) * g.b_stage_bytes;
-            for (int q = pi; q < nq; q += NPI) {
-              const int c = cbk * g.bk + (q / nj) * g.dbox, j = q % nj;
+            // (this issuer: atoms j = pi, pi + npi, ... of every channel box;
+            // no per-box division or source search, the issuing thread's
+            // own instruction time bounds how fast small boxes go out)
+            const uint32_t stage = smem_u32(sB + size_t(slot) * g.b_stage_bytes);
+            const uint32_t jstep = uint32_t(npi) * uint32_t(g.bk) * 128u;
+            for (int c = cbk * g.bk, row = 0; row < g.bk; c += g.dbox, row += g.dbox) {
               int src = 0;
               for (int k = 1; k < g.nsrc; ++k)
                 if (c >= g.src_c0[k]) src = k;
               const int y = c - g.src_c0[src];
-              const int row = c - cbk * g.bk;
-              tma_load_3d(smem_u32(stage + size_t(j) * g.bk * 128 + size_t(row) * 128),
-                          &tm.m[src], int(p0) + 64 * j, y, b, fb);
+              const void *map = &tm.m[src];
+              uint32_t dst = stage + uint32_t(pi) * uint32_t(g.bk) * 128u + uint32_t(row) * 128u;
+              for (int j = pi; j < nj; j += npi, dst += jstep)
+                tma_load_3d(dst, map, int(p0) + 64 * j, y, b, fb);
             }
             continue;
           }
           const long long row0 = p0 + (long long)khg * g.khs * g.dH * g.Wp;
-          for (int ch = pi; ch < g.chunks; ch += NPI) {
+          for (int ch = pi; ch < g.chunks; ch += npi) {
             const long long plane = (long long)b * (g.C8 / 8) + cbk * g.chunks + ch;
             const uint8_t *xsrc = xs + (plane * g.plane_rows + row0) * 16;
             if (WGX_IN_BOUNDS(xsrc, b_copy, xs, g.xs_bytes, g.err))
@@ -2368,6 +2389,7 @@ void umma_conv_run(const wgx_conv2d_params &p, const __half *in, void *packed,
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   g.err = device_error_word(dev);
   g.inject_skip = inject_skip_loads() ? 1 : 0;
+  g.split = split_mode() != 0;
   // extents for the bounds-checking build
   g.out_bytes = uint64_t(p.B) * p.OC * p.OH * p.OW * 2;
   g.xs_bytes = umma_conv_input_bytes(p, per_image_w);
