@@ -372,12 +372,18 @@ def kernel_configs(ctx, local, steps, peak_tf, peak_hbm):
     out = {}
 
     def timed(launch, n):
+        # Each step: a ~100 us device-side delay (torch.cuda._sleep, bounded),
+        # the L2 flush, then the timed call. The delay keeps the GPU busy
+        # while the host enqueues the flush, the events and the call's
+        # launches, so the event pair brackets the call's device time, not
+        # the host's launch overhead.
         s = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
         e = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
         for i in range(3):
             launch()
         for i in range(n):
             with torch.cuda.stream(ext):
+                torch.cuda._sleep(200000)
                 flush.fill_(i)
                 flush_rd.max()
                 s[i].record(ext)
@@ -526,6 +532,9 @@ def l2_flusher(local):
     flush_rd = torch.ones(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
 
     def run(i):
+        # (a bounded ~100 us device-side delay first, so the host's launches
+        # of the flush, the events and the step queue up behind it)
+        torch.cuda._sleep(200000)
         flush.fill_(i)
         flush_rd.max()
     return run

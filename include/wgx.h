@@ -156,7 +156,11 @@ WGX_API int wgx_reset(wgx_context *ctx);
 WGX_API int wgx_context_stats(const wgx_context *ctx, int64_t *n_commands, int64_t *n_kernel_launches);
 /* Replays the recorded commands eagerly (outside the captured graph)
  * `repeats` times with a CUDA event pair around each command and writes the
- * mean milliseconds of command i to ms[i] (at most `capacity` entries);
+ * mean milliseconds of command i to ms[i] (at most `capacity` entries).
+ * Each replay is held on the device (a one-thread kernel polling a mapped
+ * host word, at most 1 s) until the host has enqueued all of it: the pairs
+ * time the device work of back-to-back commands, as in a graph replay, not
+ * the host's launch rate;
  * *count receives the number of commands. The reference times whole
  * submits only (utils/benchmark/main.ts:60-77); this is the per-command
  * breakdown of that figure. */

@@ -590,6 +590,19 @@ int wgx_context_stats(const wgx_context *ctx, int64_t *n_commands, int64_t *n_ke
   });
 }
 
+// Holds the stream until the host has enqueued what follows: spins until
+// the mapped host word *flag reaches `target`, or for at most `limit_ns` of
+// %globaltimer (bounded: a host that never writes only costs the limit).
+__global__ void hold_stream(const volatile int *flag, int target, uint64_t limit_ns) {
+  uint64_t t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  do {
+    if (*flag >= target) return;
+    __nanosleep(500);
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  } while (t - t0 < limit_ns);
+}
+
 int wgx_context_profile(wgx_context *ctx, int repeats, double *ms, int capacity, int *count) {
   return guarded([&] {
     assert_alive(ctx);
@@ -601,18 +614,39 @@ int wgx_context_profile(wgx_context *ctx, int repeats, double *ms, int capacity,
     ExecEnv env = ensure_workspace(ctx);
     std::vector<cudaEvent_t> ev(size_t(n) + 1, nullptr);
     std::vector<double> total(size_t(n), 0.0);
+    // The host takes microseconds per launch; if the GPU ran each command as
+    // soon as it was enqueued, every event pair would include that wait. A
+    // one-thread kernel holds the stream until the host has enqueued the
+    // whole replay (a mapped host word it polls, bounded by 1 s), so each
+    // pair brackets the command's device time, back to back as in a graph.
+    volatile int *flag = nullptr;
+    int *dflag = nullptr;
     auto release = [&] {
+      if (flag) {
+        *flag = 1 << 30;  // frees a hold that is still polling
+        cudaStreamSynchronize(ctx->stream);
+        cudaFreeHost(const_cast<int *>(flag));
+      }
       for (auto e : ev)
         if (e) cudaEventDestroy(e);
     };
     try {
+      void *hp = nullptr;
+      check_cuda(cudaHostAlloc(&hp, sizeof(int), cudaHostAllocMapped), "profile flag");
+      flag = static_cast<volatile int *>(hp);
+      *flag = 0;
+      check_cuda(cudaHostGetDevicePointer(reinterpret_cast<void **>(&dflag), hp, 0),
+                 "profile flag");
       for (auto &e : ev) check_cuda(cudaEventCreate(&e), "profile event");
       for (int r = 0; r < repeats; ++r) {
+        hold_stream<<<1, 1, 0, ctx->stream>>>(dflag, r + 1, 1000000000ull);
+        check_cuda(cudaGetLastError(), "profile hold");
         check_cuda(cudaEventRecord(ev[0], ctx->stream), "profile record");
         for (int i = 0; i < n; ++i) {
           ctx->commands[size_t(i)].run(env);
           check_cuda(cudaEventRecord(ev[size_t(i) + 1], ctx->stream), "profile record");
         }
+        __atomic_store_n(const_cast<int *>(flag), r + 1, __ATOMIC_RELEASE);
         check_cuda(cudaEventSynchronize(ev[size_t(n)]), "profile sync");
         for (int i = 0; i < n; ++i) {
           float t = 0.f;
