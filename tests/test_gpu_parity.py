@@ -329,6 +329,27 @@ def test_mm_fp32_shapes(ctx, mkn):
     assert oracle.rel_err(y, oracle.mm(a, b, "wgsl")) <= F32_TOL
 
 
+@pytest.mark.parametrize("mkn", [
+    (1024, 512, 1024),  # 64 tiles x 2 K slices of 4 rounds
+    (768, 1024, 768),   # 36 tiles x 4 K slices
+    (2048, 256, 1024),  # 128 tiles, K not split
+    (512, 4096, 512),   # 16 tiles x 8 K slices of 8 rounds
+])
+@pytest.mark.parametrize("scale", [1.0, 1e3])
+def test_mm_fp32_tensor_core(ctx, mkn, scale):
+    """fp32 mm on tcgen05 (3xTF32: TF32 heads and fp32 tails of both
+    operands; products of at least 2^29 multiply-adds take this path)
+    against both oracle modes at the fp32 bound, with inputs spanning six
+    orders of magnitude."""
+    M, K, N = mkn
+    a, b = oracle.make_inputs([(M, K), (K, N)], seed=82, dist="uniform", dtype=np.float32)
+    a = (a * scale).astype(np.float32)
+    b[:, ::3] *= 1e-3  # columns of mixed magnitude
+    y = engine_mm(ctx, a, b)
+    assert oracle.rel_err(y, oracle.mm(a, b, "exact")) <= F32_TOL
+    assert oracle.rel_err(y, oracle.mm(a, b, "wgsl")) <= F32_TOL
+
+
 @pytest.mark.parametrize("mkn", [(512, 512, 512), (100, 72, 300), (64, 8, 1000), (300, 200, 7),
                                  (257, 1024, 129), (5, 7, 3)])
 def test_mm_fp16(ctx, mkn):

@@ -1494,6 +1494,11 @@ __global__ void __launch_bounds__(256) mm_f32_kernel(const float *__restrict__ A
 void launch_mm(const void *a, const void *b, void *out, int64_t M, int64_t N, int64_t K,
                int dtype, void *scratch, uint64_t scratch_bytes, cudaStream_t stream) {
   wgx_conv2d_params p = mm_params(M, N, K, dtype);
+  if (dtype == WGX_FLOAT32 && mm_tf32_supported(a, b, out, M, N, K)) {
+    mm_tf32_run(static_cast<const float *>(a), static_cast<const float *>(b),
+                static_cast<float *>(out), M, N, K, dw_sm_count(), stream);
+    return;
+  }
   if (dtype == WGX_FLOAT32) {
     const int64_t gy = (M + MM_T - 1) / MM_T, gx = (N + MM_T - 1) / MM_T;
     if (gy > 65535 || gx > INT32_MAX) fail("aten.mm.default: matrix too large");
