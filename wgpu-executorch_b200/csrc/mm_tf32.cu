@@ -14,7 +14,8 @@
 // oracles; measured 5e-6 at 1024^3, 2e-5 at 2048^3, against 1e-6 / 2e-6
 // for FFMA).
 //
-// Tiling: one 128 x 128 output tile per cluster of S CTAs (S = 1..8); CTA r
+// Tiling: one 128 x 128 output tile per cluster of S CTAs (S = 1..8, all
+// clusters resident at once); CTA r
 // of the cluster multiplies K slice r into its own TMEM accumulator (128
 // lanes x 128 fp32 columns), 64 K at a time: all 256 threads load the A and
 // B slices with 16-byte loads, split them and store the four operands in
@@ -41,12 +42,14 @@ constexpr uint32_t kOpBytes = kTile * kKB * 4;  // one operand of one round: 32 
 constexpr int kPitch = kTile + 4;              // partial tile row pitch (floats)
 constexpr uint32_t kSmem = 4 * kOpBytes + 1024 + 64;
 
-bool tf32_enabled() {
-  static const bool on = [] {
+// WGX_MM_TF32: 0 = never, 1 (default) = products of at least 2^29
+// multiply-adds, 2 = every size the tiling takes
+int tf32_mode() {
+  static const int mode = [] {
     const char *e = std::getenv("WGX_MM_TF32");
-    return !(e && e[0] == '0');
+    return (e && e[0] >= '0' && e[0] <= '2') ? e[0] - '0' : 1;
   }();
-  return on;
+  return mode;
 }
 
 __device__ __forceinline__ void mma_tf32(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
@@ -256,12 +259,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 // 16-byte aligned; and products of at least 2^29 multiply-adds. Below that
 // the phases of one CTA (load and split, MMAs, TMEM drain, cluster
 // reduction) do not overlap and the FFMA kernel is faster (B200, L2 flushed:
-// 512^3 25 us here, 18 us FFMA; 1024^3 47 against 73 us; 2048^3 299 against
-// 447 us).
+// 512^3 19.4 us here, 17.5 us FFMA; 1024^3 47 against 73 us; 2048^3 299
+// against 446 us).
 bool mm_tf32_supported(const void *a, const void *b, const void *c, int64_t M, int64_t N,
                        int64_t K) {
-  if (!tf32_enabled()) return false;
-  if (double(M) * double(N) * double(K) < double(1ll << 29)) return false;
+  if (tf32_mode() == 0) return false;
+  if (tf32_mode() == 1 && double(M) * double(N) * double(K) < double(1ll << 29)) return false;
   if (M < kTile || N < kTile || K < kKB || M % kTile || N % kTile || K % kKB) return false;
   if (M > (1 << 20) || N > (1 << 20) || K > (1 << 20)) return false;
   return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
@@ -273,16 +276,26 @@ void mm_tf32_run(const float *a, const float *b, float *c, int64_t M, int64_t N,
                  int n_sm, cudaStream_t stream) {
   const int64_t gx = N / kTile, gy = M / kTile, tiles = gx * gy;
   if (gy > 65535) fail("aten.mm.default: matrix too large");
-  // split K over a cluster of S CTAs while the grid stays within the SMs
-  // and every slice keeps whole 64-column rounds
-  int S = 1;
-  while (S < 8 && tiles * S * 2 <= n_sm && K % (2 * S * kKB) == 0) S *= 2;
-  const int kslice = int(K / S);
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
-  {
-    static std::mutex mu;
-    static bool attr_set[64] = {};
+  static_assert(kTile * kPitch * 4 <= 4 * kOpBytes, "partial tile fits the operand space");
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(gx), unsigned(gy), 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // clusters of S CTAs that can be resident at once (per device and S; a
+  // cluster needs S SMs of one GPC, so on B200 only 15 clusters of 8 fit)
+  static std::mutex mu;
+  static bool attr_set[64] = {};
+  static int max_clusters[64][4] = {};
+  auto resident_clusters = [&](int S) {
     std::lock_guard<std::mutex> lock(mu);
     if (dev >= 64 || !attr_set[dev]) {
       check_cuda(cudaFuncSetAttribute(mm_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -290,20 +303,26 @@ void mm_tf32_run(const float *a, const float *b, float *c, int64_t M, int64_t N,
                  "mm tf32 smem attr");
       if (dev < 64) attr_set[dev] = true;
     }
-  }
-  static_assert(kTile * kPitch * 4 <= 4 * kOpBytes, "partial tile fits the operand space");
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(gx), unsigned(gy), unsigned(S));
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = 1;
+    const int si = S == 1 ? 0 : S == 2 ? 1 : S == 4 ? 2 : 3;
+    if (dev < 64 && max_clusters[dev][si]) return max_clusters[dev][si];
+    cudaLaunchConfig_t q = cfg;
+    q.gridDim.z = unsigned(S);
+    attr[0].val.clusterDim.z = unsigned(S);
+    int n = 0;
+    check_cuda(cudaOccupancyMaxActiveClusters(&n, mm_tf32_kernel, &q), "mm tf32 cluster occupancy");
+    if (dev < 64) max_clusters[dev][si] = n;
+    return n;
+  };
+  // split K over a cluster of S CTAs while the grid stays within the SMs,
+  // every cluster is resident at once (one wave) and every slice keeps
+  // whole 64-column rounds
+  int S = 1;
+  while (S < 8 && tiles * S * 2 <= n_sm && K % (2 * S * kKB) == 0 &&
+         tiles <= resident_clusters(2 * S))
+    S *= 2;
+  const int kslice = int(K / S);
+  cfg.gridDim.z = unsigned(S);
   attr[0].val.clusterDim.z = unsigned(S);
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   int th = timer_begin("mm_tf32_kernel", stream);
   check_cuda(cudaLaunchKernelEx(&cfg, mm_tf32_kernel, a, b, c, int(M), int(N), int(K), kslice,
                                 device_error_word(dev)),
