@@ -180,7 +180,7 @@ struct ConvLaunch;  // defined in conv.cu
 void launch_mm(const void *a, const void *b, void *out, int64_t M, int64_t N, int64_t K,
                int dtype, void *scratch, uint64_t scratch_bytes, cudaStream_t stream);
 // fp32 mm on the tensor cores (3xTF32, mm_tf32.cu) for the sizes it tiles
-// (M, N multiples of 128, K of 64, 16-byte aligned, at least 2^29
+// (M, N multiples of 128, K of 32, 16-byte aligned, at least 2^29
 // multiply-adds); launch_mm uses it when mm_tf32_supported. WGX_MM_TF32=0
 // keeps every fp32 mm on the FFMA kernel, =2 takes every size it tiles.
 bool mm_tf32_supported(const void *a, const void *b, const void *c, int64_t M, int64_t N,

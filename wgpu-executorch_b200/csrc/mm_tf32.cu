@@ -17,11 +17,12 @@
 // Tiling: one 128 x 128 output tile per cluster of S CTAs (S = 1..8, all
 // clusters resident at once); CTA r
 // of the cluster multiplies K slice r into its own TMEM accumulator (128
-// lanes x 128 fp32 columns), 64 K at a time: all 256 threads load the A and
-// B slices with 16-byte loads, split them and store the four operands in
-// the K-major no-swizzle layout (rows of 4 fp32 = 16 bytes, one plane per
-// 4 K columns; B is transposed on the way), one thread issues the
-// 8 K steps x 3 MMAs (M 128, N 128, K 8). The partial tiles then go to
+// lanes x 128 fp32 columns), 32 K at a time through two operand buffers:
+// all 256 threads load the A and B slices with 16-byte loads, split them and
+// store the four operands in the K-major no-swizzle layout (rows of 4 fp32 =
+// 16 bytes, one plane per 4 K columns; B is transposed on the way), one
+// thread issues the 4 K steps x 3 MMAs (M 128, N 128, K 8); the next
+// round's loads are in flight meanwhile. The partial tiles then go to
 // shared memory and CTA r sums rows 16r.. of all S partials in rank order
 // through distributed shared memory (deterministic, no atomics) and stores
 // them. The MMA completion wait is bounded (device error word on expiry).
@@ -36,11 +37,12 @@ namespace wgx {
 namespace {
 
 constexpr int kTile = 128;
-constexpr int kKB = 64;                        // K per round
+constexpr int kKB = 32;                        // K per round
 constexpr int kThreads = 256;
-constexpr uint32_t kOpBytes = kTile * kKB * 4;  // one operand of one round: 32 KB
+constexpr uint32_t kOpBytes = kTile * kKB * 4;  // one operand of one round: 16 KB
+constexpr uint32_t kBufBytes = 4 * kOpBytes;    // A_hi, A_lo, B_hi, B_lo of one round
 constexpr int kPitch = kTile + 4;              // partial tile row pitch (floats)
-constexpr uint32_t kSmem = 4 * kOpBytes + 1024 + 64;
+constexpr uint32_t kSmem = 2 * kBufBytes + 1024 + 64;
 
 // WGX_MM_TF32: 0 = never, 1 (default) = products of at least 2^29
 // multiply-adds, 2 = every size the tiling takes
@@ -85,8 +87,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // rows x 16 bytes
   uint8_t *ops = smem;
   float *part = reinterpret_cast<float *>(smem);  // partial tile, after the MMAs
-  uint64_t *done = reinterpret_cast<uint64_t *>(smem + 4 * kOpBytes);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  // done[b]: the MMAs of the last round staged in buffer b completed
+  uint64_t *done = reinterpret_cast<uint64_t *>(smem + 2 * kBufBytes);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 2);
 
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int S = gridDim.z, rank = blockIdx.z;
@@ -94,7 +97,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kb = rank * kslice, ke = min(K, kb + kslice);
 
   if (tid == 0) {
-    mbar_init(smem_u32(done), 1);
+    mbar_init(smem_u32(&done[0]), 1);
+    mbar_init(smem_u32(&done[1]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
@@ -113,22 +117,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                          | (2u << 7) | (2u << 10)   // A, B = tf32
                          | (uint32_t(kTile >> 3) << 17) | (uint32_t(kTile >> 4) << 24);
   const uint32_t plane = kTile * 16;  // 2 KB: one plane of 4 K columns
-  int round = 0;
-  for (int k0 = kb; k0 < ke; k0 += kKB, ++round) {
-    if (round > 0) {
-      // the previous round's MMAs have read the operands
-      if (!mbar_wait(smem_u32(done), uint32_t(round - 1) & 1)) atomicOr(err, kErrMmaTimeout);
-      tc_fence_after();
-      __syncthreads();
-    }
-    // A slice: rows m0.., columns k0.. (a warp task = 8 rows x 16 columns:
-    // lane = quad * 8 + row, so 8 lanes store 8 consecutive 16-byte rows of
-    // one plane). B slice: a thread task = 4 K rows x 4 columns, transposed to
-    // rows of 4 K. Every load of the round is issued before the first use, so
-    // the round pays one memory latency, not one per task.
-    constexpr int kATasks = (kTile / 8) * (kKB / 16) / (kThreads / 32);   // 8 per warp
-    constexpr int kBTasks = (kKB / 4) * (kTile / 4) / kThreads;           // 2 per thread
-    float4 av[kATasks], bv[kBTasks][4];
+  // Rounds of 32 K, two operand buffers: the global loads of round r + 1
+  // go into registers right after round r is staged, so their latency
+  // overlaps round r's MMAs (and round r - 1's, still in flight).
+  constexpr int kATasks = (kTile / 8) * (kKB / 16) / (kThreads / 32);  // 4 per warp
+  constexpr int kBTasks = (kKB / 4) * (kTile / 4) / kThreads;          // 1 per thread
+  float4 av[kATasks], bv[kBTasks][4];
+  auto load_round = [&](int k0) {
 #pragma unroll
     for (int i = 0; i < kATasks; ++i) {
       const int t = warp + i * (kThreads / 32);
@@ -143,6 +138,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < 4; ++j)
         bv[i][j] = *reinterpret_cast<const float4 *>(B + size_t(k0 + 4 * q + j) * N + n0 + 4 * nq);
     }
+  };
+  // A: a warp task = 8 rows x 16 columns (lane = quad * 8 + row: 8 lanes
+  // store 8 consecutive 16-byte rows of one plane); B: a thread task = 4 K
+  // rows x 4 columns, transposed to rows of 4 K
+  auto stage_round = [&](uint8_t *ops) {
 #pragma unroll
     for (int i = 0; i < kATasks; ++i) {
       const int t = warp + i * (kThreads / 32);
@@ -171,29 +171,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<float4 *>(ops + 3 * kOpBytes + q * plane + n * 16) = l;
       }
     }
+  };
+  const int rounds = (ke - kb) / kKB;
+  if (rounds > 0) load_round(kb);
+  for (int rd = 0; rd < rounds; ++rd) {
+    const int buf = rd & 1;
+    uint8_t *ops = smem + size_t(buf) * kBufBytes;
+    if (rd >= 2) {
+      // the MMAs of round rd - 2 have read this buffer
+      if (!mbar_wait(smem_u32(&done[buf]), uint32_t((rd - 2) >> 1) & 1))
+        atomicOr(err, kErrMmaTimeout);
+      tc_fence_after();
+    }
+    stage_round(ops);
+    if (rd + 1 < rounds) load_round(kb + (rd + 1) * kKB);
     // generic-proxy stores -> visible to the tensor cores
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
       const uint32_t base = smem_u32(ops);
-      const int steps = min(kKB, ke - k0) / 8;
-      for (int ks = 0; ks < steps; ++ks) {
+#pragma unroll
+      for (int ks = 0; ks < kKB / 8; ++ks) {
         // K step ks: planes 2ks, 2ks+1 (LBO = one plane), rows 16 B apart
         const uint32_t off = uint32_t(ks) * 2u * plane;
         const uint64_t ah = kmajor_desc(base + 0 * kOpBytes + off, plane);
         const uint64_t al = kmajor_desc(base + 1 * kOpBytes + off, plane);
         const uint64_t bh = kmajor_desc(base + 2 * kOpBytes + off, plane);
         const uint64_t bl = kmajor_desc(base + 3 * kOpBytes + off, plane);
-        mma_tf32(tmem, al, bh, idesc, (round > 0 || ks > 0) ? 1u : 0u);
+        mma_tf32(tmem, al, bh, idesc, (rd > 0 || ks > 0) ? 1u : 0u);
         mma_tf32(tmem, ah, bl, idesc, 1u);
         mma_tf32(tmem, ah, bh, idesc, 1u);
       }
-      mma_commit(smem_u32(done));
+      mma_commit(smem_u32(&done[buf]));
     }
   }
-  // all MMAs complete before the partial tile leaves TMEM
-  if (round > 0 && !mbar_wait(smem_u32(done), uint32_t(round - 1) & 1))
+  // all MMAs complete before the partial tile leaves TMEM (the last commit
+  // covers every MMA issued before it)
+  const int round = rounds;
+  if (rounds > 0 &&
+      !mbar_wait(smem_u32(&done[(rounds - 1) & 1]), uint32_t((rounds - 1) >> 1) & 1))
     atomicOr(err, kErrMmaTimeout);
   tc_fence_after();
   __syncthreads();
@@ -255,12 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-// Sizes the tiling takes: M, N multiples of 128, K a multiple of 64, every
-// 16-byte aligned; and products of at least 2^29 multiply-adds. Below that
-// the phases of one CTA (load and split, MMAs, TMEM drain, cluster
-// reduction) do not overlap and the FFMA kernel is faster (B200, L2 flushed:
-// 512^3 19.4 us here, 17.5 us FFMA; 1024^3 47 against 73 us; 2048^3 299
-// against 446 us).
+// Sizes the tiling takes: M, N multiples of 128, K a multiple of 32, every
+// 16-byte aligned; and products of at least 2^29 multiply-adds (B200, L2
+// flushed: 512^3 17.9 us here, 18.5 us FFMA, which also rounds less;
+// 1024^3 35 against 74 us; 2048^3 203 against 449 us).
 bool mm_tf32_supported(const void *a, const void *b, const void *c, int64_t M, int64_t N,
                        int64_t K) {
   if (tf32_mode() == 0) return false;
@@ -278,7 +293,7 @@ void mm_tf32_run(const float *a, const float *b, float *c, int64_t M, int64_t N,
   if (gy > 65535) fail("aten.mm.default: matrix too large");
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
-  static_assert(kTile * kPitch * 4 <= 4 * kOpBytes, "partial tile fits the operand space");
+  static_assert(kTile * kPitch * 4 <= 2 * kBufBytes, "partial tile fits the operand space");
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
