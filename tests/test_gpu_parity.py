@@ -330,10 +330,10 @@ def test_mm_fp32_shapes(ctx, mkn):
 
 
 @pytest.mark.parametrize("mkn", [
-    (1024, 512, 1024),  # 64 tiles x 2 K slices of 4 rounds
-    (768, 1024, 768),   # 36 tiles x 4 K slices
-    (2048, 256, 1024),  # 128 tiles, K not split
-    (512, 4096, 512),   # 16 tiles x 8 K slices of 8 rounds
+    (1024, 512, 1024),  # 64 tiles, K split over clusters of 2
+    (768, 1024, 768),   # 36 tiles, K split over clusters of 4
+    (2048, 256, 1024),  # 128 tiles, K not split (8 rounds of 32 in one CTA)
+    (512, 4096, 512),   # 16 tiles, K split over clusters of 4, 32 rounds each
 ])
 @pytest.mark.parametrize("scale", [1.0, 1e3])
 def test_mm_fp32_tensor_core(ctx, mkn, scale):
