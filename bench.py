@@ -454,6 +454,29 @@ def kernel_configs(ctx, local, steps, peak_tf, peak_hbm):
     ms_mm = timed(lambda: _lib.check(_lib.lib.wgx_mm(*mm_args)), steps)
     mm_tf = 2.0 * M * N * Kd / (ms_mm * 1e-3) / 1e12
     ffma_peak = FFMA_PEAK_TFLOPS()
+    # fp32 mm at 2048^3: the 3xTF32 tensor-core kernel (products of at least
+    # 2^29 multiply-adds; configs[0] itself stays on FFMA). Peak: the measured
+    # bf16 burst halved (TF32 runs at half the f16 rate) and divided by the
+    # three TF32 products per output term.
+    M2 = 2048
+    a2 = torch.rand(M2, M2, device=dev) * 2 - 1
+    b2 = torch.rand(M2, M2, device=dev) * 2 - 1
+    c2 = torch.empty(M2, M2, device=dev)
+    mm2_args = (ctypes.c_void_p(a2.data_ptr()), ctypes.c_void_p(b2.data_ptr()),
+                ctypes.c_void_p(c2.data_ptr()), M2, M2, M2, 0, None, ctypes.c_uint64(0),
+                ctypes.c_void_p(ctx.stream))
+    ms_mm2 = timed(lambda: _lib.check(_lib.lib.wgx_mm(*mm2_args)), max(5, steps // 4))
+    mm2_tf = 2.0 * M2 ** 3 / (ms_mm2 * 1e-3) / 1e12
+    tf32x3_peak = peak_tf / 2.0 / 3.0
+    out["mm_fp32_2048_tensor_cores"] = {
+        "workload": "fp32 mm [2048,2048] @ [2048,2048] (not a BASELINE config)",
+        "value": mm2_tf, "unit": "TFLOP/s", "ms_per_call": ms_mm2,
+        "path": "3xTF32 on tcgen05.mma kind::tf32 (fp32 accumulate)",
+        "roofline": {"bound": "tensor (TF32)", "kernel": "mm_tf32_kernel", "achieved": mm2_tf,
+                     "peak": tf32x3_peak, "unit": "TFLOP/s", "frac": mm2_tf / tf32x3_peak,
+                     "peak_source": "measured bf16 burst / 2 (TF32 rate) / 3 (products per "
+                                    "term)"}}
+    del a2, b2, c2
     out["configs[0]_mm_fp32"] = {"workload": "fp32 mm [512,512] @ [512,512]",
                                  "value": mm_tf, "unit": "TFLOP/s", "ms_per_call": ms_mm,
                                  "path": "FFMA (fp32 accumulate)",

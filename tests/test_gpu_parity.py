@@ -350,6 +350,35 @@ def test_mm_fp32_tensor_core(ctx, mkn, scale):
     assert oracle.rel_err(y, oracle.mm(a, b, "wgsl")) <= F32_TOL
 
 
+def test_mm_fp32_tensor_core_first_call(tmp_path):
+    """The tensor-core fp32 mm as the first call of a fresh process, on a
+    shape whose K is not split (every per-device set-up must happen on that
+    path too): the result against the exact oracle."""
+    import os
+    import subprocess
+    import sys
+    M, K, N = 2048, 256, 1024
+    a, b = oracle.make_inputs([(M, K), (K, N)], seed=83, dist="uniform", dtype=np.float32)
+    np.save(tmp_path / "a.npy", a)
+    np.save(tmp_path / "b.npy", b)
+    script = (
+        "import sys, numpy as np; sys.path.insert(0, %r); import wgx\n"
+        "ctx = wgx.WgpuExecutionContext(0)\n"
+        "a = np.load(%r); b = np.load(%r)\n"
+        "ta = ctx.tensor('float32', a.shape).setData(a)\n"
+        "tb = ctx.tensor('float32', b.shape).setData(b)\n"
+        "out = ctx.tensor('float32', [a.shape[0], b.shape[1]])\n"
+        "ctx.recordShader(wgx.shaders.mm, [ta, tb, out]); ctx.submit(); ctx.sync()\n"
+        "np.save(%r, out.numpy())\n"
+    ) % (os.path.dirname(os.path.dirname(os.path.abspath(wgx.__file__))), str(tmp_path / "a.npy"),
+         str(tmp_path / "b.npy"), str(tmp_path / "y.npy"))
+    r = subprocess.run([sys.executable, "-c", script], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    y = np.load(tmp_path / "y.npy")
+    assert oracle.rel_err(y, oracle.mm(a, b, "exact")) <= F32_TOL
+
+
 @pytest.mark.parametrize("mkn", [(512, 512, 512), (100, 72, 300), (64, 8, 1000), (300, 200, 7),
                                  (257, 1024, 129), (5, 7, 3)])
 def test_mm_fp16(ctx, mkn):

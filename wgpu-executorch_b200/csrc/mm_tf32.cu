@@ -310,7 +310,8 @@ void mm_tf32_run(const float *a, const float *b, float *c, int64_t M, int64_t N,
   static std::mutex mu;
   static bool attr_set[64] = {};
   static int max_clusters[64][4] = {};
-  auto resident_clusters = [&](int S) {
+  {
+    // (before any launch or occupancy query on this device)
     std::lock_guard<std::mutex> lock(mu);
     if (dev >= 64 || !attr_set[dev]) {
       check_cuda(cudaFuncSetAttribute(mm_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -318,6 +319,9 @@ void mm_tf32_run(const float *a, const float *b, float *c, int64_t M, int64_t N,
                  "mm tf32 smem attr");
       if (dev < 64) attr_set[dev] = true;
     }
+  }
+  auto resident_clusters = [&](int S) {
+    std::lock_guard<std::mutex> lock(mu);
     const int si = S == 1 ? 0 : S == 2 ? 1 : S == 4 ? 2 : 3;
     if (dev < 64 && max_clusters[dev][si]) return max_clusters[dev][si];
     cudaLaunchConfig_t q = cfg;
