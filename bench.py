@@ -915,10 +915,11 @@ def run_only(args):
         ctx.sync()
         print(json.dumps({"only": args.only, "steps": args.steps, "warmup": args.warmup,
                           "kernel_launches_per_step": ctx.stats()["kernel_launches"]}))
-    elif args.only == "mm0":
-        # fp32 mm 512^3 through wgx_mm
+    elif args.only in ("mm0", "mm1024"):
+        # fp32 mm 512^3 through wgx_mm (FFMA); mm1024: 1024^3 (the
+        # 3xTF32 tensor-core kernel)
         from wgx import _lib
-        M = N = Kd = 512
+        M = N = Kd = 512 if args.only == "mm0" else 1024
         a = torch.rand(M, Kd, device="cuda:0") * 2 - 1
         bm = torch.rand(Kd, N, device="cuda:0") * 2 - 1
         c = torch.empty(M, N, device="cuda:0")
@@ -927,7 +928,7 @@ def run_only(args):
                                        ctypes.c_void_p(c.data_ptr()), M, N, Kd, 0, None,
                                        ctypes.c_uint64(0), ctypes.c_void_p(ctx.stream)))
         ctx.sync()
-        print(json.dumps({"only": "mm0", "steps": args.steps, "warmup": args.warmup}))
+        print(json.dumps({"only": args.only, "steps": args.steps, "warmup": args.warmup}))
     else:
         rng = np.random.default_rng(0)
         cfg = ONLY_CONV[args.only]
@@ -949,7 +950,8 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--only", default=None, choices=["yolo", "depthart", "mm0"] + sorted(ONLY_CONV),
+    ap.add_argument("--only", default=None,
+                    choices=["yolo", "depthart", "mm0", "mm1024"] + sorted(ONLY_CONV),
                     help="run one workload's launches only (for profilers)")
     ap.add_argument("--batch", type=int, default=0,
                     help="images per GPU for --only (default: 64 for yolo, the listed batch otherwise)")
