@@ -72,6 +72,10 @@ __device__ __forceinline__ float4 tf32_head(float4 v) {
                      __uint_as_float(__float_as_uint(v.w) & m));
 }
 
+__device__ __forceinline__ float f4_get(const float4 &v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
@@ -157,16 +161,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int t = tid + i * kThreads;
       const int nq = t % (kTile / 4), q = t / (kTile / 4);
       const float4 *v = bv[i];
-      const float col[4][4] = {{v[0].x, v[1].x, v[2].x, v[3].x},
-                               {v[0].y, v[1].y, v[2].y, v[3].y},
-                               {v[0].z, v[1].z, v[2].z, v[3].z},
-                               {v[0].w, v[1].w, v[2].w, v[3].w}};
+      // column c of the 4x4 block goes to row 4 nq + c; lanes take the
+      // columns in an order rotated by (nq / 2) % 4, so the rows that the 8
+      // lanes of one store wavefront write differ mod 8 (distinct banks)
+      const int rot = (nq >> 1) & 3;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const float4 c4 = make_float4(col[c][0], col[c][1], col[c][2], col[c][3]);
+        const int cc = (c + rot) & 3;
+        const float4 c4 = make_float4(f4_get(v[0], cc), f4_get(v[1], cc), f4_get(v[2], cc),
+                                      f4_get(v[3], cc));
         const float4 h = tf32_head(c4);
         const float4 l = make_float4(c4.x - h.x, c4.y - h.y, c4.z - h.z, c4.w - h.w);
-        const int n = 4 * nq + c;
+        const int n = 4 * nq + cc;
         *reinterpret_cast<float4 *>(ops + 2 * kOpBytes + q * plane + n * 16) = h;
         *reinterpret_cast<float4 *>(ops + 3 * kOpBytes + q * plane + n * 16) = l;
       }
@@ -274,8 +280,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Sizes the tiling takes: M, N multiples of 128, K a multiple of 32, every
 // 16-byte aligned; and products of at least 2^29 multiply-adds (B200, L2
-// flushed: 512^3 17.9 us here, 18.5 us FFMA, which also rounds less;
-// 1024^3 35 against 74 us; 2048^3 203 against 449 us).
+// flushed: 512^3 17.4 us here, 18.0 us FFMA, which also rounds less;
+// 1024^3 34 against 73 us; 2048^3 191 against 447 us).
 bool mm_tf32_supported(const void *a, const void *b, const void *c, int64_t M, int64_t N,
                        int64_t K) {
   if (tf32_mode() == 0) return false;
