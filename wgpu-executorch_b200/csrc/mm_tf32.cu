@@ -15,15 +15,15 @@
 // for FFMA).
 //
 // Tiling: one 128 x 128 output tile per cluster of S CTAs (S = 1..8, all
-// clusters resident at once); CTA r
-// of the cluster multiplies K slice r into its own TMEM accumulator (128
-// lanes x 128 fp32 columns), 32 K at a time through two operand buffers:
+// clusters resident at once); CTA r of the cluster multiplies K slice r
+// into its own TMEM accumulator (128 lanes x 128 fp32 columns), 32 K at a
+// time through two operand buffers:
 // all 256 threads load the A and B slices with 16-byte loads, split them and
 // store the four operands in the K-major no-swizzle layout (rows of 4 fp32 =
 // 16 bytes, one plane per 4 K columns; B is transposed on the way), one
 // thread issues the 4 K steps x 3 MMAs (M 128, N 128, K 8); the next
 // round's loads are in flight meanwhile. The partial tiles then go to
-// shared memory and CTA r sums rows 16r.. of all S partials in rank order
+// shared memory and CTA r sums rows r*128/S.. of all S partials in rank order
 // through distributed shared memory (deterministic, no atomics) and stores
 // them. The MMA completion wait is bounded (device error word on expiry).
 #include <cstdlib>
